@@ -1,0 +1,329 @@
+"""Benchmark of the B200 binary-UNet forward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the Bi-Real dual-skip binary UNet (base width 32, 120 bands, 3
+classes, random weights from seed 0 with the benchmark's distributions) on
+4096 independent 32x32x120 float32 patches per GPU (seeded synthetic
+inputs, bnn_synth.h). A step is one forward over the GPU's 4096 patches.
+Under torchrun each rank takes its own slice of patch indices
+[rank*4096, (rank+1)*4096) (weak scaling, no collective on the data path);
+timing is the max over ranks.
+
+  value : patches/s with the inputs already in HBM (device-pointer API),
+          CUDA events on the launching stream around the K timed steps
+  e2e   : patches/s through the public host-pointer API bnn_forward_batch,
+          pinned host input -> logits in pinned host memory, every step
+  roofline : the dominant kernel family (17 fused binary convs, POPC
+          integer pipe) from per-kernel CUDA events over the same timed
+          steps
+  cpu_baseline : the reference engine compiled from its own sources
+          (oracle/_ref/ref_bench), all host cores, bounded sample
+
+--impl reference times only the reference CPU engine (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "UNet patches/s (32x32x120)"
+SEED_MODEL, SEED_INPUT = 0, 1
+POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide, cc 7.x-10.x)
+FP32_PER_CLK_SM = 128       # fp32 add / fma results / clock / SM
+
+
+def read_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.out = tempfile.TemporaryFile(mode="w+")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return model, os.cpu_count() or 1
+
+
+def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0):
+    """Reference engine (compiled from the reference sources) on the host."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_bench")
+    if not os.path.exists(exe):
+        return None, "oracle/_ref/ref_bench not built (needs the reference tree at build time)"
+    r = subprocess.run([exe, blob_path, str(n), str(H), str(W), str(procs), str(SEED_INPUT), str(steps),
+                        str(warm), str(first)], capture_output=True, text=True,
+                       env=dict(os.environ, OMP_NUM_THREADS="1"))
+    if r.returncode != 0:
+        return None, f"ref_bench failed: {r.stderr.strip()[-200:]}"
+    secs = [float(ln.split()[2]) for ln in r.stdout.splitlines() if ln.startswith("step ")]
+    return secs, None
+
+
+def model_blob():
+    from bnns_to_c_b200 import blob as B
+
+    return B.blob_bytes(B.random_model(32, 120, 3, seed=SEED_MODEL, rules="baseline"))
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    data = model_blob()
+    with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
+        f.write(data)
+        path = f.name
+    model, cores = cpu_info()
+    n = cores * args.ref_per_core
+    secs, err = ref_bench(path, n, args.H, args.W, cores, args.steps, max(0, min(args.warmup, 1)))
+    os.unlink(path)
+    if secs is None:
+        print(json.dumps({"impl": "reference", "unavailable": err}))
+        return 0
+    v = n * len(secs) / sum(secs)
+    sample = f"{n} patches per step ({args.ref_per_core} per core), {cores} single-threaded processes, {model}"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "patches/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * sum(secs) / len(secs), 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "b1+f32", "data": "synthetic",
+        "config": {"workload": "unet_c32_32x32x120", "base_channels": 32, "H": args.H, "W": args.W,
+                   "bands": 120, "classes": 3, "patches_per_step": n},
+        "cpu_baseline": {"value": round(v, 3), "unit": "patches/s", "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "patches/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import bnns_to_c_b200 as bn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def maxall(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    P, H, W = args.patches, args.H, args.W
+    m = bn.Model(data=model_blob())
+    m.set_devices([local])
+    first = rank * P
+    din = torch.empty((P, 120, H, W), dtype=torch.float32, device="cuda")
+    dout = torch.empty((P, 3, H, W), dtype=torch.float32, device="cuda")
+    bn.synth_device(local, SEED_INPUT, first, P, 120, H, W, din)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    # ---------------- device-resident value (+ per-kernel events) ----------------
+    m.profile(True)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            m.forward_device(local, din, P, H, W, dout, stream)
+    stream.synchronize()
+    m.profile_reset()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.forward_device(local, din, P, H, W, dout, stream)
+        e1.record(stream)
+        stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    dev_ms = maxall(e0.elapsed_time(e1))
+    recs = m.profile_records()
+    m.profile(False)
+    clocks = clk.summary()
+
+    # ---------------- end to end through the public host API ----------------
+    hin = torch.empty((P, 120, H, W), dtype=torch.float32, pin_memory=True)
+    hin.copy_(din.cpu())
+    hout = torch.empty((P, 3, H, W), dtype=torch.float32, pin_memory=True)
+    hin_np, hout_np = hin.numpy(), hout.numpy()
+    for _ in range(max(1, args.warmup)):
+        m.forward_batch(hin_np, out=hout_np)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward_batch(hin_np, out=hout_np)
+    e2e_s = maxall(time.perf_counter() - t0)
+    barrier()
+    # the two paths agree (same patches, same logits)
+    same = bool(torch.equal(hout.view(torch.int32), dout.cpu().view(torch.int32)))
+
+    if rank == 0:
+        peaks = read_peaks()
+        props = torch.cuda.get_device_properties(local)
+        sms = props.multi_processor_count
+        max_mhz = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz") or 1965.0
+        by_op = {}
+        for r in recs:
+            o = by_op.setdefault(r["op"], {"ms": 0.0, "work": 0.0, "calls": 0})
+            o["ms"] += r["ms"]; o["work"] += r["work"]; o["calls"] += r["calls"]
+        total_ms = sum(o["ms"] for o in by_op.values())
+        popc_peak = sms * POPC_PER_CLK_SM * 32 * max_mhz * 1e6 / 1e9     # Gbitop/s
+        fp32_peak = sms * FP32_PER_CLK_SM * max_mhz * 1e6 / 1e9         # G fp32 op/s
+        b = by_op.get("bconv", {"ms": 1e-9, "work": 0})
+        r_ = by_op.get("conv_real", {"ms": 1e-9, "work": 0})
+        bconv_ach = b["work"] / (b["ms"] * 1e6)   # work in bitMAC (Cout*H*W*Cin*9), ms -> Gbitop/s
+        real_ach = r_["work"] / (r_["ms"] * 1e6)  # fp32 adds (Cout*H*W*Cin*9)
+        launches_per_fwd = m.launches(P, H, W)
+        chunks = -(-P // 512)
+        value = P * world * args.steps / (dev_ms / 1e3)
+        e2e = P * world * args.steps / e2e_s
+        model, cores = cpu_info()
+        cpu = None
+        if not args.no_cpu_baseline:
+            with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
+                f.write(model_blob())
+                path = f.name
+            n = cores * args.ref_per_core
+            secs, err = ref_bench(path, n, H, W, cores, 1, 0)
+            os.unlink(path)
+            if secs:
+                cpu = {"value": round(n / secs[0], 3), "unit": "patches/s", "cores": cores, "kind": "reference",
+                       "sample": f"{n} patches of the same workload, {cores} single-threaded processes of the "
+                                 f"reference engine built from its sources, {model}"}
+            else:
+                cpu = {"value": None, "unit": "patches/s", "cores": cores, "kind": "reference", "sample": err}
+        frac_split = {k: round(v["ms"] / total_ms, 4) for k, v in by_op.items()} if total_ms else {}
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "patches/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "b1+f32",
+            "data": "synthetic",
+            "config": {"workload": "unet_c32_4096x32x32x120", "base_channels": 32, "bands": 120, "classes": 3,
+                       "H": H, "W": W, "patches_per_gpu": P, "global_batch": P * world,
+                       "parallelism": f"patch-shard x{world}",
+                       "l2": f"inputs > L2 ({P * 120 * H * W * 4 / 1e9:.2f} GB read per step)"},
+            "e2e": {"value": round(e2e, 1), "unit": "patches/s", "h2d_bytes_per_step": P * 120 * H * W * 4,
+                    "d2h_bytes_per_step": P * 3 * H * W * 4, "api": "bnn_forward_batch (pinned host buffers)",
+                    "matches_device_path": same},
+            "gpu_launches": launches_per_fwd * args.steps * (1 + chunks) + 0,
+            "roofline": {"bound": "popc", "kernel": "bconv3x3 (17 fused binary convs)",
+                         "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
+                         "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
+                         "peak_source": f"nominal: {sms} SMs x {POPC_PER_CLK_SM} POPC/clk x 32 bit x {max_mhz:.0f} MHz",
+                         "time_share": frac_split.get("bconv")},
+            "rooflines": {
+                "conv_real": {"bound": "fp32", "achieved": round(real_ach, 1), "peak": round(fp32_peak, 1),
+                              "unit": "Gflop/s (fp32 add)", "frac": round(real_ach / fp32_peak, 4),
+                              "time_share": frac_split.get("conv_real")},
+                "hbm_input": {"bytes_per_step": P * 120 * H * W * 4, "peak_gbs": peaks.get("hbm_gbs"),
+                              "min_ms": round(P * 120 * H * W * 4 / (peaks.get("hbm_gbs", 6538.9) * 1e6), 4)},
+            },
+            "per_kernel_ms": {r["label"]: round(r["ms"] / r["calls"], 4) for r in recs},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--patches", type=int, default=4096, help="patches per GPU per step")
+    ap.add_argument("--H", type=int, default=32)
+    ap.add_argument("--W", type=int, default=32)
+    ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

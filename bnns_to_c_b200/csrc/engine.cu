@@ -1,0 +1,1262 @@
+// engine.cu - the B200 forward engine behind bnn_forward and its extensions.
+//
+// Per device, a Model owns (created on first use on that device):
+//   * a weight arena: the blob's weights re-laid out once for the kernels
+//     (first conv as +-1.0f [Cout][tap][band]; binary convs as tap-major
+//     channel-packed uint32 [CoutP][9][Kw] with per-tap popcounts; folds in
+//     interval form),
+//   * an activation arena: every intermediate bit plane of one (N, H, W),
+//   * captured CUDA graphs of the whole forward, keyed by (N, H, W, in, out),
+//   * a compute stream and two copy streams for pipelined host batches.
+// The forward order is the reference's (csrc/bnn_model.c:150-253): 19
+// kernel launches (first conv, 17 fused binary convs, head).
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <tuple>
+#include <vector>
+
+#include "common.h"
+#include "kernels.cuh"
+
+namespace bnn {
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) return set_error(BNN_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+static inline int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
+static inline int cw_of(int c) { return (c + 31) >> 5; }
+
+// -------------------------------------------------------------------
+// device-side layer descriptions
+// -------------------------------------------------------------------
+struct BinLayer {
+    int Cin, Cout, CoutP, cw0, cw1, Kw, sC;  // sC: channels from the first source
+    uint32_t* wt = nullptr;
+    int* wpop = nullptr;
+    FoldIv* fold = nullptr;
+    FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
+};
+
+struct Profiler {
+    struct Rec {
+        std::string label, optype;
+        double work = 0, ms = 0;
+        int calls = 0;
+    };
+    bool on = false;
+    std::vector<Rec> recs;
+    std::mutex mu;
+    void add(const std::string& label, const char* optype, double work, double ms) {
+        std::lock_guard<std::mutex> g(mu);
+        for (auto& r : recs)
+            if (r.label == label) { r.work += work; r.ms += ms; r.calls++; return; }
+        recs.push_back(Rec{label, optype, work, ms, 1});
+    }
+};
+
+struct Arena {
+    int N = 0, H = 0, W = 0;
+    void* base = nullptr;
+    size_t bytes = 0;
+    uint32_t *enc_h[4], *skip[4], *down[4], *bott_h, *bott_x, *dec_h[4], *dec_x[4];
+};
+
+struct GraphKey {
+    int N, H, W;
+    const void* in;
+    const void* out;
+    bool operator<(const GraphKey& o) const {
+        return std::tie(N, H, W, in, out) < std::tie(o.N, o.H, o.W, o.in, o.out);
+    }
+};
+
+struct DevState {
+    int device = -1;
+    std::mutex mu;
+    void* wbase = nullptr;
+    float* ri_wf = nullptr;
+    float* ri_fold = nullptr;
+    int ri_CinP = 0, ri_CIP = 0;
+    BinLayer enc1[4], enc2[4], bott1, bott2, dec1[4], dec2[4];
+    float *head_W = nullptr, *head_b = nullptr;
+    Arena ar;
+    cudaStream_t cs = nullptr, h2d = nullptr, d2h = nullptr;
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    // pipelined host batches: two device staging slots
+    float* pin[2] = {nullptr, nullptr};
+    float* pout[2] = {nullptr, nullptr};
+    size_t pcap = 0;  // patches per slot
+    int pbands = 0, pclasses = 0, pH = 0, pW = 0;
+    cudaEvent_t ev_in[2], ev_comp[2], ev_out[2];
+    cudaEvent_t ev_last;  // completion of the last forward enqueued on this device
+    bool events = false;
+};
+
+struct Engine {
+    std::mutex mu;
+    std::map<int, std::unique_ptr<DevState>> devs;
+    std::vector<int> devices;  // empty: current device
+    int chunk = 512;
+    Profiler prof;
+};
+
+void* engine_create() { return new (std::nothrow) Engine(); }
+
+static void dev_release(DevState* d) {
+    if (!d || d->device < 0) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->device);
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+    if (d->cs) cudaStreamSynchronize(d->cs);
+    if (d->h2d) cudaStreamSynchronize(d->h2d);
+    if (d->d2h) cudaStreamSynchronize(d->d2h);
+    cudaFree(d->wbase);
+    cudaFree(d->ar.base);
+    for (int s = 0; s < 2; ++s) { cudaFree(d->pin[s]); cudaFree(d->pout[s]); }
+    if (d->events)
+    {
+        for (int s = 0; s < 2; ++s) {
+            cudaEventDestroy(d->ev_in[s]); cudaEventDestroy(d->ev_comp[s]); cudaEventDestroy(d->ev_out[s]);
+        }
+        cudaEventDestroy(d->ev_last);
+    }
+    if (d->cs) cudaStreamDestroy(d->cs);
+    if (d->h2d) cudaStreamDestroy(d->h2d);
+    if (d->d2h) cudaStreamDestroy(d->d2h);
+    cudaSetDevice(prev);
+}
+
+void engine_destroy(void* e) {
+    Engine* E = (Engine*)e;
+    if (!E) return;
+    for (auto& kv : E->devs) dev_release(kv.second.get());
+    delete E;
+}
+
+// -------------------------------------------------------------------
+// host-side relayout of the blob into the device formats
+// -------------------------------------------------------------------
+static FoldIv to_iv(int type, int t, int lo, int hi) {
+    const int MN = INT32_MIN, MX = INT32_MAX;
+    switch (type) {
+        case 0: return FoldIv{MN, MX, t > 0 ? 0 : 1, 0};
+        case 1: return FoldIv{t, MX, 0, 0};
+        case 2: return FoldIv{MN, t, 0, 0};
+        case 3: return FoldIv{lo, hi, 0, 0};
+        case 4: return FoldIv{lo, hi, 1, 0};
+        default: return FoldIv{MX, MN, 0, 0};  // empty: always -1
+    }
+}
+
+struct HostBin {
+    std::vector<uint32_t> wt;
+    std::vector<int> wpop;
+    std::vector<FoldIv> fold, fold2;
+};
+
+// kidx-ordered uint64 rows (bit (ci*9+t)) -> [CoutP][9][Kw] with the first
+// sC channels in words [0, cw0) and the rest in words [cw0, cw0+cw1).
+static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, int sC, BinLayer& L,
+                         HostBin& h) {
+    L.Cin = Cin; L.Cout = Cout; L.sC = sC;
+    L.cw0 = cw_of(sC);
+    L.cw1 = Cin > sC ? cw_of(Cin - sC) : 0;
+    L.Kw = L.cw0 + L.cw1;
+    L.CoutP = cdiv(Cout, 128) * 128;
+    h.wt.assign((size_t)L.CoutP * 9 * L.Kw, 0u);
+    h.wpop.assign((size_t)L.CoutP * 9, 0);
+    for (int co = 0; co < Cout; ++co) {
+        const uint64_t* row = packed + (size_t)co * nwords;
+        for (int ci = 0; ci < Cin; ++ci) {
+            const int word = ci < sC ? (ci >> 5) : L.cw0 + ((ci - sC) >> 5);
+            const int bit = ci < sC ? (ci & 31) : ((ci - sC) & 31);
+            for (int t = 0; t < 9; ++t) {
+                const int k = ci * 9 + t;
+                if ((row[k >> 6] >> (k & 63)) & 1ull) {
+                    h.wt[((size_t)co * 9 + t) * L.Kw + word] |= 1u << bit;
+                    h.wpop[(size_t)co * 9 + t] += 1;
+                }
+            }
+        }
+    }
+}
+
+static void folds_of(const Act* a, int CoutP, std::vector<FoldIv>& v) {
+    v.assign((size_t)CoutP, FoldIv{INT32_MAX, INT32_MIN, 0, 0});
+    for (int c = 0; c < a->C; ++c) v[c] = to_iv(a->type[c], a->t[c], a->lo[c], a->hi[c]);
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Opt every kernel into the dynamic shared memory its largest tile needs.
+// Done once per device (a context-level attribute), before any capture.
+template <int BN, int TM, int TN, int KC>
+static cudaError_t attr_bconv() {
+    return cudaFuncSetAttribute(bconv3x3_kernel<BN, TM, TN, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)BconvCfg<BN, TM, TN, KC>::smem_bytes(512));
+}
+template <int BN, int TM, int TN>
+static cudaError_t attr_bconv_kc() {
+    cudaError_t e;
+    if ((e = attr_bconv<BN, TM, TN, 8>()) != cudaSuccess) return e;
+    if ((e = attr_bconv<BN, TM, TN, 4>()) != cudaSuccess) return e;
+    if ((e = attr_bconv<BN, TM, TN, 2>()) != cudaSuccess) return e;
+    return attr_bconv<BN, TM, TN, 1>();
+}
+static int set_kernel_attrs(int device) {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    std::lock_guard<std::mutex> g(mu);
+    if (device >= 0 && device < 64 && done[device]) return BNN_OK;
+    cudaError_t e;
+    if ((e = attr_bconv_kc<32, 4, 4>()) != cudaSuccess || (e = attr_bconv_kc<64, 8, 4>()) != cudaSuccess ||
+        (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  RI_HP * 260 * 4)) != cudaSuccess)
+        return set_error(BNN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (device >= 0 && device < 64) done[device] = true;
+    return BNN_OK;
+}
+
+// upload everything to device d (called with d->mu held, device current)
+static int dev_init(const Model* m, DevState* d) {
+    Topology tp;
+    int rc = validate_topology(m, &tp);
+    if (rc) return rc;
+    if ((rc = set_kernel_attrs(d->device))) return rc;
+    // first conv
+    const Conv* c1 = &m->enc_conv1[0];
+    const Act* a1 = &m->enc_act1[0];
+    const int Cin = c1->Cin, CoutR = c1->Cout, CoutRP = cdiv(CoutR, 32) * 32;
+    d->ri_CinP = cdiv(Cin, 4) * 4;
+    d->ri_CIP = d->ri_CinP + (((d->ri_CinP / 4) % 2 == 0) ? 4 : 0);
+    std::vector<float> wf((size_t)CoutRP * 9 * d->ri_CinP, 0.0f), rfold((size_t)CoutRP * 5, 0.0f);
+    for (int co = 0; co < CoutR; ++co) {
+        for (int ci = 0; ci < Cin; ++ci)
+            for (int t = 0; t < 9; ++t)
+                wf[((size_t)co * 9 + t) * d->ri_CinP + ci] = (float)c1->wsign[((size_t)co * Cin + ci) * 9 + t];
+        rfold[co * 5 + 0] = c1->alpha[co];
+        rfold[co * 5 + 1] = a1->A[co];
+        rfold[co * 5 + 2] = a1->B[co];
+        rfold[co * 5 + 3] = a1->slope[co];
+        rfold[co * 5 + 4] = a1->rsign[co];
+    }
+    // binary convs
+    struct Item {
+        BinLayer* L;
+        const Conv* c;
+        const Act* a;
+        const Act* a2;
+        int sC;
+        HostBin h;
+    };
+    std::vector<Item> items;
+    for (int i = 0; i < 4; ++i) {
+        if (i > 0) items.push_back({&d->enc1[i], &m->enc_conv1[i], &m->enc_act1[i], nullptr, m->enc_conv1[i].Cin, {}});
+        items.push_back({&d->enc2[i], &m->enc_conv2[i], &m->enc_act2_skip[i], &m->enc_act2_down[i],
+                         m->enc_conv2[i].Cin, {}});
+    }
+    items.push_back({&d->bott1, &m->bott_conv1, &m->bott_act1, nullptr, m->bott_conv1.Cin, {}});
+    items.push_back({&d->bott2, &m->bott_conv2, &m->bott_act2, nullptr, m->bott_conv2.Cin, {}});
+    for (int i = 0; i < 4; ++i) {
+        items.push_back({&d->dec1[i], &m->dec_conv1[i], &m->dec_act1[i], nullptr, tp.enc[3 - i], {}});
+        items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
+    }
+    size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4);
+    for (auto& it : items) {
+        relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
+        folds_of(it.a, it.L->CoutP, it.h.fold);
+        if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
+        total += align256(it.h.wt.size() * 4) + align256(it.h.wpop.size() * 4) +
+                 align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
+    }
+    const size_t hw = (size_t)m->head_Cout * m->head_Cin;
+    total += align256(hw * 4) + align256((size_t)m->head_Cout * 4);
+    void* base = nullptr;
+    if (cudaMalloc(&base, total) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_OOM, "cudaMalloc weights (%zu bytes) on device %d", total, d->device);
+    }
+    d->wbase = base;
+    char* p = (char*)base;
+    auto put = [&](const void* src, size_t bytes) -> void* {
+        void* dst = p;
+        if (bytes) cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+        p += align256(bytes);
+        return dst;
+    };
+    d->ri_wf = (float*)put(wf.data(), wf.size() * 4);
+    d->ri_fold = (float*)put(rfold.data(), rfold.size() * 4);
+    for (auto& it : items) {
+        it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
+        it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
+        it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
+        it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
+    }
+    d->head_W = (float*)put(m->head_W, hw * 4);
+    d->head_b = (float*)put(m->head_bias, (size_t)m->head_Cout * 4);
+    CK(cudaGetLastError());
+    CK(cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+    for (int s = 0; s < 2; ++s) {
+        CK(cudaEventCreateWithFlags(&d->ev_in[s], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&d->ev_comp[s], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&d->ev_out[s], cudaEventDisableTiming));
+    }
+    CK(cudaEventCreateWithFlags(&d->ev_last, cudaEventDisableTiming));
+    CK(cudaEventRecord(d->ev_last, d->cs));
+    d->events = true;
+    return BNN_OK;
+}
+
+static int get_dev(const Model* m, int device, DevState** out) {
+    Engine* E = (Engine*)m->engine;
+    if (!E) return set_error(BNN_ERR_ARG, "model has no engine");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "no CUDA device available");
+    }
+    if (device < 0 || device >= ndev) return set_error(BNN_ERR_ARG, "device %d out of range [0,%d)", device, ndev);
+    DevState* d;
+    {
+        std::lock_guard<std::mutex> g(E->mu);
+        auto& slot = E->devs[device];
+        if (!slot) slot.reset(new DevState());
+        d = slot.get();
+    }
+    std::lock_guard<std::mutex> g(d->mu);
+    if (d->device < 0) {
+        CK(cudaSetDevice(device));
+        d->device = device;
+        int rc = dev_init(m, d);
+        if (rc) {
+            dev_release(d);
+            d->device = -1;
+            d->wbase = nullptr;
+            return rc;
+        }
+    }
+    *out = d;
+    return BNN_OK;
+}
+
+// -------------------------------------------------------------------
+// activation arena
+// -------------------------------------------------------------------
+static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
+    Arena& a = d->ar;
+    if (a.base && a.N >= N && a.H == H && a.W == W) return BNN_OK;
+    Topology tp;
+    validate_topology(m, &tp);
+    int Nn = std::max(N, a.H == H && a.W == W ? a.N : 0);
+    size_t off = 0;
+    std::vector<std::pair<uint32_t**, size_t>> plan;
+    auto add = [&](uint32_t** slot, int h, int w, int c) {
+        size_t bytes = (size_t)Nn * h * w * cw_of(c) * 4;
+        plan.push_back({slot, off});
+        off += align256(bytes + 4);
+    };
+    for (int i = 0; i < 4; ++i) {
+        const int h = H >> i, w = W >> i;
+        add(&a.enc_h[i], h, w, tp.enc[i]);
+        add(&a.skip[i], h, w, tp.enc[i]);
+        add(&a.down[i], h >> 1, w >> 1, tp.enc[i]);
+    }
+    add(&a.bott_h, H >> 4, W >> 4, m->bott_conv1.Cout);
+    add(&a.bott_x, H >> 4, W >> 4, tp.bott);
+    for (int i = 0; i < 4; ++i) {
+        const int l = 3 - i;
+        add(&a.dec_h[i], H >> l, W >> l, m->dec_conv1[i].Cout);
+        add(&a.dec_x[i], H >> l, W >> l, tp.dec[i]);
+    }
+    // graphs bake in arena pointers
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+    if (a.base) {
+        CK(cudaEventSynchronize(d->ev_last));
+        CK(cudaStreamSynchronize(d->cs));
+        cudaFree(a.base);
+        a.base = nullptr;
+    }
+    void* base = nullptr;
+    if (cudaMalloc(&base, off) != cudaSuccess) {
+        cudaGetLastError();
+        a.N = 0;
+        return set_error(BNN_ERR_OOM, "cudaMalloc activation arena (%zu bytes)", off);
+    }
+    a.base = base;
+    a.bytes = off;
+    a.N = Nn; a.H = H; a.W = W;
+    for (auto& pr : plan) *pr.first = (uint32_t*)((char*)base + pr.second);
+    return BNN_OK;
+}
+
+// -------------------------------------------------------------------
+// launchers
+// -------------------------------------------------------------------
+struct TileGeo {
+    int TR, TC, TNI, tiles_x, tiles_y, tiles, HP;
+};
+
+static TileGeo tile_geo(int N, int H, int W, int BM) {
+    TileGeo g;
+    if (H * W <= BM) {
+        g.TR = H; g.TC = W;
+        g.TNI = std::max(1, std::min(BM / (H * W), 512 / ((H + 2) * (W + 2))));
+        g.tiles_x = g.tiles_y = 1;
+        g.tiles = cdiv(N, g.TNI);
+    } else if (2 * W <= BM) {
+        g.TC = W;
+        g.TR = std::min(2 * (BM / (2 * W)), ((H + 1) / 2) * 2);
+        g.TNI = 1;
+        g.tiles_x = 1;
+        g.tiles_y = cdiv(H, g.TR);
+        g.tiles = N * g.tiles_y;
+    } else {
+        g.TR = 2; g.TC = BM / 2; g.TNI = 1;
+        g.tiles_x = cdiv(W, g.TC);
+        g.tiles_y = cdiv(H, 2);
+        g.tiles = N * g.tiles_x * g.tiles_y;
+    }
+    g.HP = g.TNI * (g.TR + 2) * (g.TC + 2);
+    return g;
+}
+
+template <int BN, int TM, int TN, int KC>
+static int launch_bconv_t(BconvParams p, int N, cudaStream_t st) {
+    using Cfg = BconvCfg<BN, TM, TN, KC>;
+    TileGeo g = tile_geo(N, p.H, p.W, Cfg::BM);
+    p.TR = g.TR; p.TC = g.TC; p.TNI = g.TNI; p.tiles_x = g.tiles_x; p.tiles_y = g.tiles_y; p.HP = g.HP;
+    const size_t smem = Cfg::smem_bytes(g.HP);
+    dim3 grid((unsigned)g.tiles, (unsigned)cdiv(p.Cout, BN));
+    bconv3x3_kernel<BN, TM, TN, KC><<<grid, Cfg::NT, smem, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+template <int BN, int TM, int TN>
+static int launch_bconv_kc(BconvParams p, int N, cudaStream_t st) {
+    const int Kw = p.Kw;
+    if (Kw % 8 == 0) return launch_bconv_t<BN, TM, TN, 8>(p, N, st);
+    if (Kw % 4 == 0) return launch_bconv_t<BN, TM, TN, 4>(p, N, st);
+    if (Kw % 2 == 0) return launch_bconv_t<BN, TM, TN, 2>(p, N, st);
+    return launch_bconv_t<BN, TM, TN, 1>(p, N, st);
+}
+
+static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
+    if (p.Cout <= 32) return launch_bconv_kc<32, 4, 4>(p, N, st);
+    if (p.Cout <= 64) return launch_bconv_kc<64, 8, 4>(p, N, st);
+    return launch_bconv_kc<128, 8, 8>(p, N, st);
+}
+
+// one binary conv layer of the forward
+static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, int h1, int w1, int N, int H,
+                   int W, uint32_t* out, uint32_t* out2, int32_t* P, int32_t* P2, cudaStream_t st) {
+    if (N <= 0 || H <= 0 || W <= 0) return BNN_OK;
+    BconvParams p{};
+    p.in0 = in0; p.in1 = in1; p.cw0 = L.cw0; p.cw1 = L.cw1; p.Kw = L.Kw;
+    p.N = N; p.H = H; p.W = W;
+    p.h1 = h1; p.w1 = w1;
+    // reference up_cat (csrc/bnn_model.c:130-148): offset d/2 when the skip is larger
+    const int upH = 2 * h1, upW = 2 * w1;
+    p.oh = H > upH ? (H - upH) / 2 : 0;
+    p.ow = W > upW ? (W - upW) / 2 : 0;
+    p.cH = std::min(upH, H);
+    p.cW = std::min(upW, W);
+    p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
+    p.wt = L.wt; p.wpop = L.wpop; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
+    p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
+    return launch_bconv(p, N, st);
+}
+
+static int run_realin(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out, float* dbg,
+                      cudaStream_t st) {
+    if (N <= 0) return BNN_OK;
+    RealinParams p{};
+    p.x = x; p.wf = d->ri_wf; p.fold = d->ri_fold; p.out = out; p.dbg = dbg;
+    p.N = N; p.Cin = m->enc_conv1[0].Cin; p.CinP = d->ri_CinP; p.CIP = d->ri_CIP;
+    p.H = H; p.W = W; p.Cout = m->enc_conv1[0].Cout; p.cwo = cw_of(p.Cout);
+    p.tiles_x = cdiv(W, RI_TC); p.tiles_y = cdiv(H, RI_TR);
+    const size_t smem = (size_t)RI_HP * p.CIP * 4;
+    cudaError_t e;
+    dim3 grid((unsigned)((size_t)N * p.tiles_x * p.tiles_y), (unsigned)cdiv(p.Cout, 32));
+    realin3x3_fold_kernel<<<grid, 128, smem, st>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int H, int W, float* out,
+                    cudaStream_t st) {
+    if (N <= 0) return BNN_OK;
+    HeadParams p{in, d->head_W, d->head_b, out, N, H, W, m->head_Cin, cw_of(m->head_Cin), m->head_Cout};
+    const size_t total = (size_t)N * H * W;
+    unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
+    head1x1_kernel<<<blocks, 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+// -------------------------------------------------------------------
+// the forward: 19 launches in the reference's order
+// -------------------------------------------------------------------
+struct Dbg {  // optional debug outputs of one forward (device pointers)
+    float* realin = nullptr;
+    int32_t* P[17] = {nullptr};
+    int32_t* Pd[4] = {nullptr};
+};
+
+struct ProfCtx {
+    Profiler* prof = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<std::tuple<std::string, const char*, double, cudaEvent_t, cudaEvent_t>> marks;
+    cudaEvent_t last = nullptr;
+    void begin(const std::string& label, const char* optype, double work) {
+        if (!prof) return;
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, st);
+        marks.emplace_back(label, optype, work, a, b);
+    }
+    void end() {
+        if (!prof) return;
+        cudaEventRecord(std::get<4>(marks.back()), st);
+    }
+    int finish() {
+        if (!prof) return BNN_OK;
+        CK(cudaStreamSynchronize(st));
+        for (auto& mk : marks) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, std::get<3>(mk), std::get<4>(mk));
+            prof->add(std::get<0>(mk), std::get<1>(mk), std::get<2>(mk), ms);
+            cudaEventDestroy(std::get<3>(mk));
+            cudaEventDestroy(std::get<4>(mk));
+        }
+        marks.clear();
+        return BNN_OK;
+    }
+};
+
+static int forward_launches(const Model* m, DevState* d, const float* x, int N, int H, int W, float* logits,
+                            cudaStream_t st, const Dbg* dbg, ProfCtx* pc) {
+    static const char* EN[4] = {"enc1", "enc2", "enc3", "enc4"};
+    static const char* DN[4] = {"dec4", "dec3", "dec2", "dec1"};
+    Arena& a = d->ar;
+    int rc;
+    const double NHW = (double)N * H * W;
+    auto work = [&](const BinLayer& L, int h, int w) { return (double)N * h * w * L.Cout * (double)L.Cin * 9.0; };
+    int li = 0;
+    if (pc) pc->begin("enc1.conv1+act1", "conv_real", NHW * m->enc_conv1[0].Cout * m->enc_conv1[0].Cin * 9.0);
+    rc = run_realin(d, m, x, N, H, W, a.enc_h[0], dbg ? dbg->realin : nullptr, st);
+    if (pc) pc->end();
+    if (rc) return rc;
+    for (int i = 0; i < 4; ++i) {
+        const int h = H >> i, w = W >> i;
+        if (i > 0) {
+            if (pc) pc->begin(std::string(EN[i]) + ".conv1+act1", "bconv", work(d->enc1[i], h, w));
+            rc = run_bin(d->enc1[i], a.down[i - 1], nullptr, 0, 0, N, h, w, a.enc_h[i], nullptr,
+                         dbg ? dbg->P[li] : nullptr, nullptr, st);
+            if (pc) pc->end();
+            if (rc) return rc;
+            ++li;
+        }
+        if (pc) pc->begin(std::string(EN[i]) + ".conv2+skip+pool+down", "bconv", work(d->enc2[i], h, w));
+        rc = run_bin(d->enc2[i], a.enc_h[i], nullptr, 0, 0, N, h, w, a.skip[i], a.down[i],
+                     dbg ? dbg->P[li] : nullptr, dbg ? dbg->Pd[i] : nullptr, st);
+        if (pc) pc->end();
+        if (rc) return rc;
+        ++li;
+    }
+    const int h4 = H >> 4, w4 = W >> 4;
+    if (pc) pc->begin("bott.conv1+act1", "bconv", work(d->bott1, h4, w4));
+    rc = run_bin(d->bott1, a.down[3], nullptr, 0, 0, N, h4, w4, a.bott_h, nullptr, dbg ? dbg->P[li] : nullptr,
+                 nullptr, st);
+    if (pc) pc->end();
+    if (rc) return rc;
+    ++li;
+    if (pc) pc->begin("bott.conv2+act2", "bconv", work(d->bott2, h4, w4));
+    rc = run_bin(d->bott2, a.bott_h, nullptr, 0, 0, N, h4, w4, a.bott_x, nullptr, dbg ? dbg->P[li] : nullptr,
+                 nullptr, st);
+    if (pc) pc->end();
+    if (rc) return rc;
+    ++li;
+    const uint32_t* xprev = a.bott_x;
+    int hp = h4, wp = w4;
+    for (int i = 0; i < 4; ++i) {
+        const int l = 3 - i, h = H >> l, w = W >> l;
+        if (pc) pc->begin(std::string(DN[i]) + ".upcat+conv1+act1", "bconv", work(d->dec1[i], h, w));
+        rc = run_bin(d->dec1[i], a.skip[l], xprev, hp, wp, N, h, w, a.dec_h[i], nullptr,
+                     dbg ? dbg->P[li] : nullptr, nullptr, st);
+        if (pc) pc->end();
+        if (rc) return rc;
+        ++li;
+        if (pc) pc->begin(std::string(DN[i]) + ".conv2+act2", "bconv", work(d->dec2[i], h, w));
+        rc = run_bin(d->dec2[i], a.dec_h[i], nullptr, 0, 0, N, h, w, a.dec_x[i], nullptr,
+                     dbg ? dbg->P[li] : nullptr, nullptr, st);
+        if (pc) pc->end();
+        if (rc) return rc;
+        ++li;
+        xprev = a.dec_x[i];
+        hp = h; wp = w;
+    }
+    if (pc) pc->begin("head", "head", NHW * m->head_Cout * m->head_Cin);
+    rc = run_head(d, m, a.dec_x[3], N, H, W, logits, st);
+    if (pc) pc->end();
+    return rc;
+}
+
+static int check_hw(int N, int H, int W) {
+    if (N < 0) return set_error(BNN_ERR_ARG, "N = %d", N);
+    // below 16 an encoder level is one pixel wide, where the reference's
+    // maxpool_P writes past its H/2 = 0 output (bnn_maxpool.c:29-30): the
+    // reference has no defined result there, so it is refused here.
+    if (H < 16 || W < 16) return set_error(BNN_ERR_ARG, "H=%d W=%d: the v1 forward needs H, W >= 16", H, W);
+    if ((size_t)H * W > ((size_t)1 << 28)) return set_error(BNN_ERR_ARG, "H*W too large");
+    return BNN_OK;
+}
+
+// forward on device buffers; graph replay unless profiling / debugging
+static int forward_device(const Model* m, DevState* d, const float* x, int N, int H, int W, float* logits,
+                          cudaStream_t user, const Dbg* dbg) {
+    int rc = arena_reserve(m, d, N, H, W);
+    if (rc) return rc;
+    Engine* E = (Engine*)m->engine;
+    if (N == 0) return BNN_OK;
+    // the activation arena is shared by every forward on this device: work
+    // enqueued on different streams is ordered through ev_last
+    CK(cudaStreamWaitEvent(user, d->ev_last, 0));
+    if (E->prof.on || dbg) {
+        ProfCtx pc;
+        ProfCtx* ppc = nullptr;
+        if (E->prof.on) { pc.prof = &E->prof; pc.st = user; ppc = &pc; }
+        rc = forward_launches(m, d, x, N, H, W, logits, user, dbg, ppc);
+        if (rc) return rc;
+        CK(cudaEventRecord(d->ev_last, user));
+        return ppc ? ppc->finish() : BNN_OK;
+    }
+    GraphKey key{N, H, W, x, logits};
+    auto it = d->graphs.find(key);
+    if (it == d->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(d->cs, cudaStreamCaptureModeThreadLocal));
+        rc = forward_launches(m, d, x, N, H, W, logits, d->cs, nullptr, nullptr);
+        cudaError_t e = cudaStreamEndCapture(d->cs, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+        if (d->graphs.size() > 64) {
+            for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+            d->graphs.clear();
+        }
+        it = d->graphs.emplace(key, ex).first;
+    }
+    CK(cudaGraphLaunch(it->second, user));
+    CK(cudaEventRecord(d->ev_last, user));
+    return BNN_OK;
+}
+
+static int current_device(int* dev) {
+    if (cudaGetDevice(dev) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "no CUDA device available");
+    }
+    return BNN_OK;
+}
+
+// pipelined host batch on one device: chunks of `chunk` patches, H2D of the
+// next chunk and D2H of the previous one overlap the current forward
+static int host_batch_on(const Model* m, int device, const float* in, int N, int H, int W, float* out, int chunk) {
+    CK(cudaSetDevice(device));
+    DevState* d = nullptr;
+    int rc = get_dev(m, device, &d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> g(d->mu);
+    const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
+    const int C = std::max(1, std::min(chunk, N));
+    if (d->pcap < (size_t)C || d->pbands != m->n_bands || d->pclasses != m->n_classes || d->pH != H || d->pW != W) {
+        CK(cudaDeviceSynchronize());
+        for (int s = 0; s < 2; ++s) {
+            cudaFree(d->pin[s]); cudaFree(d->pout[s]);
+            d->pin[s] = d->pout[s] = nullptr;
+        }
+        d->pcap = 0;
+        for (int s = 0; s < 2; ++s) {
+            if (cudaMalloc(&d->pin[s], (size_t)C * ip * 4) != cudaSuccess ||
+                cudaMalloc(&d->pout[s], (size_t)C * op * 4) != cudaSuccess) {
+                cudaGetLastError();
+                return set_error(BNN_ERR_OOM, "cudaMalloc staging (%d patches)", C);
+            }
+        }
+        d->pcap = (size_t)C; d->pbands = m->n_bands; d->pclasses = m->n_classes; d->pH = H; d->pW = W;
+    }
+    const int nch = cdiv(N, C);
+    for (int k = 0; k < nch; ++k) {
+        const int s = k & 1;
+        const int lo = k * C, n = std::min(C, N - lo);
+        if (k >= 2) CK(cudaStreamWaitEvent(d->h2d, d->ev_comp[s], 0));  // slot free for input
+        CK(cudaMemcpyAsync(d->pin[s], in + (size_t)lo * ip, (size_t)n * ip * 4, cudaMemcpyHostToDevice, d->h2d));
+        CK(cudaEventRecord(d->ev_in[s], d->h2d));
+        CK(cudaStreamWaitEvent(d->cs, d->ev_in[s], 0));
+        if (k >= 2) CK(cudaStreamWaitEvent(d->cs, d->ev_out[s], 0));  // output slot drained
+        rc = forward_device(m, d, d->pin[s], n, H, W, d->pout[s], d->cs, nullptr);
+        if (rc) return rc;
+        CK(cudaEventRecord(d->ev_comp[s], d->cs));
+        CK(cudaStreamWaitEvent(d->d2h, d->ev_comp[s], 0));
+        CK(cudaMemcpyAsync(out + (size_t)lo * op, d->pout[s], (size_t)n * op * 4, cudaMemcpyDeviceToHost, d->d2h));
+        CK(cudaEventRecord(d->ev_out[s], d->d2h));
+    }
+    CK(cudaStreamSynchronize(d->d2h));
+    CK(cudaStreamSynchronize(d->cs));
+    return BNN_OK;
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+// ===================================================================
+// C ABI
+// ===================================================================
+BNN_API int bnn_forward_device(const Model* m, int device, const float* d_input, int N, int H, int W,
+                               float* d_logits, void* stream) {
+    if (!m) return set_error(BNN_ERR_ARG, "model is NULL");
+    int rc = check_hw(N, H, W);
+    if (rc) return rc;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_ARG, "cannot select device %d", device);
+    }
+    DevState* d = nullptr;
+    rc = get_dev(m, device, &d);
+    if (!rc) {
+        std::lock_guard<std::mutex> g(d->mu);
+        rc = forward_device(m, d, d_input, N, H, W, d_logits, (cudaStream_t)stream, nullptr);
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+BNN_API int bnn_forward_batch(const Model* m, const float* input, int N, int H, int W, float* logits) {
+    if (!m || (!input && N > 0) || (!logits && N > 0)) return set_error(BNN_ERR_ARG, "NULL argument");
+    int rc = check_hw(N, H, W);
+    if (rc) return rc;
+    if (N == 0) return BNN_OK;
+    Engine* E = (Engine*)m->engine;
+    std::vector<int> devs;
+    {
+        std::lock_guard<std::mutex> g(E->mu);
+        devs = E->devices;
+    }
+    int prev = 0;
+    if (devs.empty()) {
+        if ((rc = current_device(&prev))) return rc;
+        devs.push_back(prev);
+    } else {
+        cudaGetDevice(&prev);
+    }
+    const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
+    const int nd = (int)devs.size();
+    if (nd == 1) {
+        rc = host_batch_on(m, devs[0], input, N, H, W, logits, E->chunk);
+        cudaSetDevice(prev);
+        return rc;
+    }
+    std::vector<int> st(nd, BNN_OK);
+    std::vector<std::string> msg(nd);
+    std::vector<std::thread> th;
+    for (int r = 0; r < nd; ++r) {
+        const int lo = (int)((long)N * r / nd), hi = (int)((long)N * (r + 1) / nd);
+        th.emplace_back([&, r, lo, hi]() {
+            if (hi > lo) st[r] = host_batch_on(m, devs[r], input + (size_t)lo * ip, hi - lo, H, W,
+                                               logits + (size_t)lo * op, E->chunk);
+            if (st[r]) msg[r] = bnn_last_error();
+        });
+    }
+    for (auto& t : th) t.join();
+    cudaSetDevice(prev);
+    for (int r = 0; r < nd; ++r)
+        if (st[r]) return set_error(st[r], "device %d: %s", devs[r], msg[r].c_str());
+    return BNN_OK;
+}
+
+BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float* logits) {
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (!rc) rc = check_hw(1, H, W);
+    if (!rc) rc = host_batch_on(m, dev, input, 1, H, W, logits, 1);
+    if (rc) {
+        fprintf(stderr, "%s\n", bnn_last_error());
+        exit(1);
+    }
+}
+
+BNN_API int bnn_set_devices(Model* m, const int* devices, int n) {
+    if (!m || n < 0 || (n > 0 && !devices)) return set_error(BNN_ERR_ARG, "bad arguments");
+    int ndev = 0;
+    if (n > 0 && (cudaGetDeviceCount(&ndev) != cudaSuccess)) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "no CUDA device available");
+    }
+    for (int i = 0; i < n; ++i) {
+        if (devices[i] < 0 || devices[i] >= ndev) return set_error(BNN_ERR_ARG, "device %d out of range", devices[i]);
+        for (int j = 0; j < i; ++j)
+            if (devices[j] == devices[i]) return set_error(BNN_ERR_ARG, "device %d listed twice", devices[i]);
+    }
+    Engine* E = (Engine*)m->engine;
+    std::lock_guard<std::mutex> g(E->mu);
+    E->devices.assign(devices, devices + n);
+    return BNN_OK;
+}
+
+BNN_API int bnn_get_devices(const Model* m, int* devices, int cap) {
+    if (!m) return set_error(BNN_ERR_ARG, "model is NULL");
+    Engine* E = (Engine*)m->engine;
+    std::lock_guard<std::mutex> g(E->mu);
+    for (int i = 0; i < (int)E->devices.size() && i < cap; ++i) devices[i] = E->devices[i];
+    return (int)E->devices.size();
+}
+
+BNN_API int bnn_set_chunk(Model* m, int patches) {
+    if (!m || patches < 1) return set_error(BNN_ERR_ARG, "chunk must be >= 1");
+    ((Engine*)m->engine)->chunk = patches;
+    return BNN_OK;
+}
+
+BNN_API int bnn_forward_launches(const Model* m, int N, int H, int W) {
+    if (!m || N <= 0 || H < 16 || W < 16) return 0;
+    return 19;
+}
+
+// ---------------- profiler ----------------
+BNN_API int bnn_profile_enable(Model* m, int on) {
+    if (!m) return set_error(BNN_ERR_ARG, "model is NULL");
+    ((Engine*)m->engine)->prof.on = on != 0;
+    return BNN_OK;
+}
+BNN_API void bnn_profile_reset(Model* m) {
+    if (!m) return;
+    Profiler& P = ((Engine*)m->engine)->prof;
+    std::lock_guard<std::mutex> g(P.mu);
+    P.recs.clear();
+}
+BNN_API int bnn_profile_count(const Model* m) {
+    if (!m) return 0;
+    Profiler& P = ((Engine*)m->engine)->prof;
+    std::lock_guard<std::mutex> g(P.mu);
+    return (int)P.recs.size();
+}
+BNN_API int bnn_profile_get(const Model* m, int i, const char** label, const char** optype, double* work, double* ms,
+                            int* calls) {
+    if (!m) return set_error(BNN_ERR_ARG, "model is NULL");
+    Profiler& P = ((Engine*)m->engine)->prof;
+    std::lock_guard<std::mutex> g(P.mu);
+    if (i < 0 || i >= (int)P.recs.size()) return set_error(BNN_ERR_ARG, "profile index %d", i);
+    const auto& r = P.recs[i];
+    if (label) *label = r.label.c_str();
+    if (optype) *optype = r.optype.c_str();
+    if (work) *work = r.work;
+    if (ms) *ms = r.ms;
+    if (calls) *calls = r.calls;
+    return BNN_OK;
+}
+// same two tables as the reference's prof_report (csrc/bnn_prof.c:42-77)
+BNN_API void bnn_profile_report(const Model* m, void* file) {
+    if (!m) return;
+    FILE* o = file ? (FILE*)file : stderr;
+    Profiler& P = ((Engine*)m->engine)->prof;
+    std::lock_guard<std::mutex> g(P.mu);
+    if (P.recs.empty()) return;
+    double tot = 0;
+    for (auto& r : P.recs) tot += r.ms;
+    fprintf(o, "\n# per-op (execution order, device time summed over calls)\n");
+    fprintf(o, "%-26s %-10s %6s %12s %10s %7s %10s\n", "layer", "op", "calls", "work", "ms", "%", "Gwork/s");
+    for (auto& r : P.recs)
+        fprintf(o, "%-26s %-10s %6d %12.4g %10.4f %6.2f %10.1f\n", r.label.c_str(), r.optype.c_str(), r.calls, r.work,
+                r.ms, tot > 0 ? 100.0 * r.ms / tot : 0.0, r.ms > 0 ? r.work / (r.ms * 1e6) : 0.0);
+    fprintf(o, "\n# roll-up by op type\n");
+    fprintf(o, "%-10s %6s %12s %10s %7s\n", "op", "calls", "work", "ms", "%");
+    std::vector<std::string> seen;
+    for (auto& r : P.recs)
+        if (std::find(seen.begin(), seen.end(), r.optype) == seen.end()) seen.push_back(r.optype);
+    for (auto& s : seen) {
+        double ms = 0, w = 0;
+        int c = 0;
+        for (auto& r : P.recs)
+            if (r.optype == s) { ms += r.ms; w += r.work; c += r.calls; }
+        fprintf(o, "%-10s %6d %12.4g %10.4f %6.2f\n", s.c_str(), c, w, ms, tot > 0 ? 100.0 * ms / tot : 0.0);
+    }
+    fprintf(o, "# total per-op: %.4f ms\n", tot);
+}
+
+// ---------------- stage dump ----------------
+BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W, float* logits, bnn_stage_cb cb,
+                               void* ctx) {
+    if (!m || !input || !logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    int rc = check_hw(1, H, W);
+    if (rc) return rc;
+    int dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    DevState* d = nullptr;
+    if ((rc = get_dev(m, dev, &d))) return rc;
+    std::lock_guard<std::mutex> g(d->mu);
+    if ((rc = arena_reserve(m, d, 1, H, W))) return rc;
+    Topology tp;
+    validate_topology(m, &tp);
+    const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
+    // layer geometry in forward order
+    struct LG { const char* name; int C, h, w; const BinLayer* L; };
+    static const char* PN[17] = {"enc1.conv2.P", "enc2.conv1.P", "enc2.conv2.P", "enc3.conv1.P", "enc3.conv2.P",
+                                 "enc4.conv1.P", "enc4.conv2.P", "bottleneck.conv1.P", "bottleneck.conv2.P",
+                                 "dec4.conv1.P", "dec4.conv2.P", "dec3.conv1.P", "dec3.conv2.P", "dec2.conv1.P",
+                                 "dec2.conv2.P", "dec1.conv1.P", "dec1.conv2.P"};
+    std::vector<LG> lg;
+    for (int i = 0; i < 4; ++i) {
+        if (i > 0) lg.push_back({PN[lg.size()], d->enc1[i].Cout, H >> i, W >> i, &d->enc1[i]});
+        lg.push_back({PN[lg.size()], d->enc2[i].Cout, H >> i, W >> i, &d->enc2[i]});
+    }
+    lg.push_back({PN[lg.size()], d->bott1.Cout, H >> 4, W >> 4, &d->bott1});
+    lg.push_back({PN[lg.size()], d->bott2.Cout, H >> 4, W >> 4, &d->bott2});
+    for (int i = 0; i < 4; ++i) {
+        lg.push_back({PN[lg.size()], d->dec1[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec1[i]});
+        lg.push_back({PN[lg.size()], d->dec2[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec2[i]});
+    }
+    size_t words = 0;
+    std::vector<size_t> poff(17), pdoff(4);
+    for (int k = 0; k < 17; ++k) { poff[k] = words; words += (size_t)lg[k].C * lg[k].h * lg[k].w + 1; }
+    for (int i = 0; i < 4; ++i) { pdoff[i] = words; words += (size_t)tp.enc[i] * (H >> (i + 1)) * (W >> (i + 1)) + 1; }
+    const size_t ri_words = (size_t)m->enc_conv1[0].Cout * H * W;
+    void* buf = nullptr;
+    if (cudaMalloc(&buf, (words + ri_words + ip + op) * 4) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_OOM, "cudaMalloc stage buffers");
+    }
+    int32_t* P = (int32_t*)buf;
+    float* dri = (float*)(P + words);
+    float* din = dri + ri_words;
+    float* dout = din + ip;
+    Dbg dbg;
+    dbg.realin = dri;
+    for (int k = 0; k < 17; ++k) dbg.P[k] = P + poff[k];
+    for (int i = 0; i < 4; ++i) dbg.Pd[i] = P + pdoff[i];
+    rc = BNN_OK;
+    auto fail = [&](int code) { cudaFree(buf); return code; };
+    if (cudaMemcpy(din, input, ip * 4, cudaMemcpyHostToDevice) != cudaSuccess) return fail(set_error(BNN_ERR_CUDA, "H2D"));
+    rc = forward_launches(m, d, din, 1, H, W, dout, d->cs, &dbg, nullptr);
+    if (rc) return fail(rc);
+    if (cudaStreamSynchronize(d->cs) != cudaSuccess) return fail(set_error(BNN_ERR_CUDA, "forward: %s", cudaGetErrorString(cudaGetLastError())));
+    std::vector<int32_t> hP(words);
+    std::vector<float> hri(ri_words);
+    cudaMemcpy(hP.data(), P, words * 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(hri.data(), dri, ri_words * 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(logits, dout, op * 4, cudaMemcpyDeviceToHost);
+    // activations: unpack bit planes from the arena
+    Arena& a = d->ar;
+    auto bits_to_i8 = [&](const uint32_t* dbits, int C, int h, int w, std::vector<int8_t>& o) {
+        const int cw = cw_of(C);
+        std::vector<uint32_t> hb((size_t)h * w * cw);
+        cudaMemcpy(hb.data(), dbits, hb.size() * 4, cudaMemcpyDeviceToHost);
+        o.assign((size_t)C * h * w, 0);
+        for (int c = 0; c < C; ++c)
+            for (int px = 0; px < h * w; ++px)
+                o[(size_t)c * h * w + px] = ((hb[(size_t)px * cw + (c >> 5)] >> (c & 31)) & 1u) ? 1 : -1;
+    };
+    std::vector<int8_t> act;
+    static const char* EN[4] = {"enc1", "enc2", "enc3", "enc4"};
+    static const char* DN[4] = {"dec4", "dec3", "dec2", "dec1"};
+    char nm[64];
+    int k = 0;
+    std::vector<std::vector<int8_t>> skips(4);
+    for (int i = 0; i < 4; ++i) {
+        const int h = H >> i, w = W >> i;
+        if (i == 0) {
+            cb(ctx, "enc1.conv1.out", 2, m->enc_conv1[0].Cout, H, W, hri.data());
+        } else {
+            cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]);
+            ++k;
+        }
+        bits_to_i8(a.enc_h[i], tp.enc[i], h, w, act);
+        snprintf(nm, sizeof nm, "%s.act1", EN[i]);
+        cb(ctx, nm, 0, tp.enc[i], h, w, act.data());
+        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]);
+        ++k;
+        bits_to_i8(a.skip[i], tp.enc[i], h, w, skips[i]);
+        snprintf(nm, sizeof nm, "%s.act2_skip", EN[i]);
+        cb(ctx, nm, 0, tp.enc[i], h, w, skips[i].data());
+        snprintf(nm, sizeof nm, "%s.pool.P", EN[i]);
+        cb(ctx, nm, 1, tp.enc[i], h >> 1, w >> 1, hP.data() + pdoff[i]);
+        bits_to_i8(a.down[i], tp.enc[i], h >> 1, w >> 1, act);
+        snprintf(nm, sizeof nm, "%s.act2_down", EN[i]);
+        cb(ctx, nm, 0, tp.enc[i], h >> 1, w >> 1, act.data());
+    }
+    const int h4 = H >> 4, w4 = W >> 4;
+    cb(ctx, lg[k].name, 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
+    bits_to_i8(a.bott_h, d->bott1.Cout, h4, w4, act);
+    cb(ctx, "bottleneck.act1", 0, d->bott1.Cout, h4, w4, act.data());
+    cb(ctx, lg[k].name, 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
+    std::vector<int8_t> xprev;
+    bits_to_i8(a.bott_x, tp.bott, h4, w4, xprev);
+    cb(ctx, "bottleneck.act2", 0, tp.bott, h4, w4, xprev.data());
+    int xC = tp.bott, hp = h4, wp = w4;
+    for (int i = 0; i < 4; ++i) {
+        const int l = 3 - i, h = H >> l, w = W >> l, sC = tp.enc[l];
+        // the reference's concat tensor (0 where the upsample does not reach)
+        std::vector<int8_t> cat((size_t)(sC + xC) * h * w, 0);
+        memcpy(cat.data(), skips[l].data(), (size_t)sC * h * w);
+        const int cH = std::min(2 * hp, h), cW = std::min(2 * wp, w);
+        const int oh = h > 2 * hp ? (h - 2 * hp) / 2 : 0, ow = w > 2 * wp ? (w - 2 * wp) / 2 : 0;
+        for (int c = 0; c < xC; ++c)
+            for (int y = 0; y < cH; ++y)
+                for (int x = 0; x < cW; ++x)
+                    cat[((size_t)(sC + c) * h + oh + y) * w + ow + x] = xprev[((size_t)c * hp + y / 2) * wp + x / 2];
+        snprintf(nm, sizeof nm, "%s.cat", DN[i]);
+        cb(ctx, nm, 0, sC + xC, h, w, cat.data());
+        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
+        bits_to_i8(a.dec_h[i], d->dec1[i].Cout, h, w, act);
+        snprintf(nm, sizeof nm, "%s.act1", DN[i]);
+        cb(ctx, nm, 0, d->dec1[i].Cout, h, w, act.data());
+        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
+        bits_to_i8(a.dec_x[i], tp.dec[i], h, w, xprev);
+        snprintf(nm, sizeof nm, "%s.act2", DN[i]);
+        cb(ctx, nm, 0, tp.dec[i], h, w, xprev.data());
+        xC = tp.dec[i]; hp = h; wp = w;
+    }
+    cb(ctx, "logits", 2, m->n_classes, H, W, logits);
+    cudaFree(buf);
+    return BNN_OK;
+}
+
+// ---------------- standalone fused layer (isolated-kernel benchmark) ----------------
+struct bnn_bconv_layer {
+    int device;
+    BinLayer L;
+    void* base;
+};
+
+BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t* packed, const int32_t* type,
+                                   const int32_t* t, const int32_t* lo, const int32_t* hi, const int32_t* ptype,
+                                   const int32_t* pt, const int32_t* plo, const int32_t* phi, bnn_bconv_layer** out) {
+    if (!out || !packed || !type || !t || !lo || !hi || Cin <= 0 || Cout <= 0)
+        return set_error(BNN_ERR_ARG, "bad arguments");
+    *out = nullptr;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(device));
+    int arc = set_kernel_attrs(device);
+    if (arc) { cudaSetDevice(prev); return arc; }
+    auto* Lh = new (std::nothrow) bnn_bconv_layer();
+    if (!Lh) return set_error(BNN_ERR_OOM, "OOM");
+    Lh->device = device;
+    HostBin h;
+    relayout_bin(packed, (9 * Cin + 63) / 64, Cin, Cout, Cin, Lh->L, h);
+    Act a{0, Cout, (int32_t*)type, (int32_t*)t, (int32_t*)lo, (int32_t*)hi, nullptr, nullptr, nullptr, nullptr};
+    folds_of(&a, Lh->L.CoutP, h.fold);
+    const bool pool = ptype && pt && plo && phi;
+    if (pool) {
+        Act a2{0, Cout, (int32_t*)ptype, (int32_t*)pt, (int32_t*)plo, (int32_t*)phi, nullptr, nullptr, nullptr, nullptr};
+        folds_of(&a2, Lh->L.CoutP, h.fold2);
+    }
+    size_t total = align256(h.wt.size() * 4) + align256(h.wpop.size() * 4) + 2 * align256(h.fold.size() * sizeof(FoldIv));
+    if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
+        cudaGetLastError();
+        delete Lh;
+        cudaSetDevice(prev);
+        return set_error(BNN_ERR_OOM, "cudaMalloc layer");
+    }
+    char* p = (char*)Lh->base;
+    auto put = [&](const void* src, size_t bytes) -> void* {
+        void* dst = p;
+        if (bytes) cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+        p += align256(bytes);
+        return dst;
+    };
+    Lh->L.wt = (uint32_t*)put(h.wt.data(), h.wt.size() * 4);
+    Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
+    Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
+    Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;
+    cudaError_t e = cudaGetLastError();
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        cudaFree(Lh->base);
+        delete Lh;
+        return set_error(BNN_ERR_CUDA, "layer upload: %s", cudaGetErrorString(e));
+    }
+    *out = Lh;
+    return BNN_OK;
+}
+
+BNN_API int bnn_bconv_layer_run(const bnn_bconv_layer* Lh, const uint32_t* d_in, int N, int H, int W, uint32_t* d_out,
+                                uint32_t* d_out_pool, int32_t* d_P, int32_t* d_Ppool, void* stream) {
+    if (!Lh || !d_in || !d_out || N < 0 || H < 1 || W < 1) return set_error(BNN_ERR_ARG, "bad arguments");
+    if ((d_out_pool || d_Ppool) && !Lh->L.fold2) return set_error(BNN_ERR_ARG, "layer has no pooled fold");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(Lh->device));
+    int rc = run_bin(Lh->L, d_in, nullptr, 0, 0, N, H, W, d_out, d_out_pool, d_P, d_Ppool, (cudaStream_t)stream);
+    cudaSetDevice(prev);
+    return rc;
+}
+
+BNN_API void bnn_bconv_layer_destroy(bnn_bconv_layer* Lh) {
+    if (!Lh) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(Lh->device);
+    cudaFree(Lh->base);
+    cudaSetDevice(prev);
+    delete Lh;
+}
+
+// ---------------- helpers ----------------
+BNN_API int bnn_synth_device(int device, uint32_t seed, uint32_t first, int N, int bands, int H, int W, float* d_out,
+                             void* stream) {
+    if (N < 0 || bands <= 0 || H <= 0 || W <= 0 || (!d_out && N > 0)) return set_error(BNN_ERR_ARG, "bad arguments");
+    if (N == 0) return BNN_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(device));
+    const size_t per = (size_t)bands * H * W, total = per * N;
+    synth_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(seed, first, per, total, d_out);
+    cudaError_t e = cudaGetLastError();
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "synth launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+BNN_API int bnn_pack_act_device(const int8_t* d_a, int N, int C, int H, int W, uint32_t* d_bits, void* stream) {
+    if (N < 0 || C <= 0 || H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "bad arguments");
+    if (N == 0) return BNN_OK;
+    pack_act_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(d_a, N, C, H, W, d_bits);
+    CK(cudaGetLastError());
+    return BNN_OK;
+}
+
+BNN_API int bnn_unpack_act_device(const uint32_t* d_bits, int N, int C, int H, int W, int8_t* d_a, void* stream) {
+    if (N < 0 || C <= 0 || H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "bad arguments");
+    if (N == 0) return BNN_OK;
+    unpack_act_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(d_bits, N, C, H, W, d_a);
+    CK(cudaGetLastError());
+    return BNN_OK;
+}
+
+// ---------------- host-pointer kernel shims ----------------
+BNN_API int bnn_gpu_bconv_dispatch(const int8_t* a, const uint64_t* packed_w, int32_t* P, int Cin, int H, int W,
+                                   int Cout, int kh, int kw, int pad, int stride) {
+    if (kh != 3 || kw != 3 || stride != 1 || (pad != 0 && pad != 1))
+        return set_error(BNN_ERR_UNSUPPORTED, "bconv %dx%d pad %d stride %d: only 3x3 stride 1 pad 0/1", kh, kw, pad,
+                         stride);
+    if (!a || !packed_w || !P || Cin <= 0 || Cout <= 0 || H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "bad arguments");
+    const int Ho = H + 2 * pad - 2, Wo = W + 2 * pad - 2;
+    if (Ho <= 0 || Wo <= 0) return BNN_OK;
+    std::vector<int32_t> zeros(Cout, 0);
+    bnn_bconv_layer* L = nullptr;
+    int rc;
+    int dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = bnn_bconv_layer_create(dev, Cin, Cout, packed_w, zeros.data(), zeros.data(), zeros.data(), zeros.data(),
+                                     nullptr, nullptr, nullptr, nullptr, &L)))
+        return rc;
+    const int cw = cw_of(Cin);
+    const size_t na = (size_t)Cin * H * W, nbits = (size_t)H * W * cw, nP = (size_t)Cout * H * W;
+    void* buf = nullptr;
+    if (cudaMalloc(&buf, na + 16 + nbits * 4 + (size_t)H * W * cw_of(Cout) * 4 + nP * 4) != cudaSuccess) {
+        cudaGetLastError();
+        bnn_bconv_layer_destroy(L);
+        return set_error(BNN_ERR_OOM, "cudaMalloc");
+    }
+    int8_t* da = (int8_t*)buf;
+    uint32_t* dbits = (uint32_t*)((char*)buf + ((na + 15) & ~(size_t)15));
+    uint32_t* dout = dbits + nbits;
+    int32_t* dP = (int32_t*)(dout + (size_t)H * W * cw_of(Cout));
+    rc = BNN_OK;
+    if (cudaMemcpy(da, a, na, cudaMemcpyHostToDevice) != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "H2D");
+    if (!rc) rc = bnn_pack_act_device(da, 1, Cin, H, W, dbits, nullptr);
+    if (!rc) rc = bnn_bconv_layer_run(L, dbits, 1, H, W, dout, nullptr, dP, nullptr, nullptr);
+    if (!rc && cudaDeviceSynchronize() != cudaSuccess)
+        rc = set_error(BNN_ERR_CUDA, "bconv: %s", cudaGetErrorString(cudaGetLastError()));
+    if (!rc) {
+        std::vector<int32_t> full(nP);
+        cudaMemcpy(full.data(), dP, nP * 4, cudaMemcpyDeviceToHost);
+        // pad 0 = the interior of the pad-1 result (every tap in bounds there)
+        for (int co = 0; co < Cout; ++co)
+            for (int y = 0; y < Ho; ++y)
+                for (int x = 0; x < Wo; ++x)
+                    P[((size_t)co * Ho + y) * Wo + x] = full[((size_t)co * H + y + 1 - pad) * W + x + 1 - pad];
+    }
+    cudaFree(buf);
+    bnn_bconv_layer_destroy(L);
+    return rc;
+}
+
+BNN_API int bnn_gpu_conv_realin(const float* x, const int8_t* wsign, const float* alpha, float* out, int Cin, int H,
+                                int W, int Cout, int kh, int kw, int pad, int stride) {
+    if (kh != 3 || kw != 3 || pad != 1 || stride != 1)
+        return set_error(BNN_ERR_UNSUPPORTED, "realin %dx%d pad %d stride %d: only 3x3 pad 1 stride 1", kh, kw, pad,
+                         stride);
+    if (!x || !wsign || !alpha || !out || Cin <= 0 || Cin > 256 || Cout <= 0 || H <= 0 || W <= 0)
+        return set_error(BNN_ERR_ARG, "bad arguments");
+    int rc, dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = set_kernel_attrs(dev))) return rc;
+    DevState d;  // a throwaway state holding only the first-conv tables
+    d.device = dev;
+    const int CoutP = cdiv(Cout, 32) * 32;
+    d.ri_CinP = cdiv(Cin, 4) * 4;
+    d.ri_CIP = d.ri_CinP + (((d.ri_CinP / 4) % 2 == 0) ? 4 : 0);
+    std::vector<float> wf((size_t)CoutP * 9 * d.ri_CinP, 0.0f), fold((size_t)CoutP * 5, 0.0f);
+    for (int co = 0; co < Cout; ++co) {
+        for (int ci = 0; ci < Cin; ++ci)
+            for (int t = 0; t < 9; ++t) wf[((size_t)co * 9 + t) * d.ri_CinP + ci] = (float)wsign[((size_t)co * Cin + ci) * 9 + t];
+        fold[co * 5] = alpha[co];
+        fold[co * 5 + 1] = 1.0f;  // identity fold; only the conv output is returned
+    }
+    Model mm;
+    memset(&mm, 0, sizeof mm);
+    mm.enc_conv1[0].Cin = Cin;
+    mm.enc_conv1[0].Cout = Cout;
+    const size_t nx = (size_t)Cin * H * W, no = (size_t)Cout * H * W, nb = (size_t)H * W * cw_of(Cout);
+    void* buf = nullptr;
+    const size_t bytes = (wf.size() + fold.size() + nx + no + nb) * 4;
+    if (cudaMalloc(&buf, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_OOM, "cudaMalloc");
+    }
+    d.ri_wf = (float*)buf;
+    d.ri_fold = d.ri_wf + wf.size();
+    float* dx = d.ri_fold + fold.size();
+    float* dout = dx + nx;
+    uint32_t* dbits = (uint32_t*)(dout + no);
+    rc = BNN_OK;
+    if (cudaMemcpy(d.ri_wf, wf.data(), wf.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d.ri_fold, fold.data(), fold.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dx, x, nx * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = set_error(BNN_ERR_CUDA, "H2D");
+    if (!rc) rc = run_realin(&d, &mm, dx, 1, H, W, dbits, dout, nullptr);
+    if (!rc && cudaDeviceSynchronize() != cudaSuccess)
+        rc = set_error(BNN_ERR_CUDA, "realin: %s", cudaGetErrorString(cudaGetLastError()));
+    if (!rc && cudaMemcpy(out, dout, no * 4, cudaMemcpyDeviceToHost) != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "D2H");
+    cudaFree(buf);
+    d.device = -1;  // nothing else to release
+    return rc;
+}

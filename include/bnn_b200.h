@@ -1,0 +1,146 @@
+/* bnn_b200.h - extensions of the B200 binary-UNet engine beyond the
+ * reference's three-call API (bnn_model.h). Plain C ABI: pointers, sizes and
+ * int status codes only; `stream` arguments are cudaStream_t passed as
+ * void* (NULL = the legacy default stream).
+ *
+ * Bit-packed activation layout used by every device-pointer call:
+ *   uint32 [N][H][W][ceil(C/32)], channel c -> bit (c & 31) of word (c >> 5),
+ *   bit 1 = +1, bit 0 = -1, unused high bits of the last word are 0.
+ *
+ * Each entry point notes the reference interface it replaces or extends
+ * (paths within Sboyle132/BNNs_to_C).
+ */
+#ifndef BNN_B200_H
+#define BNN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#include "bnn_model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    BNN_OK = 0,
+    BNN_ERR_IO = 1,          /* file cannot be opened / read */
+    BNN_ERR_FORMAT = 2,      /* blob violates the v1 layout (reference bnn_model.c:66-96) */
+    BNN_ERR_UNSUPPORTED = 3, /* valid blob, but a topology bnn_forward cannot run */
+    BNN_ERR_ARG = 4,         /* bad argument (size, pointer, device) */
+    BNN_ERR_CUDA = 5,        /* CUDA runtime error (message names the call) */
+    BNN_ERR_OOM = 6          /* host or device allocation failed */
+};
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *bnn_last_error(void);
+
+/* Status-returning forms of bnn_load (reference csrc/bnn_model.c:66-96):
+ * identical parsing and the same error conditions, but no exit(). The
+ * in-memory form parses `n` bytes at `data`. */
+int bnn_load_ex(const char *path, Model **out);
+int bnn_load_mem(const void *data, size_t n, Model **out);
+
+/* Batched forward with host pointers: input [N][n_bands][H][W] float32 ->
+ * logits [N][n_classes][H][W] float32; each patch's result equals
+ * bnn_forward on that patch (reference csrc/bnn_model.c:150-253). Patches
+ * are sharded by index in contiguous slices over the Model's devices
+ * (bnn_set_devices), one host thread per device; on each device copies in,
+ * compute and copies out overlap chunk by chunk. Page-locked host buffers
+ * (cudaHostAlloc / cudaHostRegister) give full copy bandwidth. Blocks until
+ * the logits are in host memory. */
+int bnn_forward_batch(const Model *m, const float *input, int N, int H, int W,
+                      float *logits);
+
+/* Batched forward on device memory of `device`: enqueued on `stream`,
+ * returns without synchronising. d_input and d_logits must stay valid until
+ * the stream reaches this work. Repeated calls with the same (N, H, W) on
+ * the same stream replay one captured CUDA graph. */
+int bnn_forward_device(const Model *m, int device, const float *d_input, int N,
+                       int H, int W, float *d_logits, void *stream);
+
+/* Devices used by bnn_forward_batch, in shard order. n = 0 restores the
+ * default: the calling thread's current device. */
+int bnn_set_devices(Model *m, const int *devices, int n);
+int bnn_get_devices(const Model *m, int *devices, int cap);
+
+/* Patches per pipelined chunk in bnn_forward_batch (default 512). */
+int bnn_set_chunk(Model *m, int patches);
+
+/* Debug / parity: one patch on the current device, every intermediate
+ * copied back and reported in bnn_forward's order with the names
+ * "<block>.conv<k>.P" (int32 [C][H][W]), "<block>.<act>" (int8 +-1
+ * [C][H][W]), "enc1.conv1.out" (float32, the real conv output),
+ * "<block>.pool.P", "<dec>.cat" (int8; 0 where the upsample does not
+ * reach, as in the reference's up_cat) and "logits". kind: 0 int8, 1 int32,
+ * 2 float32. The stages are the reference forward's intermediates
+ * (csrc/bnn_model.c:150-253), which its own forward frees unseen. */
+typedef void (*bnn_stage_cb)(void *ctx, const char *name, int kind, int C,
+                             int H, int W, const void *data);
+int bnn_forward_stages(const Model *m, const float *input, int H, int W,
+                       float *logits, bnn_stage_cb cb, void *ctx);
+
+/* Per-op profiler: the reference's PROF/prof_report (csrc/bnn_prof.h:13-32,
+ * csrc/bnn_prof.c:42-77) done with CUDA events around each kernel launch.
+ * While enabled, forwards launch eagerly (no graph) and accumulate
+ * per-label device time. Work units as the reference: out_elems * taps. */
+int bnn_profile_enable(Model *m, int on);
+void bnn_profile_reset(Model *m);
+int bnn_profile_count(const Model *m);
+int bnn_profile_get(const Model *m, int i, const char **label,
+                    const char **optype, double *work, double *ms, int *calls);
+void bnn_profile_report(const Model *m, void *file /* FILE* */);
+
+/* GPU-backed host-pointer form of the reference's bconv_dispatch
+ * (csrc/bnn_conv.c:216-223, same signature and result): int8 +-1 input
+ * [Cin][H][W] (values <= 0 count as -1, as in the reference), kidx-packed
+ * weights, int32 P [Cout][Ho][Wo]. kh = kw = 3, stride 1, pad 0 or 1. */
+int bnn_gpu_bconv_dispatch(const int8_t *a, const uint64_t *packed_w, int32_t *P,
+                           int Cin, int H, int W, int Cout, int kh, int kw,
+                           int pad, int stride);
+
+/* GPU-backed host-pointer form of conv_realin_naive for the 3x3 pad-1
+ * stride-1 first conv (csrc/bnn_conv_realin.c:66-116,165-172): bit-identical
+ * float32 output, same operation order. */
+int bnn_gpu_conv_realin(const float *x, const int8_t *wsign, const float *alpha,
+                        float *out, int Cin, int H, int W, int Cout, int kh,
+                        int kw, int pad, int stride);
+
+/* One fused binary 3x3 conv layer on device buffers (the isolated-kernel
+ * benchmark): P (reference bconv_dispatch, csrc/bnn_conv.c:216-223) ->
+ * per-channel integer fold (apply_fold_int, csrc/bnn_fold.c:37-60) -> bit
+ * pack; optionally also 2x2 max-pool of P (maxpool_P, csrc/bnn_maxpool.c:
+ * 28-48) -> second fold -> bit pack. The accumulator never leaves the chip
+ * unless d_P / d_Ppool are given (debug). Weights: kidx-packed uint64
+ * [Cout][ceil(9*Cin/64)] as in the blob; fold arrays: [Cout] each; the
+ * pooled fold arrays may be NULL (no pooled output). */
+typedef struct bnn_bconv_layer bnn_bconv_layer;
+int bnn_bconv_layer_create(int device, int Cin, int Cout,
+                           const uint64_t *packed_kidx, const int32_t *type,
+                           const int32_t *t, const int32_t *lo, const int32_t *hi,
+                           const int32_t *pool_type, const int32_t *pool_t,
+                           const int32_t *pool_lo, const int32_t *pool_hi,
+                           bnn_bconv_layer **out);
+int bnn_bconv_layer_run(const bnn_bconv_layer *L, const uint32_t *d_in, int N,
+                        int H, int W, uint32_t *d_out, uint32_t *d_out_pool,
+                        int32_t *d_P, int32_t *d_Ppool, void *stream);
+void bnn_bconv_layer_destroy(bnn_bconv_layer *L);
+
+/* Seeded synthetic patches (bnn_synth.h) written on `device`:
+ * [N][bands][H][W] float32 for patch indices first..first+N-1. */
+int bnn_synth_device(int device, uint32_t seed, uint32_t first_patch, int N,
+                     int bands, int H, int W, float *d_out, void *stream);
+
+/* int8 +-1 [N][C][H][W] <-> bit-packed [N][H][W][ceil(C/32)] on device
+ * (values > 0 -> bit 1). */
+int bnn_pack_act_device(const int8_t *d_a, int N, int C, int H, int W,
+                        uint32_t *d_bits, void *stream);
+int bnn_unpack_act_device(const uint32_t *d_bits, int N, int C, int H, int W,
+                          int8_t *d_a, void *stream);
+
+/* Number of this library's kernel launches one forward of (N, H, W)
+ * issues (for launch accounting in benchmarks). */
+int bnn_forward_launches(const Model *m, int N, int H, int W);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

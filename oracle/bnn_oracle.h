@@ -1,0 +1,68 @@
+/* bnn_oracle.h - TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C, CPU-only restatement of the reference engine's v1 forward path
+ * (Sboyle132/BNNs_to_C csrc/bnn_model.c and the kernels it calls), written
+ * from the reference's documented semantics, used as the checker for the
+ * B200 engine. Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg may load it; the product library never links it.
+ *
+ * Parity pin: every function here is checked against the reference's own
+ * sources compiled unmodified into oracle/_ref/ (recipe: oracle/Makefile),
+ * through golden fixtures committed under tests/golden/.
+ */
+#ifndef BNN_ORACLE_H
+#define BNN_ORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Stage callback: kind 0 = int8 (+-1 activation or concat), 1 = int32 P,
+ * 2 = float32 (real conv output, logits). Layout [C][H][W]. */
+typedef void (*oracle_stage_cb)(void *ctx, const char *name, int kind,
+                                int C, int H, int W, const void *data);
+
+typedef struct OModel OModel;
+
+OModel *oracle_load(const char *path, char *err, int errlen);
+void oracle_free(OModel *m);
+int oracle_n_bands(const OModel *m);
+int oracle_n_classes(const OModel *m);
+int oracle_base_channels(const OModel *m);
+/* returns 0 on success */
+int oracle_forward(const OModel *m, const float *input, int H, int W,
+                   float *logits, oracle_stage_cb cb, void *ctx);
+/* n patches of [bands][H][W], contiguous */
+int oracle_forward_batch(const OModel *m, const float *input, int n, int H,
+                         int W, float *logits);
+
+/* kernels */
+void oracle_pack_weights(const int8_t *wsign, uint64_t *packed, int Cout,
+                         int Cin, int kh, int kw);
+void oracle_bconv_P(const int8_t *a, const uint64_t *packed_w, int32_t *P,
+                    int Cin, int H, int W, int Cout, int kh, int kw, int pad,
+                    int stride);
+void oracle_realin(const float *x, const int8_t *wsign, const float *alpha,
+                   float *out, int Cin, int H, int W, int Cout, int kh,
+                   int kw, int pad, int stride);
+void oracle_fold_int(const int32_t *P, int8_t *out, int C, int H, int W,
+                     const int32_t *type, const int32_t *t, const int32_t *lo,
+                     const int32_t *hi);
+void oracle_fold_real(const float *x, int8_t *out, int C, int H, int W,
+                      const float *A, const float *B, const float *slope,
+                      const float *rsign);
+void oracle_maxpool(const int32_t *P, int32_t *Pout, int C, int H, int W,
+                    int k, int stride);
+void oracle_up_cat(const int8_t *skip, int sC, int sH, int sW,
+                   const int8_t *x, int xC, int hH, int hW, int8_t *out);
+void oracle_head(const float *a, const float *Wt, const float *bias,
+                 float *logits, int Cin, int H, int W, int Cout);
+void oracle_synth(uint32_t seed, uint32_t patch0, int n, int bands, int H,
+                  int W, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,245 @@
+"""Generate the golden fixtures under tests/golden/ from the REFERENCE itself.
+
+Run in a container that has the reference tree (default /root/reference) and
+the reference build from ``make -C oracle`` (oracle/_ref/). The GPU box has
+neither; it only reads the committed outputs of this script.
+
+What it records:
+  * blob byte-identity: each fixture model is written twice, once by
+    ``bnns_to_c_b200.blob`` and once by the reference's own record emitters
+    (python/bnn2c/blob.py:67-114, driven in the order of its v1 writer
+    :181-199) from equivalent torch modules; the script fails unless the
+    bytes are identical, then saves the blob.
+  * whole-net stages: the reference kernels, unmodified, chained in
+    bnn_forward order by oracle/ref_stages.c -> every P, every +-1 plane,
+    the real conv output and the logits, for seeded synthetic inputs; plus
+    the logits of the reference CLI (csrc/main.c) on the same input, which
+    must equal the chained logits exactly.
+  * kernel cases: reference bconv_dispatch P on the edge-shape list of
+    csrc/bench_bconv.c:103-107 and on the pad=0 self-test case of
+    python/verify/bconv_harness.py:113-118; maxpool_P on the shapes of
+    python/verify/maxpool_harness.py:77.
+
+usage: python tests/golden/make_golden.py [--ref /root/reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import hashlib
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.abspath(os.path.join(HERE, "..", ".."))
+sys.path.insert(0, ROOT)
+
+from bnns_to_c_b200 import blob as B  # noqa: E402
+
+STAGE_CB = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int,
+                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p)
+DT = {0: np.int8, 1: np.int32, 2: np.float32}
+
+# (name, base, rules, model seed, [(H, W, synth seed, n patches)])
+MODELS = [
+    ("unet_c8_mixed_s1", 8, "mixed", 1, [(32, 32, 7, 2), (37, 23, 8, 1)]),
+    ("unet_c16_base_s2", 16, "baseline", 2, [(32, 32, 9, 1), (16, 48, 10, 1)]),
+]
+# base 32 (benchmark widths): blob not committed (1 MB); pinned by sha256
+C32 = ("unet_c32_base_s0", 32, "baseline", 0, [(32, 32, 11, 1)])
+
+
+def ref_blob_bytes(model: dict, ref: str) -> bytes:
+    """Write ``model`` through the reference's own emitters."""
+    import torch
+    sys.path.insert(0, os.path.join(ref, "python", "verify"))
+    sys.path.insert(0, os.path.join(ref, "python", "bnn2c"))
+    import blob as RB  # the reference's python/bnn2c/blob.py
+
+    def conv_mod(c, alpha=None):
+        w = c["wsign"].astype(np.float32)
+        if alpha is not None:
+            w = w * alpha[:, None, None, None]
+        cout, cin, kh, kw = w.shape
+        mod = torch.nn.Conv2d(cin, cout, (kh, kw), padding=c.get("pad", 1),
+                              stride=c.get("stride", 1), bias=False)
+        with torch.no_grad():
+            mod.weight.copy_(torch.from_numpy(w))
+        return mod
+
+    def rule(a):
+        if a["kind"] == "int":
+            return ("int", None, a["type"], a["t"], a["lo"], a["hi"])
+        return ("real", None, a["A"], a["B"], a["slope"], a["rsign"])
+
+    path = tempfile.mktemp(suffix=".blob")
+    import struct
+    with open(path, "wb") as f:
+        f.write(RB.MAGIC)
+        f.write(struct.pack("<5i", RB.VERSION, model["base_channels"], model["n_bands"],
+                            model["n_classes"], 0))
+        for i, st in enumerate(RB.ENC):
+            c1 = model[f"{st}.conv1"]
+            if i == 0:
+                RB._w_conv_real(f, conv_mod(c1, c1["alpha"]))
+            else:
+                RB._w_conv_bin(f, conv_mod(c1))
+            RB._w_act(f, rule(model[f"{st}.act1"]))
+            RB._w_conv_bin(f, conv_mod(model[f"{st}.conv2"]))
+            RB._w_act(f, rule(model[f"{st}.act2_skip"]))
+            RB._w_act(f, rule(model[f"{st}.act2_down"]))
+        RB._w_conv_bin(f, conv_mod(model["bottleneck.conv1"]))
+        RB._w_act(f, rule(model["bottleneck.act1"]))
+        RB._w_conv_bin(f, conv_mod(model["bottleneck.conv2"]))
+        RB._w_act(f, rule(model["bottleneck.act2"]))
+        for st in RB.DEC:
+            RB._w_conv_bin(f, conv_mod(model[f"{st}.conv1"]))
+            RB._w_act(f, rule(model[f"{st}.act1"]))
+            RB._w_conv_bin(f, conv_mod(model[f"{st}.conv2"]))
+            RB._w_act(f, rule(model[f"{st}.act2"]))
+        head = torch.nn.Conv2d(model["head"]["W"].shape[1], model["head"]["W"].shape[0], 1)
+        with torch.no_grad():
+            head.weight.copy_(torch.from_numpy(model["head"]["W"][:, :, None, None]))
+            head.bias.copy_(torch.from_numpy(model["head"]["bias"]))
+        RB._w_head(f, head)
+    data = open(path, "rb").read()
+    rt = RB.read_blob(path)  # the reference reader's round-trip asserts
+    assert len(rt["convs"]) == 18 and len(rt["acts"]) == 22
+    os.unlink(path)
+    return data
+
+
+def pinned_model(name, base, rules, seed, ref):
+    """random_model written by both writers and byte-compared (the
+    reference emitter recomputes alpha = mean|w|; random_model's alphas are
+    exact under that recomputation)."""
+    m = B.random_model(base, 120, 3, seed=seed, rules=rules)
+    rb = ref_blob_bytes(m, ref)
+    tmp = tempfile.mktemp(suffix=".blob")
+    open(tmp, "wb").write(rb)
+    assert np.array_equal(m["enc1.conv1"]["alpha"], B.read_blob(tmp)["convs"][0]["alpha"])
+    os.unlink(tmp)
+    ours = B.blob_bytes(m)
+    if ours != rb:
+        raise SystemExit(f"{name}: blob bytes differ from the reference writer")
+    return m, ours
+
+
+def ref_lib():
+    lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref.so"))
+    lib.bnn_load.restype = ctypes.c_void_p
+    lib.bnn_load.argtypes = [ctypes.c_char_p]
+    lib.bnn_free.argtypes = [ctypes.c_void_p]
+    lib.ref_stages.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_void_p, STAGE_CB, ctypes.c_void_p]
+    lib.bconv_dispatch.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 8
+    lib.pack_weights.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4
+    lib.maxpool_P.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 5
+    return lib
+
+
+def synth(seed, first, n, bands, H, W):
+    lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "liboracle.so"))
+    lib.oracle_synth.argtypes = [ctypes.c_uint32, ctypes.c_uint32] + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    out = np.empty((n, bands, H, W), np.float32)
+    lib.oracle_synth(seed, first, n, bands, H, W, out.ctypes.data)
+    return out
+
+
+def run_stages(lib, blob_path, x, H, W):
+    m = lib.bnn_load(blob_path.encode())
+    stages = {}
+
+    def cb(ctx, name, kind, C, h, w, data):
+        n = C * h * w
+        arr = np.ctypeslib.as_array(ctypes.cast(data, ctypes.POINTER(
+            {0: ctypes.c_int8, 1: ctypes.c_int32, 2: ctypes.c_float}[kind])), shape=(max(n, 1),))
+        stages[name.decode()] = arr[:n].copy().reshape(C, h, w)
+
+    logits = np.zeros((3, H, W), np.float32)
+    fn = STAGE_CB(cb)
+    lib.ref_stages(m, x.ctypes.data, H, W, logits.ctypes.data, fn, None)
+    lib.bnn_free(m)
+    return stages
+
+
+def ref_cli_logits(blob_path, x, H, W):
+    with tempfile.TemporaryDirectory() as d:
+        inp, out = os.path.join(d, "in.bin"), os.path.join(d, "out.bin")
+        x.astype("<f4").tofile(inp)
+        subprocess.run([os.path.join(ROOT, "oracle", "_ref", "bnn_infer"), blob_path, inp, out,
+                        str(H), str(W)], check=True, capture_output=True,
+                       env=dict(os.environ, OMP_NUM_THREADS="1"))
+        return np.fromfile(out, "<f4").reshape(3, H, W)
+
+
+def kernel_cases(lib):
+    rng = np.random.default_rng(1234)
+    res = {}
+    edge = [(1, 1, 1, 4), (3, 1, 5, 4), (5, 5, 1, 8), (7, 4, 4, 6), (16, 3, 3, 16),
+            (17, 5, 7, 8), (130, 3, 10, 8), (192, 3, 12, 8), (63, 4, 6, 8), (64, 4, 6, 8),
+            (65, 4, 6, 8), (130, 3, 3, 8), (48, 9, 9, 16)]
+    cases = [(cin, h, w, cout, 1) for cin, h, w, cout in edge] + [(3, 6, 6, 5, 0)]
+    for i, (cin, h, w, cout, pad) in enumerate(cases):
+        a = rng.choice(np.array([-1, 1], np.int8), size=(cin, h, w))
+        ws = rng.choice(np.array([-1, 1], np.int8), size=(cout, cin, 3, 3))
+        nw = (cin * 9 + 63) // 64
+        packed = np.zeros((cout, nw), np.uint64)
+        lib.pack_weights(ws.ctypes.data, packed.ctypes.data, cout, cin, 3, 3)
+        assert np.array_equal(packed, B.pack_kidx(ws))
+        ho, wo = h + 2 * pad - 2, w + 2 * pad - 2
+        P = np.zeros((cout, ho, wo), np.int32)
+        lib.bconv_dispatch(a.ctypes.data, packed.ctypes.data, P.ctypes.data, cin, h, w, cout,
+                           3, 3, pad, 1)
+        res[f"bconv{i}_a"], res[f"bconv{i}_w"], res[f"bconv{i}_P"] = a, packed, P
+        res[f"bconv{i}_shape"] = np.array([cin, h, w, cout, pad], np.int32)
+    for i, (c, h, w) in enumerate([(8, 8, 8), (16, 6, 10), (4, 4, 4), (5, 7, 9)]):
+        P = rng.integers(-300, 300, size=(c, h, w)).astype(np.int32)
+        out = np.zeros((c, (h - 2) // 2 + 1, (w - 2) // 2 + 1), np.int32)
+        lib.maxpool_P(P.ctypes.data, out.ctypes.data, c, h, w, 2, 2)
+        res[f"pool{i}_in"], res[f"pool{i}_out"] = P, out
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    lib = ref_lib()
+    manifest = []
+    for name, base, rules, seed, runs in MODELS + [C32]:
+        m, data = pinned_model(name, base, rules, seed, args.ref)
+        sha = hashlib.sha256(data).hexdigest()
+        bpath = os.path.join(HERE, name + ".blob")
+        tmpb = tempfile.mktemp(suffix=".blob")
+        open(tmpb, "wb").write(data)
+        if name != C32[0]:
+            open(bpath, "wb").write(data)
+        for H, W, sseed, n in runs:
+            x = synth(sseed, 0, n, 120, H, W)
+            out = {"H": np.int32(H), "W": np.int32(W), "seed": np.int32(sseed), "n": np.int32(n),
+                   "blob_sha256": np.array(sha)}
+            for p in range(n):
+                st = run_stages(lib, tmpb, np.ascontiguousarray(x[p]), H, W)
+                cli = ref_cli_logits(tmpb, x[p], H, W)
+                if not np.array_equal(cli.view(np.int32), st["logits"].view(np.int32)):
+                    raise SystemExit(f"{name}: CLI logits != chained stage logits")
+                for k, v in st.items():
+                    out[f"p{p}/{k}"] = v
+            np.savez_compressed(os.path.join(HERE, f"{name}_{H}x{W}.npz"), **out)
+            manifest.append(f"{name} {H}x{W} seed={sseed} n={n} blob_sha256={sha}")
+        os.unlink(tmpb)
+    np.savez_compressed(os.path.join(HERE, "kernels.npz"), **kernel_cases(lib))
+    with open(os.path.join(HERE, "MANIFEST.txt"), "w") as f:
+        f.write("# generated by tests/golden/make_golden.py from the reference build\n")
+        f.write("\n".join(manifest) + "\n")
+    print("\n".join(manifest))
+
+
+if __name__ == "__main__":
+    main()

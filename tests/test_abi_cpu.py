@@ -1,0 +1,153 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports
+every declared entry point, the blob parser reproduces the reference
+loader's accept/reject behaviour (csrc/bnn_model.c:66-96), the drop-in
+bnn_load exits(1) with the reference's messages, and the Python blob
+writer/reader round-trips."""
+
+import ctypes
+import os
+import re
+import struct
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import bnns_to_c_b200 as bn
+from bnns_to_c_b200 import blob as B
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+GOLD = os.path.join(ROOT, "tests", "golden")
+C8 = os.path.join(GOLD, "unet_c8_mixed_s1.blob")
+
+
+def declared_functions():
+    names = []
+    for h in ("bnn_model.h", "bnn_b200.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(bnn_\w+)\s*\(", src, flags=re.M):
+            if "typedef" not in src[max(0, m.start() - 20):m.start() + 10]:
+                names.append(m.group(1))
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(bn.LIB_PATH)
+    names = declared_functions()
+    assert len(names) >= 25
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", bn.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    # only the C ABI is exported (no C++ or CUDA runtime internals)
+    assert all(s.startswith("bnn_") for s in exported), sorted(s for s in exported if not s.startswith("bnn_"))
+
+
+def test_load_parses_header_without_gpu():
+    m = bn.Model(C8)
+    assert (m.version, m.base_channels, m.n_bands, m.n_classes, m.upsampler) == (1, 8, 120, 3, 0)
+    m.close()
+
+
+def _status(data):
+    L = bn.lib()
+    h = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(data, len(data))
+    rc = L.bnn_load_mem(buf, len(data), ctypes.byref(h))
+    if rc == 0:
+        L.bnn_free(h.value)
+    return rc, L.bnn_last_error().decode()
+
+
+def test_loader_rejections_match_reference():
+    data = open(C8, "rb").read()
+    assert _status(data) == (0, "")
+    assert _status(data[:100])[1] == "short read"
+    assert _status(data[:-1])[1] == "short read"
+    assert _status(data + b"\0")[1] == "trailing bytes in blob"
+    assert _status(b"XNNC" + data[4:])[1] == "bad magic"
+    assert _status(b"")[1] == "short read"
+    # first conv tag -> 7
+    bad = data[:24] + struct.pack("<i", 7) + data[28:]
+    assert _status(bad)[1] == "bad conv tag 7"
+    # locate the first act record: conv header 7 ints + wsign + alpha
+    cout, cin = struct.unpack("<2i", data[28:36])
+    act_off = 24 + 28 + cout * cin * 9 + cout * 4
+    assert struct.unpack("<i", data[act_off:act_off + 4])[0] == 3
+    bad = data[:act_off] + struct.pack("<i", 9) + data[act_off + 4:]
+    assert _status(bad)[1] == "bad act tag 9"
+    bad = data[:-(3 * 4 + 8 * 3 * 4 + 3 * 4)] + struct.pack("<i", 5) + data[-(2 * 4 + 8 * 3 * 4 + 3 * 4):]
+    assert _status(bad)[1] == "bad head tag 5"
+
+
+def test_loader_topology_validation():
+    m = B.random_model(8, 120, 3, seed=4)
+    m["enc2.act1"] = dict(m["enc2.act1"])
+    good = B.blob_bytes(m)
+    assert _status(good)[0] == 0
+    # a real fold where the forward has an integer accumulator: the
+    # reference would pass xreal = NULL to apply_fold_real
+    m2 = B.random_model(8, 120, 3, seed=4)
+    c = len(m2["enc2.act1"]["type"])
+    m2["enc2.act1"] = {"kind": "real", "A": np.ones(c, np.float32), "B": np.zeros(c, np.float32),
+                       "slope": np.ones(c, np.float32), "rsign": np.zeros(c, np.float32)}
+    rc, msg = _status(B.blob_bytes(m2))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "enc2.act1" in msg
+    # channel chain broken: head sized for a different width
+    m3 = B.random_model(8, 120, 3, seed=4)
+    m3["head"]["W"] = np.zeros((3, 9), np.float32)
+    rc, msg = _status(B.blob_bytes(m3))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "head" in msg
+    # 1x1 conv where the forward needs 3x3
+    m4 = B.random_model(8, 120, 3, seed=4)
+    m4["enc3.conv2"] = {"tag": "bin", "wsign": m4["enc3.conv2"]["wsign"][:, :, :1, :1], "pad": 0}
+    rc, msg = _status(B.blob_bytes(m4))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "enc3.conv2" in msg
+
+
+def test_dropin_bnn_load_exits_like_reference(tmp_path):
+    p = tmp_path / "t.blob"
+    p.write_bytes(open(C8, "rb").read() + b"x")
+    code = ("import ctypes,sys; L=ctypes.CDLL(sys.argv[1]); L.bnn_load.restype=ctypes.c_void_p; "
+            "L.bnn_load(sys.argv[2].encode()); print('returned')")
+    r = subprocess.run([sys.executable, "-c", code, bn.LIB_PATH, str(p)], capture_output=True, text=True)
+    assert r.returncode == 1 and "trailing bytes in blob" in r.stderr and "returned" not in r.stdout
+    r = subprocess.run([sys.executable, "-c", code, bn.LIB_PATH, str(tmp_path / "nope.blob")],
+                       capture_output=True, text=True)
+    assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+def test_forward_without_gpu_raises_not_falls_back():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    m = bn.Model(C8)
+    with pytest.raises(bn.BnnError) as e:
+        m.forward(np.zeros((120, 32, 32), np.float32))
+    assert e.value.code == bn.BNN_ERR_CUDA
+
+
+def test_blob_roundtrip_and_committed_bytes():
+    for name, base, rules, seed in (("unet_c8_mixed_s1", 8, "mixed", 1), ("unet_c16_base_s2", 16, "baseline", 2)):
+        data = B.blob_bytes(B.random_model(base, 120, 3, seed=seed, rules=rules))
+        assert data == open(os.path.join(GOLD, name + ".blob"), "rb").read()
+    r = B.read_blob(C8)
+    assert len(r["convs"]) == 18 and len(r["acts"]) == 22
+    m = B.random_model(8, 120, 3, seed=1, rules="mixed")
+    w = m["enc2.conv1"]["wsign"]
+    assert np.array_equal(B.unpack_kidx(r["convs"][2]["packed"], w.shape[1], 3, 3), w)
+
+
+def test_pack_kidx_bit_order():
+    w = -np.ones((2, 1, 3, 3), np.int8)
+    w[0, 0, 0, 0] = 1   # kidx 0
+    w[1, 0, 2, 2] = 1   # kidx 8
+    p = B.pack_kidx(w)
+    assert p.shape == (2, 1) and int(p[0, 0]) == 1 and int(p[1, 0]) == 1 << 8
+
+
+def test_cli_usage_matches_reference():
+    r = subprocess.run([bn.CLI_PATH], capture_output=True, text=True)
+    assert r.returncode == 1 and "usage:" in r.stderr and "input.bin|rand output.bin [H W [reps]]" in r.stderr

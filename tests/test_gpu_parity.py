@@ -1,0 +1,238 @@
+"""GPU parity: every kernel and the whole forward, through the C ABI,
+against the CPU oracle (itself pinned to the reference build) and the
+reference's golden fixtures. Integer stages and +-1 planes must be
+bit-exact; the float stages (first conv output, logits) are bit-exact too
+because the kernels keep the reference's fp32 operation order (the
+reference's own logits gate is 1e-5 absolute, which this exceeds)."""
+
+import glob
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import bnns_to_c_b200 as bn  # noqa: E402
+from bnns_to_c_b200 import blob as B  # noqa: E402
+from oracle_util import OModel, bconv_P, fold_int, maxpool, realin, synth  # noqa: E402
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def same_bits(a, b):
+    return a.shape == b.shape and np.array_equal(np.ascontiguousarray(a).view(np.uint8),
+                                                 np.ascontiguousarray(b).view(np.uint8))
+
+
+# ------------------------------------------------------------------ kernels
+def test_bconv_dispatch_edge_shapes():
+    """Reference bench_bconv.c edge-shape list + bconv_harness pad=0 case."""
+    g = np.load(os.path.join(GOLD, "kernels.npz"))
+    i = 0
+    while f"bconv{i}_a" in g.files:
+        cin, h, w, cout, pad = (int(v) for v in g[f"bconv{i}_shape"])
+        P = bn.gpu_bconv_dispatch(g[f"bconv{i}_a"], g[f"bconv{i}_w"], cout, pad)
+        assert np.array_equal(P, g[f"bconv{i}_P"]), (cin, h, w, cout, pad)
+        i += 1
+
+
+@pytest.mark.parametrize("cin,cout,H,W", [(120, 32, 32, 32), (120, 16, 37, 23), (7, 8, 16, 16),
+                                          (121, 40, 20, 33), (64, 64, 17, 64), (3, 5, 5, 7)])
+def test_realin_bit_exact(cin, cout, H, W):
+    rng = np.random.default_rng(cin * 1000 + cout)
+    x = synth(21, cout, 1, cin, H, W)[0]
+    ws = np.where(rng.random((cout, cin, 3, 3)) < 0.5, 1, -1).astype(np.int8)
+    alpha = rng.uniform(0.5, 1.5, cout).astype(np.float32)
+    assert same_bits(bn.gpu_conv_realin(x, ws, alpha), realin(x, ws, alpha))
+
+
+def _rand_fold(rng, c, cin):
+    sd = max(1, int(np.sqrt(9 * cin)))
+    return {"type": rng.choice(np.array([0, 1, 2, 3, 4, 9], np.int32), c),
+            "t": rng.integers(-sd, sd + 1, c).astype(np.int32),
+            "lo": rng.integers(-2 * sd, sd, c).astype(np.int32),
+            "hi": rng.integers(-sd, 2 * sd, c).astype(np.int32)}
+
+
+def _unpack(bits, n, c, H, W):
+    d = torch.empty((n, c, H, W), dtype=torch.int8, device="cuda")
+    bn.unpack_act_device(bits, n, c, H, W, d)
+    torch.cuda.synchronize()
+    return d.cpu().numpy()
+
+
+@pytest.mark.parametrize("cin,cout,H,W,n", [(64, 64, 16, 16, 2), (128, 128, 16, 16, 2), (256, 256, 8, 8, 3),
+                                            (512, 512, 4, 4, 5), (64, 64, 32, 32, 1), (48, 40, 17, 13, 2),
+                                            (32, 32, 2, 2, 40), (96, 32, 32, 32, 1), (768, 256, 4, 4, 3),
+                                            (16, 200, 9, 70, 1)])
+def test_fused_layer_vs_oracle(cin, cout, H, W, n):
+    rng = np.random.default_rng(cin + 7 * cout + H)
+    a = np.where(rng.random((n, cin, H, W)) < 0.5, 1, -1).astype(np.int8)
+    ws = np.where(rng.random((cout, cin, 3, 3)) < 0.5, 1, -1).astype(np.int8)
+    packed = B.pack_kidx(ws)
+    f1, f2 = _rand_fold(rng, cout, cin), _rand_fold(rng, cout, cin)
+    L = bn.BconvLayer(0, cin, cout, packed, f1, f2)
+    cwi, cwo = (cin + 31) // 32, (cout + 31) // 32
+    da = torch.from_numpy(a).cuda()
+    bits = torch.empty((n, H, W, cwi), dtype=torch.int32, device="cuda")
+    bn.pack_act_device(da, n, cin, H, W, bits)
+    out = torch.zeros((n, H, W, cwo), dtype=torch.int32, device="cuda")
+    outp = torch.zeros((n, H // 2, W // 2, cwo), dtype=torch.int32, device="cuda")
+    P = torch.zeros((n, cout, H, W), dtype=torch.int32, device="cuda")
+    Pp = torch.zeros((n, cout, H // 2, W // 2), dtype=torch.int32, device="cuda")
+    L.run(bits, n, H, W, out, outp, P, Pp)
+    torch.cuda.synchronize()
+    got_a, got_p = _unpack(out, n, cout, H, W), _unpack(outp, n, cout, H // 2, W // 2)
+    P, Pp = P.cpu().numpy(), Pp.cpu().numpy()
+    for i in range(n):
+        Pr = bconv_P(a[i], packed, cout)
+        assert np.array_equal(P[i], Pr)
+        assert np.array_equal(got_a[i], fold_int(Pr, f1))
+        Pd = maxpool(Pr)
+        assert np.array_equal(Pp[i], Pd)
+        assert np.array_equal(got_p[i], fold_int(Pd, f2))
+    # unused high bits of the last output word stay zero
+    if cout % 32:
+        w = out.cpu().numpy()[..., -1].view(np.uint32)
+        assert not np.any(w >> (cout % 32))
+
+
+# ------------------------------------------------------------------ whole net
+def _fixtures():
+    return sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz")))
+
+
+def _blob_path(name, tmp_path):
+    p = os.path.join(GOLD, name + ".blob")
+    if os.path.exists(p):
+        return p
+    q = tmp_path / (name + ".blob")
+    q.write_bytes(B.blob_bytes(B.random_model(32, 120, 3, seed=0, rules="baseline")))
+    return str(q)
+
+
+@pytest.mark.parametrize("npz", _fixtures(), ids=[os.path.basename(f) for f in _fixtures()])
+def test_forward_stages_match_reference(npz, tmp_path):
+    g = np.load(npz)
+    name = os.path.basename(npz).rsplit("_", 1)[0]
+    H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
+    m = bn.Model(_blob_path(name, tmp_path))
+    x = synth(seed, 0, n, 120, H, W)
+    for p in range(n):
+        st = m.stages(x[p])
+        keys = [k[len(f"p{p}/"):] for k in g.files if k.startswith(f"p{p}/")]
+        assert set(keys) == set(st), set(keys) ^ set(st)
+        for k in keys:
+            assert same_bits(st[k], g[f"p{p}/{k}"]), k
+    # the batched path gives the same logits as the stage-by-stage path
+    lg = m.forward_batch(x)
+    for p in range(n):
+        assert same_bits(lg[p], g[f"p{p}/logits"])
+
+
+def test_batch_chunks_and_device_api_agree():
+    m = bn.Model(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    om = OModel(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    x = synth(99, 0, 7, 120, 32, 48)
+    ref = om.forward_batch(x)
+    m.set_chunk(3)  # 3 chunks, the last one partial
+    assert same_bits(m.forward_batch(x), ref)
+    m.set_chunk(512)
+    assert same_bits(m.forward_batch(x), ref)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((7, 3, 32, 48), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    for _ in range(2):  # second call replays the captured graph
+        dy.zero_()
+        m.forward_device(0, dx, 7, 32, 48, dy, s)
+        s.synchronize()
+        assert same_bits(dy.cpu().numpy(), ref)
+
+
+def test_synth_device_matches_host():
+    d = torch.empty((3, 120, 32, 32), dtype=torch.float32, device="cuda")
+    bn.synth_device(0, 1234, 4000, 3, 120, 32, 32, d)
+    torch.cuda.synchronize()
+    assert same_bits(d.cpu().numpy(), synth(1234, 4000, 3, 120, 32, 32))
+
+
+def test_cli_matches_reference_logits(tmp_path):
+    g = np.load(os.path.join(GOLD, "unet_c16_base_s2_16x48.npz"))
+    x = synth(int(g["seed"]), 0, 1, 120, 16, 48)[0]
+    inp, out = tmp_path / "in.bin", tmp_path / "out.bin"
+    x.astype("<f4").tofile(inp)
+    r = subprocess.run([bn.CLI_PATH, os.path.join(GOLD, "unet_c16_base_s2.blob"), str(inp), str(out), "16", "48", "3"],
+                       capture_output=True, text=True, env=dict(os.environ, BNN_PROFILE="1"))
+    assert r.returncode == 0, r.stderr
+    assert "# forward   :" in r.stderr and "# per-op" in r.stderr
+    got = np.fromfile(out, "<f4").reshape(3, 16, 48)
+    assert same_bits(got, g["p0/logits"])
+
+
+def test_refuses_sizes_the_reference_cannot_run():
+    m = bn.Model(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    with pytest.raises(bn.BnnError) as e:
+        m.forward(np.zeros((120, 8, 32), np.float32))
+    assert e.value.code == bn.BNN_ERR_ARG
+
+
+def test_profiler_records_every_launch():
+    m = bn.Model(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    m.profile(True)
+    m.forward_batch(synth(5, 0, 4, 120, 32, 32))
+    recs = m.profile_records()
+    assert len(recs) == m.launches(4, 32, 32) == 19
+    assert sum(r["op"] == "bconv" for r in recs) == 17
+    assert all(r["ms"] > 0 and r["calls"] == 1 for r in recs)
+
+
+@pytest.mark.slow
+def test_full_batch_properties():
+    """Benchmark size (c=32, 4096 patches of 32x32x120): sampled patches
+    equal the oracle, and the result does not depend on how the batch is
+    split (shard invariance, the property the multi-GPU split relies on)."""
+    m = bn.Model.__new__(bn.Model)
+    data = B.blob_bytes(B.random_model(32, 120, 3, seed=0, rules="baseline"))
+    m.__init__(data=data)
+    N, H, W = 4096, 32, 32
+    dx = torch.empty((N, 120, H, W), dtype=torch.float32, device="cuda")
+    bn.synth_device(0, 17, 0, N, 120, H, W, dx)
+    full = torch.empty((N, 3, H, W), dtype=torch.float32, device="cuda")
+    m.forward_device(0, dx, N, H, W, full)
+    part = torch.empty_like(full)
+    m.forward_device(0, dx[:1000], 1000, H, W, part[:1000])
+    m.forward_device(0, dx[1000:], N - 1000, H, W, part[1000:])
+    torch.cuda.synchronize()
+    assert torch.equal(full.view(torch.int32), part.view(torch.int32))
+    import tempfile
+    with tempfile.NamedTemporaryFile(suffix=".blob") as f:
+        f.write(data)
+        f.flush()
+        om = OModel(f.name)
+        idx = [0, 1, 2047, 4095]
+        ref = om.forward_batch(synth(17, 0, N, 120, H, W)[idx]) if False else \
+            np.stack([om.forward_batch(synth(17, i, 1, 120, H, W))[0] for i in idx])
+    got = full[idx].cpu().numpy()
+    assert same_bits(got, ref)
+    # every logit finite, every class wins somewhere in the batch
+    am = full.argmax(1)
+    assert torch.isfinite(full).all() and len(torch.unique(am)) == 3
+
+
+def test_multi_device_shards_match_single():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    m = bn.Model(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    x = synth(3, 0, 9, 120, 32, 32)
+    ref = m.forward_batch(x)
+    m.set_devices(list(range(torch.cuda.device_count())))
+    assert same_bits(m.forward_batch(x), ref)

@@ -1,0 +1,91 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures made
+by tests/golden/make_golden.py from the reference sources compiled
+unmodified). Pins the oracle before any GPU result is compared with it."""
+
+import glob
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from bnns_to_c_b200 import blob as B
+from oracle_util import OModel, bconv_P, maxpool, synth
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def fixtures():
+    out = []
+    for f in sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz"))):
+        base = os.path.basename(f)
+        name = base.rsplit("_", 1)[0]
+        out.append((name, f))
+    return out
+
+
+def blob_for(name, tmp_path):
+    """Committed blob, or (base-32 model) regenerated from its seed and
+    checked against the recorded sha256."""
+    p = os.path.join(GOLD, name + ".blob")
+    if os.path.exists(p):
+        return p
+    assert name == "unet_c32_base_s0"
+    data = B.blob_bytes(B.random_model(32, 120, 3, seed=0, rules="baseline"))
+    q = tmp_path / (name + ".blob")
+    q.write_bytes(data)
+    return str(q)
+
+
+@pytest.mark.parametrize("name,npz", fixtures(), ids=[os.path.basename(f) for _, f in fixtures()])
+def test_oracle_matches_reference_stages(name, npz, tmp_path):
+    g = np.load(npz)
+    path = blob_for(name, tmp_path)
+    assert hashlib.sha256(open(path, "rb").read()).hexdigest() == str(g["blob_sha256"])
+    H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
+    x = synth(seed, 0, n, 120, H, W)
+    m = OModel(path)
+    for p in range(n):
+        st = m.stages(x[p])
+        keys = [k[len(f"p{p}/"):] for k in g.files if k.startswith(f"p{p}/")]
+        assert set(keys) == set(st), set(keys) ^ set(st)
+        for k in keys:
+            ref = g[f"p{p}/{k}"]
+            got = st[k]
+            assert got.shape == ref.shape, k
+            # every stage bit-exact, floats included (same operation order)
+            assert np.array_equal(got.view(np.uint8), ref.view(np.uint8)), k
+
+
+def test_oracle_bconv_edge_shapes():
+    g = np.load(os.path.join(GOLD, "kernels.npz"))
+    i = 0
+    while f"bconv{i}_a" in g.files:
+        cin, h, w, cout, pad = g[f"bconv{i}_shape"]
+        P = bconv_P(g[f"bconv{i}_a"], g[f"bconv{i}_w"], int(cout), int(pad))
+        assert np.array_equal(P, g[f"bconv{i}_P"]), (cin, h, w, cout, pad)
+        i += 1
+    assert i == 14
+
+
+def test_oracle_maxpool():
+    g = np.load(os.path.join(GOLD, "kernels.npz"))
+    for i in range(4):
+        assert np.array_equal(maxpool(g[f"pool{i}_in"]), g[f"pool{i}_out"])
+
+
+def test_oracle_refuses_tiny_sizes():
+    m = OModel(os.path.join(GOLD, "unet_c8_mixed_s1.blob"))
+    with pytest.raises(ValueError):
+        m.stages(np.zeros((120, 8, 8), np.float32))
+
+
+def test_synth_distribution_and_determinism():
+    a = synth(3, 10, 2, 120, 16, 16)
+    b = synth(3, 11, 1, 120, 16, 16)
+    assert np.array_equal(a[1], b[0])  # a pure function of (seed, patch, element)
+    v = synth(5, 0, 4, 120, 32, 32).ravel()
+    assert abs(v.mean()) < 0.01 and abs(v.std() - 1.0) < 0.01
+    assert np.abs(v).max() <= 3.47
+    # pinned value (guards the generator against silent changes)
+    assert float(synth(0, 0, 1, 1, 1, 1)[0, 0, 0, 0]).hex() == "0x1.fd9d880000000p-1"
