@@ -78,6 +78,7 @@ def lib():
         "bnn_profile_report": (None, [vp, vp]),
         "bnn_gpu_bconv_dispatch": (ip, [vp, vp, vp] + [ip] * 8),
         "bnn_gpu_conv_realin": (ip, [vp, vp, vp, vp] + [ip] * 8),
+        "bnn_gpu_bconv_dispatch_noalloc": (ip, [vp, vp, vp] + [ip] * 8),
         "bnn_bconv_layer_create": (ip, [ip, ip, ip] + [vp] * 9 + [ctypes.POINTER(vp)]),
         "bnn_bconv_layer_run": (ip, [vp, vp, ip, ip, ip, vp, vp, vp, vp, vp]),
         "bnn_bconv_layer_destroy": (None, [vp]),

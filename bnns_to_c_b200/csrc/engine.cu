@@ -1260,3 +1260,136 @@ BNN_API int bnn_gpu_conv_realin(const float* x, const int8_t* wsign, const float
     d.device = -1;  // nothing else to release
     return rc;
 }
+
+// ===================================================================
+// Allocation-free bconv_dispatch.
+//
+// For callers that must not allocate device memory: processes whose GPU
+// memory is fixed up front by an allocator or memory budget of their own (an
+// extra cudaMalloc can fail there, or fragment the pool), and latency-bound
+// loops that cannot afford the device-wide synchronisation cudaFree implies.
+// bnn_gpu_bconv_dispatch stages its operands in cudaMalloc'd buffers; this
+// variant carves the same buffers out of one file-scope static device array
+// of BNN_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
+// until the process exits.
+// ===================================================================
+namespace bnn {
+
+static constexpr size_t kNoAllocScratch = BNN_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64];  // device address of g_noalloc_scratch, per device
+
+// Once per device, with that device current: the array's name in host code
+// is only a host-side stand-in, so its device address comes from
+// cudaGetSymbolAddress.
+static int noalloc_scratch(int dev, unsigned char** out) {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (dev < 0 || dev >= 64) return set_error(BNN_ERR_ARG, "device %d out of range for the static scratch", dev);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(BNN_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        int rc = set_kernel_attrs(dev);
+        if (rc) return rc;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = (unsigned char*)g_noalloc_addr[dev];
+    return BNN_OK;
+}
+
+// kidx-ordered weights (bit ci*9+t of row co) -> tap-major words + per-tap
+// popcounts, one thread per (co, tap); rows co >= Cout are written as zero,
+// so nothing in the shared array has to be cleared first.
+__global__ void noalloc_relayout_kernel(const uint64_t* packed, int nwords, int Cin, int Cout, int CoutP, int Kw,
+                                        uint32_t* wt, int* wpop, FoldIv* fold) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= CoutP * 9) return;
+    const int co = g / 9, t = g - co * 9;
+    int pop = 0;
+    for (int w = 0; w < Kw; ++w) {
+        uint32_t word = 0u;
+        if (co < Cout)
+            for (int b = 0; b < 32; ++b) {
+                const int ci = w * 32 + b;
+                if (ci >= Cin) break;
+                const int k = ci * 9 + t;
+                if ((packed[(size_t)co * nwords + (k >> 6)] >> (k & 63)) & 1ull) word |= 1u << b;
+            }
+        wt[(size_t)g * Kw + w] = word;
+        pop += __popc(word);
+    }
+    wpop[g] = pop;
+    if (t == 0) fold[co] = FoldIv{0, 0, 0, 0};  // P is the output; the fold is unused
+}
+
+// P [Cout][H][W] (pad-1 geometry) -> interior [Cout][H-2][W-2] for pad 0
+__global__ void noalloc_crop_kernel(const int32_t* P, int Cout, int H, int W, int32_t* out) {
+    const int Ho = H - 2, Wo = W - 2;
+    const size_t total = (size_t)Cout * Ho * Wo;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+        const int x = (int)(g % Wo), y = (int)((g / Wo) % Ho);
+        const size_t c = g / ((size_t)Wo * Ho);
+        out[g] = P[(c * H + y + 1) * W + x + 1];
+    }
+}
+
+}  // namespace bnn
+
+BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* packed_w, int32_t* P, int Cin, int H,
+                                           int W, int Cout, int kh, int kw, int pad, int stride) {
+    if (kh != 3 || kw != 3 || stride != 1 || (pad != 0 && pad != 1))
+        return set_error(BNN_ERR_UNSUPPORTED, "bconv %dx%d pad %d stride %d: only 3x3 stride 1 pad 0/1", kh, kw, pad,
+                         stride);
+    if (!a || !packed_w || !P || Cin <= 0 || Cout <= 0 || H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "bad arguments");
+    const int Ho = H + 2 * pad - 2, Wo = W + 2 * pad - 2;
+    if (Ho <= 0 || Wo <= 0) return BNN_OK;
+    int rc, dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    // layout of the static scratch for this call (256-byte aligned regions)
+    const int nwords = (9 * Cin + 63) / 64, Kw = cw_of(Cin), CoutP = cdiv(Cout, 128) * 128;
+    const size_t n_a = (size_t)Cin * H * W, n_pk = (size_t)Cout * nwords * 8, n_bits = (size_t)H * W * Kw * 4,
+                 n_wt = (size_t)CoutP * 9 * Kw * 4, n_pop = (size_t)CoutP * 9 * 4, n_fold = (size_t)CoutP * sizeof(FoldIv),
+                 n_out = (size_t)H * W * cw_of(Cout) * 4, n_P = (size_t)Cout * H * W * 4,
+                 n_crop = pad == 0 ? (size_t)Cout * Ho * Wo * 4 : 0;
+    const size_t need = align256(n_a) + align256(n_pk) + align256(n_bits) + align256(n_wt) + align256(n_pop) +
+                        align256(n_fold) + align256(n_out) + align256(n_P) + align256(n_crop);
+    if (need > kNoAllocScratch)
+        return set_error(BNN_ERR_ARG,
+                         "bconv Cin=%d H=%d W=%d Cout=%d needs %zu bytes of scratch, above the %zu-byte static array",
+                         Cin, H, W, Cout, need, kNoAllocScratch);
+    unsigned char* base = nullptr;
+    if ((rc = noalloc_scratch(dev, &base))) return rc;
+    unsigned char* p = base;
+    auto take = [&](size_t bytes) { unsigned char* r = p; p += align256(bytes); return r; };
+    int8_t* da = (int8_t*)take(n_a);
+    uint64_t* dpk = (uint64_t*)take(n_pk);
+    uint32_t* dbits = (uint32_t*)take(n_bits);
+    BinLayer L;
+    L.Cin = Cin; L.Cout = Cout; L.CoutP = CoutP; L.cw0 = Kw; L.cw1 = 0; L.Kw = Kw; L.sC = Cin;
+    L.wt = (uint32_t*)take(n_wt);
+    L.wpop = (int*)take(n_pop);
+    L.fold = (FoldIv*)take(n_fold);
+    L.fold2 = nullptr;
+    uint32_t* dout = (uint32_t*)take(n_out);
+    int32_t* dP = (int32_t*)take(n_P);
+    int32_t* dcrop = (int32_t*)take(n_crop);
+    // every region below is fully rewritten by this call before it is read
+    CK(cudaMemcpy(da, a, n_a, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dpk, packed_w, n_pk, cudaMemcpyHostToDevice));
+    noalloc_relayout_kernel<<<cdiv((long)CoutP * 9, 128), 128>>>(dpk, nwords, Cin, Cout, CoutP, Kw, L.wt, L.wpop, L.fold);
+    CK(cudaGetLastError());
+    pack_act_kernel<<<148 * 4, 256>>>(da, 1, Cin, H, W, dbits);
+    CK(cudaGetLastError());
+    if ((rc = run_bin(L, dbits, nullptr, 0, 0, 1, H, W, dout, nullptr, dP, nullptr, nullptr))) return rc;
+    const int32_t* src = dP;
+    if (pad == 0) {
+        noalloc_crop_kernel<<<148 * 4, 256>>>(dP, Cout, H, W, dcrop);
+        CK(cudaGetLastError());
+        src = dcrop;
+    }
+    CK(cudaMemcpy(P, src, (size_t)Cout * Ho * Wo * 4, cudaMemcpyDeviceToHost));
+    return BNN_OK;
+}

@@ -97,6 +97,28 @@ int bnn_gpu_bconv_dispatch(const int8_t *a, const uint64_t *packed_w, int32_t *P
                            int Cin, int H, int W, int Cout, int kh, int kw,
                            int pad, int stride);
 
+/* Allocation-free twin of bnn_gpu_bconv_dispatch: same arguments, same
+ * result, but it never calls cudaMalloc or cudaFree (nor any allocating
+ * library routine). It has no counterpart in the reference: it is for
+ * callers that cannot let this library allocate device memory - processes
+ * whose GPU memory is fixed up front by their own allocator or budget, and
+ * latency-bound loops that cannot take the device-wide synchronisation of
+ * cudaFree. Its staging buffers live in one static device array of
+ * BNN_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * the process exits; a call whose buffers do not fit returns BNN_ERR_ARG
+ * before touching the GPU (it needs about 1.2*Cin*H*W + 8*Cout*H*W +
+ * 2.3*Cout*Cin bytes, each buffer rounded up to 256).
+ * The first call on a device looks up that array's device address (once per
+ * device, with the device current); make that first call before any stream
+ * capture. All calls share the one array and it keeps the last call's
+ * contents: calls that overlap on the GPU (from several host threads on one
+ * device) race, so serialise them. Runs on the current device and returns
+ * when P is in host memory. */
+#define BNN_NOALLOC_SCRATCH_BYTES (32u << 20)
+int bnn_gpu_bconv_dispatch_noalloc(const int8_t *a, const uint64_t *packed_w,
+                                   int32_t *P, int Cin, int H, int W, int Cout,
+                                   int kh, int kw, int pad, int stride);
+
 /* GPU-backed host-pointer form of conv_realin_naive for the 3x3 pad-1
  * stride-1 first conv (csrc/bnn_conv_realin.c:66-116,165-172): bit-identical
  * float32 output, same operation order. */
