@@ -86,6 +86,7 @@ def lib():
         "bnn_pack_act_device": (ip, [vp, ip, ip, ip, ip, vp, vp]),
         "bnn_unpack_act_device": (ip, [vp, ip, ip, ip, ip, vp, vp]),
         "bnn_forward_launches": (ip, [vp, ip, ip, ip]),
+        "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -176,6 +177,16 @@ class Model:
         fn = STAGE_CB(cb)
         _check(lib().bnn_forward_stages(self.handle, _ptr(x), H, W, _ptr(logits), fn, None))
         return out
+
+    def first_conv_device(self, device, d_in, n, H, W, d_bits, exact=False, stream=None):
+        """First conv + real fold alone on device memory; returns the number
+        of outputs the production path sent to the exact fix-up."""
+        und = ctypes.c_uint()
+        _check(lib().bnn_first_conv_device(self.handle, device, _ptr(d_in), n, H, W, _ptr(d_bits),
+                                           1 if exact else 0, ctypes.byref(und),
+                                           stream if stream is None or isinstance(stream, int)
+                                           else stream.cuda_stream))
+        return und.value
 
     def set_devices(self, devices):
         arr = (ctypes.c_int * max(1, len(devices)))(*devices)

@@ -11,6 +11,7 @@
 // The forward order is the reference's (csrc/bnn_model.c:150-253): 19
 // kernel launches (first conv, 17 fused binary convs, head).
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -69,6 +70,9 @@ struct Arena {
     void* base = nullptr;
     size_t bytes = 0;
     uint32_t *enc_h[4], *skip[4], *down[4], *bott_h, *bott_x, *dec_h[4], *dec_x[4];
+    uint32_t* rm_list;        // first conv: undecided (pixel, channel) pairs
+    unsigned int* rm_ctl;     // [entries, overflow]
+    int rm_cap;
 };
 
 struct GraphKey {
@@ -87,6 +91,8 @@ struct DevState {
     float* ri_wf = nullptr;
     float* ri_fold = nullptr;
     int ri_CinP = 0, ri_CIP = 0;
+    uint4* rm_wfrag = nullptr;  // first conv +-1 int8 weights in mma B-fragment order
+    int* rm_exact = nullptr;    // per channel: fold not monotone -> exact path
     BinLayer enc1[4], enc2[4], bott1, bott2, dec1[4], dec2[4];
     float *head_W = nullptr, *head_b = nullptr;
     Arena ar;
@@ -224,7 +230,9 @@ static int set_kernel_attrs(int device) {
     if ((e = attr_bconv_kc<32, 4, 4>()) != cudaSuccess || (e = attr_bconv_kc<64, 8, 4>()) != cudaSuccess ||
         (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  RI_HP * 260 * 4)) != cudaSuccess)
+                                  RI_HP * 260 * 4)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
+            cudaSuccess)
         return set_error(BNN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     if (device >= 0 && device < 64) done[device] = true;
     return BNN_OK;
@@ -253,6 +261,37 @@ static int dev_init(const Model* m, DevState* d) {
         rfold[co * 5 + 3] = a1->slope[co];
         rfold[co * 5 + 4] = a1->rsign[co];
     }
+    // the same weights as int8 mma B fragments (realin_mma_kernel): for
+    // channel group g, tap t, k-step kk, lane l = 4*gid + tig, n-tile nt:
+    // b0 = bands kk*32 + tig*4 + 0..3 and b1 = bands kk*32 + 16 + tig*4 + 0..3
+    // of channel g*32 + nt*8 + gid
+    const int ngrp = cdiv(CoutR, 32);
+    std::vector<uint32_t> wfrag((size_t)ngrp * 9 * 4 * 32 * 8, 0u);
+    std::vector<int> rexact((size_t)CoutRP, 0);
+    if (Cin <= RM_CINP) {
+        for (int g = 0; g < ngrp; ++g)
+            for (int t = 0; t < 9; ++t)
+                for (int kk = 0; kk < 4; ++kk)
+                    for (int l = 0; l < 32; ++l)
+                        for (int nt = 0; nt < 4; ++nt)
+                            for (int h = 0; h < 2; ++h) {
+                                const int co = g * 32 + nt * 8 + (l >> 2);
+                                uint32_t word = 0;
+                                for (int i = 0; i < 4; ++i) {
+                                    const int ci = kk * 32 + h * 16 + (l & 3) * 4 + i;
+                                    int v = 0;
+                                    if (co < CoutR && ci < Cin) v = c1->wsign[((size_t)co * Cin + ci) * 9 + t] > 0 ? 1 : -1;
+                                    word |= (uint32_t)(uint8_t)(int8_t)v << (8 * i);
+                                }
+                                wfrag[((((size_t)g * 9 + t) * 4 + kk) * 32 + l) * 8 + nt * 2 + h] = word;
+                            }
+    }
+    for (int co = 0; co < CoutR; ++co) {
+        const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
+        bool ok = v[3] >= 0.0f;
+        for (float f : v) ok = ok && std::isfinite(f);
+        rexact[co] = ok ? 0 : 1;
+    }
     // binary convs
     struct Item {
         BinLayer* L;
@@ -274,7 +313,8 @@ static int dev_init(const Model* m, DevState* d) {
         items.push_back({&d->dec1[i], &m->dec_conv1[i], &m->dec_act1[i], nullptr, tp.enc[3 - i], {}});
         items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
     }
-    size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4);
+    size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
+                   align256(rexact.size() * 4);
     for (auto& it : items) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
         folds_of(it.a, it.L->CoutP, it.h.fold);
@@ -299,6 +339,8 @@ static int dev_init(const Model* m, DevState* d) {
     };
     d->ri_wf = (float*)put(wf.data(), wf.size() * 4);
     d->ri_fold = (float*)put(rfold.data(), rfold.size() * 4);
+    d->rm_wfrag = (uint4*)put(wfrag.data(), wfrag.size() * 4);
+    d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
@@ -383,6 +425,14 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
         add(&a.dec_h[i], H >> l, W >> l, m->dec_conv1[i].Cout);
         add(&a.dec_x[i], H >> l, W >> l, tp.dec[i]);
     }
+    // undecided-output list of the first conv: sized for ~1 in 64 outputs, at
+    // least 64 K entries; beyond it the fix-up recomputes the whole batch
+    const size_t outs = (size_t)Nn * H * W * m->enc_conv1[0].Cout;
+    const int cap = (int)std::min<size_t>(std::max<size_t>(outs / 64, 65536), (size_t)1 << 24);
+    const size_t list_off = off;
+    off += align256((size_t)cap * 8);
+    const size_t ctl_off = off;
+    off += 256;
     // graphs bake in arena pointers
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
     d->graphs.clear();
@@ -402,6 +452,9 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
     a.bytes = off;
     a.N = Nn; a.H = H; a.W = W;
     for (auto& pr : plan) *pr.first = (uint32_t*)((char*)base + pr.second);
+    a.rm_list = (uint32_t*)((char*)base + list_off);
+    a.rm_ctl = (unsigned int*)((char*)base + ctl_off);
+    a.rm_cap = cap;
     return BNN_OK;
 }
 
@@ -484,8 +537,8 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     return launch_bconv(p, N, st);
 }
 
-static int run_realin(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out, float* dbg,
-                      cudaStream_t st) {
+static int run_realin_exact(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
+                            float* dbg, cudaStream_t st) {
     if (N <= 0) return BNN_OK;
     RealinParams p{};
     p.x = x; p.wf = d->ri_wf; p.fold = d->ri_fold; p.out = out; p.dbg = dbg;
@@ -499,6 +552,90 @@ static int run_realin(DevState* d, const Model* m, const float* x, int N, int H,
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin launch: %s", cudaGetErrorString(e));
     return BNN_OK;
+}
+
+// e2 / T of realin_mma_kernel for a full window (the largest taps count):
+// g(Cin-1) + g(8) * (1 + g(Cin-1)), g(n) = n u / (1 - n u), u = 2^-24,
+// padded by 2^-30 relative and rounded up to float
+static float first_conv_c9(int Cin) {
+    const double u = std::ldexp(1.0, -24);
+    auto g = [&](int n) { return n * u / (1.0 - n * u); };
+    const double c = (g(Cin - 1) + g(8) * (1.0 + g(Cin - 1))) * (1.0 + std::ldexp(1.0, -30));
+    float f = (float)c;
+    if ((double)f < c) f = std::nextafter(f, 1.0f);
+    return f;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on libcuda)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)f;
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// input [N][C][H][W] f32 as a 4-D TMA map with the (40, 6, 8, 1) box
+static bool first_conv_tmap(const float* x, int N, int C, int H, int W, CUtensorMap* tm) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || (W % 4) != 0 || ((uintptr_t)x & 15)) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)C, (cuuint64_t)N};
+    const cuuint64_t strides[3] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4, (cuuint64_t)C * H * W * 4};
+    const cuuint32_t box[4] = {RM_BX, RM_BY, RM_BC, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool first_conv_fast_ok(const Model* m, int N, int H, int W) {
+    return m->enc_conv1[0].Cin <= RM_CINP && (W % 4) == 0 && (size_t)N * H * W < ((size_t)1 << 31) &&
+           encode_tiled() != nullptr;
+}
+
+// first conv -> bit plane: int8 tensor cores decided by the error bound, then
+// the exact fix-up of undecided outputs (a memset and 2 kernels)
+static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
+                           cudaStream_t st) {
+    if (N <= 0) return BNN_OK;
+    Arena& a = d->ar;
+    CUtensorMap tm;
+    if (!first_conv_tmap(x, N, m->enc_conv1[0].Cin, H, W, &tm))
+        return run_realin_exact(d, m, x, N, H, W, out, nullptr, st);
+    CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
+    RealinMmaParams p{};
+    p.wfrag = d->rm_wfrag; p.fold = d->ri_fold; p.exact_ch = d->rm_exact; p.out = out;
+    p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
+    p.N = N; p.Cin = m->enc_conv1[0].Cin; p.H = H; p.W = W; p.Cout = m->enc_conv1[0].Cout; p.cwo = cw_of(p.Cout);
+    p.tiles_x = cdiv(W, RM_TC); p.tiles_y = cdiv(H, RM_TR);
+    p.c9 = first_conv_c9(p.Cin);
+    dim3 grid((unsigned)((size_t)N * p.tiles_x * p.tiles_y), (unsigned)cdiv(p.Cout, 32));
+    realin_mma_kernel<<<grid, 128, RM_SMEM, st>>>(tm, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin mma launch: %s", cudaGetErrorString(e));
+    RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, p.Cin, d->ri_CinP, H, W,
+                      p.Cout, p.cwo};
+    realin_fixup_kernel<<<148 * 4, 128, 0, st>>>(f);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+static int run_first_conv(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
+                          cudaStream_t st) {
+    if (first_conv_fast_ok(m, N, H, W)) return run_realin_fast(d, m, x, N, H, W, out, st);
+    return run_realin_exact(d, m, x, N, H, W, out, nullptr, st);
 }
 
 static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int H, int W, float* out,
@@ -518,6 +655,7 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
 // -------------------------------------------------------------------
 struct Dbg {  // optional debug outputs of one forward (device pointers)
     float* realin = nullptr;
+    uint32_t* realin_bits = nullptr;  // scratch for the exact kernel that produces `realin`
     int32_t* P[17] = {nullptr};
     int32_t* Pd[4] = {nullptr};
 };
@@ -564,7 +702,11 @@ static int forward_launches(const Model* m, DevState* d, const float* x, int N, 
     auto work = [&](const BinLayer& L, int h, int w) { return (double)N * h * w * L.Cout * (double)L.Cin * 9.0; };
     int li = 0;
     if (pc) pc->begin("enc1.conv1+act1", "conv_real", NHW * m->enc_conv1[0].Cout * m->enc_conv1[0].Cin * 9.0);
-    rc = run_realin(d, m, x, N, H, W, a.enc_h[0], dbg ? dbg->realin : nullptr, st);
+    // the stage dump's float output of the first conv comes from the exact
+    // kernel; the bit plane used downstream is always the production path's
+    if (dbg && dbg->realin) rc = run_realin_exact(d, m, x, N, H, W, dbg->realin_bits, dbg->realin, st);
+    else rc = BNN_OK;
+    if (!rc) rc = run_first_conv(d, m, x, N, H, W, a.enc_h[0], st);
     if (pc) pc->end();
     if (rc) return rc;
     for (int i = 0; i < 4; ++i) {
@@ -846,7 +988,44 @@ BNN_API int bnn_set_chunk(Model* m, int patches) {
 
 BNN_API int bnn_forward_launches(const Model* m, int N, int H, int W) {
     if (!m || N <= 0 || H < 16 || W < 16) return 0;
-    return 19;
+    return first_conv_fast_ok(m, N, H, W) ? 20 : 19;  // + the first conv's fix-up kernel
+}
+
+BNN_API int bnn_first_conv_device(const Model* m, int device, const float* d_input, int N, int H, int W,
+                                  uint32_t* d_bits, int exact, unsigned int* undecided, void* stream) {
+    if (!m || !d_input || !d_bits) return set_error(BNN_ERR_ARG, "NULL argument");
+    int rc = check_hw(N, H, W);
+    if (rc) return rc;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_ARG, "cannot select device %d", device);
+    }
+    DevState* d = nullptr;
+    rc = get_dev(m, device, &d);
+    if (!rc) {
+        std::lock_guard<std::mutex> g(d->mu);
+        cudaStream_t st = (cudaStream_t)stream;
+        rc = arena_reserve(m, d, N, H, W);
+        if (!rc) {
+            cudaStreamWaitEvent(st, d->ev_last, 0);
+            const bool fast = !exact && first_conv_fast_ok(m, N, H, W);
+            rc = fast ? run_realin_fast(d, m, d_input, N, H, W, d_bits, st)
+                      : run_realin_exact(d, m, d_input, N, H, W, d_bits, nullptr, st);
+            if (!rc) cudaEventRecord(d->ev_last, st);
+            if (!rc && undecided) {
+                unsigned int ctl[2] = {0, 0};
+                if (fast && cudaMemcpyAsync(ctl, d->ar.rm_ctl, sizeof ctl, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    rc = set_error(BNN_ERR_CUDA, "D2H ctl");
+                if (!rc && cudaStreamSynchronize(st) != cudaSuccess)
+                    rc = set_error(BNN_ERR_CUDA, "first conv: %s", cudaGetErrorString(cudaGetLastError()));
+                *undecided = ctl[1] ? 0xffffffffu : ctl[0];
+            }
+        }
+    }
+    cudaSetDevice(prev);
+    return rc;
 }
 
 // ---------------- profiler ----------------
@@ -947,8 +1126,9 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     for (int k = 0; k < 17; ++k) { poff[k] = words; words += (size_t)lg[k].C * lg[k].h * lg[k].w + 1; }
     for (int i = 0; i < 4; ++i) { pdoff[i] = words; words += (size_t)tp.enc[i] * (H >> (i + 1)) * (W >> (i + 1)) + 1; }
     const size_t ri_words = (size_t)m->enc_conv1[0].Cout * H * W;
+    const size_t rb_words = (size_t)H * W * cw_of(m->enc_conv1[0].Cout);
     void* buf = nullptr;
-    if (cudaMalloc(&buf, (words + ri_words + ip + op) * 4) != cudaSuccess) {
+    if (cudaMalloc(&buf, (words + ri_words + ip + op + rb_words) * 4) != cudaSuccess) {
         cudaGetLastError();
         return set_error(BNN_ERR_OOM, "cudaMalloc stage buffers");
     }
@@ -958,6 +1138,7 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     float* dout = din + ip;
     Dbg dbg;
     dbg.realin = dri;
+    dbg.realin_bits = (uint32_t*)(dout + op);
     for (int k = 0; k < 17; ++k) dbg.P[k] = P + poff[k];
     for (int i = 0; i < 4; ++i) dbg.Pd[i] = P + pdoff[i];
     rc = BNN_OK;
@@ -1252,7 +1433,7 @@ BNN_API int bnn_gpu_conv_realin(const float* x, const int8_t* wsign, const float
         cudaMemcpy(d.ri_fold, fold.data(), fold.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dx, x, nx * 4, cudaMemcpyHostToDevice) != cudaSuccess)
         rc = set_error(BNN_ERR_CUDA, "H2D");
-    if (!rc) rc = run_realin(&d, &mm, dx, 1, H, W, dbits, dout, nullptr);
+    if (!rc) rc = run_realin_exact(&d, &mm, dx, 1, H, W, dbits, dout, nullptr);
     if (!rc && cudaDeviceSynchronize() != cudaSuccess)
         rc = set_error(BNN_ERR_CUDA, "realin: %s", cudaGetErrorString(cudaGetLastError()));
     if (!rc && cudaMemcpy(out, dout, no * 4, cudaMemcpyDeviceToHost) != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "D2H");

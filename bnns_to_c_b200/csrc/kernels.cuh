@@ -16,6 +16,7 @@
 // popc(weight bits of that tap), which the epilogue subtracts again.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/bnn_synth.h"
@@ -406,6 +407,366 @@ __global__ void __launch_bounds__(128) realin3x3_fold_kernel(const RealinParams 
     {
         const int j = tid >> 5, y = y0 + j, x = x0 + lane;
         if (y < p.H && x < p.W) p.out[(((size_t)n * p.H + y) * p.W + x) * p.cwo + blockIdx.y] = words[tid];
+    }
+}
+
+// ---------------------------------------------------------------------
+// First conv on int8 tensor cores, decided by an error bound.
+//
+// Only sign(r) of the first conv's folded output is kept, so the fp32 sum
+// need not be recomputed in the reference's order if its sign is certain:
+//  1. Inputs become fixed point q = clamp(rint(x * 2^18), +-2^22), split
+//     into three int8 planes q = d2*2^16 + d1*2^8 + d0 (d2 signed, d1 and
+//     d0 unsigned). The exact per-element error |x - q*2^-18| (at most
+//     2^-19, or the clamped excess) is bounded from above and kept.
+//  2. mma.sync m16n8k32 with +-1 int8 weights gives the three plane sums
+//     exactly (int32); Q = S2*2^16 + S1*2^8 + S0 is exact in double, and
+//     |ACC - Q*2^-18| <= e1 = sum over the window of the element errors,
+//     ACC being the exact conv value.
+//  3. The reference's fp32 accumulator (sequential over bands per tap, then
+//     over taps, csrc/bnn_conv_realin.c:99-109) is within
+//     e2 = (g(Cin-1) + g(taps-1)*(1 + g(Cin-1))) * T of ACC, where
+//     g(n) = n*2^-24 / (1 - n*2^-24) (Higham's recursive-summation bound) and
+//     T = sum of |x| over the window; the 9-tap coefficient is used for
+//     every pixel (the largest, so border pixels are bounded too).
+//  4. The fold (alpha*, fma with A and B, slope on the negative side,
+//     +rsign, > 0) is monotone in the accumulator when slope >= 0 and all
+//     parameters are finite, so if it gives the same bit at both ends of
+//     [Q*2^-18 - e, Q*2^-18 + e] (rounded outward to float), that is the
+//     reference's bit. Otherwise (or if e is not finite: inf / NaN inputs)
+//     the output is listed for realin_fixup_kernel, which recomputes it in
+//     the reference's exact fp32 order.
+// Input staging: TMA bulk tensor loads of 8 bands x 6 rows x 40 columns
+// (starting 4 columns left of the tile so the copy is 16-byte aligned),
+// zero-filled outside the image, double-buffered against the quantisation.
+// Every mbarrier wait is bounded; a wait that gives up raises ctl[1] and the
+// fix-up then recomputes the whole batch exactly.
+// Tile: 4 rows x 32 columns x 32 output channels, 4 warps (one image row
+// each: two 16-pixel m-tiles x four 8-channel n-tiles x three planes).
+// ---------------------------------------------------------------------
+constexpr int RM_TR = 4, RM_TC = 32, RM_HC = RM_TC + 2, RM_HP = (RM_TR + 2) * RM_HC;
+constexpr int RM_CINP = 128, RM_PITCH = RM_CINP + 16;   // plane bytes per halo pixel
+constexpr int RM_BX = 40, RM_BY = RM_TR + 2, RM_BC = 8;  // TMA box (cols, rows, bands)
+constexpr int RM_BOX_BYTES = RM_BX * RM_BY * RM_BC * 4;
+constexpr int RM_FIX = 18;                              // fixed-point fraction bits
+constexpr size_t RM_SMEM = (size_t)3 * RM_HP * RM_PITCH + RM_HP * 4 + 2 * RM_BOX_BYTES + 128;
+
+struct RealinMmaParams {
+    const uint4* wfrag;        // [Cout/32][9 taps][4 k-steps][32 lanes][2]: mma B fragments, +-1 int8
+    const float* fold;         // [CoutP][5]: alpha, A, B, slope, rsign
+    const int* exact_ch;       // [CoutP]: 1 = fold not monotone, always take the exact path
+    uint32_t* out;             // [N][H][W][cwo]
+    uint32_t* list;            // undecided outputs: (pixel index, channel) pairs
+    unsigned int* ctl;         // [0] = entries, [1] = overflow / staging failure
+    int cap;                   // list capacity (entries)
+    int N, Cin, H, W, Cout, cwo, tiles_x, tiles_y;
+    float c9;                  // e2 / T for a full 3x3 window, rounded up
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_s8s8(int* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_u8s8(int* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// bounded wait on an mbarrier phase; false if it did not complete in time
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (int it = 0; it < (1 << 22); ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];\n" ::"r"(dst),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
+// the reference's real fold (csrc/bnn_fold.c:62-77) on one accumulator value
+__device__ __forceinline__ int real_fold_bit(float acc, const float* f) {
+    const float o = __fmul_rn(__ldg(f), acc);
+    float z = __fmaf_rn(__ldg(f + 1), o, __ldg(f + 2));
+    if (z < 0.0f) z = __fmul_rn(__ldg(f + 3), z);
+    return __fadd_rn(z, __ldg(f + 4)) > 0.0f;
+}
+
+// quantise one value; accumulate its error + c9*|x| (rounded up) into bnd
+__device__ __forceinline__ uint32_t rm_quant(float x, float c9, float& bnd) {
+    int q = __float2int_rn(__fmul_rn(x, (float)(1 << RM_FIX)));
+    q = max(-(1 << 22), min(1 << 22, q));
+    const float qf = __fmul_rn((float)q, 1.0f / (float)(1 << RM_FIX));
+    const float err = fmaxf(fabsf(__fsub_ru(x, qf)), fabsf(__fsub_rd(x, qf)));
+    bnd = __fadd_ru(bnd, __fmaf_ru(c9, fabsf(x), err));
+    return (uint32_t)q;
+}
+
+__global__ void __launch_bounds__(128, 2) realin_mma_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                             const RealinMmaParams p) {
+    extern __shared__ __align__(128) unsigned char rm_smem[];
+    unsigned char* box = rm_smem;                                       // [2][RM_BC][RM_BY][RM_BX] f32
+    unsigned char* planes = rm_smem + 2 * RM_BOX_BYTES;                 // [3][RM_HP][RM_PITCH]
+    float* bpx = reinterpret_cast<float*>(planes + 3 * RM_HP * RM_PITCH);  // [RM_HP] error bound per pixel
+    __shared__ __align__(8) unsigned long long bars[2];
+    __shared__ int staged_ok;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = p.tiles_x * p.tiles_y;
+    const int n = blockIdx.x / per, r0 = blockIdx.x - n * per;
+    const int y0 = (r0 / p.tiles_x) * RM_TR, x0 = (r0 % p.tiles_x) * RM_TC;
+    const int nch = (p.Cin + RM_BC - 1) / RM_BC;
+    const uint32_t bar0 = smem_u32(&bars[0]), bar1 = smem_u32(&bars[1]);
+
+    if (tid == 0) {
+        staged_ok = 1;
+        mbar_init(bar0, 1);
+        mbar_init(bar1, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    // bands nch*8 .. 127 of every plane stay zero
+    for (int e = tid; e < 3 * RM_HP; e += 128) {
+        uint32_t* row = reinterpret_cast<uint32_t*>(planes + e * RM_PITCH);
+        for (int w = nch * RM_BC / 4; w < RM_CINP / 4; ++w) row[w] = 0u;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int k = 0; k < 2 && k < nch; ++k) {
+            const uint32_t bar = k ? bar1 : bar0;
+            mbar_expect_tx(bar, RM_BOX_BYTES);
+            tma_load_4d(smem_u32(box + k * RM_BOX_BYTES), &tmap, x0 - 4, y0 - 1, k * RM_BC, n, bar);
+        }
+    }
+
+    // ---- quantise 8 bands at a time into the byte planes; thread owns halo
+    //      pixels tid and tid + 128
+    float bnd[2] = {0.0f, 0.0f};
+    for (int k = 0; k < nch; ++k) {
+        const int b = k & 1;
+        if (!mbar_wait(b ? bar1 : bar0, (k >> 1) & 1)) staged_ok = 0;
+        const float* bx = reinterpret_cast<const float*>(box + b * RM_BOX_BYTES);
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const int hp = tid + 128 * s;
+            if (hp < RM_HP) {
+                const int r = hp / RM_HC, c = hp - r * RM_HC;
+                uint32_t q[RM_BC];
+#pragma unroll
+                for (int i = 0; i < RM_BC; ++i) q[i] = rm_quant(bx[(i * RM_BY + r) * RM_BX + c + 3], p.c9, bnd[s]);
+                uint32_t w2[2], w1[2], w0[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    w2[h] = w1[h] = w0[h] = 0u;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t v = q[h * 4 + i];
+                        w2[h] |= ((v >> 16) & 255u) << (8 * i);
+                        w1[h] |= ((v >> 8) & 255u) << (8 * i);
+                        w0[h] |= (v & 255u) << (8 * i);
+                    }
+                }
+                unsigned char* dst = planes + hp * RM_PITCH + k * RM_BC;
+                *reinterpret_cast<uint2*>(dst) = make_uint2(w2[0], w2[1]);
+                *reinterpret_cast<uint2*>(dst + RM_HP * RM_PITCH) = make_uint2(w1[0], w1[1]);
+                *reinterpret_cast<uint2*>(dst + 2 * RM_HP * RM_PITCH) = make_uint2(w0[0], w0[1]);
+            }
+        }
+        __syncthreads();  // box b is free again
+        if (tid == 0 && k + 2 < nch) {
+            const uint32_t bar = b ? bar1 : bar0;
+            mbar_expect_tx(bar, RM_BOX_BYTES);
+            tma_load_4d(smem_u32(box + b * RM_BOX_BYTES), &tmap, x0 - 4, y0 - 1, (k + 2) * RM_BC, n, bar);
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+        if (tid + 128 * s < RM_HP) bpx[tid + 128 * s] = bnd[s];
+    __syncthreads();
+    if (!staged_ok && tid == 0) atomicExch(p.ctl + 1, 1u);  // fix-up redoes the batch exactly
+
+    // ---- int8 MMAs: warp = tile row, 2 m-tiles x 4 n-tiles x 3 planes
+    int acc[3][2][4][4];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) acc[k][mt][nt][v] = 0;
+    const int g = blockIdx.y;
+    const uint4* wf = p.wfrag + (size_t)g * 9 * 4 * 32 * 2;
+    const uint32_t sbase = smem_u32(planes);
+    const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lcol = (lane >> 4) * 16;
+    const int ksteps = (nch * RM_BC + 31) / 32;
+#pragma unroll 1
+    for (int t = 0; t < 9; ++t) {
+        const int dy = t / 3, dx = t % 3;
+#pragma unroll 1
+        for (int kk = 0; kk < ksteps; ++kk) {
+            const uint4 bq0 = __ldg(wf + ((t * 4 + kk) * 32 + lane) * 2);
+            const uint4 bq1 = __ldg(wf + ((t * 4 + kk) * 32 + lane) * 2 + 1);
+            const uint32_t bb[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const int hp = (warp + dy) * RM_HC + mt * 16 + lrow + dx;
+                const uint32_t addr = sbase + hp * RM_PITCH + kk * 32 + lcol;
+                uint32_t a2[4], a1[4], a0[4];
+                ldsm_x4(addr, a2);
+                ldsm_x4(addr + RM_HP * RM_PITCH, a1);
+                ldsm_x4(addr + 2 * RM_HP * RM_PITCH, a0);
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    mma_s8s8(acc[0][mt][nt], a2, bb[2 * nt], bb[2 * nt + 1]);
+                    mma_u8s8(acc[1][mt][nt], a1, bb[2 * nt], bb[2 * nt + 1]);
+                    mma_u8s8(acc[2][mt][nt], a0, bb[2 * nt], bb[2 * nt + 1]);
+                }
+            }
+        }
+    }
+
+    // ---- decide each output's bit from the interval, or list it
+    const int gid = lane >> 2, tig = lane & 3;
+    const int y = y0 + warp;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int col = mt * 16 + gid + half * 8;
+            const int x = x0 + col;
+            const bool valid = y < p.H && x < p.W;
+            uint32_t bits = 0u;
+            if (valid) {
+                float ef = 0.0f;
+#pragma unroll
+                for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bpx[(warp + t / 3) * RM_HC + col + t % 3]);
+                const bool finite = ef <= 3.0e38f;  // false for inf and NaN
+                const double e = (double)ef;
+                const size_t pix = ((size_t)n * p.H + y) * p.W + x;
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int v = half * 2 + j;
+                        const int cl = nt * 8 + tig * 2 + j, co = g * 32 + cl;
+                        if (co >= p.Cout) continue;
+                        const double q = (double)acc[0][mt][nt][v] * 65536.0 + (double)acc[1][mt][nt][v] * 256.0 +
+                                         (double)acc[2][mt][nt][v];
+                        const double a = q * (1.0 / (double)(1 << RM_FIX));
+                        const float lo = __double2float_rd(__dsub_rd(a, e)), hi = __double2float_ru(__dadd_ru(a, e));
+                        const float* f = p.fold + (size_t)co * 5;
+                        const int blo = real_fold_bit(lo, f), bhi = real_fold_bit(hi, f);
+                        if (finite && blo == bhi && !__ldg(p.exact_ch + co)) {
+                            bits |= (uint32_t)blo << cl;
+                        } else {
+                            const unsigned int slot = atomicAdd(p.ctl, 1u);
+                            if (slot < (unsigned)p.cap) {
+                                p.list[2 * (size_t)slot] = (uint32_t)pix;
+                                p.list[2 * (size_t)slot + 1] = (uint32_t)co;
+                            } else {
+                                atomicExch(p.ctl + 1, 1u);
+                            }
+                        }
+                    }
+                }
+            }
+            bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+            bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+            if (valid && tig == 0) p.out[(((size_t)n * p.H + y) * p.W + x) * p.cwo + g] = bits;
+        }
+    }
+}
+
+// exact first-conv accumulator of one output, in the reference's order
+__device__ float realin_exact_acc(const float* x, const float* wf, int Cin, int CinP, int H, int W, int n, int co,
+                                  int y, int xx) {
+    const size_t plane = (size_t)H * W;
+    const float* xn = x + (size_t)n * Cin * plane;
+    float acc = 0.0f;
+    for (int t = 0; t < 9; ++t) {
+        const int iy = y + t / 3 - 1, ix = xx + t % 3 - 1;
+        if ((unsigned)iy >= (unsigned)H || (unsigned)ix >= (unsigned)W) continue;
+        const float* src = xn + (size_t)iy * W + ix;
+        const float* w = wf + ((size_t)co * 9 + t) * CinP;
+        float s = 0.0f;
+        for (int ci = 0; ci < Cin; ++ci) s = __fmaf_rn(__ldg(src + ci * plane), __ldg(w + ci), s);
+        acc = __fadd_rn(acc, s);
+    }
+    return acc;
+}
+
+// Undecided outputs of realin_mma_kernel, recomputed exactly. If the list
+// overflowed, every output of the batch is recomputed (correct, slow).
+struct RealinFixParams {
+    const float* x;
+    const float* wf;     // [CoutP][9][CinP] +-1.0f
+    const float* fold;   // [CoutP][5]
+    uint32_t* out;
+    const uint32_t* list;
+    const unsigned int* ctl;
+    int cap, N, Cin, CinP, H, W, Cout, cwo;
+};
+
+__global__ void realin_fixup_kernel(const RealinFixParams p) {
+    const unsigned int cnt = min(p.ctl[0], (unsigned)p.cap);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t g0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p.ctl[1] == 0u) {
+        for (size_t i = g0; i < cnt; i += stride) {
+            const uint32_t pix = p.list[2 * i], co = p.list[2 * i + 1];
+            const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
+            const float acc = realin_exact_acc(p.x, p.wf, p.Cin, p.CinP, p.H, p.W, n, (int)co, y, xx);
+            if (real_fold_bit(acc, p.fold + (size_t)co * 5))
+                atomicOr(p.out + (size_t)pix * p.cwo + (co >> 5), 1u << (co & 31));
+        }
+    } else {
+        const size_t words = (size_t)p.N * p.H * p.W * p.cwo;
+        for (size_t i = g0; i < words; i += stride) {
+            const size_t pix = i / p.cwo;
+            const int wd = (int)(i - pix * p.cwo);
+            const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
+            uint32_t bits = 0u;
+            for (int b = 0; b < 32; ++b) {
+                const int co = wd * 32 + b;
+                if (co >= p.Cout) break;
+                const float acc = realin_exact_acc(p.x, p.wf, p.Cin, p.CinP, p.H, p.W, n, co, y, xx);
+                bits |= (uint32_t)real_fold_bit(acc, p.fold + (size_t)co * 5) << b;
+            }
+            p.out[i] = bits;
+        }
     }
 }
 

@@ -158,6 +158,19 @@ int bnn_pack_act_device(const int8_t *d_a, int N, int C, int H, int W,
 int bnn_unpack_act_device(const uint32_t *d_bits, int N, int C, int H, int W,
                           int8_t *d_a, void *stream);
 
+/* The first conv + real fold alone (enc1.conv1 -> enc1.act1 bit plane,
+ * reference csrc/bnn_model.c:156-167) on device memory: d_input [N][bands]
+ * [H][W] float32 -> d_bits [N][H][W][ceil(C/32)]. exact = 0 runs the
+ * production path (int8 tensor cores decided by an error bound, undecided
+ * outputs recomputed in the reference's fp32 order); exact = 1 runs the
+ * all-fp32 exact-order kernel. Both give the reference's bits. If
+ * `undecided` is not NULL the call synchronises and stores how many outputs
+ * the production path sent to the exact fix-up (0xffffffff: the list
+ * overflowed and the whole batch was recomputed exactly). */
+int bnn_first_conv_device(const Model *m, int device, const float *d_input,
+                          int N, int H, int W, uint32_t *d_bits, int exact,
+                          unsigned int *undecided, void *stream);
+
 /* Number of this library's kernel launches one forward of (N, H, W)
  * issues (for launch accounting in benchmarks). */
 int bnn_forward_launches(const Model *m, int N, int H, int W);

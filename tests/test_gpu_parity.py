@@ -190,7 +190,8 @@ def test_profiler_records_every_launch():
     m.profile(True)
     m.forward_batch(synth(5, 0, 4, 120, 32, 32))
     recs = m.profile_records()
-    assert len(recs) == m.launches(4, 32, 32) == 19
+    # 19 profiled ops; the first conv's op is two kernels (tensor-core pass + exact fix-up)
+    assert len(recs) == 19 and m.launches(4, 32, 32) == 20
     assert sum(r["op"] == "bconv" for r in recs) == 17
     assert all(r["ms"] > 0 and r["calls"] == 1 for r in recs)
 
@@ -233,3 +234,96 @@ def test_multi_device_shards_match_single():
     ref = m.forward_batch(x)
     m.set_devices(list(range(torch.cuda.device_count())))
     assert same_bits(m.forward_batch(x), ref)
+
+
+# ------------------------------------------------------------------ first conv: tensor-core path
+def _first_conv_bits(m, x, exact):
+    n, _, H, W = x.shape
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    cw = (m.enc_c1_cout + 31) // 32
+    bits = torch.zeros((n, H, W, cw), dtype=torch.int32, device="cuda")
+    und = m.first_conv_device(0, dx, n, H, W, bits, exact=exact)
+    torch.cuda.synchronize()
+    return bits.cpu().numpy(), und
+
+
+def _model(base=32, seed=0, mutate=None):
+    mdl = B.random_model(base, 120, 3, seed=seed, rules="baseline")
+    if mutate:
+        mutate(mdl)
+    m = bn.Model(data=B.blob_bytes(mdl))
+    m.enc_c1_cout = mdl["enc1.conv1"]["wsign"].shape[0]
+    return m
+
+
+def test_first_conv_tensor_path_matches_exact_order():
+    m = _model()
+    x = synth(41, 0, 256, 120, 32, 32)
+    fast, und = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
+    outs = 256 * 32 * 32 * 32
+    assert 0 <= und < outs // 500, und  # the error bound decides > 99.8% of the outputs
+
+
+def test_first_conv_fixup_exercised_near_threshold():
+    """Folds tuned so r sits near 0 for many outputs: many undecided,
+    all resolved exactly."""
+    x = synth(42, 0, 16, 120, 32, 32)
+
+    def near_zero(mdl):
+        a = mdl["enc1.act1"]
+        a["A"][:] = 1.0
+        a["B"][:] = 0.0
+        a["rsign"][:] = 0.0  # r = alpha*acc (or slope*alpha*acc): decided by sign(acc) alone
+    m = _model(mutate=near_zero)
+    # inputs whose window sums cancel: each band repeated with its sign flipped
+    x[:, 60:] = -x[:, :60]
+    fast, und = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
+    assert und > 0
+
+
+def test_first_conv_nonmonotone_channels_and_overflow():
+    def neg_slope(mdl):
+        mdl["enc1.act1"]["slope"][::2] = -0.2  # half the channels: V-shaped fold
+    m = _model(mutate=neg_slope)
+    x = synth(43, 0, 8, 120, 32, 32)
+    fast, und = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact) and und >= 8 * 1024 * 16
+    # every channel non-monotone and a big batch: the list overflows, the
+    # fix-up recomputes the whole batch
+    def all_neg(mdl):
+        mdl["enc1.act1"]["slope"][:] = -0.2
+    m2 = _model(mutate=all_neg)
+    x2 = synth(44, 0, 96, 120, 32, 32)
+    fast, und = _first_conv_bits(m2, x2, False)
+    exact, _ = _first_conv_bits(m2, x2, True)
+    assert und == 0xFFFFFFFF and np.array_equal(fast, exact)
+
+
+def test_first_conv_nonfinite_and_extreme_inputs():
+    m = _model()
+    x = synth(45, 0, 6, 120, 32, 32)
+    x[0, 5, 3, 7] = np.nan
+    x[1, 100, 31, 31] = np.inf
+    x[2] *= 1e30           # huge values
+    x[3] *= 1e-38          # subnormal range
+    x[4, :, :16] = 0.0     # exact zeros
+    x[5, ::2] *= 1e6       # mixed dynamic range
+    fast, _ = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
+    om_bits = None  # the exact kernel itself is pinned to the oracle by test_realin_bit_exact
+    del om_bits
+
+
+@pytest.mark.parametrize("H,W", [(17, 40), (33, 33), (64, 16)])
+def test_first_conv_tensor_path_odd_sizes(H, W):
+    m = _model(base=16, seed=3)
+    x = synth(46, 0, 3, 120, H, W)
+    fast, _ = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
