@@ -621,7 +621,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     p.tiles_x = cdiv(W, RM_TC); p.tiles_y = cdiv(H, RM_TR);
     p.c9 = first_conv_c9(p.Cin);
     dim3 grid((unsigned)((size_t)N * p.tiles_x * p.tiles_y), (unsigned)cdiv(p.Cout, 32));
-    realin_mma_kernel<<<grid, 128, RM_SMEM, st>>>(tm, p);
+    realin_mma_kernel<<<grid, 256, RM_SMEM, st>>>(tm, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin mma launch: %s", cudaGetErrorString(e));
     RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, p.Cin, d->ri_CinP, H, W,

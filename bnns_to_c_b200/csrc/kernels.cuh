@@ -415,14 +415,15 @@ __global__ void __launch_bounds__(128) realin3x3_fold_kernel(const RealinParams 
 //
 // Only sign(r) of the first conv's folded output is kept, so the fp32 sum
 // need not be recomputed in the reference's order if its sign is certain:
-//  1. Inputs become fixed point q = clamp(rint(x * 2^18), +-2^22), split
-//     into three int8 planes q = d2*2^16 + d1*2^8 + d0 (d2 signed, d1 and
-//     d0 unsigned). The exact per-element error |x - q*2^-18| (at most
-//     2^-19, or the clamped excess) is bounded from above and kept.
+//  1. Inputs become fixed point q = rint(x * 2^18) (exact RN rounding with
+//     the 1.5*2^23 addend, so |x - q*2^-18| <= 2^-19), split into three int8
+//     planes q = d2*2^16 + d1*2^8 + d0 (the low three bytes of q: d2 signed,
+//     d1 and d0 unsigned). A halo pixel with any |x| >= 16 (q would not fit
+//     24 bits) or a non-finite x gets an infinite bound instead.
 //  2. mma.sync m16n8k32 with +-1 int8 weights gives the three plane sums
 //     exactly (int32); Q = S2*2^16 + S1*2^8 + S0 is exact in double, and
-//     |ACC - Q*2^-18| <= e1 = sum over the window of the element errors,
-//     ACC being the exact conv value.
+//     |ACC - Q*2^-18| <= e1 = (#terms in the window) * 2^-19, ACC being the
+//     exact conv value.
 //  3. The reference's fp32 accumulator (sequential over bands per tap, then
 //     over taps, csrc/bnn_conv_realin.c:99-109) is within
 //     e2 = (g(Cin-1) + g(taps-1)*(1 + g(Cin-1))) * T of ACC, where
@@ -449,7 +450,8 @@ constexpr int RM_CINP = 128, RM_PITCH = RM_CINP + 16;   // plane bytes per halo 
 constexpr int RM_BX = 40, RM_BY = RM_TR + 2, RM_BC = 8;  // TMA box (cols, rows, bands)
 constexpr int RM_BOX_BYTES = RM_BX * RM_BY * RM_BC * 4;
 constexpr int RM_FIX = 18;                              // fixed-point fraction bits
-constexpr size_t RM_SMEM = (size_t)3 * RM_HP * RM_PITCH + RM_HP * 4 + 2 * RM_BOX_BYTES + 128;
+constexpr int RM_NST = 3;                               // TMA stages
+constexpr size_t RM_SMEM = (size_t)3 * RM_HP * RM_PITCH + RM_HP * 4 + RM_NST * RM_BOX_BYTES + 128;
 
 struct RealinMmaParams {
     const uint4* wfrag;        // [Cout/32][9 taps][4 k-steps][32 lanes][2]: mma B fragments, +-1 int8
@@ -509,6 +511,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+// pull a box into L2 ahead of its shared-memory load
+__device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];\n" ::"l"(tmap), "r"(c0),
+                 "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
     asm volatile(
@@ -516,6 +525,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
         "[%6];\n" ::"r"(dst),
         "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
+}
+
+// the reference's real fold on parameters in shared memory
+__device__ __forceinline__ int real_fold_bit_s(float acc, const float* f) {
+    const float o = __fmul_rn(f[0], acc);
+    float z = __fmaf_rn(f[1], o, f[2]);
+    if (z < 0.0f) z = __fmul_rn(f[3], z);
+    return __fadd_rn(z, f[4]) > 0.0f;
 }
 
 // the reference's real fold (csrc/bnn_fold.c:62-77) on one accumulator value
@@ -526,141 +543,162 @@ __device__ __forceinline__ int real_fold_bit(float acc, const float* f) {
     return __fadd_rn(z, __ldg(f + 4)) > 0.0f;
 }
 
-// quantise one value; accumulate its error + c9*|x| (rounded up) into bnd
-__device__ __forceinline__ uint32_t rm_quant(float x, float c9, float& bnd) {
-    int q = __float2int_rn(__fmul_rn(x, (float)(1 << RM_FIX)));
-    q = max(-(1 << 22), min(1 << 22, q));
-    const float qf = __fmul_rn((float)q, 1.0f / (float)(1 << RM_FIX));
-    const float err = fmaxf(fabsf(__fsub_ru(x, qf)), fabsf(__fsub_rd(x, qf)));
-    bnd = __fadd_ru(bnd, __fmaf_ru(c9, fabsf(x), err));
-    return (uint32_t)q;
+// fixed point of one value: the integer nearest x * 2^18 (ties to even) as
+// its 32-bit two's complement, valid for |x| < 16 (the caller flags others)
+__device__ __forceinline__ uint32_t rm_fix(float x) {
+    const float t = __fadd_rn(__fmul_rn(x, (float)(1 << RM_FIX)), 12582912.0f);  // 1.5 * 2^23
+    return (uint32_t)(__float_as_int(t) - 0x4B400000);
 }
 
-__global__ void __launch_bounds__(128, 2) realin_mma_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(256, 2) realin_mma_kernel(const __grid_constant__ CUtensorMap tmap,
                                                              const RealinMmaParams p) {
     extern __shared__ __align__(128) unsigned char rm_smem[];
-    unsigned char* box = rm_smem;                                       // [2][RM_BC][RM_BY][RM_BX] f32
-    unsigned char* planes = rm_smem + 2 * RM_BOX_BYTES;                 // [3][RM_HP][RM_PITCH]
+    unsigned char* box = rm_smem;                                       // [RM_NST][RM_BC][RM_BY][RM_BX] f32
+    unsigned char* planes = rm_smem + RM_NST * RM_BOX_BYTES;            // [3][RM_HP][RM_PITCH]
     float* bpx = reinterpret_cast<float*>(planes + 3 * RM_HP * RM_PITCH);  // [RM_HP] error bound per pixel
-    __shared__ __align__(8) unsigned long long bars[2];
+    __shared__ __align__(8) unsigned long long bars[RM_NST];
     __shared__ int staged_ok;
+    __shared__ uint32_t words[RM_TR * RM_TC];
+    __shared__ float fold_s[32][5];
+    __shared__ int exact_s[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int per = p.tiles_x * p.tiles_y;
     const int n = blockIdx.x / per, r0 = blockIdx.x - n * per;
     const int y0 = (r0 / p.tiles_x) * RM_TR, x0 = (r0 % p.tiles_x) * RM_TC;
     const int nch = (p.Cin + RM_BC - 1) / RM_BC;
-    const uint32_t bar0 = smem_u32(&bars[0]), bar1 = smem_u32(&bars[1]);
 
     if (tid == 0) {
+        // the whole tile (all band chunks) heads for L2 at once; the
+        // shared-memory loads below then wait on L2, not HBM
+        for (int k = 0; k < nch; ++k) tma_prefetch_4d(&tmap, x0 - 4, y0 - 1, k * RM_BC, n);
         staged_ok = 1;
-        mbar_init(bar0, 1);
-        mbar_init(bar1, 1);
+        for (int b = 0; b < RM_NST; ++b) mbar_init(smem_u32(&bars[b]), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    if (tid < RM_TR * RM_TC) words[tid] = 0u;
+    if (tid < 32) {
+        const int co = blockIdx.y * 32 + tid;  // CoutP = multiple of 32: always in bounds
+#pragma unroll
+        for (int i = 0; i < 5; ++i) fold_s[tid][i] = p.fold[(size_t)co * 5 + i];
+        exact_s[tid] = p.exact_ch[co];
+    }
     // bands nch*8 .. 127 of every plane stay zero
-    for (int e = tid; e < 3 * RM_HP; e += 128) {
+    for (int e = tid; e < 3 * RM_HP; e += 256) {
         uint32_t* row = reinterpret_cast<uint32_t*>(planes + e * RM_PITCH);
         for (int w = nch * RM_BC / 4; w < RM_CINP / 4; ++w) row[w] = 0u;
     }
     __syncthreads();
     if (tid == 0) {
-        for (int k = 0; k < 2 && k < nch; ++k) {
-            const uint32_t bar = k ? bar1 : bar0;
+        for (int k = 0; k < RM_NST && k < nch; ++k) {
+            const uint32_t bar = smem_u32(&bars[k]);
             mbar_expect_tx(bar, RM_BOX_BYTES);
             tma_load_4d(smem_u32(box + k * RM_BOX_BYTES), &tmap, x0 - 4, y0 - 1, k * RM_BC, n, bar);
         }
     }
 
-    // ---- quantise 8 bands at a time into the byte planes; thread owns halo
-    //      pixels tid and tid + 128
-    float bnd[2] = {0.0f, 0.0f};
+    // ---- quantise 8 bands at a time into the byte planes; thread = halo pixel
+    float tsum = 0.0f, amax = 0.0f;  // sum |x| (rounded up), max |x| of this halo pixel
+    const int hp = tid;
+    const int hr = hp / RM_HC, hcol = hp - hr * RM_HC;
     for (int k = 0; k < nch; ++k) {
-        const int b = k & 1;
-        if (!mbar_wait(b ? bar1 : bar0, (k >> 1) & 1)) staged_ok = 0;
-        const float* bx = reinterpret_cast<const float*>(box + b * RM_BOX_BYTES);
+        const int b = k % RM_NST;
+        if (!mbar_wait(smem_u32(&bars[b]), (k / RM_NST) & 1)) staged_ok = 0;
+        if (hp < RM_HP) {
+            const float* bx = reinterpret_cast<const float*>(box + b * RM_BOX_BYTES);
+            uint32_t q[RM_BC];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            const int hp = tid + 128 * s;
-            if (hp < RM_HP) {
-                const int r = hp / RM_HC, c = hp - r * RM_HC;
-                uint32_t q[RM_BC];
-#pragma unroll
-                for (int i = 0; i < RM_BC; ++i) q[i] = rm_quant(bx[(i * RM_BY + r) * RM_BX + c + 3], p.c9, bnd[s]);
-                uint32_t w2[2], w1[2], w0[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    w2[h] = w1[h] = w0[h] = 0u;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t v = q[h * 4 + i];
-                        w2[h] |= ((v >> 16) & 255u) << (8 * i);
-                        w1[h] |= ((v >> 8) & 255u) << (8 * i);
-                        w0[h] |= (v & 255u) << (8 * i);
-                    }
-                }
-                unsigned char* dst = planes + hp * RM_PITCH + k * RM_BC;
-                *reinterpret_cast<uint2*>(dst) = make_uint2(w2[0], w2[1]);
-                *reinterpret_cast<uint2*>(dst + RM_HP * RM_PITCH) = make_uint2(w1[0], w1[1]);
-                *reinterpret_cast<uint2*>(dst + 2 * RM_HP * RM_PITCH) = make_uint2(w0[0], w0[1]);
+            for (int i = 0; i < RM_BC; ++i) {
+                const float x = bx[(i * RM_BY + hr) * RM_BX + hcol + 3];
+                tsum = __fadd_ru(tsum, fabsf(x));
+                amax = fmaxf(amax, fabsf(x));
+                q[i] = rm_fix(x);
             }
+            uint32_t w2[2], w1[2], w0[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                // byte j of four values -> one word (PRMT gathers)
+                const uint32_t lo0 = __byte_perm(q[h * 4 + 0], q[h * 4 + 1], 0x5140);  // b0 b0' b1 b1'
+                const uint32_t hi0 = __byte_perm(q[h * 4 + 2], q[h * 4 + 3], 0x5140);
+                w0[h] = __byte_perm(lo0, hi0, 0x5410);                                   // bytes 0
+                w1[h] = __byte_perm(lo0, hi0, 0x7632);                                   // bytes 1
+                w2[h] = __byte_perm(__byte_perm(q[h * 4 + 0], q[h * 4 + 1], 0x6262),
+                                    __byte_perm(q[h * 4 + 2], q[h * 4 + 3], 0x6262), 0x5410);  // bytes 2
+            }
+            unsigned char* dst = planes + hp * RM_PITCH + k * RM_BC;
+            *reinterpret_cast<uint2*>(dst) = make_uint2(w2[0], w2[1]);
+            *reinterpret_cast<uint2*>(dst + RM_HP * RM_PITCH) = make_uint2(w1[0], w1[1]);
+            *reinterpret_cast<uint2*>(dst + 2 * RM_HP * RM_PITCH) = make_uint2(w0[0], w0[1]);
         }
         __syncthreads();  // box b is free again
-        if (tid == 0 && k + 2 < nch) {
-            const uint32_t bar = b ? bar1 : bar0;
+        if (tid == 0 && k + RM_NST < nch) {
+            const uint32_t bar = smem_u32(&bars[b]);
             mbar_expect_tx(bar, RM_BOX_BYTES);
-            tma_load_4d(smem_u32(box + b * RM_BOX_BYTES), &tmap, x0 - 4, y0 - 1, (k + 2) * RM_BC, n, bar);
+            tma_load_4d(smem_u32(box + b * RM_BOX_BYTES), &tmap, x0 - 4, y0 - 1, (k + RM_NST) * RM_BC, n, bar);
         }
     }
-#pragma unroll
-    for (int s = 0; s < 2; ++s)
-        if (tid + 128 * s < RM_HP) bpx[tid + 128 * s] = bnd[s];
+    if (hp < RM_HP) {
+        // Cin*2^-19 (rounding) + c9*sum|x| (reference rounding); inf if a value
+        // does not fit the 24-bit fixed point, NaN/inf propagate through tsum
+        const float e = __fmaf_ru(p.c9, tsum, __fmul_ru((float)p.Cin, 1.0f / (float)(1 << (RM_FIX + 1))));
+        bpx[hp] = amax < 16.0f ? e : __int_as_float(0x7f800000);
+    }
     __syncthreads();
     if (!staged_ok && tid == 0) atomicExch(p.ctl + 1, 1u);  // fix-up redoes the batch exactly
 
-    // ---- int8 MMAs: warp = tile row, 2 m-tiles x 4 n-tiles x 3 planes
-    int acc[3][2][4][4];
+    // ---- int8 MMAs: warp pair per tile row; warp = 2 m-tiles x 2 n-tiles x 3 planes,
+    //      fragments of the next k-step loaded while the current one computes
+    const int row = warp >> 1, nhalf = warp & 1;
+    int acc[3][2][2][4];
 #pragma unroll
     for (int k = 0; k < 3; ++k)
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
+            for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int v = 0; v < 4; ++v) acc[k][mt][nt][v] = 0;
     const int g = blockIdx.y;
     const uint4* wf = p.wfrag + (size_t)g * 9 * 4 * 32 * 2;
     const uint32_t sbase = smem_u32(planes);
     const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lcol = (lane >> 4) * 16;
-    const int ksteps = (nch * RM_BC + 31) / 32;
+    // lane's ldmatrix row address for tap (0,0), m-tile 0, band 0, plane 0
+    const uint32_t abase = sbase + (row * RM_HC + lrow) * RM_PITCH + lcol;
+    const uint4* wl = wf + lane * 2 + nhalf;  // + (t*4 + kk) * 64
+    constexpr uint32_t PL = RM_HP * RM_PITCH, MT = 16 * RM_PITCH;
+    // all 128 bands (4 k-steps) per tap; bands past Cin are zero in both operands
+    uint32_t fa[2][3][2][4];
+    uint4 fb[2];
+    auto load = [&](int buf, int t, int kk) {
+        const uint32_t at = abase + ((t / 3) * RM_HC + (t % 3)) * RM_PITCH + kk * 32;
+        fb[buf] = __ldg(wl + (t * 4 + kk) * 64);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) ldsm_x4(at + k * PL + mt * MT, fa[buf][k][mt]);
+    };
+    load(0, 0, 0);
 #pragma unroll 1
     for (int t = 0; t < 9; ++t) {
-        const int dy = t / 3, dx = t % 3;
-#pragma unroll 1
-        for (int kk = 0; kk < ksteps; ++kk) {
-            const uint4 bq0 = __ldg(wf + ((t * 4 + kk) * 32 + lane) * 2);
-            const uint4 bq1 = __ldg(wf + ((t * 4 + kk) * 32 + lane) * 2 + 1);
-            const uint32_t bb[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int hp = (warp + dy) * RM_HC + mt * 16 + lrow + dx;
-                const uint32_t addr = sbase + hp * RM_PITCH + kk * 32 + lcol;
-                uint32_t a2[4], a1[4], a0[4];
-                ldsm_x4(addr, a2);
-                ldsm_x4(addr + RM_HP * RM_PITCH, a1);
-                ldsm_x4(addr + 2 * RM_HP * RM_PITCH, a0);
+        for (int kk = 0; kk < 4; ++kk) {
+            const int cb = kk & 1;
+            if (kk < 3) load(cb ^ 1, t, kk + 1);
+            else if (t < 8) load(cb ^ 1, t + 1, 0);
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    mma_s8s8(acc[0][mt][nt], a2, bb[2 * nt], bb[2 * nt + 1]);
-                    mma_u8s8(acc[1][mt][nt], a1, bb[2 * nt], bb[2 * nt + 1]);
-                    mma_u8s8(acc[2][mt][nt], a0, bb[2 * nt], bb[2 * nt + 1]);
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    const uint32_t b0 = nt ? fb[cb].z : fb[cb].x, b1 = nt ? fb[cb].w : fb[cb].y;
+                    mma_s8s8(acc[0][mt][nt], fa[cb][0][mt], b0, b1);
+                    mma_u8s8(acc[1][mt][nt], fa[cb][1][mt], b0, b1);
+                    mma_u8s8(acc[2][mt][nt], fa[cb][2][mt], b0, b1);
                 }
-            }
         }
     }
 
     // ---- decide each output's bit from the interval, or list it
     const int gid = lane >> 2, tig = lane & 3;
-    const int y = y0 + warp;
+    const int y = y0 + row;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
@@ -672,24 +710,24 @@ __global__ void __launch_bounds__(128, 2) realin_mma_kernel(const __grid_constan
             if (valid) {
                 float ef = 0.0f;
 #pragma unroll
-                for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bpx[(warp + t / 3) * RM_HC + col + t % 3]);
+                for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bpx[(row + t / 3) * RM_HC + col + t % 3]);
                 const bool finite = ef <= 3.0e38f;  // false for inf and NaN
                 const double e = (double)ef;
                 const size_t pix = ((size_t)n * p.H + y) * p.W + x;
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
+                for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const int v = half * 2 + j;
-                        const int cl = nt * 8 + tig * 2 + j, co = g * 32 + cl;
+                        const int cl = (nhalf * 2 + nt) * 8 + tig * 2 + j, co = g * 32 + cl;
                         if (co >= p.Cout) continue;
                         const double q = (double)acc[0][mt][nt][v] * 65536.0 + (double)acc[1][mt][nt][v] * 256.0 +
                                          (double)acc[2][mt][nt][v];
                         const double a = q * (1.0 / (double)(1 << RM_FIX));
                         const float lo = __double2float_rd(__dsub_rd(a, e)), hi = __double2float_ru(__dadd_ru(a, e));
-                        const float* f = p.fold + (size_t)co * 5;
-                        const int blo = real_fold_bit(lo, f), bhi = real_fold_bit(hi, f);
-                        if (finite && blo == bhi && !__ldg(p.exact_ch + co)) {
+                        const float* f = fold_s[cl];
+                        const int blo = real_fold_bit_s(lo, f), bhi = real_fold_bit_s(hi, f);
+                        if (finite && blo == bhi && !exact_s[cl]) {
                             bits |= (uint32_t)blo << cl;
                         } else {
                             const unsigned int slot = atomicAdd(p.ctl, 1u);
@@ -705,8 +743,13 @@ __global__ void __launch_bounds__(128, 2) realin_mma_kernel(const __grid_constan
             }
             bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
             bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
-            if (valid && tig == 0) p.out[(((size_t)n * p.H + y) * p.W + x) * p.cwo + g] = bits;
+            if (tig == 0 && bits) atomicOr(&words[row * RM_TC + col], bits);
         }
+    }
+    __syncthreads();
+    if (tid < RM_TR * RM_TC) {
+        const int yy = y0 + tid / RM_TC, xx = x0 + tid % RM_TC;
+        if (yy < p.H && xx < p.W) p.out[(((size_t)n * p.H + yy) * p.W + xx) * p.cwo + g] = words[tid];
     }
 }
 
@@ -740,21 +783,54 @@ struct RealinFixParams {
     int cap, N, Cin, CinP, H, W, Cout, cwo;
 };
 
+// one warp per listed output: lane t < 9 sums tap t over the bands in order
+// (loads issued ahead of the chain), lane 0 then adds the in-bounds taps in
+// order, as the reference does
+__device__ float realin_exact_acc_warp(const float* x, const float* wf, int Cin, int CinP, int H, int W, int n,
+                                       int co, int y, int xx, int lane) {
+    const size_t plane = (size_t)H * W;
+    const int iy = y + lane / 3 - 1, ix = xx + lane % 3 - 1;
+    const bool inb = lane < 9 && (unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W;
+    float s = 0.0f;
+    if (inb) {
+        const float* src = x + (size_t)n * Cin * plane + (size_t)iy * W + ix;
+        const float* w = wf + ((size_t)co * 9 + lane) * CinP;
+        int ci = 0;
+        for (; ci + 8 <= Cin; ci += 8) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __ldg(src + (size_t)(ci + i) * plane);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = __fmaf_rn(v[i], __ldg(w + ci + i), s);
+        }
+        for (; ci < Cin; ++ci) s = __fmaf_rn(__ldg(src + (size_t)ci * plane), __ldg(w + ci), s);
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const float st = __shfl_sync(0xffffffffu, s, t);
+        const int ty = y + t / 3 - 1, tx = xx + t % 3 - 1;
+        if ((unsigned)ty < (unsigned)H && (unsigned)tx < (unsigned)W) acc = __fadd_rn(acc, st);
+    }
+    return acc;
+}
+
 __global__ void realin_fixup_kernel(const RealinFixParams p) {
     const unsigned int cnt = min(p.ctl[0], (unsigned)p.cap);
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t g0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
     if (p.ctl[1] == 0u) {
-        for (size_t i = g0; i < cnt; i += stride) {
+        const size_t wstride = ((size_t)gridDim.x * blockDim.x) >> 5;
+        for (size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < cnt; i += wstride) {
             const uint32_t pix = p.list[2 * i], co = p.list[2 * i + 1];
             const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
-            const float acc = realin_exact_acc(p.x, p.wf, p.Cin, p.CinP, p.H, p.W, n, (int)co, y, xx);
-            if (real_fold_bit(acc, p.fold + (size_t)co * 5))
+            const float acc = realin_exact_acc_warp(p.x, p.wf, p.Cin, p.CinP, p.H, p.W, n, (int)co, y, xx, lane);
+            if (lane == 0 && real_fold_bit(acc, p.fold + (size_t)co * 5))
                 atomicOr(p.out + (size_t)pix * p.cwo + (co >> 5), 1u << (co & 31));
         }
     } else {
+        const size_t stride = (size_t)gridDim.x * blockDim.x;
         const size_t words = (size_t)p.N * p.H * p.W * p.cwo;
-        for (size_t i = g0; i < words; i += stride) {
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += stride) {
             const size_t pix = i / p.cwo;
             const int wd = (int)(i - pix * p.cwo);
             const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
