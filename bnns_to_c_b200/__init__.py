@@ -86,6 +86,7 @@ def lib():
         "bnn_pack_act_device": (ip, [vp, ip, ip, ip, ip, vp, vp]),
         "bnn_unpack_act_device": (ip, [vp, ip, ip, ip, ip, vp, vp]),
         "bnn_forward_launches": (ip, [vp, ip, ip, ip]),
+        "bnn_set_bconv_kernel": (ip, [ip]),
         "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
     }
     for name, (res, args) in sig.items():
@@ -280,6 +281,11 @@ class BconvLayer:
             self.close()
         except Exception:
             pass
+
+
+def set_bconv_kernel(kind: str):
+    """'tc' (int8 tensor cores, default) or 'popc' (XOR + POPC)."""
+    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1}[kind]))
 
 
 def synth_device(device, seed, first, n, bands, H, W, d_out, stream=None):

@@ -44,6 +44,7 @@ struct BinLayer {
     int Cin, Cout, CoutP, cw0, cw1, Kw, sC;  // sC: channels from the first source
     uint32_t* wt = nullptr;
     int* wpop = nullptr;
+    int8_t* w8 = nullptr;     // tensor-core kernel weights [Kw][9][CoutP][32]
     FoldIv* fold = nullptr;
     FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
 };
@@ -168,6 +169,7 @@ static FoldIv to_iv(int type, int t, int lo, int hi) {
 
 struct HostBin {
     std::vector<uint32_t> wt;
+    std::vector<int8_t> w8;
     std::vector<int> wpop;
     std::vector<FoldIv> fold, fold2;
 };
@@ -182,6 +184,7 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
     L.Kw = L.cw0 + L.cw1;
     L.CoutP = cdiv(Cout, 128) * 128;
     h.wt.assign((size_t)L.CoutP * 9 * L.Kw, 0u);
+    h.w8.assign((size_t)L.Kw * 9 * L.CoutP * 32, (int8_t)0);
     h.wpop.assign((size_t)L.CoutP * 9, 0);
     for (int co = 0; co < Cout; ++co) {
         const uint64_t* row = packed + (size_t)co * nwords;
@@ -190,10 +193,12 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
             const int bit = ci < sC ? (ci & 31) : ((ci - sC) & 31);
             for (int t = 0; t < 9; ++t) {
                 const int k = ci * 9 + t;
-                if ((row[k >> 6] >> (k & 63)) & 1ull) {
+                const bool plus = (row[k >> 6] >> (k & 63)) & 1ull;
+                if (plus) {
                     h.wt[((size_t)co * 9 + t) * L.Kw + word] |= 1u << bit;
                     h.wpop[(size_t)co * 9 + t] += 1;
                 }
+                h.w8[(((size_t)word * 9 + t) * L.CoutP + co) * 32 + bit] = plus ? 1 : -1;
             }
         }
     }
@@ -213,6 +218,11 @@ static cudaError_t attr_bconv() {
     return cudaFuncSetAttribute(bconv3x3_kernel<BN, TM, TN, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)BconvCfg<BN, TM, TN, KC>::smem_bytes(512));
 }
+template <int BN>
+static cudaError_t attr_bmma() {
+    return cudaFuncSetAttribute(bconv_mma_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)BmmaCfg<BN>::smem_bytes(512));
+}
 template <int BN, int TM, int TN>
 static cudaError_t attr_bconv_kc() {
     cudaError_t e;
@@ -228,7 +238,8 @@ static int set_kernel_attrs(int device) {
     if (device >= 0 && device < 64 && done[device]) return BNN_OK;
     cudaError_t e;
     if ((e = attr_bconv_kc<32, 4, 4>()) != cudaSuccess || (e = attr_bconv_kc<64, 8, 4>()) != cudaSuccess ||
-        (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess ||
+        (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess || (e = attr_bmma<32>()) != cudaSuccess ||
+        (e = attr_bmma<64>()) != cudaSuccess || (e = attr_bmma<128>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -319,7 +330,7 @@ static int dev_init(const Model* m, DevState* d) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
-        total += align256(it.h.wt.size() * 4) + align256(it.h.wpop.size() * 4) +
+        total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wpop.size() * 4) +
                  align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
     }
     const size_t hw = (size_t)m->head_Cout * m->head_Cin;
@@ -343,6 +354,7 @@ static int dev_init(const Model* m, DevState* d) {
     d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
+        it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
         it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
         it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -461,6 +473,9 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
 // -------------------------------------------------------------------
 // launchers
 // -------------------------------------------------------------------
+// binary conv implementation: 0 = int8 tensor cores (default), 1 = XOR/POPC
+static int g_bconv_kind = 0;
+
 struct TileGeo {
     int TR, TC, TNI, tiles_x, tiles_y, tiles, HP;
 };
@@ -511,7 +526,25 @@ static int launch_bconv_kc(BconvParams p, int N, cudaStream_t st) {
     return launch_bconv_t<BN, TM, TN, 1>(p, N, st);
 }
 
+template <int BN>
+static int launch_bmma(BconvParams p, int N, cudaStream_t st) {
+    using Cfg = BmmaCfg<BN>;
+    TileGeo g = tile_geo(N, p.H, p.W, Cfg::BM);
+    p.TR = g.TR; p.TC = g.TC; p.TNI = g.TNI; p.tiles_x = g.tiles_x; p.tiles_y = g.tiles_y; p.HP = g.HP;
+    dim3 grid((unsigned)g.tiles, (unsigned)cdiv(p.Cout, BN));
+    bconv_mma_kernel<BN><<<grid, Cfg::NT, Cfg::smem_bytes(g.HP), st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv mma launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
+    if (g_bconv_kind == 0) {
+        if (p.Cout <= 32) return launch_bmma<32>(p, N, st);
+        if (p.Cout <= 64) return launch_bmma<64>(p, N, st);
+        return launch_bmma<128>(p, N, st);
+    }
     if (p.Cout <= 32) return launch_bconv_kc<32, 4, 4>(p, N, st);
     if (p.Cout <= 64) return launch_bconv_kc<64, 8, 4>(p, N, st);
     return launch_bconv_kc<128, 8, 8>(p, N, st);
@@ -532,7 +565,9 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     p.cH = std::min(upH, H);
     p.cW = std::min(upW, W);
     p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
-    p.wt = L.wt; p.wpop = L.wpop; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
+    p.wt = L.wt; p.wpop = L.wpop; p.w8 = L.w8; p.CoutP = L.CoutP; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
+    if ((g_bconv_kind == 0 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
+        return set_error(BNN_ERR_ARG, "binary conv layer has no weights for the selected kernel");
     p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
     return launch_bconv(p, N, st);
 }
@@ -954,6 +989,12 @@ BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float
     }
 }
 
+BNN_API int bnn_set_bconv_kernel(int kind) {
+    if (kind != 0 && kind != 1) return set_error(BNN_ERR_ARG, "bconv kernel kind %d (0 = tensor core, 1 = popc)", kind);
+    g_bconv_kind = kind;
+    return BNN_OK;
+}
+
 BNN_API int bnn_set_devices(Model* m, const int* devices, int n) {
     if (!m || n < 0 || (n > 0 && !devices)) return set_error(BNN_ERR_ARG, "bad arguments");
     int ndev = 0;
@@ -1258,7 +1299,8 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         Act a2{0, Cout, (int32_t*)ptype, (int32_t*)pt, (int32_t*)plo, (int32_t*)phi, nullptr, nullptr, nullptr, nullptr};
         folds_of(&a2, Lh->L.CoutP, h.fold2);
     }
-    size_t total = align256(h.wt.size() * 4) + align256(h.wpop.size() * 4) + 2 * align256(h.fold.size() * sizeof(FoldIv));
+    size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wpop.size() * 4) +
+                   2 * align256(h.fold.size() * sizeof(FoldIv));
     if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
         delete Lh;
@@ -1273,6 +1315,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         return dst;
     };
     Lh->L.wt = (uint32_t*)put(h.wt.data(), h.wt.size() * 4);
+    Lh->L.w8 = (int8_t*)put(h.w8.data(), h.w8.size());
     Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
     Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
     Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -1482,10 +1525,11 @@ static int noalloc_scratch(int dev, unsigned char** out) {
 }
 
 // kidx-ordered weights (bit ci*9+t of row co) -> tap-major words + per-tap
-// popcounts, one thread per (co, tap); rows co >= Cout are written as zero,
-// so nothing in the shared array has to be cleared first.
+// popcounts (XOR/POPC kernel) and +-1 int8 rows (tensor-core kernel), one
+// thread per (co, tap); rows co >= Cout and channels >= Cin are written as
+// zero, so nothing in the shared array has to be cleared first.
 __global__ void noalloc_relayout_kernel(const uint64_t* packed, int nwords, int Cin, int Cout, int CoutP, int Kw,
-                                        uint32_t* wt, int* wpop, FoldIv* fold) {
+                                        uint32_t* wt, int8_t* w8, int* wpop, FoldIv* fold) {
     const int g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= CoutP * 9) return;
     const int co = g / 9, t = g - co * 9;
@@ -1500,6 +1544,8 @@ __global__ void noalloc_relayout_kernel(const uint64_t* packed, int nwords, int 
                 if ((packed[(size_t)co * nwords + (k >> 6)] >> (k & 63)) & 1ull) word |= 1u << b;
             }
         wt[(size_t)g * Kw + w] = word;
+        int8_t* row8 = w8 + (((size_t)w * 9 + t) * CoutP + co) * 32;
+        for (int b = 0; b < 32; ++b) row8[b] = (co < Cout && w * 32 + b < Cin) ? (((word >> b) & 1u) ? 1 : -1) : 0;
         pop += __popc(word);
     }
     wpop[g] = pop;
@@ -1532,10 +1578,12 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
     // layout of the static scratch for this call (256-byte aligned regions)
     const int nwords = (9 * Cin + 63) / 64, Kw = cw_of(Cin), CoutP = cdiv(Cout, 128) * 128;
     const size_t n_a = (size_t)Cin * H * W, n_pk = (size_t)Cout * nwords * 8, n_bits = (size_t)H * W * Kw * 4,
-                 n_wt = (size_t)CoutP * 9 * Kw * 4, n_pop = (size_t)CoutP * 9 * 4, n_fold = (size_t)CoutP * sizeof(FoldIv),
+                 n_wt = (size_t)CoutP * 9 * Kw * 4, n_w8 = (size_t)Kw * 9 * CoutP * 32, n_pop = (size_t)CoutP * 9 * 4,
+                 n_fold = (size_t)CoutP * sizeof(FoldIv),
                  n_out = (size_t)H * W * cw_of(Cout) * 4, n_P = (size_t)Cout * H * W * 4,
                  n_crop = pad == 0 ? (size_t)Cout * Ho * Wo * 4 : 0;
-    const size_t need = align256(n_a) + align256(n_pk) + align256(n_bits) + align256(n_wt) + align256(n_pop) +
+    const size_t need = align256(n_a) + align256(n_pk) + align256(n_bits) + align256(n_wt) + align256(n_w8) +
+                        align256(n_pop) +
                         align256(n_fold) + align256(n_out) + align256(n_P) + align256(n_crop);
     if (need > kNoAllocScratch)
         return set_error(BNN_ERR_ARG,
@@ -1551,6 +1599,7 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
     BinLayer L;
     L.Cin = Cin; L.Cout = Cout; L.CoutP = CoutP; L.cw0 = Kw; L.cw1 = 0; L.Kw = Kw; L.sC = Cin;
     L.wt = (uint32_t*)take(n_wt);
+    L.w8 = (int8_t*)take(n_w8);
     L.wpop = (int*)take(n_pop);
     L.fold = (FoldIv*)take(n_fold);
     L.fold2 = nullptr;
@@ -1560,7 +1609,8 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
     // every region below is fully rewritten by this call before it is read
     CK(cudaMemcpy(da, a, n_a, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(dpk, packed_w, n_pk, cudaMemcpyHostToDevice));
-    noalloc_relayout_kernel<<<cdiv((long)CoutP * 9, 128), 128>>>(dpk, nwords, Cin, Cout, CoutP, Kw, L.wt, L.wpop, L.fold);
+    noalloc_relayout_kernel<<<cdiv((long)CoutP * 9, 128), 128>>>(dpk, nwords, Cin, Cout, CoutP, Kw, L.wt, L.w8, L.wpop,
+                                                                 L.fold);
     CK(cudaGetLastError());
     pack_act_kernel<<<148 * 4, 256>>>(da, 1, Cin, H, W, dbits);
     CK(cudaGetLastError());

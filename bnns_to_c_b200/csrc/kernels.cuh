@@ -39,8 +39,10 @@ struct BconvParams {
     int N, H, W;
     int h1, w1, oh, ow, cH, cW;  // upsample placement (reference up_cat)
     int Cin, Cout, cwo;
-    const uint32_t* wt;   // [CoutP][9][Kw]
-    const int* wpop;      // [CoutP][9]
+    const uint32_t* wt;   // [CoutP][9][Kw]      (POPC kernel)
+    const int* wpop;      // [CoutP][9]          (POPC kernel)
+    const int8_t* w8;     // [Kw][9][CoutP][32]  (tensor-core kernel): +-1, 0 for absent channels
+    int CoutP;
     const FoldIv* fold;   // [CoutP]
     const FoldIv* fold2;  // pooled-branch fold, or nullptr
     uint32_t* out;        // [N][H][W][cwo]
@@ -109,6 +111,52 @@ __device__ __forceinline__ void ld_b(const uint32_t* p, uint32_t* v) {
     for (int q = 0; q < TN / 4; ++q) {
         uint4 t = *reinterpret_cast<const uint4*>(p + 4 * q);
         v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+}
+
+// Fold + pack from a P tile in shared memory (P[slot][channel], pitch PSP),
+// one output word (32 channels) per item; with a pooled output, also the 2x2
+// max of P (slots m, m+1, m+TC, m+TC+1 of the same image) -> second fold.
+template <int BN, int BM, int PSP, int NT>
+__device__ __forceinline__ void bconv_store_epilogue(const BconvParams& p, const int32_t* Ps, const FoldIv* fs,
+                                                     const FoldIv* fs2, int n0, int y0, int x0, int TRC, int cout0,
+                                                     int tid) {
+    constexpr int WPT = BN / 32;
+    const int word0 = cout0 >> 5;
+    for (int e = tid; e < BM * WPT; e += NT) {
+        const int m = e / WPT, w = e - m * WPT;
+        const int i = m / TRC, rem = m - i * TRC, yy = rem / p.TC, xx = rem - yy * p.TC;
+        const int n = n0 + i, y = y0 + yy, x = x0 + xx;
+        // words wholly past Cout (Cout not a multiple of BN) do not exist
+        if (i >= p.TNI || n >= p.N || y >= p.H || x >= p.W || cout0 + w * 32 >= p.Cout) continue;
+        const int32_t* Pm = Ps + m * PSP + w * 32;
+        uint32_t bits = 0u;
+#pragma unroll 8
+        for (int b = 0; b < 32; ++b) {
+            const int c = w * 32 + b;
+            if (cout0 + c < p.Cout) bits |= (uint32_t)fold_bit(Pm[b], fs[c]) << b;
+        }
+        p.out[(((size_t)n * p.H + y) * p.W + x) * p.cwo + word0 + w] = bits;
+        if (p.P) {
+            for (int b = 0; b < 32 && cout0 + w * 32 + b < p.Cout; ++b)
+                p.P[(((size_t)n * p.Cout + cout0 + w * 32 + b) * p.H + y) * p.W + x] = Pm[b];
+        }
+        if (p.out2 && !(yy & 1) && !(xx & 1) && y + 1 < p.H && x + 1 < p.W) {
+            const int Hh = p.H >> 1, Wh = p.W >> 1;
+            const int32_t* P01 = Pm + PSP;
+            const int32_t* P10 = Pm + p.TC * PSP;
+            const int32_t* P11 = P10 + PSP;
+            uint32_t bits2 = 0u;
+            for (int b = 0; b < 32; ++b) {
+                const int c = w * 32 + b;
+                if (cout0 + c >= p.Cout) break;
+                const int mx = max(max(Pm[b], P01[b]), max(P10[b], P11[b]));
+                bits2 |= (uint32_t)fold_bit(mx, fs2[c]) << b;
+                if (p.P2)
+                    p.P2[(((size_t)n * p.Cout + cout0 + c) * Hh + (y >> 1)) * Wh + (x >> 1)] = mx;
+            }
+            p.out2[(((size_t)n * Hh + (y >> 1)) * Wh + (x >> 1)) * p.cwo + word0 + w] = bits2;
+        }
     }
 }
 
@@ -245,44 +293,7 @@ __global__ void __launch_bounds__(256, 2) bconv3x3_kernel(const BconvParams p) {
     }
     __syncthreads();
 
-    // ---- fold + pack, one output word (32 channels) per item
-    constexpr int WPT = BN / 32;
-    const int word0 = cout0 >> 5;
-    for (int e = tid; e < BM * WPT; e += NT) {
-        const int m = e / WPT, w = e - m * WPT;
-        const int i = m / TRC, rem = m - i * TRC, yy = rem / p.TC, xx = rem - yy * p.TC;
-        const int n = n0 + i, y = y0 + yy, x = x0 + xx;
-        // words wholly past Cout (Cout not a multiple of BN) do not exist
-        if (i >= p.TNI || n >= p.N || y >= p.H || x >= p.W || cout0 + w * 32 >= p.Cout) continue;
-        const int32_t* Pm = Ps + m * PSP + w * 32;
-        uint32_t bits = 0u;
-#pragma unroll 8
-        for (int b = 0; b < 32; ++b) {
-            const int c = w * 32 + b;
-            if (cout0 + c < p.Cout) bits |= (uint32_t)fold_bit(Pm[b], fs[c]) << b;
-        }
-        p.out[(((size_t)n * p.H + y) * p.W + x) * p.cwo + word0 + w] = bits;
-        if (p.P) {
-            for (int b = 0; b < 32 && cout0 + w * 32 + b < p.Cout; ++b)
-                p.P[(((size_t)n * p.Cout + cout0 + w * 32 + b) * p.H + y) * p.W + x] = Pm[b];
-        }
-        if (p.out2 && !(yy & 1) && !(xx & 1) && y + 1 < p.H && x + 1 < p.W) {
-            const int Hh = p.H >> 1, Wh = p.W >> 1;
-            const int32_t* P01 = Pm + PSP;
-            const int32_t* P10 = Pm + p.TC * PSP;
-            const int32_t* P11 = P10 + PSP;
-            uint32_t bits2 = 0u;
-            for (int b = 0; b < 32; ++b) {
-                const int c = w * 32 + b;
-                if (cout0 + c >= p.Cout) break;
-                const int mx = max(max(Pm[b], P01[b]), max(P10[b], P11[b]));
-                bits2 |= (uint32_t)fold_bit(mx, fs2[c]) << b;
-                if (p.P2)
-                    p.P2[(((size_t)n * p.Cout + cout0 + c) * Hh + (y >> 1)) * Wh + (x >> 1)] = mx;
-            }
-            p.out2[(((size_t)n * Hh + (y >> 1)) * Wh + (x >> 1)) * p.cwo + word0 + w] = bits2;
-        }
-    }
+    bconv_store_epilogue<BN, BM, PSP, NT>(p, Ps, fs, fs2, n0, y0, x0, TRC, cout0, tid);
 }
 
 // ---------------------------------------------------------------------
@@ -844,6 +855,160 @@ __global__ void realin_fixup_kernel(const RealinFixParams p) {
             p.out[i] = bits;
         }
     }
+}
+
+// ---------------------------------------------------------------------
+// Fused binary 3x3 conv on int8 tensor cores.
+// +-1 activations and weights are exact in int8 and an out-of-image tap is
+// an int8 0, so one mma.sync m16n8k32 s8 accumulation gives the reference's
+// P directly (no popcount correction). Bit planes stay in HBM; per 32-channel
+// word of K the CTA expands its halo tile to int8 in shared memory (nibble
+// lookup table) and copies that word's weights for all 9 taps; ldmatrix row
+// addresses give the implicit im2col for any tile geometry (the tile_geo of
+// the POPC kernel: whole small images or row bands). The P tile then goes
+// through the same fold / pool / pack epilogue as the POPC kernel.
+// Warp tile 64 slots x 32 channels (4 m-tiles x 4 n-tiles), CTA = 2 x BN/32
+// warps over 128 slots x BN channels.
+// ---------------------------------------------------------------------
+constexpr int BM_PITCH = 48;   // bytes per halo pixel / weight row in shared memory (32 + 16 pad)
+
+template <int BN>
+struct BmmaCfg {
+    static constexpr int NWARP = 2 * (BN / 32);
+    static constexpr int NT = NWARP * 32;
+    static constexpr int BM = 128;
+    static constexpr int PSP = BN + 1;
+    __host__ __device__ static size_t a_bytes(int HP) { return ((size_t)HP * BM_PITCH + 127) & ~(size_t)127; }
+    __host__ __device__ static size_t main_bytes(int HP) {
+        const size_t ab = a_bytes(HP) + (size_t)9 * BN * BM_PITCH;
+        const size_t pb = (size_t)BM * PSP * 4;
+        return ((ab > pb ? ab : pb) + 15) & ~(size_t)15;
+    }
+    static size_t smem_bytes(int HP) { return main_bytes(HP) + (size_t)BN * 2 * sizeof(FoldIv) + 64; }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(BmmaCfg<BN>::NT, 512 / BmmaCfg<BN>::NT) bconv_mma_kernel(const BconvParams p) {
+    using C = BmmaCfg<BN>;
+    constexpr int NT = C::NT, BM = C::BM, PSP = C::PSP;
+    extern __shared__ __align__(128) unsigned char bm_smem[];
+    const int HP = p.HP;
+    unsigned char* As = bm_smem;                                  // [HP][BM_PITCH] int8
+    unsigned char* Bs = bm_smem + C::a_bytes(HP);                 // [9][BN][BM_PITCH] int8
+    FoldIv* fs = reinterpret_cast<FoldIv*>(bm_smem + C::main_bytes(HP));
+    FoldIv* fs2 = fs + BN;
+    int32_t* Ps = reinterpret_cast<int32_t*>(bm_smem);            // [BM][PSP] after the main loop
+    __shared__ uint32_t lut[16];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = warp & 1, wn = warp >> 1;
+    const int cout0 = blockIdx.y * BN;
+    if (tid < 16) {
+        // nibble -> four int8 of +1 (bit set) / -1
+        const uint32_t x = ((uint32_t)tid * 0x00204081u) & 0x01010101u;
+        lut[tid] = 0xFFFFFFFFu ^ (x * 0xFEu);
+    }
+    int n0, y0, x0;
+    if (p.TNI > 1) {
+        n0 = blockIdx.x * p.TNI; y0 = 0; x0 = 0;
+    } else {
+        const int per = p.tiles_x * p.tiles_y;
+        n0 = blockIdx.x / per;
+        const int r = blockIdx.x - n0 * per;
+        y0 = (r / p.tiles_x) * p.TR;
+        x0 = (r % p.tiles_x) * p.TC;
+    }
+    const int HC = p.TC + 2, HRC = (p.TR + 2) * HC, TRC = p.TR * p.TC;
+    for (int c = tid; c < BN; c += NT) {
+        fs[c] = p.fold[cout0 + c];
+        fs2[c] = p.fold2 ? p.fold2[cout0 + c] : FoldIv{0, 0, 0, 0};
+    }
+
+    // this lane's ldmatrix row (slot) in each of its 4 m-tiles -> halo centre
+    const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lcol = (lane >> 4) * 16;
+    uint32_t arow[4];
+    const uint32_t abase = smem_u32(As), bbase = smem_u32(Bs);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        const int m = wm * 64 + mt * 16 + lrow;
+        const int i = m / TRC, rem = m - i * TRC, yy = rem / p.TC, xx = rem - yy * p.TC;
+        const int hc = (i < p.TNI) ? (i * HRC + (yy + 1) * HC + xx + 1) : (HC + 1);
+        arow[mt] = abase + hc * BM_PITCH + lcol;
+    }
+    // B ldmatrix rows: channel wn*32 + 16*j + (lane&7) + 8*(lane>>4), k half (lane>>3)&1
+    const uint32_t brow = bbase + (wn * 32 + (lane & 7) + 8 * (lane >> 4)) * BM_PITCH + ((lane >> 3) & 1) * 16;
+
+    int acc[4][4][4];
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[mt][nt][v] = 0;
+
+    __syncthreads();  // lut
+    for (int kw = 0; kw < p.Kw; ++kw) {
+        // ---- stage word kw of every halo pixel, as 32 int8 (0 outside the image)
+        for (int hp = tid; hp < HP; hp += NT) {
+            const int i = hp / HRC, rem = hp - i * HRC, r = rem / HC, cc = rem - r * HC;
+            const int n = n0 + i, y = y0 + r - 1, x = x0 + cc - 1;
+            uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+            if (n < p.N && (unsigned)y < (unsigned)p.H && (unsigned)x < (unsigned)p.W) {
+                uint32_t v = 0u;
+                if (kw < p.cw0) {
+                    v = __ldg(p.in0 + (((size_t)n * p.H + y) * p.W + x) * p.cw0 + kw);
+                } else {
+                    const int uy = y - p.oh, ux = x - p.ow;
+                    if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
+                        v = __ldg(p.in1 + (((size_t)n * p.h1 + (uy >> 1)) * p.w1 + (ux >> 1)) * p.cw1 + (kw - p.cw0));
+                }
+                lo = make_uint4(lut[v & 15], lut[(v >> 4) & 15], lut[(v >> 8) & 15], lut[(v >> 12) & 15]);
+                hi = make_uint4(lut[(v >> 16) & 15], lut[(v >> 20) & 15], lut[(v >> 24) & 15], lut[v >> 28]);
+            }
+            uint4* d = reinterpret_cast<uint4*>(As + hp * BM_PITCH);
+            d[0] = lo;
+            d[1] = hi;
+        }
+        // ---- stage word kw of the weights for all 9 taps: Bs[t][c][32 bytes]
+        for (int e = tid; e < 9 * BN * 2; e += NT) {
+            const int h = e & 1, c = (e >> 1) % BN, t = (e >> 1) / BN;
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                p.w8 + (((size_t)kw * 9 + t) * p.CoutP + cout0 + c) * 32 + h * 16));
+            *reinterpret_cast<uint4*>(Bs + (t * BN + c) * BM_PITCH + h * 16) = v;
+        }
+        __syncthreads();
+        // ---- 9 taps x one 32-byte k-step: 4 x 4 MMAs per tap
+#pragma unroll 3
+        for (int t = 0; t < 9; ++t) {
+            const int off = ((t / 3 - 1) * HC + (t % 3 - 1)) * BM_PITCH;
+            uint32_t a[4][4], b[2][4];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) ldsm_x4(arow[mt] + off, a[mt]);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) ldsm_x4(brow + (t * BN + 16 * j) * BM_PITCH, b[j]);
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt)
+                    mma_s8s8(acc[mt][nt], a[mt], b[nt >> 1][(nt & 1) * 2], b[nt >> 1][(nt & 1) * 2 + 1]);
+        }
+        __syncthreads();
+    }
+
+    // ---- P tile to shared memory, then the common fold / pool / pack epilogue
+    const int gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int m = wm * 64 + mt * 16 + gid + (v >> 1) * 8;
+                const int c = wn * 32 + nt * 8 + tig * 2 + (v & 1);
+                Ps[m * PSP + c] = acc[mt][nt][v];
+            }
+    __syncthreads();
+    bconv_store_epilogue<BN, BM, PSP, NT>(p, Ps, fs, fs2, n0, y0, x0, TRC, cout0, tid);
 }
 
 // ---------------------------------------------------------------------

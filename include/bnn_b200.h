@@ -57,6 +57,12 @@ int bnn_forward_batch(const Model *m, const float *input, int N, int H, int W,
 int bnn_forward_device(const Model *m, int device, const float *d_input, int N,
                        int H, int W, float *d_logits, void *stream);
 
+/* Process-wide choice of the binary-conv kernel, for measurement and A/B
+ * parity tests: 0 = int8 tensor cores (mma.sync, default), 1 = XOR + POPC on
+ * the integer pipe. Both compute the reference's P exactly; set it before
+ * the forwards to compare (captured graphs keep the kernel they captured). */
+int bnn_set_bconv_kernel(int kind);
+
 /* Devices used by bnn_forward_batch, in shard order. n = 0 restores the
  * default: the calling thread's current device. */
 int bnn_set_devices(Model *m, const int *devices, int n);
@@ -107,7 +113,8 @@ int bnn_gpu_bconv_dispatch(const int8_t *a, const uint64_t *packed_w, int32_t *P
  * BNN_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
  * the process exits; a call whose buffers do not fit returns BNN_ERR_ARG
  * before touching the GPU (it needs about 1.2*Cin*H*W + 8*Cout*H*W +
- * 2.3*Cout*Cin bytes, each buffer rounded up to 256).
+ * 11.3*CoutP*Cin bytes with CoutP = Cout rounded up to 128, each buffer
+ * rounded up to 256).
  * The first call on a device looks up that array's device address (once per
  * device, with the device current); make that first call before any stream
  * capture. All calls share the one array and it keeps the last call's

@@ -33,8 +33,16 @@ def same_bits(a, b):
                                                  np.ascontiguousarray(b).view(np.uint8))
 
 
+@pytest.fixture(params=["tc", "popc"])
+def bconv_kind(request):
+    """Both binary-conv implementations (int8 tensor cores, XOR + POPC)."""
+    bn.set_bconv_kernel(request.param)
+    yield request.param
+    bn.set_bconv_kernel("tc")
+
+
 # ------------------------------------------------------------------ kernels
-def test_bconv_dispatch_edge_shapes():
+def test_bconv_dispatch_edge_shapes(bconv_kind):
     """Reference bench_bconv.c edge-shape list + bconv_harness pad=0 case."""
     g = np.load(os.path.join(GOLD, "kernels.npz"))
     i = 0
@@ -74,7 +82,7 @@ def _unpack(bits, n, c, H, W):
                                             (512, 512, 4, 4, 5), (64, 64, 32, 32, 1), (48, 40, 17, 13, 2),
                                             (32, 32, 2, 2, 40), (96, 32, 32, 32, 1), (768, 256, 4, 4, 3),
                                             (16, 200, 9, 70, 1)])
-def test_fused_layer_vs_oracle(cin, cout, H, W, n):
+def test_fused_layer_vs_oracle(cin, cout, H, W, n, bconv_kind):
     rng = np.random.default_rng(cin + 7 * cout + H)
     a = np.where(rng.random((n, cin, H, W)) < 0.5, 1, -1).astype(np.int8)
     ws = np.where(rng.random((cout, cin, 3, 3)) < 0.5, 1, -1).astype(np.int8)
@@ -121,7 +129,7 @@ def _blob_path(name, tmp_path):
 
 
 @pytest.mark.parametrize("npz", _fixtures(), ids=[os.path.basename(f) for f in _fixtures()])
-def test_forward_stages_match_reference(npz, tmp_path):
+def test_forward_stages_match_reference(npz, tmp_path, bconv_kind):
     g = np.load(npz)
     name = os.path.basename(npz).rsplit("_", 1)[0]
     H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
