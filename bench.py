@@ -14,9 +14,10 @@ timing is the max over ranks.
           CUDA events on the launching stream around the K timed steps
   e2e   : patches/s through the public host-pointer API bnn_forward_batch,
           pinned host input -> logits in pinned host memory, every step
-  roofline : the dominant kernel family (17 fused binary convs, POPC
-          integer pipe) from per-kernel CUDA events over the same timed
-          steps
+  roofline : the dominant kernel family (the 17 fused binary convs, int8
+          tensor cores) from per-kernel CUDA events over the same timed
+          steps, against the int8 dense tensor peak (2x the measured bf16
+          rate); rooflines.* also give the first conv and the host link
   cpu_baseline : the reference engine compiled from its own sources
           (oracle/_ref/ref_bench), all host cores, bounded sample
 
@@ -40,8 +41,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "UNet patches/s (32x32x120)"
 SEED_MODEL, SEED_INPUT = 0, 1
-POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide, cc 7.x-10.x)
-FP32_PER_CLK_SM = 128       # fp32 add / fma results / clock / SM
+POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
+MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (probe-measured on this pool)
 
 
 def read_peaks():
@@ -189,6 +190,7 @@ def run_ours(args):
         return float(t.item())
 
     P, H, W = args.patches, args.H, args.W
+    bn.set_bconv_kernel(args.bconv)
     m = bn.Model(data=model_blob())
     m.set_devices([local])
     first = rank * P
@@ -222,7 +224,7 @@ def run_ours(args):
     clocks = clk.summary()
 
     # ---------------- end to end through the public host API ----------------
-    e2e_s, same = None, None
+    e2e_s, same, h2d_gbs = None, None, None
     if not args.no_e2e:
         hin = torch.empty((P, 120, H, W), dtype=torch.float32, pin_memory=True)
         hin.copy_(din.cpu())
@@ -238,6 +240,14 @@ def run_ours(args):
         barrier()
         # the two paths agree (same patches, same logits)
         same = bool(torch.equal(hout.view(torch.int32), dout.cpu().view(torch.int32)))
+        # the host link by itself: one pinned 2 GB host->device copy, CUDA events
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        din.copy_(hin, non_blocking=True)
+        c0.record()
+        din.copy_(hin, non_blocking=True)
+        c1.record()
+        torch.cuda.synchronize()
+        h2d_gbs = hin.numel() * 4 / (c0.elapsed_time(c1) * 1e6)
 
     if rank == 0:
         peaks = read_peaks()
@@ -249,14 +259,19 @@ def run_ours(args):
             o = by_op.setdefault(r["op"], {"ms": 0.0, "work": 0.0, "calls": 0})
             o["ms"] += r["ms"]; o["work"] += r["work"]; o["calls"] += r["calls"]
         total_ms = sum(o["ms"] for o in by_op.values())
-        popc_peak = sms * POPC_PER_CLK_SM * 32 * max_mhz * 1e6 / 1e9     # Gbitop/s
-        fp32_peak = sms * FP32_PER_CLK_SM * max_mhz * 1e6 / 1e9         # G fp32 op/s
+        clk = max_mhz * 1e6
+        popc_peak = sms * POPC_PER_CLK_SM * 32 * clk / 1e9              # G bitMAC/s
+        mma_sync_peak = sms * MMA_SYNC_I8_PER_CLK_SM * clk / 1e9         # G int8 MAC/s, legacy path
+        bf16 = peaks.get("bf16_tflops")
+        tensor_i8_peak = bf16 * 1e3 if bf16 else 2.25e6                  # G int8 MAC/s = 2x bf16 MAC rate
         b = by_op.get("bconv", {"ms": 1e-9, "work": 0})
         r_ = by_op.get("conv_real", {"ms": 1e-9, "work": 0})
-        bconv_ach = b["work"] / (b["ms"] * 1e6)   # work in bitMAC (Cout*H*W*Cin*9), ms -> Gbitop/s
-        real_ach = r_["work"] / (r_["ms"] * 1e6)  # fp32 adds (Cout*H*W*Cin*9)
+        bconv_ach = b["work"] / (b["ms"] * 1e6)   # work = Cout*H*W*Cin*9 binary MACs (reference PROF unit)
+        # first conv: int8 MACs the tensor cores execute (3 planes x 128 padded bands)
+        real_macs = 3 * 128 / 120 * r_["work"]
+        real_ach = real_macs / (r_["ms"] * 1e6)
         launches_per_fwd = m.launches(P, H, W)
-        chunks = -(-P // 512)
+        chunks = -(-P // 256)
         value = P * world * args.steps / (dev_ms / 1e3)
         e2e = P * world * args.steps / e2e_s if e2e_s else None
         model, cores = cpu_info()
@@ -287,16 +302,33 @@ def run_ours(args):
             "e2e": {"value": round(e2e, 1) if e2e else None, "unit": "patches/s",
                     "h2d_bytes_per_step": P * 120 * H * W * 4,
                     "d2h_bytes_per_step": P * 3 * H * W * 4, "api": "bnn_forward_batch (pinned host buffers)",
-                    "matches_device_path": same},
+                    "matches_device_path": same,
+                    "h2d_link_gbs": round(h2d_gbs, 2) if h2d_gbs else None,
+                    "frac_of_h2d_link": round(e2e * P * 120 * H * W * 4 / P / (h2d_gbs * 1e9), 4)
+                    if (e2e and h2d_gbs) else None},
             "gpu_launches": launches_per_fwd * args.steps * (1 + (0 if args.no_e2e else chunks)),
-            "roofline": {"bound": "popc", "kernel": "bconv3x3 (17 fused binary convs)",
-                         "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
-                         "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
-                         "peak_source": f"nominal: {sms} SMs x {POPC_PER_CLK_SM} POPC/clk x 32 bit x {max_mhz:.0f} MHz",
-                         "time_share": frac_split.get("bconv")},
+            "roofline": (
+                {"bound": "tensor", "kernel": "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
+                 "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
+                 "unit": "Gbitop/s (1 bitop = 1 binary MAC, run as one int8 MAC)",
+                 "frac": round(bconv_ach / tensor_i8_peak, 4), "traffic": None,
+                 "peak_source": "int8 dense tensor rate = 2x the measured cuBLAS bf16 rate in MEASURED_PEAKS.json"
+                 if bf16 else "fallback 2.25 P int8 MAC/s",
+                 "frac_of_mma_sync_measured": round(bconv_ach / mma_sync_peak, 4),
+                 "time_share": frac_split.get("bconv")}
+                if args.bconv == "tc" else
+                {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
+                 "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
+                 "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
+                 "peak_source": f"nominal {sms} SMs x {POPC_PER_CLK_SM} POPC/clk x 32 bit x {max_mhz:.0f} MHz "
+                                "(probe: 15.6 POPC/clk/SM)",
+                 "time_share": frac_split.get("bconv")}),
             "rooflines": {
-                "conv_real": {"bound": "fp32", "achieved": round(real_ach, 1), "peak": round(fp32_peak, 1),
-                              "unit": "Gflop/s (fp32 add)", "frac": round(real_ach / fp32_peak, 4),
+                "conv_real": {"bound": "tensor", "kernel": "realin_mma_kernel + realin_fixup_kernel",
+                              "achieved": round(real_ach, 1), "peak": round(tensor_i8_peak, 1),
+                              "unit": "G int8 MAC/s executed (3 planes x 128 bands x 9 taps x 32 ch per pixel)",
+                              "frac": round(real_ach / tensor_i8_peak, 4),
+                              "frac_of_mma_sync_measured": round(real_ach / mma_sync_peak, 4),
                               "time_share": frac_split.get("conv_real")},
                 "hbm_input": {"bytes_per_step": P * 120 * H * W * 4, "peak_gbs": peaks.get("hbm_gbs"),
                               "min_ms": round(P * 120 * H * W * 4 / (peaks.get("hbm_gbs", 6538.9) * 1e6), 4)},
@@ -323,6 +355,8 @@ def main():
     ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
+    ap.add_argument("--bconv", default="tc", choices=["tc", "popc"],
+                    help="binary-conv kernel: int8 tensor cores (default) or XOR + POPC")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

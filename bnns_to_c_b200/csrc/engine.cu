@@ -113,7 +113,7 @@ struct Engine {
     std::mutex mu;
     std::map<int, std::unique_ptr<DevState>> devs;
     std::vector<int> devices;  // empty: current device
-    int chunk = 512;
+    int chunk = 256;
     Profiler prof;
 };
 

@@ -68,7 +68,7 @@ int bnn_set_bconv_kernel(int kind);
 int bnn_set_devices(Model *m, const int *devices, int n);
 int bnn_get_devices(const Model *m, int *devices, int cap);
 
-/* Patches per pipelined chunk in bnn_forward_batch (default 512). */
+/* Patches per pipelined chunk in bnn_forward_batch (default 256). */
 int bnn_set_chunk(Model *m, int patches);
 
 /* Debug / parity: one patch on the current device, every intermediate
