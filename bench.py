@@ -307,8 +307,12 @@ def run_ours(args):
                     "frac_of_h2d_link": round(e2e * P * 120 * H * W * 4 / P / (h2d_gbs * 1e9), 4)
                     if (e2e and h2d_gbs) else None},
             "gpu_launches": launches_per_fwd * args.steps * (1 + (0 if args.no_e2e else chunks)),
+            "device_wait_timeouts": bn.device_wait_timeouts(local),
             "roofline": (
-                {"bound": "tensor", "kernel": "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
+                {"bound": "tensor",
+                 "kernel": ("bconv_umma_kernel (tcgen05 int8, non-pooled binary convs) + bconv_mma_kernel "
+                            "(int8 mma.sync, pooled encoder convs)") if args.bconv == "tc" else
+                           "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
                  "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
                  "unit": "Gbitop/s (1 bitop = 1 binary MAC, run as one int8 MAC)",
                  "frac": round(bconv_ach / tensor_i8_peak, 4), "traffic": None,
@@ -316,7 +320,7 @@ def run_ours(args):
                  if bf16 else "fallback 2.25 P int8 MAC/s",
                  "frac_of_mma_sync_measured": round(bconv_ach / mma_sync_peak, 4),
                  "time_share": frac_split.get("bconv")}
-                if args.bconv == "tc" else
+                if args.bconv in ("tc", "mma") else
                 {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
                  "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
                  "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
@@ -355,8 +359,9 @@ def main():
     ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
-    ap.add_argument("--bconv", default="tc", choices=["tc", "popc"],
-                    help="binary-conv kernel: int8 tensor cores (default) or XOR + POPC")
+    ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
+                    help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
+                         "mma = mma.sync for every layer")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -87,6 +87,7 @@ def lib():
         "bnn_unpack_act_device": (ip, [vp, ip, ip, ip, ip, vp, vp]),
         "bnn_forward_launches": (ip, [vp, ip, ip, ip]),
         "bnn_set_bconv_kernel": (ip, [ip]),
+        "bnn_device_error": (ip, [ip, ctypes.POINTER(ctypes.c_uint)]),
         "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
     }
     for name, (res, args) in sig.items():
@@ -284,8 +285,15 @@ class BconvLayer:
 
 
 def set_bconv_kernel(kind: str):
-    """'tc' (int8 tensor cores, default) or 'popc' (XOR + POPC)."""
-    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1}[kind]))
+    """'tc' (tcgen05 + mma.sync, default), 'popc' (XOR + POPC) or 'mma'
+    (mma.sync for every layer)."""
+    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2}[kind]))
+
+
+def device_wait_timeouts(device=0):
+    n = ctypes.c_uint()
+    _check(lib().bnn_device_error(device, ctypes.byref(n)))
+    return n.value
 
 
 def synth_device(device, seed, first, n, bands, H, W, d_out, stream=None):

@@ -44,7 +44,9 @@ struct BinLayer {
     int Cin, Cout, CoutP, cw0, cw1, Kw, sC;  // sC: channels from the first source
     uint32_t* wt = nullptr;
     int* wpop = nullptr;
-    int8_t* w8 = nullptr;     // tensor-core kernel weights [Kw][9][CoutP][32]
+    int8_t* w8 = nullptr;     // mma.sync kernel weights [Kw][9][CoutP][32]
+    int8_t* wu = nullptr;     // tcgen05 kernel weights [Cout/ubn][Kw][9][2][ubn][16]
+    int ubn = 0;              // tcgen05 channel block (N of one MMA)
     FoldIv* fold = nullptr;
     FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
 };
@@ -169,10 +171,14 @@ static FoldIv to_iv(int type, int t, int lo, int hi) {
 
 struct HostBin {
     std::vector<uint32_t> wt;
-    std::vector<int8_t> w8;
+    std::vector<int8_t> w8, wu;
     std::vector<int> wpop;
     std::vector<FoldIv> fold, fold2;
 };
+
+// tcgen05 channel block for a layer of Cout channels: the whole layer up to
+// 256 channels (N of one MMA), 256-channel blocks beyond
+static int ws_bn(int Cout) { return Cout <= 32 ? 32 : Cout <= 64 ? 64 : Cout <= 128 ? 128 : 256; }
 
 // kidx-ordered uint64 rows (bit (ci*9+t)) -> [CoutP][9][Kw] with the first
 // sC channels in words [0, cw0) and the rest in words [cw0, cw0+cw1).
@@ -202,6 +208,18 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
             }
         }
     }
+    // tcgen05 blocks: per (channel block, word) the 9 taps' B operands in the
+    // order the kernel stages them ([tap][16-byte K half][channel][16 bytes])
+    const int bn = ws_bn(Cout), ncb = cdiv(Cout, bn);
+    L.ubn = bn;
+    h.wu.assign((size_t)ncb * L.Kw * 9 * 2 * bn * 16, (int8_t)0);
+    for (int cb = 0; cb < ncb; ++cb)
+        for (int kw = 0; kw < L.Kw; ++kw)
+            for (int t = 0; t < 9; ++t)
+                for (int hh = 0; hh < 2; ++hh)
+                    for (int c = 0; c < bn && cb * bn + c < Cout; ++c)
+                        memcpy(&h.wu[((((size_t)cb * L.Kw + kw) * 9 + t) * 2 + hh) * bn * 16 + (size_t)c * 16],
+                               &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32 + hh * 16], 16);
 }
 
 static void folds_of(const Act* a, int CoutP, std::vector<FoldIv>& v) {
@@ -217,6 +235,11 @@ template <int BN, int TM, int TN, int KC>
 static cudaError_t attr_bconv() {
     return cudaFuncSetAttribute(bconv3x3_kernel<BN, TM, TN, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)BconvCfg<BN, TM, TN, KC>::smem_bytes(512));
+}
+template <int BN, int MT>
+static cudaError_t attr_ws() {
+    return cudaFuncSetAttribute(bconv_ws_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)WsCfg<BN, MT>::max_smem);
 }
 template <int BN>
 static cudaError_t attr_bmma() {
@@ -240,6 +263,8 @@ static int set_kernel_attrs(int device) {
     if ((e = attr_bconv_kc<32, 4, 4>()) != cudaSuccess || (e = attr_bconv_kc<64, 8, 4>()) != cudaSuccess ||
         (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess || (e = attr_bmma<32>()) != cudaSuccess ||
         (e = attr_bmma<64>()) != cudaSuccess || (e = attr_bmma<128>()) != cudaSuccess ||
+        (e = attr_ws<32, 8>()) != cudaSuccess || (e = attr_ws<64, 4>()) != cudaSuccess ||
+        (e = attr_ws<128, 2>()) != cudaSuccess || (e = attr_ws<256, 1>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -330,7 +355,8 @@ static int dev_init(const Model* m, DevState* d) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
-        total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wpop.size() * 4) +
+        total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wu.size()) +
+                 align256(it.h.wpop.size() * 4) +
                  align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
     }
     const size_t hw = (size_t)m->head_Cout * m->head_Cin;
@@ -355,6 +381,7 @@ static int dev_init(const Model* m, DevState* d) {
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
+        it.L->wu = (int8_t*)put(it.h.wu.data(), it.h.wu.size());
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
         it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
         it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -473,7 +500,8 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
 // -------------------------------------------------------------------
 // launchers
 // -------------------------------------------------------------------
-// binary conv implementation: 0 = int8 tensor cores (default), 1 = XOR/POPC
+// binary conv implementation: 0 = tcgen05 for non-pooled layers and mma.sync
+// for pooled ones (default), 1 = XOR/POPC, 2 = mma.sync for every layer
 static int g_bconv_kind = 0;
 
 struct TileGeo {
@@ -539,8 +567,59 @@ static int launch_bmma(BconvParams p, int N, cudaStream_t st) {
 }
 
 
+static int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+// persistent tcgen05 kernel on the padded grid (non-pooled layers); returns
+// BNN_ERR_UNSUPPORTED (and launches nothing) when the staging does not fit
+template <int BN, int MT>
+static int launch_ws(BconvParams p, int N, cudaStream_t st) {
+    using Cfg = WsCfg<BN, MT>;
+    const long gk = std::max(1, 64 / (p.W + 1));
+    const long Gw = gk * (p.W + 1) + 1;
+    const long rows = (long)cdiv(N, gk) * (p.H + 1) + 1;
+    const long ptot = (rows - 2) * Gw;  // output positions: grid rows 1 .. rows-2
+    const long sp = ((Cfg::PI + 2 * Gw + 2) + 7) & ~7L;
+    const long groups = (ptot + Cfg::PI - 1) / Cfg::PI;
+    const long ncb = cdiv(p.Cout, BN);
+    if (sp > Cfg::MAX_SP || groups * Cfg::PI + 2 * Gw + 2 >= (1L << 31) || groups * ncb >= (1L << 31))
+        return BNN_ERR_UNSUPPORTED;
+    const int ns = Cfg::stages((int)sp, (int)Gw, p.Cout);
+    if (ns < 2) return BNN_ERR_UNSUPPORTED;
+    p.gk = (int)gk; p.Gw = (int)Gw; p.HP = (int)sp;
+    p.TR = (int)(groups * ncb); p.TC = (int)ncb; p.TNI = ns;
+    // one CTA per SM (it allocates all of TMEM): never less than 116 KB
+    const size_t smem = std::max<size_t>(
+        (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
+    const int grid = (int)std::min<long>(groups * ncb, sm_count());
+    bconv_ws_kernel<BN, MT><<<grid, Cfg::NT, smem, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
-    if (g_bconv_kind == 0) {
+    if (g_bconv_kind == 0 && !p.out2 && p.wu) {
+        int rc = BNN_ERR_UNSUPPORTED;
+        switch (p.ubn) {
+            case 32: rc = launch_ws<32, 8>(p, N, st); break;
+            case 64: rc = launch_ws<64, 4>(p, N, st); break;
+            case 128: rc = launch_ws<128, 2>(p, N, st); break;
+            case 256: rc = launch_ws<256, 1>(p, N, st); break;
+        }
+        if (rc != BNN_ERR_UNSUPPORTED) return rc;
+    }
+    if (g_bconv_kind == 0 || g_bconv_kind == 2) {
         if (p.Cout <= 32) return launch_bmma<32>(p, N, st);
         if (p.Cout <= 64) return launch_bmma<64>(p, N, st);
         return launch_bmma<128>(p, N, st);
@@ -566,7 +645,8 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     p.cW = std::min(upW, W);
     p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
     p.wt = L.wt; p.wpop = L.wpop; p.w8 = L.w8; p.CoutP = L.CoutP; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
-    if ((g_bconv_kind == 0 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
+    p.wu = L.wu; p.ubn = L.ubn;
+    if ((g_bconv_kind != 1 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
         return set_error(BNN_ERR_ARG, "binary conv layer has no weights for the selected kernel");
     p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
     return launch_bconv(p, N, st);
@@ -990,8 +1070,20 @@ BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float
 }
 
 BNN_API int bnn_set_bconv_kernel(int kind) {
-    if (kind != 0 && kind != 1) return set_error(BNN_ERR_ARG, "bconv kernel kind %d (0 = tensor core, 1 = popc)", kind);
+    if (kind < 0 || kind > 2)
+        return set_error(BNN_ERR_ARG, "bconv kernel kind %d (0 = tcgen05 + mma.sync, 1 = popc, 2 = mma.sync)", kind);
     g_bconv_kind = kind;
+    return BNN_OK;
+}
+
+BNN_API int bnn_device_error(int device, unsigned int* wait_timeouts) {
+    if (!wait_timeouts) return set_error(BNN_ERR_ARG, "NULL argument");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(device));
+    cudaError_t e = cudaMemcpyFromSymbol(wait_timeouts, g_bnn_wait_timeouts, sizeof(unsigned int));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "read device error counter: %s", cudaGetErrorString(e));
     return BNN_OK;
 }
 
@@ -1299,7 +1391,8 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         Act a2{0, Cout, (int32_t*)ptype, (int32_t*)pt, (int32_t*)plo, (int32_t*)phi, nullptr, nullptr, nullptr, nullptr};
         folds_of(&a2, Lh->L.CoutP, h.fold2);
     }
-    size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wpop.size() * 4) +
+    size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wu.size()) +
+                   align256(h.wpop.size() * 4) +
                    2 * align256(h.fold.size() * sizeof(FoldIv));
     if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
@@ -1316,6 +1409,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     };
     Lh->L.wt = (uint32_t*)put(h.wt.data(), h.wt.size() * 4);
     Lh->L.w8 = (int8_t*)put(h.w8.data(), h.w8.size());
+    Lh->L.wu = (int8_t*)put(h.wu.data(), h.wu.size());
     Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
     Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
     Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;

@@ -51,8 +51,15 @@ struct BconvParams {
     int32_t* P2;          // debug: [N][Cout][H/2][W/2] or nullptr
     int TR, TC, TNI;      // tile: rows, cols, whole images per tile
     int tiles_x, tiles_y; // tiles per image (TNI == 1)
-    int HP;               // halo pixels = TNI*(TR+2)*(TC+2)
+    int HP;               // halo pixels = TNI*(TR+2)*(TC+2) (tcgen05 kernel: staged grid positions)
+    int gk, Gw;           // tcgen05 kernel: images per grid row, grid width
+    const int8_t* wu;     // tcgen05 kernel weights [Cout/BN][Kw][9][2][BN][16]
+    int ubn;              // BN of wu
 };
+
+// set by a kernel whose bounded wait on an mbarrier gave up (never expected;
+// read by bnn_device_error)
+__device__ unsigned int g_bnn_wait_timeouts = 0;
 
 template <int KC>
 struct KcTraits {
@@ -1009,6 +1016,437 @@ __global__ void __launch_bounds__(BmmaCfg<BN>::NT, 512 / BmmaCfg<BN>::NT) bconv_
             }
     __syncthreads();
     bconv_store_epilogue<BN, BM, PSP, NT>(p, Ps, fs, fs2, n0, y0, x0, TRC, cout0, tid);
+}
+
+// ---------------------------------------------------------------------
+// Fused binary 3x3 conv on tcgen05 (kind::i8, accumulators in TMEM),
+// persistent and warp-specialised.
+//
+// Padded grid: the batch is laid out as a grid of images, gk per grid row,
+// separated by single rows and columns of zeros (one more row and column of
+// zeros around the edge): grid width Gw = gk*(W+1) + 1, image n pixel (y, x)
+// at grid row 1 + (n/gk)*(H+1) + y, column 1 + (n%gk)*(W+1) + x. An output at
+// grid position p reads p + (dy-1)*Gw + (dx-1) for tap (dy, dx), and grid
+// positions that are not image pixels are zeros, so with the staged positions
+// stored consecutively ([k half][position][16 bytes]) every tap's A operand
+// of 128 consecutive positions is one shared-memory descriptor shifted by
+// (dy*Gw + dx)*16 bytes: the im2col is free. The MMAs compute every grid
+// position; only image pixels are stored.
+//
+// Work item: MT tiles of 128 consecutive output positions x BN output
+// channels (one channel block); items are dealt round-robin to one CTA per
+// SM. K runs over 32-channel words; one pipeline stage holds one word of an
+// item: A = the int8 expansion of the item's PI + 2*Gw + 2 staged positions,
+// B = the word's weights for the 9 taps (one bulk copy of a block laid out
+// for it at load time). Roles:
+//   warps 4-7  producers: gather the input words of the staged positions
+//              (the skip tensor or, for the concat's upper words, the
+//              half-res tensor), expand bits to +-1 bytes, fill the stage;
+//   warp 8     allocates TMEM; one lane issues MT*9 MMAs per stage and
+//              commits them to the stage's "empty" barrier, and to the
+//              accumulator's "full" barrier after an item's last word;
+//   warps 0-3  epilogue: TMEM -> registers (warp w reads lanes 32w..32w+31),
+//              integer fold, bit pack, store; then free the accumulator.
+// TMEM holds NBUF = 512/(BN*MT) accumulators, so the epilogue of one item
+// overlaps the MMAs of the next. Non-pooled layers only (a 2x2 pool quad can
+// straddle items). Every wait is bounded; a wait that gives up aborts the
+// whole CTA (all later waits return at once) and bumps g_bnn_wait_timeouts.
+// ---------------------------------------------------------------------
+template <int BN, int MT>
+struct WsCfg {
+    static constexpr int NBUF = 512 / (BN * MT);
+    static constexpr int PI = 128 * MT;  // output positions per item
+    static constexpr int NEPI = 256;     // warps 0-7: epilogue (two per TMEM lane quarter)
+    static constexpr int NPROD = 224;     // warps 8-14: producers
+    static constexpr int NT = 512;       // + warp 15: TMEM allocation and MMA issue
+    static constexpr int MAX_SP = PI + 648;  // Gw up to 320
+    static constexpr int NQ = (MAX_SP + NPROD - 1) / NPROD;  // staged positions per producer thread
+    static constexpr size_t b_bytes = (size_t)9 * 2 * BN * 16;
+    static constexpr size_t max_smem = (size_t)224 * 1024;  // dynamic; ~0.3 KB static besides
+    __host__ __device__ static size_t a_bytes(int SP) { return (size_t)2 * SP * 16; }
+    __host__ __device__ static size_t stage_bytes(int SP) { return (a_bytes(SP) + b_bytes + 127) & ~(size_t)127; }
+    // (lo, span) per channel, channels rounded up to 32, + the inverted-fold masks
+    __host__ __device__ static size_t fold_bytes(int Cout) {
+        return (size_t)((Cout + 31) & ~31) * sizeof(int2) + (size_t)((Cout + 31) / 32) * 4;
+    }
+    // two pixel tables (current and next item) + the column table + folds
+    __host__ __device__ static size_t fixed_bytes(int SP, int Gw, int Cout) {
+        return (size_t)2 * SP * sizeof(int2) + (((size_t)Gw * 4 + 15) & ~(size_t)15) + fold_bytes(Cout);
+    }
+    static int stages(int SP, int Gw, int Cout) {
+        const size_t n = (max_smem - fixed_bytes(SP, Gw, Cout)) / stage_bytes(SP);
+        return n > 8 ? 8 : (int)n;
+    }
+    static_assert(NBUF == 1 || NBUF == 2, "TMEM holds one or two accumulators");
+};
+
+__device__ __forceinline__ void tc_alloc(uint32_t smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_dst), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+// D[tmem] (+)= A(smem desc) x B(smem desc), int8 x int8 -> int32
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    const uint32_t z = 0u;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar)
+                 : "memory");
+}
+// 32 consecutive TMEM columns of this thread's lane
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// K-major, no swizzle: 8-row core matrices of 16-byte rows, rows 16 bytes
+// apart (SBO = 128 bytes between 8-row groups), LBO between the two 16-byte
+// halves of the 32-byte K step
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+// expect `bytes` of transactions on the current phase without arriving
+__device__ __forceinline__ void mbar_expect_tx_only(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// plain (non-tensor, non-multicast) bulk copy global -> this CTA's shared memory
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// bounded wait that also gives up at once when the CTA has aborted; a wait
+// that runs out sets the abort flag
+__device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    for (int it = 0; it < (1 << 22); ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((it & 255) == 255 && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    return false;
+}
+
+// Walks grid positions in steps of a fixed stride without divisions: row gr,
+// column gc, image-block row ib and row yy within it (gr = 1 + ib*(H+1) + yy).
+// colmap[gc] = (image slot << 16) | x for image columns, -1 for separators.
+struct GridWalk {
+    int gr, gc, ib, yy;
+    int sa, sb;  // stride = sa*Gw + sb, 0 <= sb < Gw
+    __device__ __forceinline__ void init(const BconvParams& p, int pos, int stride) {
+        // pos >= -1: position -1 sits in row -1
+        gr = pos >= 0 ? pos / p.Gw : -1;
+        gc = pos - gr * p.Gw;
+        const int rr = gr - 1;
+        ib = rr >= 0 ? rr / (p.H + 1) : -1;
+        yy = rr - ib * (p.H + 1);
+        sa = stride / p.Gw;
+        sb = stride - sa * p.Gw;
+    }
+    __device__ __forceinline__ void step(const BconvParams& p) {
+        gc += sb;
+        int d = sa;
+        if (gc >= p.Gw) { gc -= p.Gw; ++d; }
+        gr += d;
+        yy += d;
+        while (yy > p.H) { yy -= p.H + 1; ++ib; }
+    }
+    // pixel index (n*H + y)*W + x, or -1 for a zero position
+    __device__ __forceinline__ int pixel(const BconvParams& p, const int* colmap, int& n, int& x) const {
+        if (ib < 0 || yy >= p.H) return -1;
+        const int cm = colmap[gc];
+        if (cm < 0) return -1;
+        n = ib * p.gk + (cm >> 16);
+        if (n >= p.N) return -1;
+        x = cm & 0xFFFF;
+        return (n * p.H + yy) * p.W + x;
+    }
+};
+
+// p.HP = staged positions per item (SP); p.TR = items; p.TC = channel blocks;
+// p.TNI = pipeline stages
+template <int BN, int MT>
+__global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
+    using C = WsCfg<BN, MT>;
+    constexpr int NBUF = C::NBUF, PI = C::PI, NQ = C::NQ, NPROD = C::NPROD, NEPI = C::NEPI;
+    constexpr int NCH = BN / 32, NPAIR = MT * NCH;  // epilogue units: (tile, 32-column chunk)
+    extern __shared__ __align__(1024) unsigned char ws_smem[];
+    __shared__ __align__(8) unsigned long long full_b[8], empty_b[8], accf_b[2], acce_b[2];
+    __shared__ uint32_t tmem_s;
+    __shared__ uint32_t lut[16];
+    __shared__ int abort_s;
+    volatile int* abort_v = &abort_s;
+
+    const int SP = p.HP, n_items = p.TR, ncb = p.TC, NS = p.TNI;
+    const size_t SB = C::stage_bytes(SP);
+    int2* pxu = reinterpret_cast<int2*>(ws_smem + (size_t)NS * SB);  // [2][SP] (pixel, upsampled pixel)
+    int* colmap = reinterpret_cast<int*>(pxu + 2 * SP);              // [Gw]
+    // folds as (lo, span): lo <= P < hi  <=>  (unsigned)(P - lo) < span;
+    // the inverted folds as one bit mask per 32 channels
+    const int CoutR = (p.Cout + 31) & ~31;
+    int2* fu = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(colmap) + ((p.Gw * 4 + 15) & ~15));
+    uint32_t* finv = reinterpret_cast<uint32_t*>(fu + CoutR);  // [CoutR/32]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 15) {
+        tc_alloc(smem_u32(&tmem_s), 512);
+        tc_relinquish();
+    }
+    if (tid == 0) {
+        abort_s = 0;
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_b[s]), NPROD);
+            mbar_init(smem_u32(&empty_b[s]), 1);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(smem_u32(&accf_b[b]), 1);
+            mbar_init(smem_u32(&acce_b[b]), NEPI);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (tid < 16) {
+        const uint32_t x = ((uint32_t)tid * 0x00204081u) & 0x01010101u;
+        lut[tid] = 0xFFFFFFFFu ^ (x * 0xFEu);
+    }
+    for (int c = tid; c < p.Gw; c += C::NT) {
+        int cm = -1;
+        if (c > 0) {
+            const int jb = (c - 1) / (p.W + 1), xx = (c - 1) - jb * (p.W + 1);
+            if (xx < p.W && jb < p.gk) cm = (jb << 16) | xx;
+        }
+        colmap[c] = cm;
+    }
+    for (int c = tid; c < CoutR; c += C::NT) {
+        int2 e = make_int2(0, 0);  // channels past Cout: never set (masked off anyway)
+        if (c < p.Cout) {
+            const FoldIv f = p.fold[c];
+            e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
+        }
+        fu[c] = e;
+    }
+    for (int w = tid; w < CoutR / 32; w += C::NT) {
+        uint32_t m = 0u;
+        for (int i = 0; i < 32 && w * 32 + i < p.Cout; ++i) m |= (uint32_t)(p.fold[w * 32 + i].inv & 1) << i;
+        finv[w] = m;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    const uint32_t sm0 = smem_u32(ws_smem);
+
+    if (warp >= 8 && warp < 15) {
+        // ------------------------------------------------------------ producers
+        const int pt = tid - NEPI;
+        // map the staged positions q = pt + NPROD*j of `item` into table `tb`
+        auto map_item = [&](int item, int2* tb) {
+            const int pg = item / ncb;
+            GridWalk g;
+            g.init(p, pg * PI - 1 + pt, NPROD);  // staged position 0 = first output - Gw - 1
+            for (int q = pt; q < SP; q += NPROD, g.step(p)) {
+                int n = 0, x = 0, up = -1;
+                const int px = g.pixel(p, colmap, n, x);
+                if (px >= 0 && p.cw1 > 0) {
+                    const int uy = g.yy - p.oh, ux = x - p.ow;
+                    if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
+                        up = (n * p.h1 + (uy >> 1)) * p.w1 + (ux >> 1);
+                }
+                tb[q] = make_int2(px, up);
+            }
+        };
+        auto load_words = [&](const int2* tb, int kw, uint32_t* v) {
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                const int q = pt + NPROD * j;
+                v[j] = 0u;
+                if (q < SP) {
+                    const int2 e = tb[q];
+                    if (e.x >= 0) {
+                        if (kw < p.cw0) v[j] = __ldg(p.in0 + (size_t)e.x * p.cw0 + kw);
+                        else if (e.y >= 0) v[j] = __ldg(p.in1 + (size_t)e.y * p.cw1 + (kw - p.cw0));
+                    }
+                }
+            }
+        };
+        int stage = 0, tb = 0;
+        uint32_t phase = 0;
+        int item = blockIdx.x;
+        uint32_t vn[NQ];
+        if (item < n_items) {
+            map_item(item, pxu);
+            load_words(pxu, 0, vn);
+        }
+        while (item < n_items && !*abort_v) {
+            const int cb = item % ncb;
+            const int2* cur = pxu + tb * SP;
+            bool ok = true;
+            for (int kw = 0; kw < p.Kw; ++kw) {
+                uint32_t v[NQ];
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) v[j] = vn[j];
+                // issue the next stage's loads before this stage's wait and stores
+                if (kw + 1 < p.Kw) {
+                    load_words(cur, kw + 1, vn);
+                } else if (item + (int)gridDim.x < n_items) {
+                    int2* nxt = pxu + (tb ^ 1) * SP;
+                    map_item(item + gridDim.x, nxt);
+                    load_words(nxt, 0, vn);
+                }
+                const uint32_t fb = smem_u32(&full_b[stage]);
+                if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
+                unsigned char* As = ws_smem + (size_t)stage * SB;
+                if (pt == 0) {
+                    mbar_expect_tx_only(fb, (uint32_t)C::b_bytes);
+                    bulk_g2s(sm0 + (uint32_t)(stage * SB + C::a_bytes(SP)),
+                             p.wu + ((size_t)cb * p.Kw + kw) * C::b_bytes, (uint32_t)C::b_bytes, fb);
+                }
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) {
+                    const int q = pt + NPROD * j;
+                    if (q < SP) {
+                        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                        if (cur[q].x >= 0) {  // an image pixel: +-1 (an uncovered concat word reads as -1)
+                            const uint32_t w = v[j];
+                            lo = make_uint4(lut[w & 15], lut[(w >> 4) & 15], lut[(w >> 8) & 15], lut[(w >> 12) & 15]);
+                            hi = make_uint4(lut[(w >> 16) & 15], lut[(w >> 20) & 15], lut[(w >> 24) & 15],
+                                            lut[w >> 28]);
+                        }
+                        *reinterpret_cast<uint4*>(As + (size_t)q * 16) = lo;
+                        *reinterpret_cast<uint4*>(As + ((size_t)SP + q) * 16) = hi;
+                    }
+                }
+                fence_async_smem();
+                mbar_arrive(fb);
+                if (++stage == NS) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            tb ^= 1;
+            item += gridDim.x;
+        }
+    } else if (warp == 15) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc =
+                (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((128u >> 4) << 24);
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+                const int buf = NBUF == 2 ? (it & 1) : 0;
+                const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+                if (!mbar_wait_ab(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, abort_v)) break;
+                tc_fence_after();
+                const uint32_t dcol = tmem + (uint32_t)(buf * BN * MT);
+                bool ok = true;
+                for (int kw = 0; kw < p.Kw; ++kw) {
+                    if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_s = sm0 + (uint32_t)(stage * SB), b_s = a_s + (uint32_t)C::a_bytes(SP);
+#pragma unroll 1
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int t = 0; t < 9; ++t) {
+                            const uint64_t ad =
+                                tc_desc(a_s + (uint32_t)(mt * 128 + (t / 3) * p.Gw + t % 3) * 16, (uint32_t)SP * 16);
+                            const uint64_t bd = tc_desc(b_s + (uint32_t)(t * 2 * BN * 16), BN * 16);
+                            tc_mma_i8(dcol + mt * BN, ad, bd, idesc, (kw > 0 || t > 0) ? 1u : 0u);
+                        }
+                    tc_commit(smem_u32(&empty_b[stage]));
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(smem_u32(&accf_b[buf]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // warp w reads TMEM lanes 32*(w%4).. and takes every other (tile, chunk)
+        const int quad = warp & 3, half = warp >> 2, r = quad * 32 + lane;
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+            const int buf = NBUF == 2 ? (it & 1) : 0;
+            const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+            const int cb = item % ncb, pg = item / ncb, cout0 = cb * BN;
+            if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
+            tc_fence_after();
+            GridWalk g;
+            g.init(p, p.Gw + pg * PI + r, 128);
+            int gmt = 0;
+#pragma unroll 1
+            for (int i = half; i < NPAIR; i += 2) {
+                const int mt = i / NCH, c0 = (i % NCH) * 32;
+                for (; gmt < mt; ++gmt) g.step(p);
+                uint32_t v[32];
+                tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN * MT + mt * BN + c0), v);
+                int n = 0, x = 0;
+                const int px = g.pixel(p, colmap, n, x);
+                if (px >= 0 && cout0 + c0 < p.Cout) {
+                    const int cw = (cout0 + c0) >> 5, lim = p.Cout - cout0 - c0;
+                    const int2* f = fu + cout0 + c0;
+                    uint32_t bits = 0u;
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        bits |= (uint32_t)((unsigned)((int)v[k] - f[k].x) < (unsigned)f[k].y) << k;
+                    bits ^= finv[cw];
+                    if (lim < 32) bits &= (1u << lim) - 1u;
+                    p.out[(size_t)px * p.cwo + cw] = bits;
+                    if (p.P) {  // debug: the accumulators themselves, [N][Cout][H][W]
+                        int* Pp = p.P + (((size_t)n * p.Cout + cout0 + c0) * p.H + g.yy) * p.W + x;
+                        const int hw = p.H * p.W;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k)
+                            if (k < lim) Pp[(size_t)k * hw] = (int)v[k];
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce_b[buf]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
+        // let any MMA or bulk copy still in flight land before TMEM and shared
+        // memory are released (bounded; the result is flagged as untrustworthy)
+        for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
+        if (tid == 0) atomicAdd(&g_bnn_wait_timeouts, 1u);
+    }
+    if (warp == 15) {
+        tc_fence_after();
+        tc_dealloc(tmem, 512);
+    }
 }
 
 // ---------------------------------------------------------------------

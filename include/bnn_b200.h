@@ -58,10 +58,18 @@ int bnn_forward_device(const Model *m, int device, const float *d_input, int N,
                        int H, int W, float *d_logits, void *stream);
 
 /* Process-wide choice of the binary-conv kernel, for measurement and A/B
- * parity tests: 0 = int8 tensor cores (mma.sync, default), 1 = XOR + POPC on
- * the integer pipe. Both compute the reference's P exactly; set it before
- * the forwards to compare (captured graphs keep the kernel they captured). */
+ * parity tests: 0 = tcgen05 int8 MMAs for the non-pooled layers and
+ * mma.sync int8 for the pooled encoder convs (default), 1 = XOR + POPC on
+ * the integer pipe, 2 = mma.sync int8 for every layer. All compute the
+ * reference's P exactly; set it before the forwards to compare (captured
+ * graphs keep the kernels they captured). */
 int bnn_set_bconv_kernel(int kind);
+
+/* Number of bounded device-side waits (mbarriers of the TMA / tcgen05
+ * pipelines) that gave up on `device` since the library was loaded; a
+ * non-zero count means some output of those launches is not to be trusted.
+ * Expected to stay 0. */
+int bnn_device_error(int device, unsigned int *wait_timeouts);
 
 /* Devices used by bnn_forward_batch, in shard order. n = 0 restores the
  * default: the calling thread's current device. */
