@@ -191,6 +191,7 @@ def run_ours(args):
 
     P, H, W = args.patches, args.H, args.W
     bn.set_bconv_kernel(args.bconv)
+    bn.set_first_conv_kernel(args.first)
     m = bn.Model(data=model_blob())
     m.set_devices([local])
     first = rank * P
@@ -328,7 +329,9 @@ def run_ours(args):
                                 "(probe: 15.6 POPC/clk/SM)",
                  "time_share": frac_split.get("bconv")}),
             "rooflines": {
-                "conv_real": {"bound": "tensor", "kernel": "realin_mma_kernel + realin_fixup_kernel",
+                "conv_real": {"bound": "tensor",
+                              "kernel": ("realin_ws_kernel (tcgen05)" if args.first == "tc" else
+                                         "realin_mma_kernel (mma.sync)") + " + realin_fixup_kernel",
                               "achieved": round(real_ach, 1), "peak": round(tensor_i8_peak, 1),
                               "unit": "G int8 MAC/s executed (3 planes x 128 bands x 9 taps x 32 ch per pixel)",
                               "frac": round(real_ach / tensor_i8_peak, 4),
@@ -359,6 +362,8 @@ def main():
     ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
+    ap.add_argument("--first", default="tc", choices=["tc", "mma"],
+                    help="first conv kernel: tcgen05 (default) or mma.sync")
     ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
                          "mma = mma.sync for every layer")

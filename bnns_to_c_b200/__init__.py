@@ -88,6 +88,7 @@ def lib():
         "bnn_forward_launches": (ip, [vp, ip, ip, ip]),
         "bnn_set_bconv_kernel": (ip, [ip]),
         "bnn_device_error": (ip, [ip, ctypes.POINTER(ctypes.c_uint)]),
+        "bnn_set_first_conv_kernel": (ip, [ip]),
         "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
     }
     for name, (res, args) in sig.items():
@@ -288,6 +289,11 @@ def set_bconv_kernel(kind: str):
     """'tc' (tcgen05 + mma.sync, default), 'popc' (XOR + POPC) or 'mma'
     (mma.sync for every layer)."""
     _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2}[kind]))
+
+
+def set_first_conv_kernel(kind):
+    """'tc' (tcgen05, default) or 'mma' (mma.sync) for the first conv."""
+    _check(lib().bnn_set_first_conv_kernel({"tc": 0, "mma": 1}[kind]))
 
 
 def device_wait_timeouts(device=0):

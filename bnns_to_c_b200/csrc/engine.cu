@@ -11,6 +11,7 @@
 // The forward order is the reference's (csrc/bnn_model.c:150-253): 19
 // kernel launches (first conv, 17 fused binary convs, head).
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -96,6 +97,8 @@ struct DevState {
     int ri_CinP = 0, ri_CIP = 0;
     uint4* rm_wfrag = nullptr;  // first conv +-1 int8 weights in mma B-fragment order
     int* rm_exact = nullptr;    // per channel: fold not monotone -> exact path
+    int8_t* rw_wu = nullptr;    // first conv +-1 int8 weights for realin_ws_kernel (Cin <= 128, Cout <= 32)
+    RwThr* rw_thr = nullptr;    // first conv fold thresholds for realin_ws_kernel
     BinLayer enc1[4], enc2[4], bott1, bott2, dec1[4], dec2[4];
     float *head_W = nullptr, *head_b = nullptr;
     Arena ar;
@@ -268,10 +271,64 @@ static int set_kernel_attrs(int device) {
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
+            cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
             cudaSuccess)
         return set_error(BNN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     if (device >= 0 && device < 64) done[device] = true;
     return BNN_OK;
+}
+
+// The reference's real fold on one float accumulator, with the device's
+// operations and rounding (IEEE binary32, round to nearest, one fused
+// multiply-add).
+__attribute__((optimize("fp-contract=off"))) static int host_real_fold(float acc, const float* f) {
+    const float o = f[0] * acc;
+    float z = std::fmaf(f[1], o, f[2]);
+    if (z < 0.0f) z = f[3] * z;
+    return (z + f[4]) > 0.0f;
+}
+// finite floats <-> ordered integer keys (-0 and +0 share key 0)
+static int64_t float_key(float x) {
+    int32_t b;
+    memcpy(&b, &x, 4);
+    return b >= 0 ? (int64_t)b : -(int64_t)(b & 0x7fffffff);
+}
+static float key_float(int64_t k) {
+    const uint32_t b = k >= 0 ? (uint32_t)k : ((uint32_t)(-k) | 0x80000000u);
+    float x;
+    memcpy(&x, &b, 4);
+    return x;
+}
+
+// RwThr of one first-conv channel (f = alpha, A, B, slope, rsign): the fold
+// is monotone in the accumulator (the channel is not exact), so one
+// bisection over the ordered finite floats finds where it flips
+static RwThr fold_threshold(const float* f, bool exact) {
+    const long long BIG = 1ll << 62;
+    RwThr t{BIG, 1, exact ? 1 : 0};
+    if (exact) return t;
+    const int64_t klo = float_key(-FLT_MAX), khi = float_key(FLT_MAX);
+    const int flo = host_real_fold(-FLT_MAX, f), fhi = host_real_fold(FLT_MAX, f);
+    if (flo == fhi) {
+        t.C = flo ? -BIG : BIG;
+        return t;
+    }
+    int64_t a = klo, b = khi;  // f(a) = flo, f(b) = fhi
+    while (b - a > 1) {
+        const int64_t mid = a + (b - a) / 2;
+        if (host_real_fold(key_float(mid), f) == flo) a = mid;
+        else b = mid;
+    }
+    auto clamp = [&](double v) { return v >= (double)BIG ? BIG : v <= -(double)BIG ? -BIG : (long long)v; };
+    if (fhi) {  // increasing: 1 from tau = key_float(b) on
+        t.sgn = 1;
+        t.C = clamp(std::ceil((double)key_float(b) * 262144.0));
+    } else {    // decreasing: 1 up to tau = key_float(a)
+        t.sgn = -1;
+        t.C = -clamp(std::floor((double)key_float(a) * 262144.0));
+    }
+    return t;
 }
 
 // upload everything to device d (called with d->mu held, device current)
@@ -322,11 +379,29 @@ static int dev_init(const Model* m, DevState* d) {
                                 wfrag[((((size_t)g * 9 + t) * 4 + kk) * 32 + l) * 8 + nt * 2 + h] = word;
                             }
     }
+    // the same weights for realin_ws_kernel: [chunk][tap][16-band half][channel][16 bands]
+    std::vector<int8_t> rwu;
+    if (Cin <= RM_CINP && CoutR <= 32) {
+        rwu.assign(RW_WBYTES, (int8_t)0);
+        for (int kc = 0; kc < 4; ++kc)
+            for (int t = 0; t < 9; ++t)
+                for (int h = 0; h < 2; ++h)
+                    for (int co = 0; co < CoutR; ++co)
+                        for (int i = 0; i < 16; ++i) {
+                            const int ci = kc * 32 + h * 16 + i;
+                            if (ci < Cin)
+                                rwu[((((size_t)kc * 9 + t) * 2 + h) * 32 + co) * 16 + i] =
+                                    c1->wsign[((size_t)co * Cin + ci) * 9 + t] > 0 ? 1 : -1;
+                        }
+    }
+    std::vector<RwThr> rthr;
+    if (!rwu.empty()) rthr.assign(32, RwThr{1ll << 62, 1, 0});
     for (int co = 0; co < CoutR; ++co) {
         const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
         bool ok = v[3] >= 0.0f;
         for (float f : v) ok = ok && std::isfinite(f);
         rexact[co] = ok ? 0 : 1;
+        if (!rthr.empty()) rthr[co] = fold_threshold(v, !ok);
     }
     // binary convs
     struct Item {
@@ -350,7 +425,7 @@ static int dev_init(const Model* m, DevState* d) {
         items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
     }
     size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
-                   align256(rexact.size() * 4);
+                   align256(rexact.size() * 4) + align256(rwu.size()) + align256(rthr.size() * sizeof(RwThr));
     for (auto& it : items) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
         folds_of(it.a, it.L->CoutP, it.h.fold);
@@ -378,6 +453,8 @@ static int dev_init(const Model* m, DevState* d) {
     d->ri_fold = (float*)put(rfold.data(), rfold.size() * 4);
     d->rm_wfrag = (uint4*)put(wfrag.data(), wfrag.size() * 4);
     d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
+    d->rw_wu = rwu.empty() ? nullptr : (int8_t*)put(rwu.data(), rwu.size());
+    d->rw_thr = rthr.empty() ? nullptr : (RwThr*)put(rthr.data(), rthr.size() * sizeof(RwThr));
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
@@ -701,13 +778,14 @@ static EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// input [N][C][H][W] f32 as a 4-D TMA map with the (40, 6, 8, 1) box
-static bool first_conv_tmap(const float* x, int N, int C, int H, int W, CUtensorMap* tm) {
+// input [N][C][H][W] f32 as a 4-D TMA map with a (bx, by, bc, 1) box
+static bool first_conv_tmap(const float* x, int N, int C, int H, int W, CUtensorMap* tm, int bx = RM_BX,
+                            int by = RM_BY, int bc = RM_BC) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn || (W % 4) != 0 || ((uintptr_t)x & 15)) return false;
     const cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)C, (cuuint64_t)N};
     const cuuint64_t strides[3] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4, (cuuint64_t)C * H * W * 4};
-    const cuuint32_t box[4] = {RM_BX, RM_BY, RM_BC, 1};
+    const cuuint32_t box[4] = {(cuuint32_t)bx, (cuuint32_t)by, (cuuint32_t)bc, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -719,6 +797,28 @@ static bool first_conv_fast_ok(const Model* m, int N, int H, int W) {
            encode_tiled() != nullptr;
 }
 
+// first conv implementation: 0 = tcgen05 where the shape allows (default),
+// 1 = mma.sync
+static int g_first_kind = 0;
+
+// realin_ws_kernel geometry for (H, W); false if the shape does not fit it
+struct RwGeo {
+    int R, Wp, SP, NS;
+    size_t smem;
+};
+static bool rw_geometry(int H, int W, RwGeo* g) {
+    if ((W % 4) != 0 || W > RW_MT * 128 - 1) return false;
+    g->Wp = W + 1;
+    g->R = std::min(H, (RW_MT * 128 - W) / g->Wp + 1);  // every output row of the item inside the tiles
+    g->SP = (RW_MT * 128 + 2 * g->Wp + 2 + 7) & ~7;
+    if (g->R < 1 || g->SP > RW_MAX_SP || g->R + 2 > 256) return false;
+    const size_t fixed = rw_fixed_bytes(W, g->R, g->SP);
+    if (fixed + 2 * rw_stage_bytes(g->SP) > RW_MAX_SMEM) return false;
+    g->NS = (int)std::min<size_t>(4, (RW_MAX_SMEM - fixed) / rw_stage_bytes(g->SP));
+    g->smem = std::max<size_t>(fixed + (size_t)g->NS * rw_stage_bytes(g->SP), (size_t)116 * 1024);
+    return true;
+}
+
 // first conv -> bit plane: int8 tensor cores decided by the error bound, then
 // the exact fix-up of undecided outputs (a memset and 2 kernels)
 static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
@@ -726,6 +826,30 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     if (N <= 0) return BNN_OK;
     Arena& a = d->ar;
     CUtensorMap tm;
+    RwGeo geo;
+    const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
+    if (g_first_kind == 0 && d->rw_wu && d->rw_thr && Cout <= 32 && Cin <= RM_CINP && rw_geometry(H, W, &geo) &&
+        first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32)) {
+        CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
+        RealinWsParams p{};
+        p.wu = d->rw_wu; p.thr = d->rw_thr; p.out = out;
+        p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
+        p.N = N; p.Cin = Cin; p.H = H; p.W = W; p.Cout = Cout; p.cwo = cw_of(Cout);
+        p.R = geo.R; p.Wp = geo.Wp; p.SP = geo.SP; p.NS = geo.NS; p.KC = cdiv(Cin, 32);
+        p.ipi = cdiv(H, geo.R);
+        p.n_items = N * p.ipi;
+        p.c9 = first_conv_c9(Cin);
+        const int grid = std::min(p.n_items, sm_count());
+        realin_ws_kernel<<<grid, 512, geo.smem, st>>>(tm, p);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
+        RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
+                          Cout, p.cwo};
+        realin_fixup_kernel<<<148 * 4, 128, 0, st>>>(f);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
+        return BNN_OK;
+    }
     if (!first_conv_tmap(x, N, m->enc_conv1[0].Cin, H, W, &tm))
         return run_realin_exact(d, m, x, N, H, W, out, nullptr, st);
     CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
@@ -1073,6 +1197,13 @@ BNN_API int bnn_set_bconv_kernel(int kind) {
     if (kind < 0 || kind > 2)
         return set_error(BNN_ERR_ARG, "bconv kernel kind %d (0 = tcgen05 + mma.sync, 1 = popc, 2 = mma.sync)", kind);
     g_bconv_kind = kind;
+    return BNN_OK;
+}
+
+BNN_API int bnn_set_first_conv_kernel(int kind) {
+    if (kind != 0 && kind != 1)
+        return set_error(BNN_ERR_ARG, "first conv kernel kind %d (0 = tcgen05, 1 = mma.sync)", kind);
+    g_first_kind = kind;
     return BNN_OK;
 }
 

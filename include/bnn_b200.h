@@ -65,6 +65,12 @@ int bnn_forward_device(const Model *m, int device, const float *d_input, int N,
  * graphs keep the kernels they captured). */
 int bnn_set_bconv_kernel(int kind);
 
+/* Process-wide choice of the first conv's tensor-core kernel (A/B testing):
+ * 0 = tcgen05 (default; shapes it cannot stage fall back to 1), 1 = mma.sync.
+ * Both decide every output by the same error bound and fix up the rest in
+ * the reference's fp32 order, so both give the reference's bits. */
+int bnn_set_first_conv_kernel(int kind);
+
 /* Number of bounded device-side waits (mbarriers of the TMA / tcgen05
  * pipelines) that gave up on `device` since the library was loaded; a
  * non-zero count means some output of those launches is not to be trusted.

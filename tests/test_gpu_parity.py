@@ -258,6 +258,18 @@ def test_multi_device_shards_match_single():
 
 
 # ------------------------------------------------------------------ first conv: tensor-core path
+@pytest.fixture(params=["tc", "mma"])
+def first_kind(request):
+    """Both first-conv tensor-core kernels (tcgen05, mma.sync); no bounded
+    device wait may have given up while it ran."""
+    bn.set_first_conv_kernel(request.param)
+    before = bn.device_wait_timeouts(0)
+    yield request.param
+    bn.set_first_conv_kernel("tc")
+    torch.cuda.synchronize()
+    assert bn.device_wait_timeouts(0) == before
+
+
 def _first_conv_bits(m, x, exact):
     n, _, H, W = x.shape
     dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
@@ -268,8 +280,8 @@ def _first_conv_bits(m, x, exact):
     return bits.cpu().numpy(), und
 
 
-def _model(base=32, seed=0, mutate=None):
-    mdl = B.random_model(base, 120, 3, seed=seed, rules="baseline")
+def _model(base=32, seed=0, mutate=None, bands=120):
+    mdl = B.random_model(base, bands, 3, seed=seed, rules="baseline")
     if mutate:
         mutate(mdl)
     m = bn.Model(data=B.blob_bytes(mdl))
@@ -277,7 +289,7 @@ def _model(base=32, seed=0, mutate=None):
     return m
 
 
-def test_first_conv_tensor_path_matches_exact_order():
+def test_first_conv_tensor_path_matches_exact_order(first_kind):
     m = _model()
     x = synth(41, 0, 256, 120, 32, 32)
     fast, und = _first_conv_bits(m, x, False)
@@ -287,7 +299,7 @@ def test_first_conv_tensor_path_matches_exact_order():
     assert 0 <= und < outs // 500, und  # the error bound decides > 99.8% of the outputs
 
 
-def test_first_conv_fixup_exercised_near_threshold():
+def test_first_conv_fixup_exercised_near_threshold(first_kind):
     """Folds tuned so r sits near 0 for many outputs: many undecided,
     all resolved exactly."""
     x = synth(42, 0, 16, 120, 32, 32)
@@ -306,7 +318,7 @@ def test_first_conv_fixup_exercised_near_threshold():
     assert und > 0
 
 
-def test_first_conv_nonmonotone_channels_and_overflow():
+def test_first_conv_nonmonotone_channels_and_overflow(first_kind):
     def neg_slope(mdl):
         mdl["enc1.act1"]["slope"][::2] = -0.2  # half the channels: V-shaped fold
     m = _model(mutate=neg_slope)
@@ -325,7 +337,7 @@ def test_first_conv_nonmonotone_channels_and_overflow():
     assert und == 0xFFFFFFFF and np.array_equal(fast, exact)
 
 
-def test_first_conv_nonfinite_and_extreme_inputs():
+def test_first_conv_nonfinite_and_extreme_inputs(first_kind):
     m = _model()
     x = synth(45, 0, 6, 120, 32, 32)
     x[0, 5, 3, 7] = np.nan
@@ -341,10 +353,26 @@ def test_first_conv_nonfinite_and_extreme_inputs():
     del om_bits
 
 
-@pytest.mark.parametrize("H,W", [(17, 40), (33, 33), (64, 16)])
-def test_first_conv_tensor_path_odd_sizes(H, W):
+@pytest.mark.parametrize("H,W", [(17, 40), (33, 33), (64, 16), (16, 16), (16, 100), (40, 64), (21, 252),
+                                 (16, 124)])
+def test_first_conv_tensor_path_odd_sizes(H, W, first_kind):
+    """Sizes that exercise the tcgen05 kernel's row items (several per
+    image, a short last one, one image per item, wide rows) and the shapes
+    it hands back to the mma.sync kernel (W not a multiple of 4, boxes too
+    big for shared memory)."""
     m = _model(base=16, seed=3)
     x = synth(46, 0, 3, 120, H, W)
     fast, _ = _first_conv_bits(m, x, False)
     exact, _ = _first_conv_bits(m, x, True)
     assert np.array_equal(fast, exact)
+
+
+@pytest.mark.parametrize("bands", [1, 37, 64, 128])
+def test_first_conv_tensor_path_band_counts(bands, first_kind):
+    """Band counts that leave 1 to 4 K chunks, partly filled or full."""
+    m = _model(seed=5, bands=bands)
+    x = synth(47, 0, 4, bands, 32, 32)
+    fast, und = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
+    assert und < 4 * 32 * 32 * 32 // 100
