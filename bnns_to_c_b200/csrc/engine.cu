@@ -98,7 +98,7 @@ struct DevState {
     uint4* rm_wfrag = nullptr;  // first conv +-1 int8 weights in mma B-fragment order
     int* rm_exact = nullptr;    // per channel: fold not monotone -> exact path
     int8_t* rw_wu = nullptr;    // first conv +-1 int8 weights for realin_ws_kernel (Cin <= 128, Cout <= 32)
-    RwThr* rw_thr = nullptr;    // first conv fold thresholds for realin_ws_kernel
+    std::vector<RwThr> rw_thr;  // first conv fold thresholds for realin_ws_kernel (host copy, 32 entries)
     BinLayer enc1[4], enc2[4], bott1, bott2, dec1[4], dec2[4];
     float *head_W = nullptr, *head_b = nullptr;
     Arena ar;
@@ -425,7 +425,7 @@ static int dev_init(const Model* m, DevState* d) {
         items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
     }
     size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
-                   align256(rexact.size() * 4) + align256(rwu.size()) + align256(rthr.size() * sizeof(RwThr));
+                   align256(rexact.size() * 4) + align256(rwu.size());
     for (auto& it : items) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
         folds_of(it.a, it.L->CoutP, it.h.fold);
@@ -454,7 +454,7 @@ static int dev_init(const Model* m, DevState* d) {
     d->rm_wfrag = (uint4*)put(wfrag.data(), wfrag.size() * 4);
     d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
     d->rw_wu = rwu.empty() ? nullptr : (int8_t*)put(rwu.data(), rwu.size());
-    d->rw_thr = rthr.empty() ? nullptr : (RwThr*)put(rthr.data(), rthr.size() * sizeof(RwThr));
+    d->rw_thr = rthr;
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
@@ -828,11 +828,16 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     CUtensorMap tm;
     RwGeo geo;
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
-    if (g_first_kind == 0 && d->rw_wu && d->rw_thr && Cout <= 32 && Cin <= RM_CINP && rw_geometry(H, W, &geo) &&
+    if (g_first_kind == 0 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP && rw_geometry(H, W, &geo) &&
         first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32)) {
         CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
         RealinWsParams p{};
-        p.wu = d->rw_wu; p.thr = d->rw_thr; p.out = out;
+        p.wu = d->rw_wu; p.out = out;
+        for (int c = 0; c < 32; ++c) {
+            p.thrC[c] = d->rw_thr[c].C;
+            p.thr_neg |= (uint32_t)(d->rw_thr[c].sgn < 0) << c;
+            p.thr_exact |= (uint32_t)(d->rw_thr[c].exact != 0) << c;
+        }
         p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
         p.N = N; p.Cin = Cin; p.H = H; p.W = W; p.Cout = Cout; p.cwo = cw_of(Cout);
         p.R = geo.R; p.Wp = geo.Wp; p.SP = geo.SP; p.NS = geo.NS; p.KC = cdiv(Cin, 32);

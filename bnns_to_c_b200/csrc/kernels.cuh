@@ -1168,15 +1168,27 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 }
 
 // bounded wait that also gives up at once when the CTA has aborted; a wait
-// that runs out sets the abort flag
+// that runs out sets the abort flag. With BNN_WAIT_HINT_NS > 0 each try_wait
+// may suspend the thread up to that long (it wakes when the phase completes).
+#ifndef BNN_WAIT_HINT_NS
+#define BNN_WAIT_HINT_NS 0
+#endif
 __device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-    for (int it = 0; it < (1 << 22); ++it) {
+    for (int it = 0; it < (BNN_WAIT_HINT_NS > 0 ? (1 << 16) : (1 << 22)); ++it) {
         uint32_t done;
+#if BNN_WAIT_HINT_NS > 0
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity), "r"(BNN_WAIT_HINT_NS)
+            : "memory");
+#else
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
             : "r"(bar), "r"(parity)
             : "memory");
+#endif
         if (done) return true;
         if ((it & 255) == 255 && *abort_flag) return false;
     }
@@ -1585,8 +1597,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
 // ---------------------------------------------------------------------
 constexpr int RW_MT = 2;              // tiles per item
 constexpr int RW_NB = 2;              // fp32 box buffers
-constexpr int RW_NPROD = 192;
-constexpr int RW_NQ = 4;              // staged positions per producer thread, at most
+constexpr int RW_NEPI = 128;          // warps 0-3: epilogue (both tiles)
+constexpr int RW_NPROD = 320;         // warps 4-13: producers
+constexpr int RW_NQ = 3;              // staged positions per producer thread, at most
 constexpr int RW_MAX_SP = RW_NPROD * RW_NQ;
 constexpr size_t RW_WBYTES = (size_t)4 * 9 * 2 * 32 * 16;  // +-1 weights, 4 chunks x 9 taps
 constexpr size_t RW_MAX_SMEM = (size_t)224 * 1024;
@@ -1607,7 +1620,9 @@ struct RwThr {
 
 struct RealinWsParams {
     const int8_t* wu;      // [4 chunks][9 taps][2 halves][32 ch][16 bands] +-1 int8 (0 past Cin / Cout)
-    const RwThr* thr;      // [32] fold thresholds
+    long long thrC[32];    // fold thresholds (RwThr.C), in the constant bank
+    uint32_t thr_neg;      // bit c: channel c's fold decreases (RwThr.sgn < 0)
+    uint32_t thr_exact;    // bit c: channel c always goes to the fix-up
     uint32_t* out;         // [N][H][W][cwo]
     uint32_t* list;        // undecided outputs: (pixel index, channel) pairs
     unsigned int* ctl;     // [0] = entries, [1] = overflow / wait failure
@@ -1619,7 +1634,7 @@ struct RealinWsParams {
 __host__ __device__ inline size_t rw_box_bytes(int W, int R) { return (size_t)W * (R + 2) * 32 * 4; }
 __host__ __device__ inline size_t rw_stage_bytes(int SP) { return (size_t)3 * 2 * SP * 16; }
 __host__ __device__ inline size_t rw_fixed_bytes(int W, int R, int SP) {
-    return RW_WBYTES + RW_NB * rw_box_bytes(W, R) + (size_t)2 * SP * 4 + 32 * sizeof(RwThr);
+    return RW_WBYTES + RW_NB * rw_box_bytes(W, R) + (size_t)2 * SP * 4;
 }
 
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
@@ -1644,7 +1659,6 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
     unsigned char* boxes = rw_smem + RW_WBYTES;                        // [RW_NB][32][R+2][W] f32
     unsigned char* stages = boxes + RW_NB * box_bytes;                 // [NS][3 planes][2 halves][SP][16]
     float* bpx = reinterpret_cast<float*>(stages + NS * stage_bytes);  // [2][SP] error bound per position
-    RwThr* thr_s = reinterpret_cast<RwThr*>(bpx + 2 * SP);             // [32] (SP is a multiple of 8)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int my_items = (int)blockIdx.x < p.n_items ? (p.n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
@@ -1664,22 +1678,21 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&accf_b[b]), 2);
-            mbar_init(smem_u32(&acce_b[b]), 256);
+            mbar_init(smem_u32(&acce_b[b]), RW_NEPI);
             mbar_init(smem_u32(&bpxf_b[b]), RW_NPROD);
         }
         mbar_init(smem_u32(&wrdy_b), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (tid < 32) thr_s[tid] = p.thr[tid];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_s;
     const uint32_t sm0 = smem_u32(rw_smem);
 
-    if (warp >= 8 && warp < 14) {
+    if (warp >= 4 && warp < 14) {
         // ------------------------------------------------------------ producers
-        const int pt = tid - 256;
+        const int pt = tid - RW_NEPI;
         const int nseq = my_items * KC;
         auto issue_box = [&](int seq) {  // TMA of chunk kc of item seq/KC into buffer seq % RW_NB
             const int item = (int)blockIdx.x + (seq / KC) * (int)gridDim.x, kc = seq % KC;
@@ -1726,14 +1739,29 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
                         if (col >= 1 && row < R + 2) {
                             const float* src = bx + (size_t)row * p.W + (col - 1);
 #pragma unroll
-                            for (int g = 0; g < 4; ++g) {  // 8 bands at a time
+                            for (int g2 = 0; g2 < 4; g2 += 2) {  // 16 bands loaded at once
+                                float xv[16];
+#pragma unroll
+                                for (int i = 0; i < 16; ++i) xv[i] = src[(size_t)(g2 * 8 + i) * bstride];
+                                // sum |x| in two rounded-up chains (any order bounds the sum from above)
+                                float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                                for (int i = 0; i < 16; i += 2) {
+                                    s0 = __fadd_ru(s0, fabsf(xv[i]));
+                                    s1 = __fadd_ru(s1, fabsf(xv[i + 1]));
+                                    amax[j] = fmaxf(amax[j], fmaxf(fabsf(xv[i]), fabsf(xv[i + 1])));
+                                }
+                                tsum[j] = __fadd_ru(tsum[j], __fadd_ru(s0, s1));
+#pragma unroll
+                            for (int g = g2; g < g2 + 2; ++g) {
                                 uint32_t qv[8];
 #pragma unroll
                                 for (int i = 0; i < 8; ++i) {
-                                    const float x = src[(size_t)(g * 8 + i) * bstride];
-                                    tsum[j] = __fadd_ru(tsum[j], fabsf(x));
-                                    amax[j] = fmaxf(amax[j], fabsf(x));
-                                    qv[i] = rm_fix(x);
+                                    // rm_fix in one rounding: x * 2^18 is exact, so
+                                    // fma(x, 2^18, 1.5*2^23) == fadd(fmul(x, 2^18), 1.5*2^23)
+                                    qv[i] = (uint32_t)(__float_as_int(__fmaf_rn(xv[(g - g2) * 8 + i], (float)(1 << RM_FIX),
+                                                                               12582912.0f)) -
+                                                       0x4B400000);
                                 }
 #pragma unroll
                                 for (int h = 0; h < 2; ++h) {
@@ -1745,6 +1773,7 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
                                                                   __byte_perm(qv[h * 4 + 2], qv[h * 4 + 3], 0x6262),
                                                                   0x5410);  // bytes 2
                                 }
+                            }
                             }
                         }
 #pragma unroll
@@ -1821,10 +1850,8 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
         __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue
-        // warp w: TMEM lanes 32*(w%4).., tile w/4
-        const int quad = warp & 3, mt = warp >> 2, r = quad * 32 + lane;
-        const int qo = mt * 128 + r + Wp + 1;  // staged position of this lane's output
-        const int orow = qo / Wp, ocol = qo - orow * Wp;
+        // warp w: TMEM lanes 32w.., both tiles
+        const int quad = warp, r = quad * 32 + lane;
         for (int it = 0; it < my_items && !*abort_v; ++it) {
             const int buf = it & 1;
             const int item = (int)blockIdx.x + it * (int)gridDim.x;
@@ -1832,52 +1859,57 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
             if (!mbar_wait_ab(smem_u32(&accf_b[buf]), (uint32_t)(it >> 1) & 1u, abort_v)) break;
             if (!mbar_wait_ab(smem_u32(&bpxf_b[buf]), (uint32_t)(it >> 1) & 1u, abort_v)) break;
             tc_fence_after();
-            const int y = y0 + orow - 1, x = ocol - 1;
-            const bool valid = orow >= 1 && orow <= R && ocol >= 1 && y < p.H;
-            float ef = 0.0f;
-            if (valid) {
-                const float* bt = bpx + buf * SP;
-#pragma unroll
-                for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bt[qo + (t / 3 - 1) * Wp + (t % 3 - 1)]);
-            }
-            // E = ceil(e * 2^18) (exact scaling); e past 2^40, inf or NaN: nothing is decided
-            const bool finite = ef <= 1.0995116e12f;
-            const long long E = finite ? __float2ll_ru(ef * 262144.0f) : 0ll;
-            const size_t pix = ((size_t)n * p.H + y) * p.W + x;
-            uint32_t bits = 0u;
-            const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + mt * 96);
+            const float* bt = bpx + buf * SP;
 #pragma unroll 1
-            for (int c0 = 0; c0 < 32; c0 += 16) {
-                uint32_t s2[16], s1[16], s0[16];
-                tc_ld16(ta + c0, s2);
-                tc_ld16(ta + 32 + c0, s1);
-                tc_ld16(ta + 64 + c0, s0);
-                tc_wait_ld();
+            for (int mt = 0; mt < RW_MT; ++mt) {
+                const int qo = mt * 128 + r + Wp + 1;  // staged position of this lane's output
+                const int orow = qo / Wp, ocol = qo - orow * Wp;
+                const int y = y0 + orow - 1, x = ocol - 1;
+                const bool valid = orow >= 1 && orow <= R && ocol >= 1 && y < p.H;
+                float ef = 0.0f;
                 if (valid) {
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const int co = c0 + k;
-                        if (co >= p.Cout) continue;
-                        const long long Q = ((long long)(int)s2[k] << 16) + ((long long)(int)s1[k] << 8) +
-                                            (long long)(int)s0[k];
-                        const RwThr t = thr_s[co];
-                        const long long Qs = t.sgn > 0 ? Q : -Q;
-                        const bool ok = finite && !t.exact;
-                        if (ok && Qs - E >= t.C) {
-                            bits |= 1u << co;
-                        } else if (!(ok && Qs + E < t.C)) {
-                            const unsigned int slot = atomicAdd(p.ctl, 1u);
-                            if (slot < (unsigned)p.cap) {
-                                p.list[2 * (size_t)slot] = (uint32_t)pix;
-                                p.list[2 * (size_t)slot + 1] = (uint32_t)co;
-                            } else {
-                                atomicExch(p.ctl + 1, 1u);
+                    for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bt[qo + (t / 3 - 1) * Wp + (t % 3 - 1)]);
+                }
+                // E = ceil(e * 2^18) (exact scaling); e past 2^40, inf or NaN: nothing is decided
+                const bool finite = ef <= 1.0995116e12f;
+                const long long E = finite ? __float2ll_ru(ef * 262144.0f) : 0ll;
+                const size_t pix = ((size_t)n * p.H + y) * p.W + x;
+                uint32_t bits = 0u;
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + mt * 96);
+#pragma unroll 1
+                for (int c0 = 0; c0 < 32; c0 += 16) {
+                    uint32_t s2[16], s1[16], s0[16];
+                    tc_ld16(ta + c0, s2);
+                    tc_ld16(ta + 32 + c0, s1);
+                    tc_ld16(ta + 64 + c0, s0);
+                    tc_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int co = c0 + k;
+                            if (co >= p.Cout) continue;
+                            const long long Q = ((long long)(int)s2[k] << 16) + ((long long)(int)s1[k] << 8) +
+                                                (long long)(int)s0[k];
+                            const long long Qs = (p.thr_neg >> co) & 1u ? -Q : Q;
+                            const long long C = p.thrC[co];
+                            const bool ok = finite && !((p.thr_exact >> co) & 1u);
+                            if (ok && Qs - E >= C) {
+                                bits |= 1u << co;
+                            } else if (!(ok && Qs + E < C)) {
+                                const unsigned int slot = atomicAdd(p.ctl, 1u);
+                                if (slot < (unsigned)p.cap) {
+                                    p.list[2 * (size_t)slot] = (uint32_t)pix;
+                                    p.list[2 * (size_t)slot + 1] = (uint32_t)co;
+                                } else {
+                                    atomicExch(p.ctl + 1, 1u);
+                                }
                             }
                         }
                     }
                 }
+                if (valid) p.out[pix * p.cwo] = bits;
             }
-            if (valid) p.out[pix * p.cwo] = bits;
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_b[buf]));
         }
