@@ -186,7 +186,7 @@ static int ws_bn(int Cout) { return Cout <= 32 ? 32 : Cout <= 64 ? 64 : Cout <= 
 // kidx-ordered uint64 rows (bit (ci*9+t)) -> [CoutP][9][Kw] with the first
 // sC channels in words [0, cw0) and the rest in words [cw0, cw0+cw1).
 static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, int sC, BinLayer& L,
-                         HostBin& h) {
+                         HostBin& h, bool pooled) {
     L.Cin = Cin; L.Cout = Cout; L.sC = sC;
     L.cw0 = cw_of(sC);
     L.cw1 = Cin > sC ? cw_of(Cin - sC) : 0;
@@ -213,7 +213,8 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
     }
     // tcgen05 blocks: per (channel block, word) the 9 taps' B operands in the
     // order the kernel stages them ([tap][16-byte K half][channel][16 bytes])
-    const int bn = ws_bn(Cout), ncb = cdiv(Cout, bn);
+    // pooled layers keep four phase accumulators in TMEM: channel blocks of at most 128
+    const int bn = pooled ? std::min(ws_bn(Cout), 128) : ws_bn(Cout), ncb = cdiv(Cout, bn);
     L.ubn = bn;
     h.wu.assign((size_t)ncb * L.Kw * 9 * 2 * bn * 16, (int8_t)0);
     for (int cb = 0; cb < ncb; ++cb)
@@ -238,6 +239,11 @@ template <int BN, int TM, int TN, int KC>
 static cudaError_t attr_bconv() {
     return cudaFuncSetAttribute(bconv3x3_kernel<BN, TM, TN, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)BconvCfg<BN, TM, TN, KC>::smem_bytes(512));
+}
+template <int BN, int MT>
+static cudaError_t attr_ws_pool() {
+    return cudaFuncSetAttribute(bconv_ws_pool_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)WsPoolCfg<BN, MT>::max_smem);
 }
 template <int BN, int MT>
 static cudaError_t attr_ws() {
@@ -268,6 +274,8 @@ static int set_kernel_attrs(int device) {
         (e = attr_bmma<64>()) != cudaSuccess || (e = attr_bmma<128>()) != cudaSuccess ||
         (e = attr_ws<32, 8>()) != cudaSuccess || (e = attr_ws<64, 4>()) != cudaSuccess ||
         (e = attr_ws<128, 2>()) != cudaSuccess || (e = attr_ws<256, 1>()) != cudaSuccess ||
+        (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
+        (e = attr_ws_pool<128, 1>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -427,7 +435,7 @@ static int dev_init(const Model* m, DevState* d) {
     size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
                    align256(rexact.size() * 4) + align256(rwu.size());
     for (auto& it : items) {
-        relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h);
+        relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h, it.a2 != nullptr);
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
         total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wu.size()) +
@@ -685,7 +693,45 @@ static int launch_ws(BconvParams p, int N, cudaStream_t st) {
     return BNN_OK;
 }
 
+// the pooled layers' polyphase kernel (even H and W, no concat input)
+template <int BN, int MT>
+static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
+    using Cfg = WsPoolCfg<BN, MT>;
+    if ((p.H & 1) || (p.W & 1) || p.cw1 != 0 || !p.fold2) return BNN_ERR_UNSUPPORTED;
+    const long H2 = p.H / 2, W2 = p.W / 2;
+    const long gk = std::max(1L, 64 / (W2 + 1));
+    const long Gw = gk * (W2 + 1) + 1;
+    const long rows = (long)cdiv(N, gk) * (H2 + 1) + 1;
+    const long ptot = (rows - 2) * Gw;
+    const long sp = ((Cfg::PI + 2 * Gw + 2) + 7) & ~7L;
+    const long groups = (ptot + Cfg::PI - 1) / Cfg::PI;
+    const long ncb = cdiv(p.Cout, BN);
+    if (Gw > Cfg::MAX_GW || sp > Cfg::MAX_SP || groups * Cfg::PI + 2 * Gw + 2 >= (1L << 31) ||
+        groups * ncb >= (1L << 31) || (size_t)N * p.H * p.W >= ((size_t)1 << 31))
+        return BNN_ERR_UNSUPPORTED;
+    const int ns = Cfg::stages((int)sp, (int)Gw, p.Cout);
+    if (ns < 2) return BNN_ERR_UNSUPPORTED;
+    p.gk = (int)gk; p.Gw = (int)Gw; p.HP = (int)sp;
+    p.TR = (int)(groups * ncb); p.TC = (int)ncb; p.TNI = ns;
+    const size_t smem = std::max<size_t>(
+        (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
+    const int grid = (int)std::min<long>(groups * ncb, sm_count());
+    bconv_ws_pool_kernel<BN, MT><<<grid, Cfg::NT, smem, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 pooled launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
+    if (g_bconv_kind == 0 && p.out2 && p.wu) {
+        int rc = BNN_ERR_UNSUPPORTED;
+        switch (p.ubn) {
+            case 32: rc = launch_ws_pool<32, 2>(p, N, st); break;
+            case 64: rc = launch_ws_pool<64, 1>(p, N, st); break;
+            case 128: rc = launch_ws_pool<128, 1>(p, N, st); break;
+        }
+        if (rc != BNN_ERR_UNSUPPORTED) return rc;
+    }
     if (g_bconv_kind == 0 && !p.out2 && p.wu) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
@@ -887,7 +933,8 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
     if (N <= 0) return BNN_OK;
     HeadParams p{in, d->head_W, d->head_b, out, N, H, W, m->head_Cin, cw_of(m->head_Cin), m->head_Cout};
     const size_t total = (size_t)N * H * W;
-    unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
+    if (total >= ((size_t)1 << 31)) return set_error(BNN_ERR_ARG, "N*H*W = %zu: at most 2^31 - 1 pixels", total);
+    unsigned blocks = (unsigned)std::min<size_t>((total + 511) / 512, 148 * 8);
     head1x1_kernel<<<blocks, 256, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
@@ -1519,7 +1566,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     if (!Lh) return set_error(BNN_ERR_OOM, "OOM");
     Lh->device = device;
     HostBin h;
-    relayout_bin(packed, (9 * Cin + 63) / 64, Cin, Cout, Cin, Lh->L, h);
+    relayout_bin(packed, (9 * Cin + 63) / 64, Cin, Cout, Cin, Lh->L, h, ptype != nullptr);
     Act a{0, Cout, (int32_t*)type, (int32_t*)t, (int32_t*)lo, (int32_t*)hi, nullptr, nullptr, nullptr, nullptr};
     folds_of(&a, Lh->L.CoutP, h.fold);
     const bool pool = ptype && pt && plo && phi;

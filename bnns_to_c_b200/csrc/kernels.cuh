@@ -1199,10 +1199,16 @@ __device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, vola
 // Walks grid positions in steps of a fixed stride without divisions: row gr,
 // column gc, image-block row ib and row yy within it (gr = 1 + ib*(H+1) + yy).
 // colmap[gc] = (image slot << 16) | x for image columns, -1 for separators.
+// Grid geometry: N images of H x W, gk per grid row, grid width Gw.
+struct GridGeo {
+    int N, H, W, gk, Gw;
+};
+__device__ __forceinline__ GridGeo grid_geo(const BconvParams& p) { return GridGeo{p.N, p.H, p.W, p.gk, p.Gw}; }
+
 struct GridWalk {
     int gr, gc, ib, yy;
     int sa, sb;  // stride = sa*Gw + sb, 0 <= sb < Gw
-    __device__ __forceinline__ void init(const BconvParams& p, int pos, int stride) {
+    __device__ __forceinline__ void init(const GridGeo& p, int pos, int stride) {
         // pos >= -1: position -1 sits in row -1
         gr = pos >= 0 ? pos / p.Gw : -1;
         gc = pos - gr * p.Gw;
@@ -1212,7 +1218,7 @@ struct GridWalk {
         sa = stride / p.Gw;
         sb = stride - sa * p.Gw;
     }
-    __device__ __forceinline__ void step(const BconvParams& p) {
+    __device__ __forceinline__ void step(const GridGeo& p) {
         gc += sb;
         int d = sa;
         if (gc >= p.Gw) { gc -= p.Gw; ++d; }
@@ -1220,15 +1226,22 @@ struct GridWalk {
         yy += d;
         while (yy > p.H) { yy -= p.H + 1; ++ib; }
     }
-    // pixel index (n*H + y)*W + x, or -1 for a zero position
-    __device__ __forceinline__ int pixel(const BconvParams& p, const int* colmap, int& n, int& x) const {
-        if (ib < 0 || yy >= p.H) return -1;
+    // image n and (y, x) of the position, false for a zero position
+    __device__ __forceinline__ bool at(const GridGeo& p, const int* colmap, int& n, int& y, int& x) const {
+        if (ib < 0 || yy >= p.H) return false;
         const int cm = colmap[gc];
-        if (cm < 0) return -1;
+        if (cm < 0) return false;
         n = ib * p.gk + (cm >> 16);
-        if (n >= p.N) return -1;
+        if (n >= p.N) return false;
+        y = yy;
         x = cm & 0xFFFF;
-        return (n * p.H + yy) * p.W + x;
+        return true;
+    }
+    // pixel index (n*H + y)*W + x, or -1 for a zero position
+    __device__ __forceinline__ int pixel(const GridGeo& p, const int* colmap, int& n, int& x) const {
+        int y;
+        if (!at(p, colmap, n, y, x)) return -1;
+        return (n * p.H + y) * p.W + x;
     }
 };
 
@@ -1371,11 +1384,12 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         // map the staged positions q = pt + NPROD*j of `item` into table `tb`
         auto map_item = [&](int item, int2* tb) {
             const int pg = item / ncb;
+            const GridGeo geo = grid_geo(p);
             GridWalk g;
-            g.init(p, pg * PI - 1 + pt, NPROD);  // staged position 0 = first output - Gw - 1
-            for (int q = pt; q < SP; q += NPROD, g.step(p)) {
+            g.init(geo, pg * PI - 1 + pt, NPROD);  // staged position 0 = first output - Gw - 1
+            for (int q = pt; q < SP; q += NPROD, g.step(geo)) {
                 int n = 0, x = 0, up = -1;
-                const int px = g.pixel(p, colmap, n, x);
+                const int px = g.pixel(geo, colmap, n, x);
                 if (px >= 0 && p.cw1 > 0) {
                     const int uy = g.yy - p.oh, ux = x - p.ow;
                     if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
@@ -1509,19 +1523,20 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
             const int ncout0 = (nitem % ncb) * BN;
             if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
             tc_fence_after();
+            const GridGeo geo = grid_geo(p);
             GridWalk g;
-            g.init(p, p.Gw + pg * PI + r, 128);
+            g.init(geo, p.Gw + pg * PI + r, 128);
             int gmt = 0;
 #pragma unroll 1
             for (int i = half; i < NPAIR; i += 2) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
-                for (; gmt < mt; ++gmt) g.step(p);
+                for (; gmt < mt; ++gmt) g.step(geo);
                 const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN * MT + mt * BN + c0);
                 uint32_t v[32];
                 tc_ld32_nw(ta, v);
                 tc_wait_ld();
                 int n = 0, x = 0;
-                const int px = g.pixel(p, colmap, n, x);
+                const int px = g.pixel(geo, colmap, n, x);
                 if (px >= 0 && cout0 + c0 < p.Cout) {
                     const int cw = (cout0 + c0) >> 5, lim = p.Cout - cout0 - c0;
                     uint32_t bits = 0u;
@@ -1565,6 +1580,425 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     if (abort_s) {
         // let any MMA or bulk copy still in flight land before TMEM and shared
         // memory are released (bounded; the result is flagged as untrustworthy)
+        for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
+        if (tid == 0) atomicAdd(&g_bnn_wait_timeouts, 1u);
+    }
+    if (warp == 15) {
+        tc_fence_after();
+        tc_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------
+// Pooled layers on tcgen05: conv -> fold (full resolution) and 2x2 max-pool
+// of P -> fold2 (half resolution), for even H and W.
+//
+// Polyphase staging: the input splits into four phase images (rows y = 2i+py,
+// columns x = 2j+px), each laid out on the padded grid of the half-resolution
+// geometry (H/2 x W/2). The output of phase (py, px) at half-res (i, j) reads
+// tap (dy, dx) from phase ((py+dy-1) & 1, (px+dx-1) & 1) at (i + oy, j + ox),
+// oy = floor((py+dy-1)/2), ox likewise, so every tap of every output phase is
+// one descriptor into the staged phase region, shifted by oy*Gw + ox. The four
+// accumulators of a 2x2 pool window sit on the same TMEM lane (one per
+// phase), so the pool is a per-lane max in the epilogue: no exchange across
+// tiles. Accumulators start at the fold's -T (threshold words) as in
+// bconv_ws_kernel; fold2 adds the per-channel difference to its own
+// threshold. Issuer u takes the phases with px = u.
+// ---------------------------------------------------------------------
+template <int BN, int MT>
+struct WsPoolCfg {
+    static constexpr int NPH = 4;
+    static constexpr int NBUF = 512 / (NPH * BN * MT);
+    static constexpr int PI = 128 * MT;   // half-res positions per item
+    static constexpr int NEPI = 256, NPROD = 192, NT = 512;
+    static constexpr int MAX_GW = 128;
+    static constexpr int MAX_SP = PI + 2 * MAX_GW + 8;  // per phase
+    static constexpr int NQP = (MAX_SP + NPROD - 1) / NPROD;
+    static constexpr size_t b_bytes = (size_t)9 * 2 * BN * 16;
+    static constexpr size_t max_smem = (size_t)224 * 1024;
+    __host__ __device__ static size_t a_bytes(int SP) { return (size_t)NPH * 2 * SP * 16; }
+    __host__ __device__ static size_t stage_bytes(int SP) { return (a_bytes(SP) + b_bytes + 127) & ~(size_t)127; }
+    // per channel: two (lo, span), start, fold2 offset; per word: six masks
+    __host__ __device__ static size_t fold_bytes(int Cout) {
+        return (size_t)((Cout + 31) & ~31) * (2 * sizeof(int2) + 8) + (size_t)((Cout + 31) / 32) * 24;
+    }
+    __host__ __device__ static size_t fixed_bytes(int SP, int Gw, int Cout) {
+        return (size_t)2 * NPH * SP * 4 + (((size_t)Gw * 4 + 15) & ~(size_t)15) + fold_bytes(Cout);
+    }
+    static int stages(int SP, int Gw, int Cout) {
+        const size_t n = (max_smem - fixed_bytes(SP, Gw, Cout)) / stage_bytes(SP);
+        return n > 8 ? 8 : (int)n;
+    }
+    static_assert(NBUF == 1 || NBUF == 2, "TMEM holds one or two accumulators");
+};
+
+// p.HP = staged positions per phase (SP); p.TR = items; p.TC = channel
+// blocks; p.TNI = pipeline stages; p.gk / p.Gw: the half-res grid
+template <int BN, int MT>
+__global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams p) {
+    using C = WsPoolCfg<BN, MT>;
+    constexpr int NPH = C::NPH, NBUF = C::NBUF, PI = C::PI, NQP = C::NQP, NPROD = C::NPROD, NEPI = C::NEPI;
+    constexpr int NCH = BN / 32, NPAIR = MT * NCH;
+    constexpr int ACC = NPH * MT * BN;  // TMEM columns of one accumulator set
+    extern __shared__ __align__(1024) unsigned char wp_smem[];
+    __shared__ __align__(8) unsigned long long full_b[8], empty_b[8], accf_b[2], acce_b[2];
+    __shared__ uint32_t tmem_s;
+    __shared__ uint2 lut[256];
+    __shared__ int abort_s;
+    volatile int* abort_v = &abort_s;
+
+    const int SP = p.HP, n_items = p.TR, ncb = p.TC, NS = p.TNI;
+    const int H2 = p.H >> 1, W2 = p.W >> 1;
+    const GridGeo geo{p.N, H2, W2, p.gk, p.Gw};
+    const size_t SB = C::stage_bytes(SP);
+    int* pxs = reinterpret_cast<int*>(wp_smem + (size_t)NS * SB);  // [2][NPH][SP] full-res pixel or -1
+    int* colmap = pxs + 2 * NPH * SP;                               // [Gw]
+    const int CoutR = (p.Cout + 31) & ~31, nwo = CoutR / 32;
+    int2* fu1 = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(colmap) + ((p.Gw * 4 + 15) & ~15));
+    int2* fu2 = fu1 + CoutR;
+    int* fstart = reinterpret_cast<int*>(fu2 + CoutR);  // accumulator start (-T1 or 0)
+    int* fd2 = fstart + CoutR;                          // fold2 offset: max + fd2 = maxP - T2 (or maxP)
+    uint32_t* fm = reinterpret_cast<uint32_t*>(fd2 + CoutR);  // [6][nwo]: inv1_t inv1_b band1 inv2_t inv2_b band2
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 15) {
+        tc_alloc(smem_u32(&tmem_s), 512);
+        tc_relinquish();
+    }
+    if (tid == 0) {
+        abort_s = 0;
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_b[s]), NPROD);
+            mbar_init(smem_u32(&empty_b[s]), 2);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(smem_u32(&accf_b[b]), 2);
+            mbar_init(smem_u32(&acce_b[b]), NEPI);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    for (int b = tid; b < 256; b += C::NT) {
+        uint32_t w[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t x = (((uint32_t)b >> (4 * h)) & 15u) * 0x00204081u & 0x01010101u;
+            w[h] = 0xFFFFFFFFu ^ (x * 0xFEu);
+        }
+        lut[b] = make_uint2(w[0], w[1]);
+    }
+    for (int c = tid; c < p.Gw; c += C::NT) {
+        int cm = -1;
+        if (c > 0) {
+            const int jb = (c - 1) / (W2 + 1), xx = (c - 1) - jb * (W2 + 1);
+            if (xx < W2 && jb < p.gk) cm = (jb << 16) | xx;
+        }
+        colmap[c] = cm;
+    }
+    // fold tables: word w of fold f (0: p.fold, 1: p.fold2)
+    auto classify = [&](const FoldIv* fold, int c, int& T, int& inv_t, bool& band, int2& e, int& inv) {
+        T = -(1 << 29); inv_t = 0; band = false; e = make_int2(0, 0); inv = 0;
+        if (c >= p.Cout) return;
+        const FoldIv f = fold[c];
+        const bool lo_open = f.lo == INT_MIN, hi_open = f.hi == INT_MAX;
+        if (f.lo >= f.hi) inv_t = f.inv;
+        else if (lo_open && hi_open) inv_t = f.inv ^ 1;
+        else if (lo_open) { T = f.hi; inv_t = f.inv; }
+        else if (hi_open) { T = f.lo; inv_t = f.inv ^ 1; }
+        else band = true;
+        T = max(-(1 << 29), min(1 << 29, T));  // |P| < 2^24: clamping keeps every comparison
+        e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
+        inv = f.inv & 1;
+    };
+    for (int w = tid; w < nwo; w += C::NT) {
+        uint32_t m[6] = {0, 0, 0, 0, 0, 0};
+        int T, it, iv;
+        bool bd;
+        int2 e;
+        for (int i = 0; i < 32; ++i) {
+            const int c = w * 32 + i;
+            classify(p.fold, c, T, it, bd, e, iv);
+            fu1[c] = e;
+            fstart[c] = -T;
+            m[0] |= (uint32_t)it << i; m[1] |= (uint32_t)iv << i; m[2] |= (uint32_t)bd;
+            classify(p.fold2, c, T, it, bd, e, iv);
+            fu2[c] = e;
+            fd2[c] = -T;
+            m[3] |= (uint32_t)it << i; m[4] |= (uint32_t)iv << i; m[5] |= (uint32_t)bd;
+        }
+        // band words start at 0; fold2 offset = -start - T2 (threshold words) or -start
+        for (int i = 0; i < 32; ++i) {
+            const int c = w * 32 + i;
+            const int st = m[2] ? 0 : fstart[c];
+            fstart[c] = st;
+            fd2[c] = m[5] ? -st : -st + fd2[c];
+        }
+        for (int k = 0; k < 6; ++k) fm[k * nwo + w] = m[k];
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    const uint32_t sm0 = smem_u32(wp_smem);
+
+    const int quad = warp & 3, half = (warp >> 2) & 1;
+    auto start_vals = [&](int c, uint32_t* v) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) {
+            const int4 q = *reinterpret_cast<const int4*>(fstart + c + k);
+            v[k] = (uint32_t)q.x; v[k + 1] = (uint32_t)q.y; v[k + 2] = (uint32_t)q.z; v[k + 3] = (uint32_t)q.w;
+        }
+    };
+    if (warp < 8) {
+        for (int b = 0; b < NBUF; ++b)
+            for (int i = half; i < NPAIR; i += 2) {
+                const int mt = i / NCH, c0 = (i % NCH) * 32;
+                const int cs = (int)((blockIdx.x + (unsigned)b * gridDim.x) % (unsigned)ncb) * BN + c0;
+                uint32_t v[32];
+                start_vals(cs < CoutR ? cs : 0, v);
+#pragma unroll 1
+                for (int ph = 0; ph < NPH; ++ph)
+                    tc_st32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * ACC + (ph * MT + mt) * BN + c0), v);
+            }
+        tc_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    if (warp >= 8 && warp < 14) {
+        // ------------------------------------------------------------ producers
+        const int pt = tid - NEPI;
+        auto map_item = [&](int item, int* tb) {
+            const int pg = item / ncb;
+            for (int ph = 0; ph < NPH; ++ph) {
+                const int py = ph >> 1, pxp = ph & 1;
+                GridWalk g;
+                g.init(geo, pg * PI - 1 + pt, NPROD);
+                for (int q = pt; q < SP; q += NPROD, g.step(geo)) {
+                    int n, i, j;
+                    tb[ph * SP + q] = g.at(geo, colmap, n, i, j) ? (n * p.H + 2 * i + py) * p.W + 2 * j + pxp : -1;
+                }
+            }
+        };
+        auto load_words = [&](const int* tb, int kw, uint32_t* v) {
+#pragma unroll
+            for (int ph = 0; ph < NPH; ++ph)
+#pragma unroll
+                for (int j = 0; j < NQP; ++j) {
+                    const int q = pt + NPROD * j;
+                    uint32_t w = 0u;
+                    if (q < SP) {
+                        const int px = tb[ph * SP + q];
+                        if (px >= 0) w = __ldg(p.in0 + (size_t)px * p.cw0 + kw);
+                    }
+                    v[ph * NQP + j] = w;
+                }
+        };
+        int stage = 0, tb = 0;
+        uint32_t phase = 0;
+        int item = blockIdx.x;
+        uint32_t vn[NPH * NQP];
+        if (item < n_items) {
+            map_item(item, pxs);
+            load_words(pxs, 0, vn);
+        }
+        while (item < n_items && !*abort_v) {
+            const int cb = item % ncb;
+            const int* cur = pxs + tb * NPH * SP;
+            bool ok = true;
+            for (int kw = 0; kw < p.Kw; ++kw) {
+                uint32_t v[NPH * NQP];
+#pragma unroll
+                for (int j = 0; j < NPH * NQP; ++j) v[j] = vn[j];
+                if (kw + 1 < p.Kw) {
+                    load_words(cur, kw + 1, vn);
+                } else if (item + (int)gridDim.x < n_items) {
+                    int* nxt = pxs + (tb ^ 1) * NPH * SP;
+                    map_item(item + gridDim.x, nxt);
+                    load_words(nxt, 0, vn);
+                }
+                const uint32_t fb = smem_u32(&full_b[stage]);
+                if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
+                unsigned char* As = wp_smem + (size_t)stage * SB;
+                if (pt == 0) {
+                    mbar_expect_tx_only(fb, (uint32_t)C::b_bytes);
+                    bulk_g2s(sm0 + (uint32_t)(stage * SB + C::a_bytes(SP)),
+                             p.wu + ((size_t)cb * p.Kw + kw) * C::b_bytes, (uint32_t)C::b_bytes, fb);
+                }
+#pragma unroll
+                for (int ph = 0; ph < NPH; ++ph)
+#pragma unroll
+                    for (int j = 0; j < NQP; ++j) {
+                        const int q = pt + NPROD * j;
+                        if (q < SP) {
+                            uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                            if (cur[ph * SP + q] >= 0) {
+                                const uint32_t w = v[ph * NQP + j];
+                                const uint2 b0 = lut[w & 255], b1 = lut[(w >> 8) & 255], b2 = lut[(w >> 16) & 255],
+                                            b3 = lut[w >> 24];
+                                lo = make_uint4(b0.x, b0.y, b1.x, b1.y);
+                                hi = make_uint4(b2.x, b2.y, b3.x, b3.y);
+                            }
+                            // [phase][k half][position][16 bytes]
+                            *reinterpret_cast<uint4*>(As + ((size_t)(ph * 2) * SP + q) * 16) = lo;
+                            *reinterpret_cast<uint4*>(As + ((size_t)(ph * 2 + 1) * SP + q) * 16) = hi;
+                        }
+                    }
+                fence_async_smem();
+                mbar_arrive(fb);
+                if (++stage == NS) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            tb ^= 1;
+            item += gridDim.x;
+        }
+    } else if (warp >= 14) {
+        // ------------------------------------------------------------ MMA issuers
+        const int u = warp - 14;
+        if (lane == 0) {
+            const uint32_t idesc =
+                (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((128u >> 4) << 24);
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+                const int buf = NBUF == 2 ? (it & 1) : 0;
+                const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+                if (!mbar_wait_ab(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, abort_v)) break;
+                tc_fence_after();
+                bool ok = true;
+                for (int kw = 0; kw < p.Kw; ++kw) {
+                    if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_s = sm0 + (uint32_t)(stage * SB);
+                    const uint64_t a0 = tc_desc(a_s, (uint32_t)SP * 16);
+                    const uint64_t b0 = tc_desc(a_s + (uint32_t)C::a_bytes(SP), BN * 16);
+#pragma unroll 1
+                    for (int py = 0; py < 2; ++py) {
+                        const int ph = py * 2 + u;
+#pragma unroll 1
+                        for (int mt = 0; mt < MT; ++mt) {
+                            const uint32_t d = tmem + (uint32_t)(buf * ACC + (ph * MT + mt) * BN);
+#pragma unroll
+                            for (int t = 0; t < 9; ++t) {
+                                const int dy = t / 3, dx = t % 3;
+                                const int sy = py + dy - 1, sx = u + dx - 1;  // source row / column parity
+                                const int qph = (sy & 1) * 2 + (sx & 1);
+                                const int oy = (sy + 2) / 2 - 1, ox = (sx + 2) / 2 - 1;  // floor(s / 2)
+                                const uint64_t ad =
+                                    a0 + (uint64_t)(qph * 2 * SP + mt * 128 + (oy + 1) * p.Gw + (ox + 1));
+                                tc_mma_i8(d, ad, b0 + (uint64_t)(t * 2 * BN), idesc, 1u);
+                            }
+                        }
+                    }
+                    tc_commit(smem_u32(&empty_b[stage]));
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(smem_u32(&accf_b[buf]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int r = quad * 32 + lane;
+        const int cwo = p.cwo;
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+            const int buf = NBUF == 2 ? (it & 1) : 0;
+            const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+            const int cb = item % ncb, pg = item / ncb, cout0 = cb * BN;
+            const int nitem = item + NBUF * (int)gridDim.x;
+            const int ncout0 = (nitem % ncb) * BN;
+            if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
+            tc_fence_after();
+            GridWalk g;
+            g.init(geo, p.Gw + pg * PI + r, 128);
+            int gmt = 0;
+#pragma unroll 1
+            for (int i = half; i < NPAIR; i += 2) {
+                const int mt = i / NCH, c0 = (i % NCH) * 32;
+                for (; gmt < mt; ++gmt) g.step(geo);
+                int n = 0, hi = 0, hj = 0;
+                const bool valid = g.at(geo, colmap, n, hi, hj) && cout0 + c0 < p.Cout;
+                const int cw = (cout0 + c0) >> 5, lim = p.Cout - cout0 - c0;
+                const uint32_t lmask = lim < 32 ? (1u << lim) - 1u : 0xFFFFFFFFu;
+                uint32_t mx[32];
+                const bool restart = nitem < n_items;
+                const int cs = ncout0 + c0 < CoutR ? ncout0 + c0 : 0;
+#pragma unroll 1
+                for (int ph = 0; ph < NPH; ++ph) {
+                    const uint32_t ta =
+                        tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * ACC + (ph * MT + mt) * BN + c0);
+                    uint32_t v[32];
+                    tc_ld32_nw(ta, v);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) mx[k] = ph == 0 ? v[k] : (uint32_t)max((int)mx[k], (int)v[k]);
+                    if (valid) {
+                        uint32_t bits = 0u;
+                        if (!fm[2 * nwo + cw]) {
+#pragma unroll
+                            for (int k = 31; k >= 0; --k) bits = __funnelshift_l(v[k], bits, 1);
+                            bits ^= fm[cw];
+                        } else {
+                            const int2* f = fu1 + cout0 + c0;
+#pragma unroll
+                            for (int k = 0; k < 32; ++k)
+                                bits |= (uint32_t)((unsigned)((int)v[k] - f[k].x) < (unsigned)f[k].y) << k;
+                            bits ^= fm[nwo + cw];
+                        }
+                        const int y = 2 * hi + (ph >> 1), x = 2 * hj + (ph & 1);
+                        const size_t px = ((size_t)n * p.H + y) * p.W + x;
+                        p.out[px * cwo + cw] = bits & lmask;
+                        if (p.P) {
+                            int* Pp = p.P + (((size_t)n * p.Cout + cout0 + c0) * p.H + y) * p.W + x;
+                            const int hw = p.H * p.W;
+                            const int* st = fstart + cout0 + c0;
+#pragma unroll
+                            for (int k = 0; k < 32; ++k)
+                                if (k < lim) Pp[(size_t)k * hw] = (int)v[k] - st[k];
+                        }
+                    }
+                    // restart this phase's accumulator chunk for its next item
+                    if (restart) {
+                        start_vals(cs, v);
+                        tc_st32(ta, v);
+                    }
+                }
+                if (valid) {
+                    const int* d2 = fd2 + cout0 + c0;
+                    uint32_t bits = 0u;
+                    if (!fm[5 * nwo + cw]) {
+#pragma unroll
+                        for (int k = 31; k >= 0; --k) bits = __funnelshift_l((uint32_t)((int)mx[k] + d2[k]), bits, 1);
+                        bits ^= fm[3 * nwo + cw];
+                    } else {
+                        const int2* f = fu2 + cout0 + c0;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k)
+                            bits |= (uint32_t)((unsigned)((int)mx[k] + d2[k] - f[k].x) < (unsigned)f[k].y) << k;
+                        bits ^= fm[4 * nwo + cw];
+                    }
+                    const size_t hpx = ((size_t)n * H2 + hi) * W2 + hj;
+                    if (p.out2) p.out2[hpx * cwo + cw] = bits & lmask;
+                    if (p.P2) {
+                        int* Pp = p.P2 + (((size_t)n * p.Cout + cout0 + c0) * H2 + hi) * W2 + hj;
+                        const int hw = H2 * W2;
+                        const int* st = fstart + cout0 + c0;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k)
+                            if (k < lim) Pp[(size_t)k * hw] = (int)mx[k] - st[k];
+                    }
+                }
+            }
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce_b[buf]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
         for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
         if (tid == 0) atomicAdd(&g_bnn_wait_timeouts, 1u);
     }
@@ -1944,22 +2378,72 @@ struct HeadParams {
     int N, H, W, Cin, cwi, ncls;
 };
 
-__global__ void head1x1_kernel(const HeadParams p) {
-    const size_t HW = (size_t)p.H * p.W;
-    const size_t total = (size_t)p.N * HW;
-    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
-        const size_t n = g / HW, px = g - n * HW;
-        const uint32_t* a = p.in + g * p.cwi;
-        for (int o = 0; o < p.ncls; ++o) {
-            float acc = __ldg(p.bias + o);
-            const float* w = p.Wt + (size_t)o * p.Cin;
-            uint32_t word = 0u;
-            for (int c = 0; c < p.Cin; ++c) {
-                if ((c & 31) == 0) word = __ldg(a + (c >> 5));
-                const float wv = __ldg(w + c);
-                acc = __fadd_rn(acc, ((word >> (c & 31)) & 1u) ? wv : -wv);
+// Two pixels per thread and every class at once: 2*ncls independent
+// sequential chains (the order within each chain is the reference's), the
+// +-1 products as sign selects of weights held in shared memory. 32-bit
+// indexing (the forward keeps N*H*W < 2^31).
+constexpr int HEAD_MAXC = 8;        // classes handled per pass
+constexpr int HEAD_MAXW = 64 * 32;  // weights held in shared memory (ncls*Cin)
+__global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
+    __shared__ float ws[HEAD_MAXW];
+    __shared__ float bs[HEAD_MAXC];
+    const int nw = p.ncls * p.Cin;
+    for (int i = threadIdx.x; i < nw && i < HEAD_MAXW; i += blockDim.x) ws[i] = p.Wt[i];
+    if (threadIdx.x < p.ncls && threadIdx.x < HEAD_MAXC) bs[threadIdx.x] = p.bias[threadIdx.x];
+    __syncthreads();
+    const bool in_smem = nw <= HEAD_MAXW && p.ncls <= HEAD_MAXC;
+    const unsigned HW = (unsigned)p.H * (unsigned)p.W, total = (unsigned)p.N * HW;
+    const unsigned stride = 2u * gridDim.x * blockDim.x;
+    for (unsigned g0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x); g0 < total; g0 += stride) {
+        const bool two = g0 + 1 < total;
+        if (in_smem) {
+            for (int o0 = 0; o0 < p.ncls; o0 += 4) {
+                float acc[2][4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[0][k] = acc[1][k] = o0 + k < p.ncls ? bs[o0 + k] : 0.0f;
+                for (int cw = 0; cw < p.cwi; ++cw) {
+                    const uint32_t w0 = __ldg(p.in + (size_t)g0 * p.cwi + cw);
+                    const uint32_t w1 = two ? __ldg(p.in + (size_t)(g0 + 1) * p.cwi + cw) : 0u;
+                    const int cn = min(32, p.Cin - cw * 32);
+                    for (int b = 0; b < cn; ++b) {
+                        const int c = cw * 32 + b;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            if (o0 + k < p.ncls) {
+                                const float wv = ws[(o0 + k) * p.Cin + c];
+                                acc[0][k] = __fadd_rn(acc[0][k], ((w0 >> b) & 1u) ? wv : -wv);
+                                acc[1][k] = __fadd_rn(acc[1][k], ((w1 >> b) & 1u) ? wv : -wv);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (h == 1 && !two) break;
+                    const unsigned g = g0 + h, n = g / HW, px = g - n * HW;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (o0 + k < p.ncls) p.out[(size_t)(n * p.ncls + o0 + k) * HW + px] = acc[h][k];
+                }
             }
-            p.out[(n * p.ncls + o) * HW + px] = acc;
+        } else {
+            // weights past the shared-memory table: one chain at a time from global memory
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+                const unsigned g = g0 + h, n = g / HW, px = g - n * HW;
+                const uint32_t* a = p.in + (size_t)g * p.cwi;
+                for (int o = 0; o < p.ncls; ++o) {
+                    float acc = __ldg(p.bias + o);
+                    const float* w = p.Wt + (size_t)o * p.Cin;
+                    uint32_t word = 0u;
+                    for (int c = 0; c < p.Cin; ++c) {
+                        if ((c & 31) == 0) word = __ldg(a + (c >> 5));
+                        const float wv = __ldg(w + c);
+                        acc = __fadd_rn(acc, ((word >> (c & 31)) & 1u) ? wv : -wv);
+                    }
+                    p.out[(size_t)(n * p.ncls + o) * HW + px] = acc;
+                }
+            }
         }
     }
 }
