@@ -1153,6 +1153,17 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo_bytes) 
            ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
 }
 
+// 4 activation bits -> 4 int8 of +-1 (bit 1 -> +1, bit 0 -> -1): the
+// multiply spreads bit i to bit 8i (the shifted copies do not overlap, so no
+// carries), and ~(b * 0xFE) maps each byte b in {0, 1} to 0xFF / 0x01.
+__device__ __forceinline__ uint32_t expand4(uint32_t nib) {
+    return ~(((nib * 0x00204081u) & 0x01010101u) * 0xFEu);
+}
+__device__ __forceinline__ void expand32(uint32_t w, uint4& lo, uint4& hi) {
+    lo = make_uint4(expand4(w & 15u), expand4((w >> 4) & 15u), expand4((w >> 8) & 15u), expand4((w >> 12) & 15u));
+    hi = make_uint4(expand4((w >> 16) & 15u), expand4((w >> 20) & 15u), expand4((w >> 24) & 15u), expand4(w >> 28));
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
@@ -1255,7 +1266,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     extern __shared__ __align__(1024) unsigned char ws_smem[];
     __shared__ __align__(8) unsigned long long full_b[8], empty_b[8], accf_b[2], acce_b[2];
     __shared__ uint32_t tmem_s;
-    __shared__ uint2 lut[256];  // byte -> 8 bytes of +-1
     __shared__ int abort_s;
     volatile int* abort_v = &abort_s;
 
@@ -1292,15 +1302,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    for (int b = tid; b < 256; b += C::NT) {
-        uint32_t w[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t x = (((uint32_t)b >> (4 * h)) & 15u) * 0x00204081u & 0x01010101u;
-            w[h] = 0xFFFFFFFFu ^ (x * 0xFEu);
-        }
-        lut[b] = make_uint2(w[0], w[1]);
-    }
     for (int c = tid; c < p.Gw; c += C::NT) {
         int cm = -1;
         if (c > 0) {
@@ -1309,42 +1310,39 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         }
         colmap[c] = cm;
     }
-    for (int w = tid; w < nwo; w += C::NT) {
-        uint32_t band = 0u, it = 0u, ib = 0u;
-        for (int i = 0; i < 32; ++i) {
-            const int c = w * 32 + i;
-            int T = -(1 << 30), inv_t = 0;  // channels past Cout: bit 0
-            int2 e = make_int2(0, 0);
-            if (c < p.Cout) {
-                const FoldIv f = p.fold[c];
-                const bool lo_open = f.lo == INT_MIN, hi_open = f.hi == INT_MAX;
-                if (f.lo >= f.hi) {                 // empty: bit = inv
-                    inv_t = f.inv;
-                } else if (lo_open && hi_open) {    // const: bit = !inv
-                    inv_t = f.inv ^ 1;
-                } else if (lo_open) {               // P < hi
-                    T = f.hi; inv_t = f.inv;
-                } else if (hi_open) {               // P >= lo
-                    T = f.lo; inv_t = f.inv ^ 1;
-                } else {
-                    band = 1u;
-                }
-                e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
-                ib |= (uint32_t)(f.inv & 1) << i;
+    for (int w = warp; w < nwo; w += C::NT / 32) {  // one warp per 32-channel word, lane = channel
+        const int c = w * 32 + lane;
+        int T = -(1 << 30), inv_t = 0, inv = 0;  // channels past Cout: bit 0
+        bool band = false;
+        int2 e = make_int2(0, 0);
+        if (c < p.Cout) {
+            const FoldIv f = p.fold[c];
+            const bool lo_open = f.lo == INT_MIN, hi_open = f.hi == INT_MAX;
+            if (f.lo >= f.hi) {                 // empty: bit = inv
+                inv_t = f.inv;
+            } else if (lo_open && hi_open) {    // const: bit = !inv
+                inv_t = f.inv ^ 1;
+            } else if (lo_open) {               // P < hi
+                T = f.hi; inv_t = f.inv;
+            } else if (hi_open) {               // P >= lo
+                T = f.lo; inv_t = f.inv ^ 1;
+            } else {
+                band = true;
             }
-            T = max(-(1 << 30), min(1 << 30, T));  // |P| < 2^24: clamping keeps every comparison
-            fu[c] = e;
-            fstart[c] = -T;
-            it |= (uint32_t)(inv_t & 1) << i;
+            e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
+            inv = f.inv & 1;
         }
-        finv_t[w] = it;
-        finv_b[w] = ib;
-        fband[w] = band;
+        T = max(-(1 << 30), min(1 << 30, T));  // |P| < 2^24: clamping keeps every comparison
+        const uint32_t bw = __ballot_sync(0xffffffffu, band);
+        fu[c] = e;
+        fstart[c] = bw ? 0 : -T;  // a band word starts at 0
+        const uint32_t it = __ballot_sync(0xffffffffu, inv_t & 1), ib = __ballot_sync(0xffffffffu, inv);
+        if (lane == 0) {
+            finv_t[w] = it;
+            finv_b[w] = ib;
+            fband[w] = bw ? 1u : 0u;
+        }
     }
-    __syncthreads();
-    for (int w = tid; w < nwo; w += C::NT)
-        if (fband[w])
-            for (int i = 0; i < 32; ++i) fstart[w * 32 + i] = 0;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1449,13 +1447,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                     const int q = pt + NPROD * j;
                     if (q < SP) {
                         uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                        if (cur[q].x >= 0) {  // an image pixel: +-1 (an uncovered concat word reads as -1)
-                            const uint32_t w = v[j];
-                            const uint2 b0 = lut[w & 255], b1 = lut[(w >> 8) & 255], b2 = lut[(w >> 16) & 255],
-                                        b3 = lut[w >> 24];
-                            lo = make_uint4(b0.x, b0.y, b1.x, b1.y);
-                            hi = make_uint4(b2.x, b2.y, b3.x, b3.y);
-                        }
+                        if (cur[q].x >= 0) expand32(v[j], lo, hi);  // a pixel (an uncovered concat word: -1s)
                         *reinterpret_cast<uint4*>(As + (size_t)q * 16) = lo;
                         *reinterpret_cast<uint4*>(As + ((size_t)SP + q) * 16) = hi;
                     }
@@ -1643,7 +1635,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
     extern __shared__ __align__(1024) unsigned char wp_smem[];
     __shared__ __align__(8) unsigned long long full_b[8], empty_b[8], accf_b[2], acce_b[2];
     __shared__ uint32_t tmem_s;
-    __shared__ uint2 lut[256];
     __shared__ int abort_s;
     volatile int* abort_v = &abort_s;
 
@@ -1677,15 +1668,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
         }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    for (int b = tid; b < 256; b += C::NT) {
-        uint32_t w[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t x = (((uint32_t)b >> (4 * h)) & 15u) * 0x00204081u & 0x01010101u;
-            w[h] = 0xFFFFFFFFu ^ (x * 0xFEu);
-        }
-        lut[b] = make_uint2(w[0], w[1]);
-    }
     for (int c = tid; c < p.Gw; c += C::NT) {
         int cm = -1;
         if (c > 0) {
@@ -1709,30 +1691,27 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
         e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
         inv = f.inv & 1;
     };
-    for (int w = tid; w < nwo; w += C::NT) {
-        uint32_t m[6] = {0, 0, 0, 0, 0, 0};
-        int T, it, iv;
-        bool bd;
-        int2 e;
-        for (int i = 0; i < 32; ++i) {
-            const int c = w * 32 + i;
-            classify(p.fold, c, T, it, bd, e, iv);
-            fu1[c] = e;
-            fstart[c] = -T;
-            m[0] |= (uint32_t)it << i; m[1] |= (uint32_t)iv << i; m[2] |= (uint32_t)bd;
-            classify(p.fold2, c, T, it, bd, e, iv);
-            fu2[c] = e;
-            fd2[c] = -T;
-            m[3] |= (uint32_t)it << i; m[4] |= (uint32_t)iv << i; m[5] |= (uint32_t)bd;
-        }
+    for (int w = warp; w < nwo; w += C::NT / 32) {  // one warp per 32-channel word, lane = channel
+        const int c = w * 32 + lane;
+        int T1, T2, it1, it2, iv1, iv2;
+        bool bd1, bd2;
+        int2 e1, e2;
+        classify(p.fold, c, T1, it1, bd1, e1, iv1);
+        classify(p.fold2, c, T2, it2, bd2, e2, iv2);
+        uint32_t m[6];
+        m[0] = __ballot_sync(0xffffffffu, it1 & 1); m[1] = __ballot_sync(0xffffffffu, iv1);
+        m[2] = __ballot_sync(0xffffffffu, bd1) ? 1u : 0u;
+        m[3] = __ballot_sync(0xffffffffu, it2 & 1); m[4] = __ballot_sync(0xffffffffu, iv2);
+        m[5] = __ballot_sync(0xffffffffu, bd2) ? 1u : 0u;
+        fu1[c] = e1;
+        fu2[c] = e2;
         // band words start at 0; fold2 offset = -start - T2 (threshold words) or -start
-        for (int i = 0; i < 32; ++i) {
-            const int c = w * 32 + i;
-            const int st = m[2] ? 0 : fstart[c];
-            fstart[c] = st;
-            fd2[c] = m[5] ? -st : -st + fd2[c];
-        }
-        for (int k = 0; k < 6; ++k) fm[k * nwo + w] = m[k];
+        const int st = m[2] ? 0 : -T1;
+        fstart[c] = st;
+        fd2[c] = m[5] ? -st : -st - T2;
+        if (lane == 0)
+#pragma unroll
+            for (int k = 0; k < 6; ++k) fm[k * nwo + w] = m[k];
     }
     tc_fence_before();
     __syncthreads();
@@ -1832,13 +1811,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                         const int q = pt + NPROD * j;
                         if (q < SP) {
                             uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                            if (cur[ph * SP + q] >= 0) {
-                                const uint32_t w = v[ph * NQP + j];
-                                const uint2 b0 = lut[w & 255], b1 = lut[(w >> 8) & 255], b2 = lut[(w >> 16) & 255],
-                                            b3 = lut[w >> 24];
-                                lo = make_uint4(b0.x, b0.y, b1.x, b1.y);
-                                hi = make_uint4(b2.x, b2.y, b3.x, b3.y);
-                            }
+                            if (cur[ph * SP + q] >= 0) expand32(v[ph * NQP + j], lo, hi);
                             // [phase][k half][position][16 bytes]
                             *reinterpret_cast<uint4*>(As + ((size_t)(ph * 2) * SP + q) * 16) = lo;
                             *reinterpret_cast<uint4*>(As + ((size_t)(ph * 2 + 1) * SP + q) * 16) = hi;
@@ -2405,7 +2378,7 @@ __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
                     const uint32_t w0 = __ldg(p.in + (size_t)g0 * p.cwi + cw);
                     const uint32_t w1 = two ? __ldg(p.in + (size_t)(g0 + 1) * p.cwi + cw) : 0u;
                     const int cn = min(32, p.Cin - cw * 32);
-                    for (int b = 0; b < cn; ++b) {
+                    auto step = [&](int b) {
                         const int c = cw * 32 + b;
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
@@ -2415,6 +2388,12 @@ __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
                                 acc[1][k] = __fadd_rn(acc[1][k], ((w1 >> b) & 1u) ? wv : -wv);
                             }
                         }
+                    };
+                    if (cn == 32) {
+#pragma unroll
+                        for (int b = 0; b < 32; ++b) step(b);
+                    } else {
+                        for (int b = 0; b < cn; ++b) step(b);
                     }
                 }
 #pragma unroll
