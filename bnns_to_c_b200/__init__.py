@@ -89,6 +89,8 @@ def lib():
         "bnn_set_bconv_kernel": (ip, [ip]),
         "bnn_device_error": (ip, [ip, ctypes.POINTER(ctypes.c_uint)]),
         "bnn_set_first_conv_kernel": (ip, [ip]),
+        "bnn_forward_patched": (ip, [vp, vp, ip, ip, vp, ip]),
+        "bnn_forward_patched_device": (ip, [vp, ip, vp, ip, ip, ip, vp, vp]),
         "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
     }
     for name, (res, args) in sig.items():
@@ -194,6 +196,21 @@ class Model:
     def set_devices(self, devices):
         arr = (ctypes.c_int * max(1, len(devices)))(*devices)
         _check(lib().bnn_set_devices(self.handle, arr, len(devices)))
+
+    def forward_patched(self, cube, P=32, out=None):
+        """Whole-scene patch-wise forward (the reference's tiler): host
+        [bands, H, W] float32 -> [classes, H, W]."""
+        cube = np.ascontiguousarray(cube, np.float32)
+        _, H, W = cube.shape
+        if out is None:
+            out = np.empty((self.n_classes, H, W), np.float32)
+        _check(lib().bnn_forward_patched(self.handle, cube.ctypes.data, H, W, out.ctypes.data, P))
+        return out
+
+    def forward_patched_device(self, device, d_cube, H, W, d_logits, P=32, stream=None):
+        _check(lib().bnn_forward_patched_device(self.handle, device, _ptr(d_cube), H, W, P, _ptr(d_logits),
+                                                stream if stream is None or isinstance(stream, int)
+                                                else stream.cuda_stream))
 
     def set_chunk(self, n):
         _check(lib().bnn_set_chunk(self.handle, n))

@@ -112,6 +112,12 @@ struct DevState {
     cudaEvent_t ev_in[2], ev_comp[2], ev_out[2];
     cudaEvent_t ev_last;  // completion of the last forward enqueued on this device
     bool events = false;
+    // patched (scene) forward: a chunk of tiles in and out, and a scene slab
+    float *tin = nullptr, *tout = nullptr;
+    size_t tcap = 0;  // floats of tin / tout
+    size_t tcap_out = 0;
+    float *scube = nullptr, *slog = nullptr;
+    size_t scube_cap = 0, slog_cap = 0;  // floats
 };
 
 struct Engine {
@@ -137,6 +143,7 @@ static void dev_release(DevState* d) {
     cudaFree(d->wbase);
     cudaFree(d->ar.base);
     for (int s = 0; s < 2; ++s) { cudaFree(d->pin[s]); cudaFree(d->pout[s]); }
+    cudaFree(d->tin); cudaFree(d->tout); cudaFree(d->scube); cudaFree(d->slog);
     if (d->events)
     {
         for (int s = 0; s < 2; ++s) {
@@ -1163,6 +1170,71 @@ static int host_batch_on(const Model* m, int device, const float* in, int N, int
     return BNN_OK;
 }
 
+// device buffer of at least `n` floats, kept in *buf / *cap across calls
+static int grow(float** buf, size_t* cap, size_t n, const char* what) {
+    if (*cap >= n) return BNN_OK;
+    cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    if (cudaMalloc(buf, n * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_OOM, "cudaMalloc %s (%zu bytes)", what, n * sizeof(float));
+    }
+    *cap = n;
+    return BNN_OK;
+}
+
+// tiles per forward of the patched path
+static constexpr int kSceneChunk = 4096;
+
+// Patched forward of a [bands][H][W] scene on device d: chunks of PxP tiles
+// gathered from the cube, the batched forward (graph replay), the in-scene
+// part of their logits stitched into [classes][H][W]. Called with d->mu held.
+static int scene_device(const Model* m, DevState* d, const float* cube, int H, int W, int P, float* logits,
+                        cudaStream_t st) {
+    const int tx = cdiv(W, P), ty = cdiv(H, P), nt = tx * ty;
+    const int C = std::min(nt, kSceneChunk);
+    const size_t in_per = (size_t)m->n_bands * P * P, out_per = (size_t)m->n_classes * P * P;
+    int rc;
+    if ((rc = grow(&d->tin, &d->tcap, (size_t)C * in_per, "scene tiles"))) return rc;
+    if ((rc = grow(&d->tout, &d->tcap_out, (size_t)C * out_per, "scene tile logits"))) return rc;
+    for (int t0 = 0; t0 < nt; t0 += C) {
+        const int n = std::min(C, nt - t0);
+        const size_t gin = (size_t)n * m->n_bands * P * (((W | P) & 3) == 0 ? P / 4 : P);
+        tile_gather_kernel<<<(unsigned)std::min<size_t>((gin + 255) / 256, 148 * 32), 256, 0, st>>>(
+            cube, m->n_bands, H, W, P, tx, t0, n, d->tin);
+        CK(cudaGetLastError());
+        if ((rc = forward_device(m, d, d->tin, n, P, P, d->tout, st, nullptr))) return rc;
+        const size_t gout = (size_t)n * m->n_classes * P * (((W | P) & 3) == 0 ? P / 4 : P);
+        tile_stitch_kernel<<<(unsigned)std::min<size_t>((gout + 255) / 256, 148 * 32), 256, 0, st>>>(
+            d->tout, m->n_classes, H, W, P, tx, t0, n, logits);
+        CK(cudaGetLastError());
+    }
+    return BNN_OK;
+}
+
+// patched forward of scene rows [y0, y1) of a host cube on one device: the
+// slab in (one strided copy), scene_device, the logits slab out
+static int scene_host_on(const Model* m, int device, const float* in, int H, int W, int y0, int y1, int P,
+                         float* out) {
+    CK(cudaSetDevice(device));
+    DevState* d = nullptr;
+    int rc = get_dev(m, device, &d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> g(d->mu);
+    const int Hs = y1 - y0;
+    const size_t plane = (size_t)Hs * W;
+    if ((rc = grow(&d->scube, &d->scube_cap, (size_t)m->n_bands * plane, "scene slab"))) return rc;
+    if ((rc = grow(&d->slog, &d->slog_cap, (size_t)m->n_classes * plane, "scene logits"))) return rc;
+    CK(cudaMemcpy2DAsync(d->scube, plane * 4, in + (size_t)y0 * W, (size_t)H * W * 4, plane * 4, m->n_bands,
+                         cudaMemcpyHostToDevice, d->cs));
+    if ((rc = scene_device(m, d, d->scube, Hs, W, P, d->slog, d->cs))) return rc;
+    CK(cudaMemcpy2DAsync(out + (size_t)y0 * W, (size_t)H * W * 4, d->slog, plane * 4, plane * 4, m->n_classes,
+                         cudaMemcpyDeviceToHost, d->cs));
+    CK(cudaStreamSynchronize(d->cs));
+    return BNN_OK;
+}
+
 }  // namespace bnn
 
 using namespace bnn;
@@ -1232,6 +1304,66 @@ BNN_API int bnn_forward_batch(const Model* m, const float* input, int N, int H, 
     for (int r = 0; r < nd; ++r)
         if (st[r]) return set_error(st[r], "device %d: %s", devs[r], msg[r].c_str());
     return BNN_OK;
+}
+
+BNN_API int bnn_forward_patched(const Model* m, const float* input, int H, int W, float* logits, int P) {
+    if (!m || !input || !logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    if (H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "scene %dx%d", H, W);
+    int rc = check_hw(1, P, P);  // every tile is a PxP forward
+    if (rc) return rc;
+    Engine* E = (Engine*)m->engine;
+    std::vector<int> devs;
+    {
+        std::lock_guard<std::mutex> g(E->mu);
+        devs = E->devices;
+    }
+    int prev = 0;
+    if (devs.empty()) {
+        if ((rc = current_device(&prev))) return rc;
+        devs.push_back(prev);
+    } else {
+        cudaGetDevice(&prev);
+    }
+    const int ty = cdiv(H, P), nd = std::min((int)devs.size(), ty);
+    std::vector<int> st(nd, BNN_OK);
+    std::vector<std::string> msg(nd);
+    std::vector<std::thread> th;
+    for (int r = 0; r < nd; ++r) {
+        const int r0 = (int)((long)ty * r / nd), r1 = (int)((long)ty * (r + 1) / nd);
+        auto job = [&, r, r0, r1]() {
+            st[r] = scene_host_on(m, devs[r], input, H, W, r0 * P, std::min(r1 * P, H), P, logits);
+            if (st[r]) msg[r] = bnn_last_error();
+        };
+        if (nd == 1) job();
+        else th.emplace_back(job);
+    }
+    for (auto& t : th) t.join();
+    cudaSetDevice(prev);
+    for (int r = 0; r < nd; ++r)
+        if (st[r]) return nd == 1 ? st[r] : set_error(st[r], "device %d: %s", devs[r], msg[r].c_str());
+    return BNN_OK;
+}
+
+BNN_API int bnn_forward_patched_device(const Model* m, int device, const float* d_cube, int H, int W, int P,
+                                       float* d_logits, void* stream) {
+    if (!m || !d_cube || !d_logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    if (H <= 0 || W <= 0) return set_error(BNN_ERR_ARG, "scene %dx%d", H, W);
+    int rc = check_hw(1, P, P);
+    if (rc) return rc;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_ARG, "cannot select device %d", device);
+    }
+    DevState* d = nullptr;
+    rc = get_dev(m, device, &d);
+    if (!rc) {
+        std::lock_guard<std::mutex> g(d->mu);
+        rc = scene_device(m, d, d_cube, H, W, P, d_logits, (cudaStream_t)stream);
+    }
+    cudaSetDevice(prev);
+    return rc;
 }
 
 BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float* logits) {

@@ -2339,6 +2339,62 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------
+// Scene tiling for the patched forward (csrc/bnn_model_react.c:454-476 on the
+// v1 forward): tile t = (row t / tiles_x, column t % tiles_x) of a
+// [bands][H][W] cube is its PxP block, zero-padded past the right and bottom
+// edges; the in-scene part of each tile's logits goes back to [classes][H][W].
+// Four consecutive columns per thread when W and P are multiples of 4 (all
+// four then lie on the same side of the scene edge).
+// ---------------------------------------------------------------------
+__global__ void tile_gather_kernel(const float* __restrict__ cube, int bands, int H, int W, int P, int tiles_x,
+                                   int tile0, int ntiles, float* __restrict__ out) {
+    const int v4 = ((W | P) & 3) == 0 ? 4 : 1;
+    const int gx = P / v4;
+    const size_t total = (size_t)ntiles * bands * P * gx;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+        const int xg = (int)(g % gx);
+        size_t r = g / gx;
+        const int y = (int)(r % P);
+        r /= P;
+        const int b = (int)(r % bands);
+        const int t = (int)(r / bands);
+        const int tt = tile0 + t, py = (tt / tiles_x) * P, px = (tt % tiles_x) * P;
+        const int sy = py + y, sx = px + xg * v4;
+        float* dst = out + (((size_t)t * bands + b) * P + y) * P + xg * v4;
+        const float* src = cube + ((size_t)b * H + sy) * W + sx;
+        if (v4 == 4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (sy < H && sx < W) v = __ldg(reinterpret_cast<const float4*>(src));
+            *reinterpret_cast<float4*>(dst) = v;
+        } else {
+            *dst = (sy < H && sx < W) ? __ldg(src) : 0.0f;
+        }
+    }
+}
+
+__global__ void tile_stitch_kernel(const float* __restrict__ tiles, int classes, int H, int W, int P, int tiles_x,
+                                   int tile0, int ntiles, float* __restrict__ logits) {
+    const int v4 = ((W | P) & 3) == 0 ? 4 : 1;
+    const int gx = P / v4;
+    const size_t total = (size_t)ntiles * classes * P * gx;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+        const int xg = (int)(g % gx);
+        size_t r = g / gx;
+        const int y = (int)(r % P);
+        r /= P;
+        const int c = (int)(r % classes);
+        const int t = (int)(r / classes);
+        const int tt = tile0 + t, py = (tt / tiles_x) * P, px = (tt % tiles_x) * P;
+        const int sy = py + y, sx = px + xg * v4;
+        if (sy >= H || sx >= W) continue;
+        const float* src = tiles + (((size_t)t * classes + c) * P + y) * P + xg * v4;
+        float* dst = logits + ((size_t)c * H + sy) * W + sx;
+        if (v4 == 4) *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+        else *dst = *src;
+    }
+}
+
+// ---------------------------------------------------------------------
 // FP32 1x1 head on the last bit plane: logits = bias + sum_c W*a, sequential
 // over c from the bias (csrc/bnn_head.c:21-34, after the int8 -> float widen
 // of csrc/bnn_model.c:241-251). a = +-1 makes every product exact.

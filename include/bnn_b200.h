@@ -57,6 +57,23 @@ int bnn_forward_batch(const Model *m, const float *input, int N, int H, int W,
 int bnn_forward_device(const Model *m, int device, const float *d_input, int N,
                        int H, int W, float *d_logits, void *stream);
 
+/* Patch-wise forward of a whole scene: the reference's tiler
+ * (bnn_forward_react_patched, csrc/bnn_model_react.c:454-476, same
+ * signature) applied to the v1 network. The [n_bands][H][W] cube is cut into
+ * non-overlapping PxP tiles, zero-padded past the right and bottom edges,
+ * each tile runs through the full network as a standalone PxP image, and the
+ * in-scene part of its logits is stitched into [n_classes][H][W]. Tile rows
+ * are split over the Model's devices (bnn_set_devices). Host pointers;
+ * blocks until the logits are in host memory. P >= 16. */
+int bnn_forward_patched(const Model *m, const float *input, int H, int W,
+                        float *logits, int P);
+
+/* The same on device memory of `device`, enqueued on `stream` (tiles are
+ * gathered and stitched on the GPU, in chunks of 4096 tiles). */
+int bnn_forward_patched_device(const Model *m, int device, const float *d_cube,
+                               int H, int W, int P, float *d_logits,
+                               void *stream);
+
 /* Process-wide choice of the binary-conv kernel, for measurement and A/B
  * parity tests: 0 = tcgen05 int8 MMAs for the non-pooled layers and
  * mma.sync int8 for the pooled encoder convs (default), 1 = XOR + POPC on

@@ -490,6 +490,40 @@ int oracle_forward(const OModel *m, const float *input, int H, int W,
     return 0;
 }
 
+/* Patch-wise forward of a whole scene (csrc/bnn_model_react.c:454-476, the
+ * reference's tiler, applied to the v1 forward): non-overlapping PxP tiles,
+ * each cut from the [n_bands][H][W] cube and zero-padded at the right and
+ * bottom edges, run through the full network as a standalone PxP image; the
+ * in-scene part of each tile's logits is written to [n_classes][H][W]. */
+int oracle_forward_patched(const OModel *m, const float *input, int H, int W,
+                           float *logits, int P) {
+    const int nb = m->n_bands, ncl = m->n_classes;
+    if (P <= 0 || H <= 0 || W <= 0) return 1;
+    float *pin = (float *)malloc((size_t)nb * P * P * sizeof(float));
+    float *pout = (float *)malloc((size_t)ncl * P * P * sizeof(float));
+    if (!pin || !pout) { free(pin); free(pout); return 1; }
+    int rc = 0;
+    for (int py = 0; py < H && !rc; py += P) {
+        const int ph = py + P < H ? P : H - py;
+        for (int px = 0; px < W && !rc; px += P) {
+            const int pw = px + P < W ? P : W - px;
+            memset(pin, 0, (size_t)nb * P * P * sizeof(float));
+            for (int b = 0; b < nb; ++b)
+                for (int y = 0; y < ph; ++y)
+                    memcpy(pin + ((size_t)b * P + y) * P, input + ((size_t)b * H + py + y) * W + px,
+                           (size_t)pw * sizeof(float));
+            rc = oracle_forward(m, pin, P, P, pout, NULL, NULL);
+            for (int c = 0; c < ncl && !rc; ++c)
+                for (int y = 0; y < ph; ++y)
+                    memcpy(logits + ((size_t)c * H + py + y) * W + px, pout + ((size_t)c * P + y) * P,
+                           (size_t)pw * sizeof(float));
+        }
+    }
+    free(pin);
+    free(pout);
+    return rc;
+}
+
 int oracle_forward_batch(const OModel *m, const float *input, int n, int H,
                          int W, float *logits) {
     size_t in_per = (size_t)m->n_bands * H * W, out_per = (size_t)m->n_classes * H * W;

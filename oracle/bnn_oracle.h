@@ -35,6 +35,8 @@ int oracle_base_channels(const OModel *m);
 int oracle_forward(const OModel *m, const float *input, int H, int W,
                    float *logits, oracle_stage_cb cb, void *ctx);
 /* n patches of [bands][H][W], contiguous */
+int oracle_forward_patched(const OModel *m, const float *input, int H, int W,
+                           float *logits, int P);
 int oracle_forward_batch(const OModel *m, const float *input, int n, int H,
                          int W, float *logits);
 

@@ -30,6 +30,8 @@ def olib():
         L.oracle_forward.restype = ip
         L.oracle_forward_batch.argtypes = [vp, vp, ip, ip, ip, vp]
         L.oracle_forward_batch.restype = ip
+        L.oracle_forward_patched.argtypes = [vp, vp, ip, ip, vp, ip]
+        L.oracle_forward_patched.restype = ip
         L.oracle_pack_weights.argtypes = [vp, vp, ip, ip, ip, ip]
         L.oracle_bconv_P.argtypes = [vp, vp, vp] + [ip] * 8
         L.oracle_realin.argtypes = [vp, vp, vp, vp] + [ip] * 8
@@ -72,6 +74,15 @@ class OModel:
         rc = olib().oracle_forward(self.h, x.ctypes.data, H, W, logits.ctypes.data, fn, None)
         if rc:
             raise ValueError("oracle_forward refused the input")
+        return out
+
+    def forward_patched(self, cube, P=32):
+        cube = np.ascontiguousarray(cube, np.float32)
+        _, H, W = cube.shape
+        out = np.zeros((self.n_classes, H, W), np.float32)
+        rc = olib().oracle_forward_patched(self.h, cube.ctypes.data, H, W, out.ctypes.data, P)
+        if rc:
+            raise ValueError("oracle_forward_patched refused the input")
         return out
 
     def forward_batch(self, x):

@@ -376,3 +376,37 @@ def test_first_conv_tensor_path_band_counts(bands, first_kind):
     exact, _ = _first_conv_bits(m, x, True)
     assert np.array_equal(fast, exact)
     assert und < 4 * 32 * 32 * 32 // 100
+
+
+# ------------------------------------------------------------------ whole-scene patched forward
+@pytest.mark.parametrize("H,W,P", [(70, 50, 32), (20, 45, 16), (64, 96, 32), (33, 100, 32), (16, 16, 16)])
+def test_patched_forward_matches_oracle(H, W, P, tmp_path):
+    """bnn_forward_patched (the reference's tiler, csrc/bnn_model_react.c:454-476,
+    on the v1 forward) against the oracle tiler, bit for bit, through the host
+    and the device entry points; partial edge tiles included."""
+    from oracle_util import OModel
+    path = tmp_path / "m.blob"
+    path.write_bytes(B.blob_bytes(B.random_model(16, 120, 3, seed=13, rules="baseline")))
+    m, om = bn.Model(str(path)), OModel(str(path))
+    cube = synth(9, 0, 1, 120, H, W)[0]
+    want = om.forward_patched(cube, P)
+    got = m.forward_patched(cube, P)
+    assert same_bits(got, want)
+    dc = torch.from_numpy(cube).cuda()
+    dl = torch.full((3, H, W), float("nan"), dtype=torch.float32, device="cuda")
+    m.forward_patched_device(0, dc, H, W, dl, P)
+    torch.cuda.synchronize()
+    assert same_bits(dl.cpu().numpy(), want)
+
+
+def test_patched_forward_multi_device(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU")
+    path = tmp_path / "m.blob"
+    path.write_bytes(B.blob_bytes(B.random_model(16, 120, 3, seed=13, rules="baseline")))
+    m = bn.Model(str(path))
+    cube = synth(10, 0, 1, 120, 150, 90)[0]
+    one = m.forward_patched(cube, 32)
+    m.set_devices([0, 1])
+    two = m.forward_patched(cube, 32)
+    assert same_bits(one, two)

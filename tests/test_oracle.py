@@ -89,3 +89,28 @@ def test_synth_distribution_and_determinism():
     assert np.abs(v).max() <= 3.47
     # pinned value (guards the generator against silent changes)
     assert float(synth(0, 0, 1, 1, 1, 1)[0, 0, 0, 0]).hex() == "0x1.fd9d880000000p-1"
+
+
+@pytest.mark.parametrize("H,W,P", [(70, 50, 32), (32, 32, 32), (20, 45, 16), (64, 96, 32)])
+def test_oracle_patched_is_tiles_of_the_forward(H, W, P, tmp_path):
+    """The scene tiler (csrc/bnn_model_react.c:454-476 semantics on the v1
+    forward) equals cutting zero-padded PxP tiles by hand, running the pinned
+    per-patch oracle forward on them and stitching the in-scene parts."""
+    path = tmp_path / "m.blob"
+    path.write_bytes(B.blob_bytes(B.random_model(8, 120, 3, seed=11, rules="baseline")))
+    m = OModel(str(path))
+    cube = synth(5, 0, 1, 120, H, W)[0]
+    got = m.forward_patched(cube, P)
+    ty, tx = -(-H // P), -(-W // P)
+    tiles = np.zeros((ty * tx, 120, P, P), np.float32)
+    for r in range(ty):
+        for c in range(tx):
+            blk = cube[:, r * P:(r + 1) * P, c * P:(c + 1) * P]
+            tiles[r * tx + c, :, :blk.shape[1], :blk.shape[2]] = blk
+    lt = m.forward_batch(tiles)
+    want = np.zeros((3, H, W), np.float32)
+    for r in range(ty):
+        for c in range(tx):
+            ph, pw = min(P, H - r * P), min(P, W - c * P)
+            want[:, r * P:r * P + ph, c * P:c * P + pw] = lt[r * tx + c, :, :ph, :pw]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
