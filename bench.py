@@ -22,6 +22,13 @@ timing is the max over ranks.
           (oracle/_ref/ref_bench), all host cores, bounded sample
 
 --impl reference times only the reference CPU engine (rank 0).
+
+--workload scene runs BASELINE config 3 instead: 16 scene cubes of
+956x684x120 float32 (seeded synthetic values, cube index as the patch key)
+through the patched forward (non-overlapping zero-padded 32x32 tiles,
+30x22 = 660 per cube), the cubes split over the ranks (strong scaling of the
+fixed 16-cube job); value = tiles/s with the cubes in HBM, e2e = tiles/s
+through bnn_forward_patched from host memory (2 cubes per rank).
 """
 
 from __future__ import annotations
@@ -350,6 +357,99 @@ def run_ours(args):
     return 0
 
 
+def run_scene(args):
+    import torch
+
+    import bnns_to_c_b200 as bn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def maxall(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    H, W, Pt, total = 956, 684, 32, args.cubes
+    mine = list(range(rank, total, world))  # this rank's cubes
+    tiles = -(-H // Pt) * -(-W // Pt)
+    m = bn.Model(data=model_blob())
+    m.set_devices([local])
+    cubes = [torch.empty((120, H, W), dtype=torch.float32, device="cuda") for _ in mine]
+    logs = [torch.empty((3, H, W), dtype=torch.float32, device="cuda") for _ in mine]
+    for c, i in zip(cubes, mine):
+        bn.synth_device(local, SEED_INPUT, 1000 + i, 1, 120, H, W, c)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            for c, lg in zip(cubes, logs):
+                m.forward_patched_device(local, c, H, W, lg, Pt, stream)
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            for c, lg in zip(cubes, logs):
+                m.forward_patched_device(local, c, H, W, lg, Pt, stream)
+        e1.record(stream)
+        stream.synchronize()
+    if dist:
+        dist.barrier()
+    dev_ms = maxall(e0.elapsed_time(e1))
+    # end to end from host memory (a bounded sample: up to 2 cubes per rank)
+    ns = min(2, len(mine))
+    hc = [torch.empty((120, H, W), dtype=torch.float32, pin_memory=True) for _ in range(ns)]
+    hl = [torch.empty((3, H, W), dtype=torch.float32, pin_memory=True) for _ in range(ns)]
+    for i in range(ns):
+        hc[i].copy_(cubes[i].cpu())
+    for i in range(ns):
+        m.forward_patched(hc[i].numpy(), Pt, out=hl[i].numpy())
+    same = all(bool(torch.equal(hl[i].view(torch.int32), logs[i].cpu().view(torch.int32))) for i in range(ns))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for i in range(ns):
+            m.forward_patched(hc[i].numpy(), Pt, out=hl[i].numpy())
+    e2e_s = maxall(time.perf_counter() - t0)
+    job_tiles = tiles * total
+    if rank == 0:
+        line = {
+            "metric": "scene tiles/s (956x684x120 cubes, 32x32 tiles)",
+            "value": round(job_tiles * args.steps / (dev_ms / 1e3), 1), "unit": "tiles/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "b1+f32",
+            "data": "synthetic",
+            "config": {"workload": "scene_16x956x684x120_tiles32", "cubes": total, "tiles_per_cube": tiles,
+                       "cube_mb": round(120 * H * W * 4 / 1e6, 1), "parallelism": f"cube-shard x{world}",
+                       "l2": "inputs > L2 (each cube 314 MB)"},
+            "e2e": {"value": round(tiles * ns * world * args.steps / e2e_s, 1), "unit": "tiles/s",
+                    "h2d_bytes_per_step": 120 * H * W * 4 * ns * world, "d2h_bytes_per_step": 3 * H * W * 4 * ns * world,
+                    "api": "bnn_forward_patched (pinned host cubes)", "matches_device_path": same,
+                    "sample": f"{ns} cubes per rank"},
+            "gpu_launches": None,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -367,9 +467,14 @@ def main():
     ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
                          "mma = mma.sync for every layer")
+    ap.add_argument("--workload", default="unet", choices=["unet", "scene"],
+                    help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler")
+    ap.add_argument("--cubes", type=int, default=16, help="scene workload: cubes in the job")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "scene":
+        return run_scene(args)
     return run_ours(args)
 
 
