@@ -74,8 +74,8 @@ struct Arena {
     void* base = nullptr;
     size_t bytes = 0;
     uint32_t *enc_h[4], *skip[4], *down[4], *bott_h, *bott_x, *dec_h[4], *dec_x[4];
-    uint32_t* rm_list;        // first conv: undecided (pixel, channel) pairs
-    unsigned int* rm_ctl;     // [entries, overflow]
+    uint32_t* rm_list;        // first conv: undecided (pixel, channel group, mask) entries
+    unsigned int* rm_ctl;     // [entries, overflow, outputs]
     int rm_cap;
 };
 
@@ -561,7 +561,7 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
     const size_t outs = (size_t)Nn * H * W * m->enc_conv1[0].Cout;
     const int cap = (int)std::min<size_t>(std::max<size_t>(outs / 64, 65536), (size_t)1 << 24);
     const size_t list_off = off;
-    off += align256((size_t)cap * 8);
+    off += align256((size_t)cap * 16);
     const size_t ctl_off = off;
     off += 256;
     // graphs bake in arena pointers
@@ -883,7 +883,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
     if (g_first_kind == 0 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP && rw_geometry(H, W, &geo) &&
         first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32)) {
-        CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
+        CK(cudaMemsetAsync(a.rm_ctl, 0, 3 * sizeof(unsigned int), st));
         RealinWsParams p{};
         p.wu = d->rw_wu; p.out = out;
         for (int c = 0; c < 32; ++c) {
@@ -903,14 +903,14 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
                           Cout, p.cwo};
-        realin_fixup_kernel<<<148 * 4, 128, 0, st>>>(f);
+        realin_fixup_kernel<<<148 * 8, FIX_WARPS * 32, 0, st>>>(f);
         e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
         return BNN_OK;
     }
     if (!first_conv_tmap(x, N, m->enc_conv1[0].Cin, H, W, &tm))
         return run_realin_exact(d, m, x, N, H, W, out, nullptr, st);
-    CK(cudaMemsetAsync(a.rm_ctl, 0, 2 * sizeof(unsigned int), st));
+    CK(cudaMemsetAsync(a.rm_ctl, 0, 3 * sizeof(unsigned int), st));
     RealinMmaParams p{};
     p.wfrag = d->rm_wfrag; p.fold = d->ri_fold; p.exact_ch = d->rm_exact; p.out = out;
     p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
@@ -923,7 +923,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin mma launch: %s", cudaGetErrorString(e));
     RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, p.Cin, d->ri_CinP, H, W,
                       p.Cout, p.cwo};
-    realin_fixup_kernel<<<148 * 4, 128, 0, st>>>(f);
+    realin_fixup_kernel<<<148 * 8, FIX_WARPS * 32, 0, st>>>(f);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
     return BNN_OK;
@@ -1463,12 +1463,12 @@ BNN_API int bnn_first_conv_device(const Model* m, int device, const float* d_inp
                       : run_realin_exact(d, m, d_input, N, H, W, d_bits, nullptr, st);
             if (!rc) cudaEventRecord(d->ev_last, st);
             if (!rc && undecided) {
-                unsigned int ctl[2] = {0, 0};
+                unsigned int ctl[3] = {0, 0, 0};
                 if (fast && cudaMemcpyAsync(ctl, d->ar.rm_ctl, sizeof ctl, cudaMemcpyDeviceToHost, st) != cudaSuccess)
                     rc = set_error(BNN_ERR_CUDA, "D2H ctl");
                 if (!rc && cudaStreamSynchronize(st) != cudaSuccess)
                     rc = set_error(BNN_ERR_CUDA, "first conv: %s", cudaGetErrorString(cudaGetLastError()));
-                *undecided = ctl[1] ? 0xffffffffu : ctl[0];
+                *undecided = ctl[1] ? 0xffffffffu : ctl[2];
             }
         }
     }

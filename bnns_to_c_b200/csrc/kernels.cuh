@@ -476,8 +476,8 @@ struct RealinMmaParams {
     const float* fold;         // [CoutP][5]: alpha, A, B, slope, rsign
     const int* exact_ch;       // [CoutP]: 1 = fold not monotone, always take the exact path
     uint32_t* out;             // [N][H][W][cwo]
-    uint32_t* list;            // undecided outputs: (pixel index, channel) pairs
-    unsigned int* ctl;         // [0] = entries, [1] = overflow / staging failure
+    uint32_t* list;            // undecided outputs (realin_list)
+    unsigned int* ctl;         // [0] = entries, [1] = overflow / staging failure, [2] = outputs
     int cap;                   // list capacity (entries)
     int N, Cin, H, W, Cout, cwo, tiles_x, tiles_y;
     float c9;                  // e2 / T for a full 3x3 window, rounded up
@@ -485,6 +485,24 @@ struct RealinMmaParams {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Undecided first-conv outputs, listed one entry per pixel and 32-channel
+// group for realin_fixup_kernel: list[4s] = pixel index, [4s+1] = group,
+// [4s+2] = mask of the group's undecided channels. ctl[0] = entries,
+// ctl[1] = overflow / staging failure (the fix-up then redoes the batch),
+// ctl[2] = undecided outputs.
+__device__ __forceinline__ void realin_list(uint32_t* list, unsigned int* ctl, int cap, size_t pix, int g,
+                                            uint32_t mask) {
+    const unsigned int slot = atomicAdd(ctl, 1u);
+    if (slot < (unsigned)cap) {
+        list[4 * (size_t)slot] = (uint32_t)pix;
+        list[4 * (size_t)slot + 1] = (uint32_t)g;
+        list[4 * (size_t)slot + 2] = mask;
+    } else {
+        atomicExch(ctl + 1, 1u);
+    }
+    atomicAdd(ctl + 2, (unsigned)__popc(mask));
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
@@ -577,6 +595,7 @@ __global__ void __launch_bounds__(256, 2) realin_mma_kernel(const __grid_constan
     __shared__ __align__(8) unsigned long long bars[RM_NST];
     __shared__ int staged_ok;
     __shared__ uint32_t words[RM_TR * RM_TC];
+    __shared__ uint32_t umask[RM_TR * RM_TC];  // undecided channels per pixel
     __shared__ float fold_s[32][5];
     __shared__ int exact_s[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -593,7 +612,7 @@ __global__ void __launch_bounds__(256, 2) realin_mma_kernel(const __grid_constan
         for (int b = 0; b < RM_NST; ++b) mbar_init(smem_u32(&bars[b]), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (tid < RM_TR * RM_TC) words[tid] = 0u;
+    if (tid < RM_TR * RM_TC) { words[tid] = 0u; umask[tid] = 0u; }
     if (tid < 32) {
         const int co = blockIdx.y * 32 + tid;  // CoutP = multiple of 32: always in bounds
 #pragma unroll
@@ -724,14 +743,13 @@ __global__ void __launch_bounds__(256, 2) realin_mma_kernel(const __grid_constan
             const int col = mt * 16 + gid + half * 8;
             const int x = x0 + col;
             const bool valid = y < p.H && x < p.W;
-            uint32_t bits = 0u;
+            uint32_t bits = 0u, und = 0u;
             if (valid) {
                 float ef = 0.0f;
 #pragma unroll
                 for (int t = 0; t < 9; ++t) ef = __fadd_ru(ef, bpx[(row + t / 3) * RM_HC + col + t % 3]);
                 const bool finite = ef <= 3.0e38f;  // false for inf and NaN
                 const double e = (double)ef;
-                const size_t pix = ((size_t)n * p.H + y) * p.W + x;
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
@@ -745,29 +763,27 @@ __global__ void __launch_bounds__(256, 2) realin_mma_kernel(const __grid_constan
                         const float lo = __double2float_rd(__dsub_rd(a, e)), hi = __double2float_ru(__dadd_ru(a, e));
                         const float* f = fold_s[cl];
                         const int blo = real_fold_bit_s(lo, f), bhi = real_fold_bit_s(hi, f);
-                        if (finite && blo == bhi && !exact_s[cl]) {
-                            bits |= (uint32_t)blo << cl;
-                        } else {
-                            const unsigned int slot = atomicAdd(p.ctl, 1u);
-                            if (slot < (unsigned)p.cap) {
-                                p.list[2 * (size_t)slot] = (uint32_t)pix;
-                                p.list[2 * (size_t)slot + 1] = (uint32_t)co;
-                            } else {
-                                atomicExch(p.ctl + 1, 1u);
-                            }
-                        }
+                        if (finite && blo == bhi && !exact_s[cl]) bits |= (uint32_t)blo << cl;
+                        else und |= 1u << cl;
                     }
                 }
             }
             bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
             bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+            und |= __shfl_xor_sync(0xffffffffu, und, 1);
+            und |= __shfl_xor_sync(0xffffffffu, und, 2);
             if (tig == 0 && bits) atomicOr(&words[row * RM_TC + col], bits);
+            if (tig == 0 && und) atomicOr(&umask[row * RM_TC + col], und);
         }
     }
     __syncthreads();
     if (tid < RM_TR * RM_TC) {
         const int yy = y0 + tid / RM_TC, xx = x0 + tid % RM_TC;
-        if (yy < p.H && xx < p.W) p.out[(((size_t)n * p.H + yy) * p.W + xx) * p.cwo + g] = words[tid];
+        if (yy < p.H && xx < p.W) {
+            const size_t pix = ((size_t)n * p.H + yy) * p.W + xx;
+            p.out[pix * p.cwo + g] = words[tid];
+            if (umask[tid]) realin_list(p.list, p.ctl, p.cap, pix, g, umask[tid]);
+        }
     }
 }
 
@@ -789,8 +805,13 @@ __device__ float realin_exact_acc(const float* x, const float* wf, int Cin, int 
     return acc;
 }
 
-// Undecided outputs of realin_mma_kernel, recomputed exactly. If the list
-// overflowed, every output of the batch is recomputed (correct, slow).
+// Undecided outputs of the tensor-core first convs, recomputed exactly. One
+// warp per listed (pixel, channel group): the 3x3 x Cin input window is
+// loaded once into shared memory (every load independent), then lanes
+// 9c + t (three channels at a time) run tap t of channel c as the
+// reference's sequential fp32 chain over the bands, and lane 9c sums the
+// in-image taps in order. If the list overflowed, every output of the batch
+// is recomputed (correct, slow).
 struct RealinFixParams {
     const float* x;
     const float* wf;     // [CoutP][9][CinP] +-1.0f
@@ -801,51 +822,62 @@ struct RealinFixParams {
     int cap, N, Cin, CinP, H, W, Cout, cwo;
 };
 
-// one warp per listed output: lane t < 9 sums tap t over the bands in order
-// (loads issued ahead of the chain), lane 0 then adds the in-bounds taps in
-// order, as the reference does
-__device__ float realin_exact_acc_warp(const float* x, const float* wf, int Cin, int CinP, int H, int W, int n,
-                                       int co, int y, int xx, int lane) {
-    const size_t plane = (size_t)H * W;
-    const int iy = y + lane / 3 - 1, ix = xx + lane % 3 - 1;
-    const bool inb = lane < 9 && (unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W;
-    float s = 0.0f;
-    if (inb) {
-        const float* src = x + (size_t)n * Cin * plane + (size_t)iy * W + ix;
-        const float* w = wf + ((size_t)co * 9 + lane) * CinP;
-        int ci = 0;
-        for (; ci + 8 <= Cin; ci += 8) {
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __ldg(src + (size_t)(ci + i) * plane);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) s = __fmaf_rn(v[i], __ldg(w + ci + i), s);
-        }
-        for (; ci < Cin; ++ci) s = __fmaf_rn(__ldg(src + (size_t)ci * plane), __ldg(w + ci), s);
-    }
-    float acc = 0.0f;
-#pragma unroll
-    for (int t = 0; t < 9; ++t) {
-        const float st = __shfl_sync(0xffffffffu, s, t);
-        const int ty = y + t / 3 - 1, tx = xx + t % 3 - 1;
-        if ((unsigned)ty < (unsigned)H && (unsigned)tx < (unsigned)W) acc = __fadd_rn(acc, st);
-    }
-    return acc;
-}
+constexpr int FIX_WARPS = 4;
+constexpr int FIX_MAXC = 128;  // bands staged per window (the fast paths take Cin <= 128)
 
-__global__ void realin_fixup_kernel(const RealinFixParams p) {
+__global__ void __launch_bounds__(FIX_WARPS * 32) realin_fixup_kernel(const RealinFixParams p) {
+    __shared__ float win[FIX_WARPS][9][FIX_MAXC];
     const unsigned int cnt = min(p.ctl[0], (unsigned)p.cap);
-    const int lane = threadIdx.x & 31;
-    if (p.ctl[1] == 0u) {
-        const size_t wstride = ((size_t)gridDim.x * blockDim.x) >> 5;
-        for (size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < cnt; i += wstride) {
-            const uint32_t pix = p.list[2 * i], co = p.list[2 * i + 1];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const size_t plane = (size_t)p.H * p.W;
+    if (p.ctl[1] == 0u && p.Cin <= FIX_MAXC) {
+        float (*wv)[FIX_MAXC] = win[wib];
+        const size_t wstride = (size_t)gridDim.x * FIX_WARPS;
+        for (size_t i = (size_t)blockIdx.x * FIX_WARPS + wib; i < cnt; i += wstride) {
+            const uint32_t pix = p.list[4 * i], g = p.list[4 * i + 1];
+            uint32_t mask = p.list[4 * i + 2];
             const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
-            const float acc = realin_exact_acc_warp(p.x, p.wf, p.Cin, p.CinP, p.H, p.W, n, (int)co, y, xx, lane);
-            if (lane == 0 && real_fold_bit(acc, p.fold + (size_t)co * 5))
-                atomicOr(p.out + (size_t)pix * p.cwo + (co >> 5), 1u << (co & 31));
+            const float* xn = p.x + (size_t)n * p.Cin * plane;
+            __syncwarp();
+            for (int e = lane; e < 9 * p.Cin; e += 32) {
+                const int t = e / p.Cin, ci = e - t * p.Cin;
+                const int iy = y + t / 3 - 1, ix = xx + t % 3 - 1;
+                wv[t][ci] = ((unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W)
+                                ? __ldg(xn + (size_t)ci * plane + (size_t)iy * p.W + ix) : 0.0f;
+            }
+            __syncwarp();
+            uint32_t bits = 0u;
+            while (mask) {
+                // up to three channels of the mask, lanes 9c + t
+                int c0 = -1, c1 = -1, c2 = -1;
+                if (mask) { c0 = __ffs(mask) - 1; mask &= mask - 1; }
+                if (mask) { c1 = __ffs(mask) - 1; mask &= mask - 1; }
+                if (mask) { c2 = __ffs(mask) - 1; mask &= mask - 1; }
+                const int c = lane / 9, t = lane - c * 9;
+                const int cb = c == 0 ? c0 : c == 1 ? c1 : c == 2 ? c2 : -1;
+                float s = 0.0f;
+                const int iy = y + t / 3 - 1, ix = xx + t % 3 - 1;
+                const bool inb = (unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W;
+                if (cb >= 0 && inb) {
+                    const float* w = p.wf + ((size_t)(g * 32 + cb) * 9 + t) * p.CinP;
+                    for (int ci = 0; ci < p.Cin; ++ci) s = __fmaf_rn(wv[t][ci], __ldg(w + ci), s);
+                }
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int tt = 0; tt < 9; ++tt) {
+                        const float st = __shfl_sync(0xffffffffu, s, k * 9 + tt);
+                        const int ty = y + tt / 3 - 1, tx = xx + tt % 3 - 1;
+                        if ((unsigned)ty < (unsigned)p.H && (unsigned)tx < (unsigned)p.W) acc = __fadd_rn(acc, st);
+                    }
+                    const int ck = k == 0 ? c0 : k == 1 ? c1 : c2;
+                    if (ck >= 0 && real_fold_bit(acc, p.fold + (size_t)(g * 32 + ck) * 5)) bits |= 1u << ck;
+                }
+            }
+            if (lane == 0 && bits) atomicOr(p.out + (size_t)pix * p.cwo + g, bits);
         }
-    } else {
+    } else if (p.ctl[1] != 0u) {
         const size_t stride = (size_t)gridDim.x * blockDim.x;
         const size_t words = (size_t)p.N * p.H * p.W * p.cwo;
         for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += stride) {
@@ -2031,8 +2063,8 @@ struct RealinWsParams {
     uint32_t thr_neg;      // bit c: channel c's fold decreases (RwThr.sgn < 0)
     uint32_t thr_exact;    // bit c: channel c always goes to the fix-up
     uint32_t* out;         // [N][H][W][cwo]
-    uint32_t* list;        // undecided outputs: (pixel index, channel) pairs
-    unsigned int* ctl;     // [0] = entries, [1] = overflow / wait failure
+    uint32_t* list;        // undecided outputs (realin_list)
+    unsigned int* ctl;     // [0] = entries, [1] = overflow / wait failure, [2] = outputs
     int cap, N, Cin, H, W, Cout, cwo;
     int R, Wp, SP, ipi, n_items, NS, KC;  // rows per item, staged width, staged positions, items per image
     float c9;              // e2 / T for a full 3x3 window, rounded up
@@ -2282,7 +2314,7 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
                 const bool finite = ef <= 1.0995116e12f;
                 const long long E = finite ? __float2ll_ru(ef * 262144.0f) : 0ll;
                 const size_t pix = ((size_t)n * p.H + y) * p.W + x;
-                uint32_t bits = 0u;
+                uint32_t bits = 0u, und = 0u;
                 const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + mt * 96);
 #pragma unroll 1
                 for (int c0 = 0; c0 < 32; c0 += 16) {
@@ -2301,21 +2333,15 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
                             const long long Qs = (p.thr_neg >> co) & 1u ? -Q : Q;
                             const long long C = p.thrC[co];
                             const bool ok = finite && !((p.thr_exact >> co) & 1u);
-                            if (ok && Qs - E >= C) {
-                                bits |= 1u << co;
-                            } else if (!(ok && Qs + E < C)) {
-                                const unsigned int slot = atomicAdd(p.ctl, 1u);
-                                if (slot < (unsigned)p.cap) {
-                                    p.list[2 * (size_t)slot] = (uint32_t)pix;
-                                    p.list[2 * (size_t)slot + 1] = (uint32_t)co;
-                                } else {
-                                    atomicExch(p.ctl + 1, 1u);
-                                }
-                            }
+                            if (ok && Qs - E >= C) bits |= 1u << co;
+                            else if (!(ok && Qs + E < C)) und |= 1u << co;
                         }
                     }
                 }
-                if (valid) p.out[pix * p.cwo] = bits;
+                if (valid) {
+                    p.out[pix * p.cwo] = bits;
+                    if (und) realin_list(p.list, p.ctl, p.cap, pix, 0, und);
+                }
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_b[buf]));
