@@ -318,8 +318,8 @@ def run_ours(args):
             "device_wait_timeouts": bn.device_wait_timeouts(local),
             "roofline": (
                 {"bound": "tensor",
-                 "kernel": ("bconv_umma_kernel (tcgen05 int8, non-pooled binary convs) + bconv_mma_kernel "
-                            "(int8 mma.sync, pooled encoder convs)") if args.bconv == "tc" else
+                 "kernel": ("bconv_ws_kernel + bconv_ws_pool_kernel (17 fused binary convs, tcgen05 int8, "
+                            "persistent warp-specialised)") if args.bconv == "tc" else
                            "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
                  "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
                  "unit": "Gbitop/s (1 bitop = 1 binary MAC, run as one int8 MAC)",

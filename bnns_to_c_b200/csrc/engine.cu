@@ -186,6 +186,18 @@ struct HostBin {
     std::vector<FoldIv> fold, fold2;
 };
 
+// tiles per work item of the tcgen05 binary conv at 128 / 256 channels
+// (TMEM: two accumulator sets when BN * MT <= 256, one otherwise). Measured:
+// 512 positions x 128 channels and 256 x 256 (one set each, weights re-read
+// half as often) beat 256 x 128 and 128 x 256 (two sets) by 10-25% on the
+// 128- and 256-channel layers.
+#ifndef BNN_WS128_MT
+#define BNN_WS128_MT 4
+#endif
+#ifndef BNN_WS256_MT
+#define BNN_WS256_MT 2
+#endif
+
 // tcgen05 channel block for a layer of Cout channels: the whole layer up to
 // 256 channels (N of one MMA), 256-channel blocks beyond
 static int ws_bn(int Cout) { return Cout <= 32 ? 32 : Cout <= 64 ? 64 : Cout <= 128 ? 128 : 256; }
@@ -280,7 +292,7 @@ static int set_kernel_attrs(int device) {
         (e = attr_bconv_kc<128, 8, 8>()) != cudaSuccess || (e = attr_bmma<32>()) != cudaSuccess ||
         (e = attr_bmma<64>()) != cudaSuccess || (e = attr_bmma<128>()) != cudaSuccess ||
         (e = attr_ws<32, 8>()) != cudaSuccess || (e = attr_ws<64, 4>()) != cudaSuccess ||
-        (e = attr_ws<128, 2>()) != cudaSuccess || (e = attr_ws<256, 1>()) != cudaSuccess ||
+        (e = attr_ws<128, BNN_WS128_MT>()) != cudaSuccess || (e = attr_ws<256, BNN_WS256_MT>()) != cudaSuccess ||
         (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
         (e = attr_ws_pool<128, 1>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -744,8 +756,8 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
         switch (p.ubn) {
             case 32: rc = launch_ws<32, 8>(p, N, st); break;
             case 64: rc = launch_ws<64, 4>(p, N, st); break;
-            case 128: rc = launch_ws<128, 2>(p, N, st); break;
-            case 256: rc = launch_ws<256, 1>(p, N, st); break;
+            case 128: rc = launch_ws<128, BNN_WS128_MT>(p, N, st); break;
+            case 256: rc = launch_ws<256, BNN_WS256_MT>(p, N, st); break;
         }
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }
@@ -898,7 +910,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         p.n_items = N * p.ipi;
         p.c9 = first_conv_c9(Cin);
         const int grid = std::min(p.n_items, sm_count());
-        realin_ws_kernel<<<grid, 512, geo.smem, st>>>(tm, p);
+        realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,

@@ -2030,14 +2030,21 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 // |x| per position for the bound, and two issuers run 27 MMAs per tile
 // (9 taps x 3 planes, N = 32 channels; the weights of all chunks stay in
 // shared memory). TMEM: two accumulators of RW_MT tiles x 3 planes x 32.
-// Warps: 0-7 epilogue, 8-13 producers (thread 8*32 also drives the TMA
-// ring), 14-15 MMA issue (15 allocates TMEM). Every wait is bounded; a CTA
-// that gives up raises ctl[1] (the fix-up then recomputes the whole batch).
+// Warps: 0-3 epilogue (both tiles), 4-13 producers (the first also drives
+// the TMA ring), 14.. MMA issue (the six accumulators round-robin; the last
+// issuer warp allocates TMEM; measured: 3 or 6 issuers are slower than 2).
+// Every wait is bounded; a CTA that gives up raises ctl[1] (the fix-up then
+// recomputes the whole batch).
 // ---------------------------------------------------------------------
 constexpr int RW_MT = 2;              // tiles per item
 constexpr int RW_NB = 2;              // fp32 box buffers
 constexpr int RW_NEPI = 128;          // warps 0-3: epilogue (both tiles)
 constexpr int RW_NPROD = 320;         // warps 4-13: producers
+#ifndef BNN_RW_NISS
+#define BNN_RW_NISS 2
+#endif
+constexpr int RW_NISS = BNN_RW_NISS;  // warps 14..: MMA issue (the six accumulators round-robin)
+constexpr int RW_NT = 32 * (14 + RW_NISS);
 constexpr int RW_NQ = 3;              // staged positions per producer thread, at most
 constexpr int RW_MAX_SP = RW_NPROD * RW_NQ;
 constexpr size_t RW_WBYTES = (size_t)4 * 9 * 2 * 32 * 16;  // +-1 weights, 4 chunks x 9 taps
@@ -2084,7 +2091,7 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
         : "r"(taddr));
 }
 
-__global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const RealinWsParams p) {
     extern __shared__ __align__(1024) unsigned char rw_smem[];
     __shared__ __align__(8) unsigned long long boxf_b[RW_NB], boxe_b[RW_NB], full_b[4], empty_b[4], accf_b[2],
@@ -2101,7 +2108,7 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int my_items = (int)blockIdx.x < p.n_items ? (p.n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
-    if (warp == 15) {
+    if (warp == RW_NT / 32 - 1) {
         tc_alloc(smem_u32(&tmem_s), 512);
         tc_relinquish();
     }
@@ -2113,10 +2120,10 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
         }
         for (int s = 0; s < NS; ++s) {
             mbar_init(smem_u32(&full_b[s]), RW_NPROD);
-            mbar_init(smem_u32(&empty_b[s]), 2);
+            mbar_init(smem_u32(&empty_b[s]), RW_NISS);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(smem_u32(&accf_b[b]), 2);
+            mbar_init(smem_u32(&accf_b[b]), RW_NISS);
             mbar_init(smem_u32(&acce_b[b]), RW_NEPI);
             mbar_init(smem_u32(&bpxf_b[b]), RW_NPROD);
         }
@@ -2250,7 +2257,9 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
             mbar_arrive(smem_u32(&bpxf_b[buf]));
         }
     } else if (warp >= 14) {
-        // ------------------------------------------------------------ MMA issuers: issuer u takes tile u
+        // ------------------------------------------------------------ MMA issuers
+        // one thread issues an MMA per ~70 clk, so the six accumulators of an
+        // item (2 tiles x 3 planes, a = tile*3 + plane) go round-robin to the issuers
         const int u = warp - 14;
         if (lane == 0 && mbar_wait_ab(smem_u32(&wrdy_b), 0u, abort_v)) {
             // A: plane 0 signed, planes 1-2 unsigned; B signed; D s32; N = 32, M = 128
@@ -2263,20 +2272,21 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
                 const int buf = it & 1;
                 if (!mbar_wait_ab(smem_u32(&acce_b[buf]), (uint32_t)((it >> 1) & 1) ^ 1u, abort_v)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem + (uint32_t)(buf * 256 + u * 96);
                 bool ok = true;
                 for (int kc = 0; kc < KC; ++kc) {
                     if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t a0 = tc_desc(sm0 + (uint32_t)(RW_WBYTES + RW_NB * box_bytes + stage * stage_bytes),
                                                 (uint32_t)SP * 16);
+#pragma unroll 1
+                    for (int acc = u; acc < 6; acc += RW_NISS) {
+                        const int tile = acc / 3, pl = acc - tile * 3;
+                        const uint32_t d = tmem + (uint32_t)(buf * 256 + tile * 96 + pl * 32);
+                        const uint64_t ap = a0 + (uint64_t)(pl * 2 * SP + tile * 128);
+                        const uint32_t id = pl == 0 ? id_s : id_u;
 #pragma unroll
-                    for (int t = 0; t < 9; ++t) {
-                        const uint64_t bd = w0 + (uint64_t)((kc * 9 + t) * 2 * 32);
-                        const uint64_t at = a0 + (uint64_t)(u * 128 + (t / 3) * Wp + t % 3);
-#pragma unroll
-                        for (int pl = 0; pl < 3; ++pl)
-                            tc_mma_i8(dcol + pl * 32, at + (uint64_t)(pl * 2 * SP), bd, pl == 0 ? id_s : id_u,
+                        for (int t = 0; t < 9; ++t)
+                            tc_mma_i8(d, ap + (uint64_t)((t / 3) * Wp + t % 3), w0 + (uint64_t)((kc * 9 + t) * 2 * 32), id,
                                       (kc > 0 || t > 0) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&empty_b[stage]));
@@ -2358,7 +2368,7 @@ __global__ void __launch_bounds__(512, 1) realin_ws_kernel(const __grid_constant
             atomicAdd(&g_bnn_wait_timeouts, 1u);
         }
     }
-    if (warp == 15) {
+    if (warp == RW_NT / 32 - 1) {
         tc_fence_after();
         tc_dealloc(tmem, 512);
     }
