@@ -27,6 +27,7 @@ import numpy as np
 
 MAGIC = b"BNNC"
 VERSION = 1
+VERSION_STEM = 2   # spectral stem (python/bnn2c/blob.py:203-245, csrc/bnn_model_stem.c)
 TAG_CONV_BIN, TAG_CONV_REAL, TAG_ACT, TAG_HEAD = 1, 2, 3, 4
 RULE = {"const": 0, "ge": 1, "lt": 2, "band_in": 3, "band_out": 4}
 ENC = ["enc1", "enc2", "enc3", "enc4"]
@@ -84,13 +85,22 @@ def _write_act(f, act):
 
 
 def blob_bytes(model: dict) -> bytes:
-    """Serialise a model dict (see ``random_model``) to blob v1 bytes."""
+    """Serialise a model dict (see ``random_model``) to blob bytes: v1, or v2
+    when the model has a spectral stem ("stem.conv": the header gains
+    has_stem = n_stem_layers = 1 and the stem conv + act records come first,
+    python/bnn2c/blob.py:229-233)."""
     import io
 
     f = io.BytesIO()
     f.write(MAGIC)
-    _w_i32(f, VERSION, model["base_channels"], model["n_bands"], model["n_classes"],
-           model.get("upsampler", 0))
+    if "stem.conv" in model:
+        _w_i32(f, VERSION_STEM, model["base_channels"], model["n_bands"], model["n_classes"],
+               model.get("upsampler", 0), 1, 1)
+        _write_conv(f, model["stem.conv"])
+        _write_act(f, model["stem.act"])
+    else:
+        _w_i32(f, VERSION, model["base_channels"], model["n_bands"], model["n_classes"],
+               model.get("upsampler", 0))
     for st in ENC:
         _write_conv(f, model[f"{st}.conv1"])
         _write_act(f, model[f"{st}.act1"])
@@ -119,8 +129,9 @@ def write_blob(model: dict, path: str) -> str:
 
 
 def read_blob(path: str) -> dict:
-    """Parse a v1 blob into the reference reader's dict shape
-    (python/bnn2c/blob.py:251-313): convs (18), acts (22), head."""
+    """Parse a v1 or v2 blob into the reference reader's dict shape
+    (python/bnn2c/blob.py:251-313): convs (18), acts (22), head, and for v2
+    stem_conv / stem_act."""
     with open(path, "rb") as f:
         data = f.read()
     off = 0
@@ -138,11 +149,17 @@ def read_blob(path: str) -> dict:
 
     if take(4) != MAGIC:
         raise ValueError("bad magic")
-    version, base, bands, classes, ups = ints(5)
-    if version != VERSION:
+    (version,) = ints(1)
+    if version == VERSION:
+        base, bands, classes, ups = ints(4)
+        has_stem, n_stem = 0, 0
+    elif version == VERSION_STEM:
+        base, bands, classes, ups, has_stem, n_stem = ints(6)
+    else:
         raise ValueError(f"unsupported blob version {version}")
     out = {"version": version, "base_channels": base, "n_bands": bands,
-           "n_classes": classes, "upsampler": ups, "convs": [], "acts": [], "head": None}
+           "n_classes": classes, "upsampler": ups, "has_stem": has_stem, "n_stem_layers": n_stem,
+           "convs": [], "acts": [], "head": None, "stem_conv": None, "stem_act": None}
 
     def conv():
         (tag,) = ints(1)
@@ -169,6 +186,9 @@ def read_blob(path: str) -> dict:
         a = [np.frombuffer(take(4 * c), "<f4").copy() for _ in range(4)]
         return {"kind": "real", "C": c, "A": a[0], "B": a[1], "slope": a[2], "rsign": a[3]}
 
+    if version == VERSION_STEM:
+        out["stem_conv"] = conv()
+        out["stem_act"] = act()
     for _ in ENC:
         out["convs"].append(conv()); out["acts"].append(act())
         out["convs"].append(conv()); out["acts"].append(act()); out["acts"].append(act())
@@ -222,11 +242,14 @@ def _int_rule(rng, C, cin, mode):
 
 
 def random_model(base_channels: int = 32, n_bands: int = 120, n_classes: int = 3,
-                 seed: int = 0, rules: str = "baseline") -> dict:
-    """Random-weight v1 UNet with the distributions of the benchmark config:
+                 seed: int = 0, rules: str = "baseline", stem_channels: int = 0) -> dict:
+    """Random-weight UNet with the distributions of the benchmark config:
     real conv signs Bernoulli(0.5), alpha U(0.5,1.5); binary weights
     Bernoulli(0.5); int folds per ``rules``; real fold A~N(1,.3), B~N(0,.3),
-    slope~U(.1,.3), rsign~N(0,.1); head W~N(0,.1), bias~N(0,.1)."""
+    slope~U(.1,.3), rsign~N(0,.1); head W~N(0,.1), bias~N(0,.1).
+    ``stem_channels`` > 0 gives the v2 spectral-stem model: a real-input 1x1
+    binary-weight stem of that many channels + real fold, and enc1.conv1
+    binary (csrc/bnn_model_stem.c)."""
     rng = np.random.default_rng(seed)
     m = {"base_channels": base_channels, "n_bands": n_bands, "n_classes": n_classes,
          "upsampler": 0}
@@ -235,10 +258,23 @@ def random_model(base_channels: int = 32, n_bands: int = 120, n_classes: int = 3
     def sgn(*shape):
         return np.where(rng.random(shape) < 0.5, 1, -1).astype(np.int8)
 
+    def real_fold(c):
+        return {"kind": "real",
+                "A": rng.normal(1.0, 0.3, c).astype(np.float32),
+                "B": rng.normal(0.0, 0.3, c).astype(np.float32),
+                "slope": rng.uniform(0.1, 0.3, c).astype(np.float32),
+                "rsign": rng.normal(0.0, 0.1, c).astype(np.float32)}
+
     cin = n_bands
+    if stem_channels:
+        alpha = (np.round(rng.uniform(0.5, 1.5, stem_channels) * 256.0) / 256.0).astype(np.float32)
+        m["stem.conv"] = {"tag": "real", "wsign": sgn(stem_channels, n_bands, 1, 1), "alpha": alpha,
+                          "pad": 0, "stride": 1}
+        m["stem.act"] = real_fold(stem_channels)
+        cin = stem_channels
     for i, st in enumerate(ENC):
         c = enc[i]
-        if i == 0:
+        if i == 0 and not stem_channels:
             # alpha on a 1/256 grid: the reference writer recomputes alpha as
             # the float32 mean of |w| (blob.py:83), which is exact for these
             alpha = (np.round(rng.uniform(0.5, 1.5, c) * 256.0) / 256.0).astype(np.float32)

@@ -38,6 +38,11 @@ typedef struct {
 
 struct OModel {
     int version, base_channels, n_bands, n_classes, upsampler;
+    /* v2 (spectral stem, csrc/bnn_model_stem.h:43-47): a real-input 1x1
+     * binary-weight conv + real fold before enc1, whose conv1 is binary */
+    int has_stem;
+    OConv stem_conv;
+    OAct stem_act;
     OConv enc_conv1[4], enc_conv2[4];
     OAct enc_act1[4], enc_skip[4], enc_down[4];
     OConv bott_conv1, bott_conv2;
@@ -126,6 +131,7 @@ static void free_act(OAct *a) {
 }
 
 void oracle_free(OModel *m) {
+    if (m && m->has_stem) { free_conv(&m->stem_conv); free_act(&m->stem_act); }
     if (!m) return;
     for (int i = 0; i < 4; ++i) {
         free_conv(&m->enc_conv1[i]); free_conv(&m->enc_conv2[i]);
@@ -160,6 +166,15 @@ OModel *oracle_load(const char *path, char *err, int errlen) {
     if (!m) { free(buf); snprintf(err, (size_t)errlen, "OOM"); return NULL; }
     m->version = rd_int(&r); m->base_channels = rd_int(&r);
     m->n_bands = rd_int(&r); m->n_classes = rd_int(&r); m->upsampler = rd_int(&r);
+    if (!r.bad && m->version == 2) {
+        /* csrc/bnn_model_stem.c:82-95: has_stem, n_stem_layers (both 1), stem records */
+        m->has_stem = rd_int(&r);
+        int nsl = rd_int(&r);
+        if (!r.bad && (m->has_stem != 1 || nsl != 1))
+            rd_fail(&r, "bnn_stem: only has_stem=1, n_stem_layers=1 supported");
+        rd_conv(&r, &m->stem_conv);
+        rd_act(&r, &m->stem_act);
+    }
     for (int i = 0; i < 4; ++i) {
         rd_conv(&r, &m->enc_conv1[i]); rd_act(&r, &m->enc_act1[i]);
         rd_conv(&r, &m->enc_conv2[i]); rd_act(&r, &m->enc_skip[i]);
@@ -415,7 +430,21 @@ int oracle_forward(const OModel *m, const float *input, int H, int W,
     for (int i = 0; i < 4; ++i) {
         const OConv *c1 = &m->enc_conv1[i], *c2 = &m->enc_conv2[i];
         int8_t *h;
-        if (i == 0) {
+        if (i == 0 && m->has_stem) {
+            /* v2: 1x1 real-input stem + real fold (csrc/bnn_model_stem.c:172-187),
+             * then enc1.conv1 binary like the other levels (:189-193) */
+            const OConv *sc = &m->stem_conv;
+            float *so = xm((size_t)sc->Cout * H * W * 4);
+            oracle_realin(input, sc->wsign, sc->alpha, so, sc->Cin, H, W, sc->Cout, sc->kh, sc->kw, sc->pad,
+                          sc->stride);
+            emit(cb, ctx, "stem.conv.out", 2, sc->Cout, H, W, so);
+            int8_t *st = xm((size_t)sc->Cout * H * W);
+            fold(&m->stem_act, NULL, so, st, sc->Cout, H, W);
+            emit(cb, ctx, "stem.act", 0, sc->Cout, H, W, st);
+            free(so);
+            h = conv_fold(c1, &m->enc_act1[0], st, xH, xW, ENC[0], "conv1", "act1", cb, ctx);
+            free(st);
+        } else if (i == 0) {
             /* enc1: real-input conv + real fold (bnn_model.c:156-167) */
             float *co1 = xm((size_t)c1->Cout * H * W * 4);
             oracle_realin(input, c1->wsign, c1->alpha, co1, c1->Cin, H, W, c1->Cout,

@@ -1,7 +1,8 @@
 /* bnn_oracle.h - TEST INFRASTRUCTURE ONLY.
  *
  * A plain-C, CPU-only restatement of the reference engine's v1 forward path
- * (Sboyle132/BNNs_to_C csrc/bnn_model.c and the kernels it calls), written
+ * (Sboyle132/BNNs_to_C csrc/bnn_model.c and the kernels it calls) and of its
+ * v2 spectral-stem variant (csrc/bnn_model_stem.c), written
  * from the reference's documented semantics, used as the checker for the
  * B200 engine. Only tests/, __graft_entry__.smoke() and bench.py's
  * cpu_baseline leg may load it; the product library never links it.

@@ -11,7 +11,9 @@ What it records:
     :181-199) from equivalent torch modules; the script fails unless the
     bytes are identical, then saves the blob.
   * whole-net stages: the reference kernels, unmodified, chained in
-    bnn_forward order by oracle/ref_stages.c -> every P, every +-1 plane,
+    bnn_forward order by oracle/ref_stages.c (and, for the v2 spectral-stem
+    models, in bnn_stem_forward order by oracle/ref_stages_stem.c, logits
+    checked against the reference stem CLI csrc/main_stem.c) -> every P, every +-1 plane,
     the real conv output and the logits, for seeded synthetic inputs; plus
     the logits of the reference CLI (csrc/main.c) on the same input, which
     must equal the chained logits exactly.
@@ -52,6 +54,13 @@ MODELS = [
 ]
 # base 32 (benchmark widths): blob not committed (1 MB); pinned by sha256
 C32 = ("unet_c32_base_s0", 32, "baseline", 0, [(32, 32, 11, 1)])
+# v2 spectral-stem models (csrc/bnn_model_stem.c): (name, base, rules, seed,
+# stem channels, runs); the reference default stem width is 16
+# (python/bnn2c/export.py:120)
+STEMS = [
+    ("stem_c8_mixed_s3", 8, "mixed", 3, 16, [(32, 32, 12, 2), (37, 23, 13, 1)]),
+    ("stem_c16_base_s4", 16, "baseline", 4, 16, [(32, 32, 14, 1), (16, 48, 15, 1)]),
+]
 
 
 def ref_blob_bytes(model: dict, ref: str) -> bytes:
@@ -79,13 +88,21 @@ def ref_blob_bytes(model: dict, ref: str) -> bytes:
 
     path = tempfile.mktemp(suffix=".blob")
     import struct
+    stem = "stem.conv" in model
     with open(path, "wb") as f:
         f.write(RB.MAGIC)
-        f.write(struct.pack("<5i", RB.VERSION, model["base_channels"], model["n_bands"],
-                            model["n_classes"], 0))
+        if stem:  # the v2 header and stem records of python/bnn2c/blob.py:229-232
+            f.write(struct.pack("<7i", RB.VERSION_STEM, model["base_channels"], model["n_bands"],
+                                model["n_classes"], 0, 1, 1))
+            sc = model["stem.conv"]
+            RB._w_conv_real(f, conv_mod(sc, sc["alpha"]))
+            RB._w_act(f, rule(model["stem.act"]))
+        else:
+            f.write(struct.pack("<5i", RB.VERSION, model["base_channels"], model["n_bands"],
+                                model["n_classes"], 0))
         for i, st in enumerate(RB.ENC):
             c1 = model[f"{st}.conv1"]
-            if i == 0:
+            if i == 0 and not stem:
                 RB._w_conv_real(f, conv_mod(c1, c1["alpha"]))
             else:
                 RB._w_conv_bin(f, conv_mod(c1))
@@ -110,19 +127,22 @@ def ref_blob_bytes(model: dict, ref: str) -> bytes:
     data = open(path, "rb").read()
     rt = RB.read_blob(path)  # the reference reader's round-trip asserts
     assert len(rt["convs"]) == 18 and len(rt["acts"]) == 22
+    assert (rt["stem_conv"] is not None) == stem
     os.unlink(path)
     return data
 
 
-def pinned_model(name, base, rules, seed, ref):
+def pinned_model(name, base, rules, seed, ref, stem=0):
     """random_model written by both writers and byte-compared (the
     reference emitter recomputes alpha = mean|w|; random_model's alphas are
     exact under that recomputation)."""
-    m = B.random_model(base, 120, 3, seed=seed, rules=rules)
+    m = B.random_model(base, 120, 3, seed=seed, rules=rules, stem_channels=stem)
     rb = ref_blob_bytes(m, ref)
     tmp = tempfile.mktemp(suffix=".blob")
     open(tmp, "wb").write(rb)
-    assert np.array_equal(m["enc1.conv1"]["alpha"], B.read_blob(tmp)["convs"][0]["alpha"])
+    rt = B.read_blob(tmp)
+    real = m["stem.conv"] if stem else m["enc1.conv1"]
+    assert np.array_equal(real["alpha"], (rt["stem_conv"] if stem else rt["convs"][0])["alpha"])
     os.unlink(tmp)
     ours = B.blob_bytes(m)
     if ours != rb:
@@ -143,6 +163,16 @@ def ref_lib():
     return lib
 
 
+def ref_stem_lib():
+    lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_stem.so"))
+    lib.bnn_stem_load.restype = ctypes.c_void_p
+    lib.bnn_stem_load.argtypes = [ctypes.c_char_p]
+    lib.bnn_stem_free.argtypes = [ctypes.c_void_p]
+    lib.ref_stem_stages.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_void_p, STAGE_CB, ctypes.c_void_p]
+    return lib
+
+
 def synth(seed, first, n, bands, H, W):
     lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "liboracle.so"))
     lib.oracle_synth.argtypes = [ctypes.c_uint32, ctypes.c_uint32] + [ctypes.c_int] * 4 + [ctypes.c_void_p]
@@ -151,8 +181,8 @@ def synth(seed, first, n, bands, H, W):
     return out
 
 
-def run_stages(lib, blob_path, x, H, W):
-    m = lib.bnn_load(blob_path.encode())
+def run_stages(lib, blob_path, x, H, W, stem=False):
+    m = (lib.bnn_stem_load if stem else lib.bnn_load)(blob_path.encode())
     stages = {}
 
     def cb(ctx, name, kind, C, h, w, data):
@@ -163,16 +193,17 @@ def run_stages(lib, blob_path, x, H, W):
 
     logits = np.zeros((3, H, W), np.float32)
     fn = STAGE_CB(cb)
-    lib.ref_stages(m, x.ctypes.data, H, W, logits.ctypes.data, fn, None)
-    lib.bnn_free(m)
+    (lib.ref_stem_stages if stem else lib.ref_stages)(m, x.ctypes.data, H, W, logits.ctypes.data, fn, None)
+    (lib.bnn_stem_free if stem else lib.bnn_free)(m)
     return stages
 
 
-def ref_cli_logits(blob_path, x, H, W):
+def ref_cli_logits(blob_path, x, H, W, stem=False):
     with tempfile.TemporaryDirectory() as d:
         inp, out = os.path.join(d, "in.bin"), os.path.join(d, "out.bin")
         x.astype("<f4").tofile(inp)
-        subprocess.run([os.path.join(ROOT, "oracle", "_ref", "bnn_infer"), blob_path, inp, out,
+        cli = "bnn_infer_stem" if stem else "bnn_infer"
+        subprocess.run([os.path.join(ROOT, "oracle", "_ref", cli), blob_path, inp, out,
                         str(H), str(W)], check=True, capture_output=True,
                        env=dict(os.environ, OMP_NUM_THREADS="1"))
         return np.fromfile(out, "<f4").reshape(3, H, W)
@@ -210,10 +241,11 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     args = ap.parse_args()
-    lib = ref_lib()
+    lib, slib = ref_lib(), ref_stem_lib()
     manifest = []
-    for name, base, rules, seed, runs in MODELS + [C32]:
-        m, data = pinned_model(name, base, rules, seed, args.ref)
+    models = [(n, b, r, s, 0, runs) for n, b, r, s, runs in MODELS + [C32]] + STEMS
+    for name, base, rules, seed, stem, runs in models:
+        m, data = pinned_model(name, base, rules, seed, args.ref, stem)
         sha = hashlib.sha256(data).hexdigest()
         bpath = os.path.join(HERE, name + ".blob")
         tmpb = tempfile.mktemp(suffix=".blob")
@@ -225,8 +257,8 @@ def main():
             out = {"H": np.int32(H), "W": np.int32(W), "seed": np.int32(sseed), "n": np.int32(n),
                    "blob_sha256": np.array(sha)}
             for p in range(n):
-                st = run_stages(lib, tmpb, np.ascontiguousarray(x[p]), H, W)
-                cli = ref_cli_logits(tmpb, x[p], H, W)
+                st = run_stages(slib if stem else lib, tmpb, np.ascontiguousarray(x[p]), H, W, bool(stem))
+                cli = ref_cli_logits(tmpb, x[p], H, W, bool(stem))
                 if not np.array_equal(cli.view(np.int32), st["logits"].view(np.int32)):
                     raise SystemExit(f"{name}: CLI logits != chained stage logits")
                 for k, v in st.items():

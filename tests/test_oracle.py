@@ -17,7 +17,8 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
 def fixtures():
     out = []
-    for f in sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz"))):
+    for f in sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz")) +
+                    glob.glob(os.path.join(GOLD, "stem_*_*x*.npz"))):
         base = os.path.basename(f)
         name = base.rsplit("_", 1)[0]
         out.append((name, f))
