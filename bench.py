@@ -29,6 +29,10 @@ through the patched forward (non-overlapping zero-padded 32x32 tiles,
 30x22 = 660 per cube), the cubes split over the ranks (strong scaling of the
 fixed 16-cube job); value = tiles/s with the cubes in HBM, e2e = tiles/s
 through bnn_forward_patched from host memory (2 cubes per rank).
+
+--workload stem runs config 2's batch through the v2 spectral-stem variant
+of the network (16-channel 1x1 stem + real fold, enc1.conv1 binary), against
+the reference's stem engine (oracle/_ref/ref_bench_stem) as the CPU arm.
 """
 
 from __future__ import annotations
@@ -47,6 +51,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "UNet patches/s (32x32x120)"
+STEM_C = 16                 # v2 stem width: the reference's default (python/bnn2c spectral stem)
 SEED_MODEL, SEED_INPUT = 0, 1
 POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
 MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (probe-measured on this pool)
@@ -117,11 +122,13 @@ def cpu_info():
     return model, os.cpu_count() or 1
 
 
-def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0):
-    """Reference engine (compiled from the reference sources) on the host."""
-    exe = os.path.join(ROOT, "oracle", "_ref", "ref_bench")
+def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0, stem=False):
+    """Reference engine (compiled from the reference sources) on the host:
+    the v1 engine, or with stem=True the v2 spectral-stem engine."""
+    name = "ref_bench_stem" if stem else "ref_bench"
+    exe = os.path.join(ROOT, "oracle", "_ref", name)
     if not os.path.exists(exe):
-        return None, "oracle/_ref/ref_bench not built (needs the reference tree at build time)"
+        return None, f"oracle/_ref/{name} not built (needs the reference tree at build time)"
     r = subprocess.run([exe, blob_path, str(n), str(H), str(W), str(procs), str(SEED_INPUT), str(steps),
                         str(warm), str(first)], capture_output=True, text=True,
                        env=dict(os.environ, OMP_NUM_THREADS="1"))
@@ -131,23 +138,32 @@ def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0):
     return secs, None
 
 
-def model_blob():
+def model_blob(stem=0):
     from bnns_to_c_b200 import blob as B
 
-    return B.blob_bytes(B.random_model(32, 120, 3, seed=SEED_MODEL, rules="baseline"))
+    return B.blob_bytes(B.random_model(32, 120, 3, seed=SEED_MODEL, rules="baseline", stem_channels=stem))
+
+
+def variant(args):
+    """(stem channels, metric, workload name) of the network benched."""
+    if args.workload == "stem":
+        return (STEM_C, "v2 spectral-stem UNet patches/s (32x32x120)",
+                f"stem{STEM_C}_unet_c32_4096x32x32x120")
+    return 0, METRIC, "unet_c32_4096x32x32x120"
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    data = model_blob()
+    stem, metric, wname = variant(args)
+    data = model_blob(stem)
     with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
         f.write(data)
         path = f.name
     model, cores = cpu_info()
     n = cores * args.ref_per_core
-    secs, err = ref_bench(path, n, args.H, args.W, cores, args.steps, max(0, min(args.warmup, 1)))
+    secs, err = ref_bench(path, n, args.H, args.W, cores, args.steps, max(0, min(args.warmup, 1)), stem=bool(stem))
     os.unlink(path)
     if secs is None:
         print(json.dumps({"impl": "reference", "unavailable": err}))
@@ -155,11 +171,11 @@ def run_reference(args):
     v = n * len(secs) / sum(secs)
     sample = f"{n} patches per step ({args.ref_per_core} per core), {cores} single-threaded processes, {model}"
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "patches/s",
+        "impl": "reference", "metric": metric, "value": round(v, 3), "unit": "patches/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * sum(secs) / len(secs), 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "b1+f32", "data": "synthetic",
-        "config": {"workload": "unet_c32_32x32x120", "base_channels": 32, "H": args.H, "W": args.W,
+        "config": {"workload": wname, "base_channels": 32, "H": args.H, "W": args.W,
                    "bands": 120, "classes": 3, "patches_per_step": n},
         "cpu_baseline": {"value": round(v, 3), "unit": "patches/s", "cores": cores, "kind": "reference",
                          "sample": sample},
@@ -197,9 +213,10 @@ def run_ours(args):
         return float(t.item())
 
     P, H, W = args.patches, args.H, args.W
+    stem, metric, wname = variant(args)
     bn.set_bconv_kernel(args.bconv)
     bn.set_first_conv_kernel(args.first)
-    m = bn.Model(data=model_blob())
+    m = (bn.StemModel if stem else bn.Model)(data=model_blob(stem))
     m.set_devices([local])
     first = rank * P
     din = torch.empty((P, 120, H, W), dtype=torch.float32, device="cuda")
@@ -286,10 +303,10 @@ def run_ours(args):
         cpu = None
         if not args.no_cpu_baseline:
             with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
-                f.write(model_blob())
+                f.write(model_blob(stem))
                 path = f.name
             n = cores * args.ref_per_core
-            secs, err = ref_bench(path, n, H, W, cores, 1, 0)
+            secs, err = ref_bench(path, n, H, W, cores, 1, 0, stem=bool(stem))
             os.unlink(path)
             if secs:
                 cpu = {"value": round(n / secs[0], 3), "unit": "patches/s", "cores": cores, "kind": "reference",
@@ -299,11 +316,11 @@ def run_ours(args):
                 cpu = {"value": None, "unit": "patches/s", "cores": cores, "kind": "reference", "sample": err}
         frac_split = {k: round(v["ms"] / total_ms, 4) for k, v in by_op.items()} if total_ms else {}
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "patches/s", "n_gpus": world,
+            "metric": metric, "value": round(value, 1), "unit": "patches/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "b1+f32",
             "data": "synthetic",
-            "config": {"workload": "unet_c32_4096x32x32x120", "base_channels": 32, "bands": 120, "classes": 3,
+            "config": {"workload": wname, "base_channels": 32, "bands": 120, "classes": 3,
                        "H": H, "W": W, "patches_per_gpu": P, "global_batch": P * world,
                        "parallelism": f"patch-shard x{world}",
                        "l2": f"inputs > L2 ({P * 120 * H * W * 4 / 1e9:.2f} GB read per step)"},
@@ -336,7 +353,13 @@ def run_ours(args):
                                 "(probe: 15.6 POPC/clk/SM)",
                  "time_share": frac_split.get("bconv")}),
             "rooflines": {
-                "conv_real": {"bound": "tensor",
+                "conv_real": {"bound": "hbm", "kernel": "stem_fold_kernel (v2 stem 1x1 + fold, fp32 FFMA2)",
+                              "achieved": round(P * 120 * H * W * 4 * args.steps / (r_["ms"] * 1e6), 1),
+                              "peak": peaks.get("hbm_gbs"), "unit": "GB/s (input bands read once)",
+                              "frac": round(P * 120 * H * W * 4 * args.steps / (r_["ms"] * 1e6)
+                                            / peaks["hbm_gbs"], 4) if peaks.get("hbm_gbs") else None,
+                              "time_share": frac_split.get("conv_real")} if stem else
+                {"bound": "tensor",
                               "kernel": ("realin_ws_kernel (tcgen05)" if args.first == "tc" else
                                          "realin_mma_kernel (mma.sync)") + " + realin_fixup_kernel",
                               "achieved": round(real_ach, 1), "peak": round(tensor_i8_peak, 1),
@@ -467,8 +490,9 @@ def main():
     ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
                          "mma = mma.sync for every layer")
-    ap.add_argument("--workload", default="unet", choices=["unet", "scene"],
-                    help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler")
+    ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem"],
+                    help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler; "
+                         "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem)")
     ap.add_argument("--cubes", type=int, default=16, help="scene workload: cubes in the job")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -23,6 +23,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libbnn_b200.so")
 CLI_PATH = os.path.join(HERE, "lib", "bnn_infer")
+CLI_STEM_PATH = os.path.join(HERE, "lib", "bnn_infer_stem")
 
 BNN_OK, BNN_ERR_IO, BNN_ERR_FORMAT, BNN_ERR_UNSUPPORTED, BNN_ERR_ARG, BNN_ERR_CUDA, BNN_ERR_OOM = range(7)
 
@@ -92,6 +93,12 @@ def lib():
         "bnn_forward_patched": (ip, [vp, vp, ip, ip, vp, ip]),
         "bnn_forward_patched_device": (ip, [vp, ip, vp, ip, ip, ip, vp, vp]),
         "bnn_first_conv_device": (ip, [vp, ip, vp, ip, ip, ip, vp, ip, ctypes.POINTER(ctypes.c_uint), vp]),
+        "bnn_stem_load_ex": (ip, [cp, ctypes.POINTER(vp)]),
+        "bnn_stem_load_mem": (ip, [vp, ctypes.c_size_t, ctypes.POINTER(vp)]),
+        "bnn_stem_load": (vp, [cp]),
+        "bnn_stem_free": (None, [vp]),
+        "bnn_stem_forward": (None, [vp, vp, ip, ip, vp]),
+        "bnn_stem_as_model": (vp, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -236,6 +243,55 @@ class Model:
             recs.append({"label": lab.value.decode(), "op": op.value.decode(), "work": work.value,
                          "ms": ms.value, "calls": calls.value})
         return recs
+
+
+class _ConvS(ctypes.Structure):
+    # ConvS / Conv (include/bnn_model_stem.h, include/bnn_model.h)
+    _fields_ = [("tag", ctypes.c_int), ("Cout", ctypes.c_int), ("Cin", ctypes.c_int),
+                ("kh", ctypes.c_int), ("kw", ctypes.c_int), ("pad", ctypes.c_int),
+                ("stride", ctypes.c_int), ("nwords", ctypes.c_int),
+                ("packed", ctypes.c_void_p), ("wsign", ctypes.c_void_p), ("alpha", ctypes.c_void_p)]
+
+
+class _StemHeader(ctypes.Structure):
+    # leading public fields of StemModel (include/bnn_model_stem.h)
+    _fields_ = [("version", ctypes.c_int), ("base_channels", ctypes.c_int),
+                ("n_bands", ctypes.c_int), ("n_classes", ctypes.c_int),
+                ("upsampler", ctypes.c_int), ("has_stem", ctypes.c_int),
+                ("n_stem_layers", ctypes.c_int), ("stem_conv", _ConvS)]
+
+
+class StemModel(Model):
+    """A loaded v2 spectral-stem blob (reference ``StemModel
+    *bnn_stem_load(path)``, csrc/bnn_model_stem.c). Every ``Model`` method
+    runs the v2 forward, through the engine handle ``bnn_stem_as_model``;
+    the stage dump starts with "stem.conv.out" and "stem.act"."""
+
+    def __init__(self, path: str | None = None, data: bytes | None = None):
+        L = lib()
+        h = ctypes.c_void_p()
+        if data is not None:
+            buf = ctypes.create_string_buffer(data, len(data))
+            _check(L.bnn_stem_load_mem(buf, len(data), ctypes.byref(h)))
+        else:
+            _check(L.bnn_stem_load_ex(os.fsencode(path), ctypes.byref(h)))
+        self.stem_handle = h.value
+        self.handle = L.bnn_stem_as_model(self.stem_handle)
+        hdr = _StemHeader.from_address(self.stem_handle)
+        self.version, self.base_channels = hdr.version, hdr.base_channels
+        self.n_bands, self.n_classes, self.upsampler = hdr.n_bands, hdr.n_classes, hdr.upsampler
+        self.stem_channels = hdr.stem_conv.Cout
+
+    def close(self):
+        if getattr(self, "stem_handle", None):
+            lib().bnn_stem_free(self.stem_handle)
+        self.stem_handle = None
+        self.handle = None
+
+
+def load_stem(path: str) -> StemModel:
+    """Reference ``bnn_stem_load`` (status-raising form)."""
+    return StemModel(path)
 
 
 def load(path: str) -> Model:

@@ -11,9 +11,16 @@
  * the environment adds the per-op device-time table (the reference's
  * `make profile` build). The GPU is the calling process's current CUDA
  * device (CUDA_VISIBLE_DEVICES selects it).
+ *
+ * Built with -DBNN_INFER_STEM this is bnn_infer_stem, the v2 spectral-stem
+ * CLI with csrc/main_stem.c's semantics (same arguments; v2 blob; the
+ * report's first line is "# [stem] ... stem_channels=C").
  */
 #include "bnn_b200.h"
 #include "bnn_model.h"
+#ifdef BNN_INFER_STEM
+#include "bnn_model_stem.h"
+#endif
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -33,7 +40,11 @@ static int cmp_d(const void *a, const void *b) {
 
 int main(int argc, char **argv) {
     if (argc < 4) {
+#ifdef BNN_INFER_STEM
+        fprintf(stderr, "usage: %s weights_stem.blob input.bin|rand output.bin [H W [reps]]\n", argv[0]);
+#else
         fprintf(stderr, "usage: %s weights.blob input.bin|rand output.bin [H W [reps]]\n", argv[0]);
+#endif
         return 1;
     }
     int H = (argc > 4) ? atoi(argv[4]) : 32;
@@ -42,7 +53,12 @@ int main(int argc, char **argv) {
     if (reps < 1) reps = 1;
 
     double t0 = now_s();
+#ifdef BNN_INFER_STEM
+    StemModel *sm = bnn_stem_load(argv[1]);
+    Model *m = bnn_stem_as_model(sm);
+#else
     Model *m = bnn_load(argv[1]);
+#endif
     double t_load = now_s() - t0;
     const char *prof = getenv("BNN_PROFILE");
     if (prof && prof[0] && strcmp(prof, "0") != 0) bnn_profile_enable(m, 1);
@@ -69,7 +85,11 @@ int main(int argc, char **argv) {
 
     for (int r = 0; r < reps; ++r) {
         double f0 = now_s();
+#ifdef BNN_INFER_STEM
+        bnn_stem_forward(sm, input, H, W, logits);
+#else
         bnn_forward(m, input, H, W, logits);
+#endif
         ts[r] = (now_s() - f0) * 1e3;
     }
     qsort(ts, (size_t)reps, sizeof(double), cmp_d);
@@ -82,13 +102,22 @@ int main(int argc, char **argv) {
     fclose(fo);
     double t_write = (now_s() - w0) * 1e3;
 
+#ifdef BNN_INFER_STEM
+    fprintf(stderr, "# [stem] H=%d W=%d bands=%d classes=%d stem_channels=%d reps=%d\n", H, W, sm->n_bands,
+            sm->n_classes, sm->stem_conv.Cout, reps);
+#else
     fprintf(stderr, "# H=%d W=%d bands=%d classes=%d reps=%d\n", H, W, m->n_bands, m->n_classes, reps);
+#endif
     fprintf(stderr, "# blob load : %9.3f ms\n", t_load * 1e3);
     fprintf(stderr, "# forward   : %9.3f ms  (median; min %.3f, max %.3f)\n", med, tmin, tmax);
     fprintf(stderr, "# out write : %9.3f ms\n", t_write);
     bnn_profile_report(m, stderr);
 
     free(ts); free(input); free(logits);
+#ifdef BNN_INFER_STEM
+    bnn_stem_free(sm);
+#else
     bnn_free(m);
+#endif
     return 0;
 }

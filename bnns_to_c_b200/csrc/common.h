@@ -17,15 +17,22 @@ void clear_error();
 
 // engine lifetime (engine.cu): attached to a parsed Model by the loader
 void* engine_create();
+// the engine of a v2 (spectral-stem) model: the stem records it runs before
+// the body (arrays borrowed from the StemModel, which outlives the engine)
+void* engine_create_stem(const Conv* stem_conv, const Act* stem_act);
+// stem width of the engine's model, 0 for a v1 model
+int engine_stem_c(const void* e);
 void engine_destroy(void* e);
 
 // topology of a validated v1 model, derived once at load
 struct Topology {
+    int stem;       // v2 stem width (enc1.conv1 is binary on it), 0 for v1
     int enc[4];     // encoder widths (conv1/conv2 Cout per stage)
     int bott;       // bottleneck width
     int dec[4];     // decoder widths dec4..dec1
     int bands, classes;
 };
-int validate_topology(const Model* m, Topology* t);
+// stem_c > 0: the body of a v2 model whose stem has stem_c channels
+int validate_topology(const Model* m, Topology* t, int stem_c = 0);
 
 }  // namespace bnn

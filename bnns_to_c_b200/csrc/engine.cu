@@ -74,6 +74,7 @@ struct Arena {
     void* base = nullptr;
     size_t bytes = 0;
     uint32_t *enc_h[4], *skip[4], *down[4], *bott_h, *bott_x, *dec_h[4], *dec_x[4];
+    uint32_t* stem = nullptr; // v2: the stem's bit plane (enc1.conv1's input)
     uint32_t* rm_list;        // first conv: undecided (pixel, channel group, mask) entries
     unsigned int* rm_ctl;     // [entries, overflow, outputs]
     int rm_cap;
@@ -99,6 +100,9 @@ struct DevState {
     int* rm_exact = nullptr;    // per channel: fold not monotone -> exact path
     int8_t* rw_wu = nullptr;    // first conv +-1 int8 weights for realin_ws_kernel (Cin <= 128, Cout <= 32)
     std::vector<RwThr> rw_thr;  // first conv fold thresholds for realin_ws_kernel (host copy, 32 entries)
+    float* st_w = nullptr;      // v2 stem weights [slice][band][st_CB] (+-1, 0)
+    float* st_fold = nullptr;   // v2 stem [channel][5]: alpha, A, B, slope, rsign
+    int st_CB = 0, st_slices = 0;
     BinLayer enc1[4], enc2[4], bott1, bott2, dec1[4], dec2[4];
     float *head_W = nullptr, *head_b = nullptr;
     Arena ar;
@@ -126,9 +130,30 @@ struct Engine {
     std::vector<int> devices;  // empty: current device
     int chunk = 256;
     Profiler prof;
+    // v2 model: the stem run before the body (arrays borrowed from the
+    // StemModel that owns this engine); stem_c = 0 for a v1 model
+    int stem_c = 0;
+    Conv stem_conv{};
+    Act stem_act{};
 };
 
 void* engine_create() { return new (std::nothrow) Engine(); }
+
+void* engine_create_stem(const Conv* stem_conv, const Act* stem_act) {
+    Engine* E = new (std::nothrow) Engine();
+    if (!E) return nullptr;
+    E->stem_c = stem_conv->Cout;
+    E->stem_conv = *stem_conv;
+    E->stem_act = *stem_act;
+    return E;
+}
+
+int engine_stem_c(const void* e) { return e ? ((const Engine*)e)->stem_c : 0; }
+
+static const Engine* eng(const Model* m) { return (const Engine*)m->engine; }
+
+// topology of the model behind an engine (v1, or the body of a v2 model)
+static int topo(const Model* m, Topology* t) { return validate_topology(m, t, eng(m)->stem_c); }
 
 static void dev_release(DevState* d) {
     if (!d || d->device < 0) return;
@@ -282,6 +307,18 @@ static cudaError_t attr_bconv_kc() {
     if ((e = attr_bconv<BN, TM, TN, 2>()) != cudaSuccess) return e;
     return attr_bconv<BN, TM, TN, 1>();
 }
+// stem weights in shared memory: up to 1024 bands x 32 channels
+template <int CB>
+static cudaError_t attr_stem() {
+    const int smem = 1024 * CB * 4;
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(stem_fold_kernel<CB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(stem_fold_kernel<CB, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+        return e;
+    if (CB == 32) return cudaSuccess;
+    return cudaFuncSetAttribute(stem_fold_kernel<CB, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 static int set_kernel_attrs(int device) {
     static std::mutex mu;
     static bool done[64] = {false};
@@ -300,7 +337,9 @@ static int set_kernel_attrs(int device) {
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
             cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
-            cudaSuccess)
+            cudaSuccess ||
+        (e = attr_stem<8>()) != cudaSuccess || (e = attr_stem<16>()) != cudaSuccess ||
+        (e = attr_stem<32>()) != cudaSuccess)
         return set_error(BNN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     if (device >= 0 && device < 64) done[device] = true;
     return BNN_OK;
@@ -361,74 +400,104 @@ static RwThr fold_threshold(const float* f, bool exact) {
 // upload everything to device d (called with d->mu held, device current)
 static int dev_init(const Model* m, DevState* d) {
     Topology tp;
-    int rc = validate_topology(m, &tp);
+    int rc = topo(m, &tp);
     if (rc) return rc;
     if ((rc = set_kernel_attrs(d->device))) return rc;
-    // first conv
-    const Conv* c1 = &m->enc_conv1[0];
-    const Act* a1 = &m->enc_act1[0];
-    const int Cin = c1->Cin, CoutR = c1->Cout, CoutRP = cdiv(CoutR, 32) * 32;
-    d->ri_CinP = cdiv(Cin, 4) * 4;
-    d->ri_CIP = d->ri_CinP + (((d->ri_CinP / 4) % 2 == 0) ? 4 : 0);
-    std::vector<float> wf((size_t)CoutRP * 9 * d->ri_CinP, 0.0f), rfold((size_t)CoutRP * 5, 0.0f);
-    for (int co = 0; co < CoutR; ++co) {
-        for (int ci = 0; ci < Cin; ++ci)
-            for (int t = 0; t < 9; ++t)
-                wf[((size_t)co * 9 + t) * d->ri_CinP + ci] = (float)c1->wsign[((size_t)co * Cin + ci) * 9 + t];
-        rfold[co * 5 + 0] = c1->alpha[co];
-        rfold[co * 5 + 1] = a1->A[co];
-        rfold[co * 5 + 2] = a1->B[co];
-        rfold[co * 5 + 3] = a1->slope[co];
-        rfold[co * 5 + 4] = a1->rsign[co];
-    }
-    // the same weights as int8 mma B fragments (realin_mma_kernel): for
-    // channel group g, tap t, k-step kk, lane l = 4*gid + tig, n-tile nt:
-    // b0 = bands kk*32 + tig*4 + 0..3 and b1 = bands kk*32 + 16 + tig*4 + 0..3
-    // of channel g*32 + nt*8 + gid
-    const int ngrp = cdiv(CoutR, 32);
-    std::vector<uint32_t> wfrag((size_t)ngrp * 9 * 4 * 32 * 8, 0u);
-    std::vector<int> rexact((size_t)CoutRP, 0);
-    if (Cin <= RM_CINP) {
-        for (int g = 0; g < ngrp; ++g)
-            for (int t = 0; t < 9; ++t)
-                for (int kk = 0; kk < 4; ++kk)
-                    for (int l = 0; l < 32; ++l)
-                        for (int nt = 0; nt < 4; ++nt)
-                            for (int h = 0; h < 2; ++h) {
-                                const int co = g * 32 + nt * 8 + (l >> 2);
-                                uint32_t word = 0;
-                                for (int i = 0; i < 4; ++i) {
-                                    const int ci = kk * 32 + h * 16 + (l & 3) * 4 + i;
-                                    int v = 0;
-                                    if (co < CoutR && ci < Cin) v = c1->wsign[((size_t)co * Cin + ci) * 9 + t] > 0 ? 1 : -1;
-                                    word |= (uint32_t)(uint8_t)(int8_t)v << (8 * i);
-                                }
-                                wfrag[((((size_t)g * 9 + t) * 4 + kk) * 32 + l) * 8 + nt * 2 + h] = word;
-                            }
-    }
-    // the same weights for realin_ws_kernel: [chunk][tap][16-band half][channel][16 bands]
+    const Engine* E = eng(m);
+    const bool stem = E->stem_c > 0;
+    // first conv of a v1 model: tables of the exact, mma.sync and tcgen05
+    // kernels. wsign is -1, 0 or +1 (checked at load) and goes in as is.
+    std::vector<float> wf, rfold;
+    std::vector<uint32_t> wfrag;
+    std::vector<int> rexact;
     std::vector<int8_t> rwu;
-    if (Cin <= RM_CINP && CoutR <= 32) {
-        rwu.assign(RW_WBYTES, (int8_t)0);
-        for (int kc = 0; kc < 4; ++kc)
-            for (int t = 0; t < 9; ++t)
-                for (int h = 0; h < 2; ++h)
-                    for (int co = 0; co < CoutR; ++co)
-                        for (int i = 0; i < 16; ++i) {
-                            const int ci = kc * 32 + h * 16 + i;
-                            if (ci < Cin)
-                                rwu[((((size_t)kc * 9 + t) * 2 + h) * 32 + co) * 16 + i] =
-                                    c1->wsign[((size_t)co * Cin + ci) * 9 + t] > 0 ? 1 : -1;
-                        }
-    }
     std::vector<RwThr> rthr;
-    if (!rwu.empty()) rthr.assign(32, RwThr{1ll << 62, 1, 0});
-    for (int co = 0; co < CoutR; ++co) {
-        const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
-        bool ok = v[3] >= 0.0f;
-        for (float f : v) ok = ok && std::isfinite(f);
-        rexact[co] = ok ? 0 : 1;
-        if (!rthr.empty()) rthr[co] = fold_threshold(v, !ok);
+    // stem of a v2 model: [slice][band][CB] weights and [channel][5] folds
+    std::vector<float> sw, sfold;
+    if (stem) {
+        const Conv* sc = &E->stem_conv;
+        const Act* sa = &E->stem_act;
+        const int C = sc->Cout, Cin = sc->Cin;
+        const int CB = C <= 8 ? 8 : C <= 16 ? 16 : 32, slices = cdiv(C, CB);
+        d->st_CB = CB;
+        d->st_slices = slices;
+        sw.assign((size_t)slices * Cin * CB, 0.0f);
+        sfold.assign((size_t)slices * CB * 5, 0.0f);
+        for (int co = 0; co < C; ++co) {
+            const int sl = co / CB, c = co % CB;
+            for (int ci = 0; ci < Cin; ++ci)
+                sw[((size_t)sl * Cin + ci) * CB + c] = (float)sc->wsign[(size_t)co * Cin + ci];
+            sfold[co * 5 + 0] = sc->alpha[co];
+            sfold[co * 5 + 1] = sa->A[co];
+            sfold[co * 5 + 2] = sa->B[co];
+            sfold[co * 5 + 3] = sa->slope[co];
+            sfold[co * 5 + 4] = sa->rsign[co];
+        }
+    } else {
+        const Conv* c1 = &m->enc_conv1[0];
+        const Act* a1 = &m->enc_act1[0];
+        const int Cin = c1->Cin, CoutR = c1->Cout, CoutRP = cdiv(CoutR, 32) * 32;
+        d->ri_CinP = cdiv(Cin, 4) * 4;
+        d->ri_CIP = d->ri_CinP + (((d->ri_CinP / 4) % 2 == 0) ? 4 : 0);
+        wf.assign((size_t)CoutRP * 9 * d->ri_CinP, 0.0f);
+        rfold.assign((size_t)CoutRP * 5, 0.0f);
+        for (int co = 0; co < CoutR; ++co) {
+            for (int ci = 0; ci < Cin; ++ci)
+                for (int t = 0; t < 9; ++t)
+                    wf[((size_t)co * 9 + t) * d->ri_CinP + ci] = (float)c1->wsign[((size_t)co * Cin + ci) * 9 + t];
+            rfold[co * 5 + 0] = c1->alpha[co];
+            rfold[co * 5 + 1] = a1->A[co];
+            rfold[co * 5 + 2] = a1->B[co];
+            rfold[co * 5 + 3] = a1->slope[co];
+            rfold[co * 5 + 4] = a1->rsign[co];
+        }
+        // the same weights as int8 mma B fragments (realin_mma_kernel): for
+        // channel group g, tap t, k-step kk, lane l = 4*gid + tig, n-tile nt:
+        // b0 = bands kk*32 + tig*4 + 0..3 and b1 = bands kk*32 + 16 + tig*4 + 0..3
+        // of channel g*32 + nt*8 + gid
+        const int ngrp = cdiv(CoutR, 32);
+        wfrag.assign((size_t)ngrp * 9 * 4 * 32 * 8, 0u);
+        rexact.assign((size_t)CoutRP, 0);
+        if (Cin <= RM_CINP) {
+            for (int g = 0; g < ngrp; ++g)
+                for (int t = 0; t < 9; ++t)
+                    for (int kk = 0; kk < 4; ++kk)
+                        for (int l = 0; l < 32; ++l)
+                            for (int nt = 0; nt < 4; ++nt)
+                                for (int h = 0; h < 2; ++h) {
+                                    const int co = g * 32 + nt * 8 + (l >> 2);
+                                    uint32_t word = 0;
+                                    for (int i = 0; i < 4; ++i) {
+                                        const int ci = kk * 32 + h * 16 + (l & 3) * 4 + i;
+                                        int v = 0;
+                                        if (co < CoutR && ci < Cin) v = c1->wsign[((size_t)co * Cin + ci) * 9 + t];
+                                        word |= (uint32_t)(uint8_t)(int8_t)v << (8 * i);
+                                    }
+                                    wfrag[((((size_t)g * 9 + t) * 4 + kk) * 32 + l) * 8 + nt * 2 + h] = word;
+                                }
+        }
+        // the same weights for realin_ws_kernel: [chunk][tap][16-band half][channel][16 bands]
+        if (Cin <= RM_CINP && CoutR <= 32) {
+            rwu.assign(RW_WBYTES, (int8_t)0);
+            for (int kc = 0; kc < 4; ++kc)
+                for (int t = 0; t < 9; ++t)
+                    for (int h = 0; h < 2; ++h)
+                        for (int co = 0; co < CoutR; ++co)
+                            for (int i = 0; i < 16; ++i) {
+                                const int ci = kc * 32 + h * 16 + i;
+                                if (ci < Cin)
+                                    rwu[((((size_t)kc * 9 + t) * 2 + h) * 32 + co) * 16 + i] =
+                                        c1->wsign[((size_t)co * Cin + ci) * 9 + t];
+                            }
+        }
+        if (!rwu.empty()) rthr.assign(32, RwThr{1ll << 62, 1, 0});
+        for (int co = 0; co < CoutR; ++co) {
+            const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
+            bool ok = v[3] >= 0.0f;
+            for (float f : v) ok = ok && std::isfinite(f);
+            rexact[co] = ok ? 0 : 1;
+            if (!rthr.empty()) rthr[co] = fold_threshold(v, !ok);
+        }
     }
     // binary convs
     struct Item {
@@ -441,7 +510,8 @@ static int dev_init(const Model* m, DevState* d) {
     };
     std::vector<Item> items;
     for (int i = 0; i < 4; ++i) {
-        if (i > 0) items.push_back({&d->enc1[i], &m->enc_conv1[i], &m->enc_act1[i], nullptr, m->enc_conv1[i].Cin, {}});
+        if (i > 0 || stem)
+            items.push_back({&d->enc1[i], &m->enc_conv1[i], &m->enc_act1[i], nullptr, m->enc_conv1[i].Cin, {}});
         items.push_back({&d->enc2[i], &m->enc_conv2[i], &m->enc_act2_skip[i], &m->enc_act2_down[i],
                          m->enc_conv2[i].Cin, {}});
     }
@@ -452,7 +522,8 @@ static int dev_init(const Model* m, DevState* d) {
         items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
     }
     size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
-                   align256(rexact.size() * 4) + align256(rwu.size());
+                   align256(rexact.size() * 4) + align256(rwu.size()) + align256(sw.size() * 4) +
+                   align256(sfold.size() * 4);
     for (auto& it : items) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h, it.a2 != nullptr);
         folds_of(it.a, it.L->CoutP, it.h.fold);
@@ -482,6 +553,8 @@ static int dev_init(const Model* m, DevState* d) {
     d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
     d->rw_wu = rwu.empty() ? nullptr : (int8_t*)put(rwu.data(), rwu.size());
     d->rw_thr = rthr;
+    d->st_w = sw.empty() ? nullptr : (float*)put(sw.data(), sw.size() * 4);
+    d->st_fold = sfold.empty() ? nullptr : (float*)put(sfold.data(), sfold.size() * 4);
     for (auto& it : items) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
@@ -546,7 +619,7 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
     Arena& a = d->ar;
     if (a.base && a.N >= N && a.H == H && a.W == W) return BNN_OK;
     Topology tp;
-    validate_topology(m, &tp);
+    topo(m, &tp);
     int Nn = std::max(N, a.H == H && a.W == W ? a.N : 0);
     size_t off = 0;
     std::vector<std::pair<uint32_t**, size_t>> plan;
@@ -555,6 +628,7 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
         plan.push_back({slot, off});
         off += align256(bytes + 4);
     };
+    if (tp.stem) add(&a.stem, H, W, tp.stem);
     for (int i = 0; i < 4; ++i) {
         const int h = H >> i, w = W >> i;
         add(&a.enc_h[i], h, w, tp.enc[i]);
@@ -571,7 +645,7 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
     // undecided-output list of the first conv: sized for ~1 in 64 outputs, at
     // least 64 K entries; beyond it the fix-up recomputes the whole batch
     const size_t outs = (size_t)Nn * H * W * m->enc_conv1[0].Cout;
-    const int cap = (int)std::min<size_t>(std::max<size_t>(outs / 64, 65536), (size_t)1 << 24);
+    const int cap = tp.stem ? 0 : (int)std::min<size_t>(std::max<size_t>(outs / 64, 65536), (size_t)1 << 24);
     const size_t list_off = off;
     off += align256((size_t)cap * 16);
     const size_t ctl_off = off;
@@ -947,6 +1021,34 @@ static int run_first_conv(DevState* d, const Model* m, const float* x, int N, in
     return run_realin_exact(d, m, x, N, H, W, out, nullptr, st);
 }
 
+// v2 stem: bands -> bit plane [N][H][W][cw(stem_c)]; dbg (optional) gets
+// the conv output alpha*acc as [N][stem_c][H][W]
+static int run_stem(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out, float* dbg,
+                    cudaStream_t st) {
+    if (N <= 0) return BNN_OK;
+    const Engine* E = eng(m);
+    StemParams p{};
+    p.x = x; p.w = d->st_w; p.fold = d->st_fold; p.out = out; p.dbg = dbg;
+    p.Cin = E->stem_conv.Cin; p.HW = H * W; p.Cout = E->stem_c; p.cwo = cw_of(p.Cout);
+    const int CB = d->st_CB;
+    // PX pixels per thread: they share one patch (PX | H*W) and one aligned
+    // vector load; at most 64 accumulators per thread
+    const uintptr_t xa = (uintptr_t)x;
+    int PX = (p.HW % 4 == 0 && xa % 16 == 0) ? 4 : (p.HW % 2 == 0 && xa % 8 == 0) ? 2 : 1;
+    if (CB == 32 && PX == 4) PX = 2;
+    p.groups = (long long)N * p.HW / PX;
+    const size_t smem = (size_t)p.Cin * CB * 4;
+    const dim3 grid((unsigned)cdiv(p.groups, 256), (unsigned)d->st_slices);
+#define STEM_LAUNCH(cb, px) stem_fold_kernel<cb, px><<<grid, 256, smem, st>>>(p)
+    if (CB == 8) { if (PX == 4) STEM_LAUNCH(8, 4); else if (PX == 2) STEM_LAUNCH(8, 2); else STEM_LAUNCH(8, 1); }
+    else if (CB == 16) { if (PX == 4) STEM_LAUNCH(16, 4); else if (PX == 2) STEM_LAUNCH(16, 2); else STEM_LAUNCH(16, 1); }
+    else { if (PX == 2) STEM_LAUNCH(32, 2); else STEM_LAUNCH(32, 1); }
+#undef STEM_LAUNCH
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "stem launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
 static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int H, int W, float* out,
                     cudaStream_t st) {
     if (N <= 0) return BNN_OK;
@@ -961,12 +1063,13 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
 }
 
 // -------------------------------------------------------------------
-// the forward: 19 launches in the reference's order
+// the forward: 19 launches in the reference's order (+1 for the first conv's
+// fix-up; a v2 model: stem, 18 binary convs, head)
 // -------------------------------------------------------------------
 struct Dbg {  // optional debug outputs of one forward (device pointers)
     float* realin = nullptr;
     uint32_t* realin_bits = nullptr;  // scratch for the exact kernel that produces `realin`
-    int32_t* P[17] = {nullptr};
+    int32_t* P[18] = {nullptr};     // binary convs' P in forward order (18 with a v2 stem)
     int32_t* Pd[4] = {nullptr};
 };
 
@@ -1011,14 +1114,30 @@ static int forward_launches(const Model* m, DevState* d, const float* x, int N, 
     const double NHW = (double)N * H * W;
     auto work = [&](const BinLayer& L, int h, int w) { return (double)N * h * w * L.Cout * (double)L.Cin * 9.0; };
     int li = 0;
-    if (pc) pc->begin("enc1.conv1+act1", "conv_real", NHW * m->enc_conv1[0].Cout * m->enc_conv1[0].Cin * 9.0);
-    // the stage dump's float output of the first conv comes from the exact
-    // kernel; the bit plane used downstream is always the production path's
-    if (dbg && dbg->realin) rc = run_realin_exact(d, m, x, N, H, W, dbg->realin_bits, dbg->realin, st);
-    else rc = BNN_OK;
-    if (!rc) rc = run_first_conv(d, m, x, N, H, W, a.enc_h[0], st);
-    if (pc) pc->end();
-    if (rc) return rc;
+    const Engine* E = eng(m);
+    if (E->stem_c) {
+        // v2: stem (exact fp32 order in the production kernel itself), then
+        // enc1.conv1 binary like the other levels
+        if (pc) pc->begin("stem.conv+act", "conv_real", NHW * E->stem_c * E->stem_conv.Cin);
+        rc = run_stem(d, m, x, N, H, W, a.stem, dbg ? dbg->realin : nullptr, st);
+        if (pc) pc->end();
+        if (rc) return rc;
+        if (pc) pc->begin("enc1.conv1+act1", "bconv", work(d->enc1[0], H, W));
+        rc = run_bin(d->enc1[0], a.stem, nullptr, 0, 0, N, H, W, a.enc_h[0], nullptr, dbg ? dbg->P[li] : nullptr,
+                     nullptr, st);
+        if (pc) pc->end();
+        if (rc) return rc;
+        ++li;
+    } else {
+        if (pc) pc->begin("enc1.conv1+act1", "conv_real", NHW * m->enc_conv1[0].Cout * m->enc_conv1[0].Cin * 9.0);
+        // the stage dump's float output of the first conv comes from the exact
+        // kernel; the bit plane used downstream is always the production path's
+        if (dbg && dbg->realin) rc = run_realin_exact(d, m, x, N, H, W, dbg->realin_bits, dbg->realin, st);
+        else rc = BNN_OK;
+        if (!rc) rc = run_first_conv(d, m, x, N, H, W, a.enc_h[0], st);
+        if (pc) pc->end();
+        if (rc) return rc;
+    }
     for (int i = 0; i < 4; ++i) {
         const int h = H >> i, w = W >> i;
         if (i > 0) {
@@ -1448,6 +1567,7 @@ BNN_API int bnn_set_chunk(Model* m, int patches) {
 
 BNN_API int bnn_forward_launches(const Model* m, int N, int H, int W) {
     if (!m || N <= 0 || H < 16 || W < 16) return 0;
+    if (eng(m)->stem_c) return 20;                    // stem + 18 binary convs + head
     return first_conv_fast_ok(m, N, H, W) ? 20 : 19;  // + the first conv's fix-up kernel
 }
 
@@ -1470,9 +1590,11 @@ BNN_API int bnn_first_conv_device(const Model* m, int device, const float* d_inp
         rc = arena_reserve(m, d, N, H, W);
         if (!rc) {
             cudaStreamWaitEvent(st, d->ev_last, 0);
-            const bool fast = !exact && first_conv_fast_ok(m, N, H, W);
-            rc = fast ? run_realin_fast(d, m, d_input, N, H, W, d_bits, st)
-                      : run_realin_exact(d, m, d_input, N, H, W, d_bits, nullptr, st);
+            const bool stem = eng(m)->stem_c > 0;
+            const bool fast = !stem && !exact && first_conv_fast_ok(m, N, H, W);
+            rc = stem   ? run_stem(d, m, d_input, N, H, W, d_bits, nullptr, st)
+                 : fast ? run_realin_fast(d, m, d_input, N, H, W, d_bits, st)
+                        : run_realin_exact(d, m, d_input, N, H, W, d_bits, nullptr, st);
             if (!rc) cudaEventRecord(d->ev_last, st);
             if (!rc && undecided) {
                 unsigned int ctl[3] = {0, 0, 0};
@@ -1562,30 +1684,31 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     std::lock_guard<std::mutex> g(d->mu);
     if ((rc = arena_reserve(m, d, 1, H, W))) return rc;
     Topology tp;
-    validate_topology(m, &tp);
+    topo(m, &tp);
     const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
-    // layer geometry in forward order
-    struct LG { const char* name; int C, h, w; const BinLayer* L; };
-    static const char* PN[17] = {"enc1.conv2.P", "enc2.conv1.P", "enc2.conv2.P", "enc3.conv1.P", "enc3.conv2.P",
-                                 "enc4.conv1.P", "enc4.conv2.P", "bottleneck.conv1.P", "bottleneck.conv2.P",
-                                 "dec4.conv1.P", "dec4.conv2.P", "dec3.conv1.P", "dec3.conv2.P", "dec2.conv1.P",
-                                 "dec2.conv2.P", "dec1.conv1.P", "dec1.conv2.P"};
+    const int stc = tp.stem;
+    // binary-conv layer geometry in forward order (enc1.conv1 is one of them
+    // only behind a v2 stem)
+    struct LG { std::string name; int C, h, w; const BinLayer* L; };
+    static const char* EN[4] = {"enc1", "enc2", "enc3", "enc4"};
+    static const char* DN[4] = {"dec4", "dec3", "dec2", "dec1"};
     std::vector<LG> lg;
     for (int i = 0; i < 4; ++i) {
-        if (i > 0) lg.push_back({PN[lg.size()], d->enc1[i].Cout, H >> i, W >> i, &d->enc1[i]});
-        lg.push_back({PN[lg.size()], d->enc2[i].Cout, H >> i, W >> i, &d->enc2[i]});
+        if (i > 0 || stc) lg.push_back({std::string(EN[i]) + ".conv1.P", d->enc1[i].Cout, H >> i, W >> i, &d->enc1[i]});
+        lg.push_back({std::string(EN[i]) + ".conv2.P", d->enc2[i].Cout, H >> i, W >> i, &d->enc2[i]});
     }
-    lg.push_back({PN[lg.size()], d->bott1.Cout, H >> 4, W >> 4, &d->bott1});
-    lg.push_back({PN[lg.size()], d->bott2.Cout, H >> 4, W >> 4, &d->bott2});
+    lg.push_back({"bottleneck.conv1.P", d->bott1.Cout, H >> 4, W >> 4, &d->bott1});
+    lg.push_back({"bottleneck.conv2.P", d->bott2.Cout, H >> 4, W >> 4, &d->bott2});
     for (int i = 0; i < 4; ++i) {
-        lg.push_back({PN[lg.size()], d->dec1[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec1[i]});
-        lg.push_back({PN[lg.size()], d->dec2[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec2[i]});
+        lg.push_back({std::string(DN[i]) + ".conv1.P", d->dec1[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec1[i]});
+        lg.push_back({std::string(DN[i]) + ".conv2.P", d->dec2[i].Cout, H >> (3 - i), W >> (3 - i), &d->dec2[i]});
     }
+    const int nl = (int)lg.size();
     size_t words = 0;
-    std::vector<size_t> poff(17), pdoff(4);
-    for (int k = 0; k < 17; ++k) { poff[k] = words; words += (size_t)lg[k].C * lg[k].h * lg[k].w + 1; }
+    std::vector<size_t> poff(nl), pdoff(4);
+    for (int k = 0; k < nl; ++k) { poff[k] = words; words += (size_t)lg[k].C * lg[k].h * lg[k].w + 1; }
     for (int i = 0; i < 4; ++i) { pdoff[i] = words; words += (size_t)tp.enc[i] * (H >> (i + 1)) * (W >> (i + 1)) + 1; }
-    const size_t ri_words = (size_t)m->enc_conv1[0].Cout * H * W;
+    const size_t ri_words = (size_t)(stc ? stc : m->enc_conv1[0].Cout) * H * W;
     const size_t rb_words = (size_t)H * W * cw_of(m->enc_conv1[0].Cout);
     void* buf = nullptr;
     if (cudaMalloc(&buf, (words + ri_words + ip + op + rb_words) * 4) != cudaSuccess) {
@@ -1599,7 +1722,7 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     Dbg dbg;
     dbg.realin = dri;
     dbg.realin_bits = (uint32_t*)(dout + op);
-    for (int k = 0; k < 17; ++k) dbg.P[k] = P + poff[k];
+    for (int k = 0; k < nl; ++k) dbg.P[k] = P + poff[k];
     for (int i = 0; i < 4; ++i) dbg.Pd[i] = P + pdoff[i];
     rc = BNN_OK;
     auto fail = [&](int code) { cudaFree(buf); return code; };
@@ -1624,23 +1747,26 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
                 o[(size_t)c * h * w + px] = ((hb[(size_t)px * cw + (c >> 5)] >> (c & 31)) & 1u) ? 1 : -1;
     };
     std::vector<int8_t> act;
-    static const char* EN[4] = {"enc1", "enc2", "enc3", "enc4"};
-    static const char* DN[4] = {"dec4", "dec3", "dec2", "dec1"};
     char nm[64];
     int k = 0;
     std::vector<std::vector<int8_t>> skips(4);
     for (int i = 0; i < 4; ++i) {
         const int h = H >> i, w = W >> i;
-        if (i == 0) {
+        if (i == 0 && !stc) {
             cb(ctx, "enc1.conv1.out", 2, m->enc_conv1[0].Cout, H, W, hri.data());
         } else {
-            cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]);
+            if (i == 0) {
+                cb(ctx, "stem.conv.out", 2, stc, H, W, hri.data());
+                bits_to_i8(a.stem, stc, H, W, act);
+                cb(ctx, "stem.act", 0, stc, H, W, act.data());
+            }
+            cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h, w, hP.data() + poff[k]);
             ++k;
         }
         bits_to_i8(a.enc_h[i], tp.enc[i], h, w, act);
         snprintf(nm, sizeof nm, "%s.act1", EN[i]);
         cb(ctx, nm, 0, tp.enc[i], h, w, act.data());
-        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]);
+        cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h, w, hP.data() + poff[k]);
         ++k;
         bits_to_i8(a.skip[i], tp.enc[i], h, w, skips[i]);
         snprintf(nm, sizeof nm, "%s.act2_skip", EN[i]);
@@ -1652,10 +1778,10 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
         cb(ctx, nm, 0, tp.enc[i], h >> 1, w >> 1, act.data());
     }
     const int h4 = H >> 4, w4 = W >> 4;
-    cb(ctx, lg[k].name, 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
+    cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
     bits_to_i8(a.bott_h, d->bott1.Cout, h4, w4, act);
     cb(ctx, "bottleneck.act1", 0, d->bott1.Cout, h4, w4, act.data());
-    cb(ctx, lg[k].name, 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
+    cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h4, w4, hP.data() + poff[k]); ++k;
     std::vector<int8_t> xprev;
     bits_to_i8(a.bott_x, tp.bott, h4, w4, xprev);
     cb(ctx, "bottleneck.act2", 0, tp.bott, h4, w4, xprev.data());
@@ -1673,11 +1799,11 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
                     cat[((size_t)(sC + c) * h + oh + y) * w + ow + x] = xprev[((size_t)c * hp + y / 2) * wp + x / 2];
         snprintf(nm, sizeof nm, "%s.cat", DN[i]);
         cb(ctx, nm, 0, sC + xC, h, w, cat.data());
-        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
+        cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
         bits_to_i8(a.dec_h[i], d->dec1[i].Cout, h, w, act);
         snprintf(nm, sizeof nm, "%s.act1", DN[i]);
         cb(ctx, nm, 0, d->dec1[i].Cout, h, w, act.data());
-        cb(ctx, lg[k].name, 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
+        cb(ctx, lg[k].name.c_str(), 1, lg[k].C, h, w, hP.data() + poff[k]); ++k;
         bits_to_i8(a.dec_x[i], tp.dec[i], h, w, xprev);
         snprintf(nm, sizeof nm, "%s.act2", DN[i]);
         cb(ctx, nm, 0, tp.dec[i], h, w, xprev.data());

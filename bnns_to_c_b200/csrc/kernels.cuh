@@ -429,6 +429,116 @@ __global__ void __launch_bounds__(128) realin3x3_fold_kernel(const RealinParams 
 }
 
 // ---------------------------------------------------------------------
+// Spectral stem of the v2 model (csrc/bnn_model_stem.c:172-187): real
+// input, +-1 weights, 1x1 pad 0 stride 1, fused with the real fold and the
+// bit pack, in the reference's exact fp32 order. For a 1x1 window the
+// reference's conv_realin_naive (csrc/bnn_conv_realin.c:90-112) sums the
+// bands sequentially from +0 (s = s + x*w; acc = 0 + s, which equals s as s
+// is never -0) and scales by alpha; w = +-1 makes every product exact, so
+// fma(w, x, s) is that same rounding step. The fold is
+// csrc/bnn_fold.c:62-77 with explicit roundings (no contraction).
+//
+// One thread owns PX consecutive pixels of one patch (PX | H*W) and CB
+// output channels (a slice; blockIdx.y picks it). Its accumulators are
+// channel pairs updated by packed fp32x2 FMAs ({w_c, w_c+1} x {x, x}): two
+// independent fp32 FMAs, bit-identical to the scalar ones. The band loop
+// streams x straight from HBM (each patch plane read once, 16-byte loads
+// when PX = 4); the slice's weights sit in shared memory as [band][CB]
+// floats, read as warp-wide broadcasts.
+// ---------------------------------------------------------------------
+struct StemParams {
+    const float* x;      // [N][Cin][HW]
+    const float* w;      // [slices][Cin][CB] (+1.0f / -1.0f, zero past Cout)
+    const float* fold;   // [slices * CB][5]: alpha, A, B, slope, rsign
+    uint32_t* out;       // [N * HW][cwo]
+    float* dbg;          // optional [N][Cout][HW] conv output (alpha*acc)
+    int Cin, HW, Cout, cwo;
+    long long groups;    // N*HW / PX
+};
+
+template <int CB, int PX>
+__global__ void __launch_bounds__(256, 2) stem_fold_kernel(const StemParams p) {
+    static_assert(CB % 4 == 0 && CB <= 32 && (PX == 1 || PX == 2 || PX == 4), "stem tile");
+    extern __shared__ __align__(16) float sw[];   // [Cin][CB]
+    const int slice = blockIdx.y;
+    {
+        const float4* wg = reinterpret_cast<const float4*>(p.w + (size_t)slice * p.Cin * CB);
+        float4* s4 = reinterpret_cast<float4*>(sw);
+        for (int i = threadIdx.x; i < p.Cin * (CB / 4); i += blockDim.x) s4[i] = __ldg(wg + i);
+    }
+    __syncthreads();
+    const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= p.groups) return;
+    const long long pix = g * PX;   // global pixel n*HW + q; a group never crosses patches
+    const long long n = pix / p.HW;
+    const int q = (int)(pix - n * p.HW);
+    const float* xp = p.x + (size_t)n * p.Cin * p.HW + q;
+
+    float2 acc[PX][CB / 2];
+#pragma unroll
+    for (int j = 0; j < PX; ++j)
+#pragma unroll
+        for (int c = 0; c < CB / 2; ++c) acc[j][c] = make_float2(0.0f, 0.0f);
+
+#pragma unroll 4
+    for (int ci = 0; ci < p.Cin; ++ci) {
+        float xv[PX];
+        const float* src = xp + (size_t)ci * p.HW;
+        if constexpr (PX == 4) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(src));
+            xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
+        } else if constexpr (PX == 2) {
+            const float2 v = __ldcs(reinterpret_cast<const float2*>(src));
+            xv[0] = v.x; xv[1] = v.y;
+        } else {
+            xv[0] = __ldcs(src);
+        }
+        const float4* wr = reinterpret_cast<const float4*>(sw + ci * CB);
+#pragma unroll
+        for (int c4 = 0; c4 < CB / 4; ++c4) {
+            const float4 w4 = wr[c4];
+            const float2 wa = make_float2(w4.x, w4.y), wb = make_float2(w4.z, w4.w);
+#pragma unroll
+            for (int j = 0; j < PX; ++j) {
+                const float2 xx = make_float2(xv[j], xv[j]);
+                acc[j][2 * c4] = __ffma2_rn(wa, xx, acc[j][2 * c4]);
+                acc[j][2 * c4 + 1] = __ffma2_rn(wb, xx, acc[j][2 * c4 + 1]);
+            }
+        }
+    }
+
+    // fold: z = fma(A, alpha*acc, B); z<0 -> slope*z; r = z + rsign; bit = r > 0
+    uint32_t bits[PX];
+#pragma unroll
+    for (int j = 0; j < PX; ++j) bits[j] = 0u;
+#pragma unroll
+    for (int c = 0; c < CB; ++c) {
+        const int co = slice * CB + c;
+        if (co >= p.Cout) break;
+        const float* f = p.fold + (size_t)co * 5;
+        const float alpha = __ldg(f), A = __ldg(f + 1), B = __ldg(f + 2), sl = __ldg(f + 3), rs = __ldg(f + 4);
+#pragma unroll
+        for (int j = 0; j < PX; ++j) {
+            const float a = (c & 1) ? acc[j][c >> 1].y : acc[j][c >> 1].x;
+            const float o = __fmul_rn(alpha, a);
+            float z = __fmaf_rn(A, o, B);
+            if (z < 0.0f) z = __fmul_rn(sl, z);
+            const float rr = __fadd_rn(z, rs);
+            bits[j] |= (rr > 0.0f ? 1u : 0u) << c;
+            if (p.dbg) p.dbg[((size_t)n * p.Cout + co) * p.HW + q + j] = o;
+        }
+    }
+    // CB = 32: slice s is word s; CB < 32: one slice (Cout <= CB), word 0
+    if (PX == 4 && p.cwo == 1) {
+        *reinterpret_cast<uint4*>(p.out + pix) = make_uint4(bits[0], bits[PX > 1 ? 1 : 0], bits[PX > 2 ? 2 : 0],
+                                                             bits[PX > 3 ? 3 : 0]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < PX; ++j) p.out[(size_t)(pix + j) * p.cwo + slice] = bits[j];
+    }
+}
+
+// ---------------------------------------------------------------------
 // First conv on int8 tensor cores, decided by an error bound.
 //
 // Only sign(r) of the first conv's folded output is kept, so the fp32 sum

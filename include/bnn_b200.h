@@ -204,7 +204,10 @@ int bnn_unpack_act_device(const uint32_t *d_bits, int N, int C, int H, int W,
  * all-fp32 exact-order kernel. Both give the reference's bits. If
  * `undecided` is not NULL the call synchronises and stores how many outputs
  * the production path sent to the exact fix-up (0xffffffff: the list
- * overflowed and the whole batch was recomputed exactly). */
+ * overflowed and the whole batch was recomputed exactly). On the engine
+ * handle of a v2 model (bnn_stem_as_model) it runs the stem + stem fold
+ * instead (csrc/bnn_model_stem.c:172-187), whose kernel is exact-order by
+ * construction: `exact` is ignored and `undecided` gets 0. */
 int bnn_first_conv_device(const Model *m, int device, const float *d_input,
                           int N, int H, int W, uint32_t *d_bits, int exact,
                           unsigned int *undecided, void *stream);

@@ -8,11 +8,26 @@
  * fastest way to run the reference on many patches (its OpenMP only spans
  * one conv's rows).
  *
+ * Built with -DREF_STEM (ref_bench_stem) it times the reference's v2
+ * spectral-stem engine instead (bnn_stem_load / bnn_stem_forward).
+ *
  * usage: ref_bench blob n_patches H W procs seed steps warmup [first_patch]
  * prints one line per timed step: "step <i> <seconds>", then
  * "checksum <sum of logits of patch 0>" so callers can tie it to the GPU run.
  */
+#ifdef REF_STEM
+#include "bnn_model_stem.h"
+typedef StemModel RModel;
+#define REF_LOAD bnn_stem_load
+#define REF_FORWARD bnn_stem_forward
+#define REF_FREE bnn_stem_free
+#else
 #include "bnn_model.h"
+typedef Model RModel;
+#define REF_LOAD bnn_load
+#define REF_FORWARD bnn_forward
+#define REF_FREE bnn_free
+#endif
 #include "../include/bnn_synth.h"
 
 #include <stdio.h>
@@ -31,13 +46,13 @@ static double now_s(void) {
     return (double)t.tv_sec + 1e-9 * (double)t.tv_nsec;
 }
 
-static void run_shard(const Model *m, const float *in, float *out, int lo,
+static void run_shard(const RModel *m, const float *in, float *out, int lo,
                       int hi, int H, int W) {
     size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
-    for (int i = lo; i < hi; ++i) bnn_forward(m, in + (size_t)i * ip, H, W, out + (size_t)i * op);
+    for (int i = lo; i < hi; ++i) REF_FORWARD(m, in + (size_t)i * ip, H, W, out + (size_t)i * op);
 }
 
-static double one_step(const Model *m, const float *in, float *out, int n,
+static double one_step(const RModel *m, const float *in, float *out, int n,
                        int H, int W, int procs) {
     double t0 = now_s();
     if (procs <= 1) {
@@ -74,7 +89,7 @@ int main(int argc, char **argv) {
 #ifdef _OPENMP
     omp_set_num_threads(1);
 #endif
-    Model *m = bnn_load(argv[1]);
+    RModel *m = REF_LOAD(argv[1]);
     size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
     float *in = malloc((size_t)n * ip * sizeof(float) + 4);
     float *out = malloc((size_t)n * op * sizeof(float) + 4);
@@ -89,7 +104,7 @@ int main(int argc, char **argv) {
     double cs = 0;
     for (size_t j = 0; j < op; ++j) cs += out[j];
     printf("checksum %.9g\n", cs);
-    bnn_free(m);
+    REF_FREE(m);
     free(in); free(out);
     return 0;
 }

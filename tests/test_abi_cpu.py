@@ -20,11 +20,12 @@ from bnns_to_c_b200 import blob as B
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
 GOLD = os.path.join(ROOT, "tests", "golden")
 C8 = os.path.join(GOLD, "unet_c8_mixed_s1.blob")
+S8 = os.path.join(GOLD, "stem_c8_mixed_s3.blob")
 
 
 def declared_functions():
     names = []
-    for h in ("bnn_model.h", "bnn_b200.h"):
+    for h in ("bnn_model.h", "bnn_b200.h", "bnn_model_stem.h"):
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(bnn_\w+)\s*\(", src, flags=re.M):
@@ -151,3 +152,104 @@ def test_pack_kidx_bit_order():
 def test_cli_usage_matches_reference():
     r = subprocess.run([bn.CLI_PATH], capture_output=True, text=True)
     assert r.returncode == 1 and "usage:" in r.stderr and "input.bin|rand output.bin [H W [reps]]" in r.stderr
+
+
+# ------------------------------------------------------------------ v2 (spectral stem)
+def _stem_status(data):
+    L = bn.lib()
+    h = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(data, len(data))
+    rc = L.bnn_stem_load_mem(buf, len(data), ctypes.byref(h))
+    if rc == 0:
+        L.bnn_stem_free(h.value)
+    return rc, L.bnn_last_error().decode()
+
+
+def test_stem_load_parses_without_gpu():
+    m = bn.StemModel(S8)
+    assert (m.version, m.base_channels, m.n_bands, m.n_classes, m.upsampler) == (2, 8, 120, 3, 0)
+    assert m.stem_channels == 16
+    # the engine handle reads as a Model with the v2 body, and bnn_free on it
+    # is a no-op (the StemModel owns it)
+    hdr = bn._ModelHeader.from_address(m.handle)
+    assert (hdr.version, hdr.n_bands) == (2, 120)
+    bn.lib().bnn_free(m.handle)
+    assert bn.lib().bnn_forward_launches(m.handle, 4, 32, 32) == 20
+    m.close()
+
+
+def test_stem_loader_rejections_match_reference():
+    data = open(S8, "rb").read()
+    assert _stem_status(data) == (0, "")
+    assert _stem_status(data[:-1])[1] == "short read"
+    assert _stem_status(data + b"\0")[1] == "trailing bytes in blob"
+    assert _stem_status(b"XNNC" + data[4:])[1] == "bad magic"
+    # csrc/bnn_model_stem.c:84-85 and 89-92
+    assert _stem_status(open(C8, "rb").read())[1] == (
+        "bnn_stem: expected v2 blob, got v1 (use the v1 engine for non-stem models)")
+    for hs, ns in ((0, 1), (1, 2)):
+        bad = data[:24] + struct.pack("<2i", hs, ns) + data[32:]
+        assert _stem_status(bad)[1] == "bnn_stem: only has_stem=1, n_stem_layers=1 supported"
+    bad = data[:32] + struct.pack("<i", 7) + data[36:]
+    assert _stem_status(bad)[1] == "bad conv tag 7"
+    # a v2 blob through the v1 loader misparses and is refused, not run
+    assert _status(data)[0] != 0
+
+
+def test_stem_topology_validation():
+    def status(mut):
+        m = B.random_model(8, 120, 3, seed=6, rules="mixed", stem_channels=12)
+        mut(m)
+        return _stem_status(B.blob_bytes(m))
+
+    assert status(lambda m: None) == (0, "")
+    # a 3x3 stem: the reference would run it; this engine refuses it
+    rc, msg = status(lambda m: m["stem.conv"].update(wsign=np.ones((12, 120, 3, 3), np.int8), pad=1))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "stem.conv" in msg
+    # stem weights other than -1 / 0 / +1
+    def big(m):
+        m["stem.conv"]["wsign"] = m["stem.conv"]["wsign"].copy()
+        m["stem.conv"]["wsign"][3, 7, 0, 0] = 2
+    rc, msg = status(big)
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "wsign" in msg
+    # zero weights (np.sign of an exact 0.0) are accepted
+    def zero(m):
+        m["stem.conv"]["wsign"] = m["stem.conv"]["wsign"].copy()
+        m["stem.conv"]["wsign"][:, ::5] = 0
+    assert status(zero) == (0, "")
+    # enc1.conv1 must be binary on the stem's channels
+    def chain(m):
+        m["stem.act"] = {k: (v[:10] if isinstance(v, np.ndarray) else v) for k, v in m["stem.act"].items()}
+        m["stem.conv"] = dict(m["stem.conv"], wsign=m["stem.conv"]["wsign"][:10], alpha=m["stem.conv"]["alpha"][:10])
+    rc, msg = status(chain)
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "enc1.conv1" in msg
+
+
+def test_v1_first_conv_weights_checked():
+    m = B.random_model(8, 120, 3, seed=4)
+    m["enc1.conv1"] = dict(m["enc1.conv1"], wsign=m["enc1.conv1"]["wsign"].copy())
+    m["enc1.conv1"]["wsign"][0, :, 1, 1] = 0
+    assert _status(B.blob_bytes(m)) == (0, "")
+    m["enc1.conv1"]["wsign"][0, 0, 0, 0] = -3
+    rc, msg = _status(B.blob_bytes(m))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "enc1.conv1" in msg
+
+
+def test_dropin_bnn_stem_load_exits_like_reference(tmp_path):
+    code = ("import ctypes,sys; L=ctypes.CDLL(sys.argv[1]); L.bnn_stem_load.restype=ctypes.c_void_p; "
+            "L.bnn_stem_load(sys.argv[2].encode()); print('returned')")
+    r = subprocess.run([sys.executable, "-c", code, bn.LIB_PATH, C8], capture_output=True, text=True)
+    assert r.returncode == 1 and "expected v2 blob, got v1" in r.stderr and "returned" not in r.stdout
+
+
+def test_stem_blob_writer_matches_committed_fixtures():
+    for name, base, rules, seed in (("stem_c8_mixed_s3", 8, "mixed", 3), ("stem_c16_base_s4", 16, "baseline", 4)):
+        data = B.blob_bytes(B.random_model(base, 120, 3, seed=seed, rules=rules, stem_channels=16))
+        assert data == open(os.path.join(GOLD, name + ".blob"), "rb").read()
+        rt = B.read_blob(os.path.join(GOLD, name + ".blob"))
+        assert rt["has_stem"] == 1 and rt["stem_conv"]["wsign"].shape == (16, 120, 1, 1)
+
+
+def test_stem_cli_usage_matches_reference():
+    r = subprocess.run([bn.CLI_STEM_PATH], capture_output=True, text=True)
+    assert r.returncode == 1 and "usage:" in r.stderr and "weights_stem.blob" in r.stderr

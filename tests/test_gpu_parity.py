@@ -129,7 +129,7 @@ def test_fused_layer_vs_oracle(cin, cout, H, W, n, pool, bconv_kind):
 
 # ------------------------------------------------------------------ whole net
 def _fixtures():
-    return sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz")))
+    return sorted(glob.glob(os.path.join(GOLD, "unet_*_*x*.npz")) + glob.glob(os.path.join(GOLD, "stem_*_*x*.npz")))
 
 
 def _blob_path(name, tmp_path):
@@ -146,7 +146,8 @@ def test_forward_stages_match_reference(npz, tmp_path, bconv_kind):
     g = np.load(npz)
     name = os.path.basename(npz).rsplit("_", 1)[0]
     H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
-    m = bn.Model(_blob_path(name, tmp_path))
+    # v2 fixtures (stem_*) run through the stem engine, v1 through bnn_load's
+    m = (bn.StemModel if name.startswith("stem_") else bn.Model)(_blob_path(name, tmp_path))
     x = synth(seed, 0, n, 120, H, W)
     for p in range(n):
         st = m.stages(x[p])
@@ -410,3 +411,137 @@ def test_patched_forward_multi_device(tmp_path):
     m.set_devices([0, 1])
     two = m.forward_patched(cube, 32)
     assert same_bits(one, two)
+
+
+# ------------------------------------------------------------------ first conv: zero weights
+def test_first_conv_zero_weights(first_kind, tmp_path):
+    """wsign = 0 (np.sign of an exact 0.0 weight, which the reference's blob
+    writer can emit): the tensor-core paths take it as a 0 product, as the
+    reference's fp32 sum does."""
+    def zeros(mdl):
+        w = mdl["enc1.conv1"]["wsign"].copy()
+        w[:, ::3] = 0
+        w[5] = 0
+        mdl["enc1.conv1"]["wsign"] = w
+    mdl = B.random_model(32, 120, 3, seed=8, rules="baseline")
+    zeros(mdl)
+    path = tmp_path / "z.blob"
+    path.write_bytes(B.blob_bytes(mdl))
+    m = bn.Model(str(path))
+    m.enc_c1_cout = 32
+    x = synth(48, 0, 8, 120, 32, 32)
+    fast, _ = _first_conv_bits(m, x, False)
+    exact, _ = _first_conv_bits(m, x, True)
+    assert np.array_equal(fast, exact)
+    om = OModel(str(path))
+    assert same_bits(m.forward_batch(x[:2]), om.forward_batch(x[:2]))
+
+
+# ------------------------------------------------------------------ v2 spectral stem
+def _stem(tmp_path, stem, base=8, seed=0, bands=120, rules="mixed", mutate=None):
+    mdl = B.random_model(base, bands, 3, seed=seed, rules=rules, stem_channels=stem)
+    if mutate:
+        mutate(mdl)
+    path = tmp_path / f"stem{stem}_{bands}.blob"
+    path.write_bytes(B.blob_bytes(mdl))
+    return bn.StemModel(str(path)), OModel(str(path))
+
+
+def _same_stages(st, ost, skip_float=False):
+    assert set(st) == set(ost), set(st) ^ set(ost)
+    for k in ost:
+        if skip_float and k == "stem.conv.out":
+            continue
+        assert same_bits(st[k], ost[k]), k
+
+
+@pytest.mark.parametrize("stem,H,W", [(16, 32, 32), (8, 37, 23), (12, 16, 48), (24, 33, 34), (32, 16, 16),
+                                      (40, 20, 36), (1, 17, 17), (70, 32, 18)])
+def test_stem_widths_and_sizes_match_oracle(stem, H, W, tmp_path, bconv_kind):
+    """Stem widths on every kernel shape (8/16/32-channel slices, 1-3
+    words per pixel) and patch sizes on every pixel grouping (4, 2 or 1
+    pixels per thread): every stage, the stem's float output included, and
+    the batched logits equal the oracle's bit for bit."""
+    m, om = _stem(tmp_path, stem, seed=stem)
+    x = synth(stem + H, 0, 3, 120, H, W)
+    _same_stages(m.stages(x[0]), om.stages(x[0]))
+    assert same_bits(m.forward_batch(x), om.forward_batch(x))
+
+
+@pytest.mark.parametrize("bands", [1, 37, 300])
+def test_stem_band_counts_and_zero_weights(bands, tmp_path):
+    def zeros(mdl):
+        w = mdl["stem.conv"]["wsign"].copy()
+        w[:, ::4] = 0
+        w[2] = 0
+        mdl["stem.conv"]["wsign"] = w
+    m, om = _stem(tmp_path, 16, seed=bands, bands=bands, mutate=zeros)
+    x = synth(bands, 0, 2, bands, 32, 32)
+    _same_stages(m.stages(x[0]), om.stages(x[0]))
+    assert same_bits(m.forward_batch(x), om.forward_batch(x))
+
+
+def test_stem_nonfinite_and_extreme_inputs(tmp_path):
+    """NaN / inf / huge / subnormal bands: the +-1 planes and the logits
+    match (NaN payloads of the float stage are not compared)."""
+    m, om = _stem(tmp_path, 16, seed=21)
+    x = synth(49, 0, 5, 120, 32, 32)
+    x[0, 5, 3, 7] = np.nan
+    x[1, 100, 31, 31] = np.inf
+    x[1, 101, 31, 31] = -np.inf
+    x[2] *= 1e30
+    x[3] *= 1e-38
+    x[4, :, :16] = 0.0
+    for p in range(5):
+        _same_stages(m.stages(x[p]), om.stages(x[p]), skip_float=(p < 2))
+    assert same_bits(m.forward_batch(x), om.forward_batch(x))
+
+
+def test_stem_device_patched_and_profiler(tmp_path):
+    m, om = _stem(tmp_path, 16, base=16, seed=22, rules="baseline")
+    x = synth(50, 0, 6, 120, 32, 48)
+    ref = om.forward_batch(x)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((6, 3, 32, 48), dtype=torch.float32, device="cuda")
+    for _ in range(2):  # the second call replays the captured graph
+        dy.zero_()
+        m.forward_device(0, dx, 6, 32, 48, dy)
+        torch.cuda.synchronize()
+        assert same_bits(dy.cpu().numpy(), ref)
+    cube = synth(51, 0, 1, 120, 70, 50)[0]
+    assert same_bits(m.forward_patched(cube, 32), om.forward_patched(cube, 32))
+    # the stem alone through the first-conv entry point
+    bits = torch.zeros((6, 32, 48, 1), dtype=torch.int32, device="cuda")
+    und = m.first_conv_device(0, dx, 6, 32, 48, bits)
+    torch.cuda.synchronize()
+    want = np.stack([om.stages(x[p])["stem.act"] for p in range(6)])  # [n][C][H][W] int8
+    got = _unpack(bits, 6, 16, 32, 48)
+    assert und == 0 and np.array_equal(got, want)
+    m.profile(True)
+    m.forward_batch(x)
+    recs = m.profile_records()
+    assert len(recs) == 20 and m.launches(6, 32, 48) == 20
+    assert recs[0]["label"] == "stem.conv+act" and sum(r["op"] == "bconv" for r in recs) == 18
+
+
+def test_stem_cli_matches_reference_logits(tmp_path):
+    g = np.load(os.path.join(GOLD, "stem_c16_base_s4_16x48.npz"))
+    x = synth(int(g["seed"]), 0, 1, 120, 16, 48)[0]
+    inp, out = tmp_path / "in.bin", tmp_path / "out.bin"
+    x.astype("<f4").tofile(inp)
+    r = subprocess.run([bn.CLI_STEM_PATH, os.path.join(GOLD, "stem_c16_base_s4.blob"), str(inp), str(out), "16", "48",
+                        "2"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert "# [stem] H=16 W=48 bands=120 classes=3 stem_channels=16 reps=2" in r.stderr
+    got = np.fromfile(out, "<f4").reshape(3, 16, 48)
+    assert same_bits(got, g["p0/logits"])
+
+
+def test_stem_multi_device(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU")
+    m, _ = _stem(tmp_path, 16, seed=23)
+    x = synth(52, 0, 9, 120, 32, 32)
+    one = m.forward_batch(x)
+    m.set_devices([0, 1])
+    assert same_bits(m.forward_batch(x), one)
