@@ -353,7 +353,7 @@ def run_ours(args):
                                 "(probe: 15.6 POPC/clk/SM)",
                  "time_share": frac_split.get("bconv")}),
             "rooflines": {
-                "conv_real": {"bound": "hbm", "kernel": "stem_fold_kernel (v2 stem 1x1 + fold, fp32 FFMA2)",
+                "conv_real": {"bound": "hbm", "kernel": "stem_fold_kernel (v2 stem 1x1 + real fold, exact fp32 order)",
                               "achieved": round(P * 120 * H * W * 4 * args.steps / (r_["ms"] * 1e6), 1),
                               "peak": peaks.get("hbm_gbs"), "unit": "GB/s (input bands read once)",
                               "frac": round(P * 120 * H * W * 4 * args.steps / (r_["ms"] * 1e6)

@@ -307,16 +307,19 @@ static cudaError_t attr_bconv_kc() {
     if ((e = attr_bconv<BN, TM, TN, 2>()) != cudaSuccess) return e;
     return attr_bconv<BN, TM, TN, 1>();
 }
-// stem weights in shared memory: up to 1024 bands x 32 channels
+// stem weights in shared memory: up to 1024 bands x 32 channels; the
+// bulk-copy kernel: weights and its ring, one CTA per SM
 template <int CB>
 static cudaError_t attr_stem() {
     const int smem = 1024 * CB * 4;
+    constexpr int PXB = CB == 32 ? 2 : 4;
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(stem_fold_kernel<CB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
-        (e = cudaFuncSetAttribute(stem_fold_kernel<CB, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+        (e = cudaFuncSetAttribute(stem_fold_kernel<CB, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) ||
+        (e = cudaFuncSetAttribute(stem_bulk_kernel<CB, PXB>, cudaFuncAttributeMaxDynamicSharedMemorySize, SB_SMEM)))
         return e;
-    if (CB == 32) return cudaSuccess;
-    return cudaFuncSetAttribute(stem_fold_kernel<CB, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if constexpr (CB == 32) return cudaSuccess;
+    else return cudaFuncSetAttribute(stem_fold_kernel<CB, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 static int set_kernel_attrs(int device) {
@@ -1031,9 +1034,32 @@ static int run_stem(DevState* d, const Model* m, const float* x, int N, int H, i
     p.x = x; p.w = d->st_w; p.fold = d->st_fold; p.out = out; p.dbg = dbg;
     p.Cin = E->stem_conv.Cin; p.HW = H * W; p.Cout = E->stem_c; p.cwo = cw_of(p.Cout);
     const int CB = d->st_CB;
+    const uintptr_t xa = (uintptr_t)x;
+    // default (measured on B200, 4096 patches of 32x32x120): stems up to 16
+    // channels run the register-streamed kernel (8 ch: 0.33 ms = 92% of HBM;
+    // 16 ch: 0.44 ms), wider ones the bulk-copy kernel (32 ch: 0.93 ms vs
+    // 1.25 ms) where rows are 16-byte aligned and its ring fits;
+    // set_first_conv_kernel(1) swaps the two
+    const bool want_bulk = (CB == 32) == (g_first_kind == 0);
+    {
+        const int PXb = CB == 32 ? 2 : 4;
+        const int nst = sb_stages(p.Cin, CB, PXb);
+        const long long pixels = (long long)N * p.HW;
+        const long long items = (pixels + SB_NC * PXb - 1) / (SB_NC * PXb);
+        if (want_bulk && p.HW % 4 == 0 && p.HW >= 256 && xa % 16 == 0 && nst >= 2 && items < (1ll << 31)) {
+            p.groups = pixels / 4;
+            const size_t smem = (size_t)sb_wbytes(p.Cin, CB) + (size_t)nst * sb_stage_bytes(PXb) + 2 * SB_MAXST * 8;
+            const dim3 grid((unsigned)std::min<long long>(items, sm_count()), (unsigned)d->st_slices);
+            if (CB == 8) stem_bulk_kernel<8, 4><<<grid, SB_NT, smem, st>>>(p, (int)items, nst);
+            else if (CB == 16) stem_bulk_kernel<16, 4><<<grid, SB_NT, smem, st>>>(p, (int)items, nst);
+            else stem_bulk_kernel<32, 2><<<grid, SB_NT, smem, st>>>(p, (int)items, nst);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "stem launch: %s", cudaGetErrorString(e));
+            return BNN_OK;
+        }
+    }
     // PX pixels per thread: they share one patch (PX | H*W) and one aligned
     // vector load; at most 64 accumulators per thread
-    const uintptr_t xa = (uintptr_t)x;
     int PX = (p.HW % 4 == 0 && xa % 16 == 0) ? 4 : (p.HW % 2 == 0 && xa % 8 == 0) ? 2 : 1;
     if (CB == 32 && PX == 4) PX = 2;
     p.groups = (long long)N * p.HW / PX;

@@ -85,7 +85,10 @@ int bnn_set_bconv_kernel(int kind);
 /* Process-wide choice of the first conv's tensor-core kernel (A/B testing):
  * 0 = tcgen05 (default; shapes it cannot stage fall back to 1), 1 = mma.sync.
  * Both decide every output by the same error bound and fix up the rest in
- * the reference's fp32 order, so both give the reference's bits. */
+ * the reference's fp32 order, so both give the reference's bits. For a v2
+ * model's stem: 0 = the measured-faster of its two exact-order kernels for
+ * the stem's width (register-streamed up to 16 channels, input streamed by
+ * bulk copies through a shared-memory ring above), 1 = the other one. */
 int bnn_set_first_conv_kernel(int kind);
 
 /* Number of bounded device-side waits (mbarriers of the TMA / tcgen05
