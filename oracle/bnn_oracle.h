@@ -1,8 +1,9 @@
 /* bnn_oracle.h - TEST INFRASTRUCTURE ONLY.
  *
  * A plain-C, CPU-only restatement of the reference engine's v1 forward path
- * (Sboyle132/BNNs_to_C csrc/bnn_model.c and the kernels it calls) and of its
- * v2 spectral-stem variant (csrc/bnn_model_stem.c), written
+ * (Sboyle132/BNNs_to_C csrc/bnn_model.c and the kernels it calls), of its
+ * v2 spectral-stem variant (csrc/bnn_model_stem.c) and of the v3 ReActNet
+ * engine (csrc/bnn_model_react.c, in bnn_oracle_react.c), written
  * from the reference's documented semantics, used as the checker for the
  * B200 engine. Only tests/, __graft_entry__.smoke() and bench.py's
  * cpu_baseline leg may load it; the product library never links it.
@@ -64,6 +65,24 @@ void oracle_head(const float *a, const float *Wt, const float *bias,
                  float *logits, int Cin, int H, int W, int Cout);
 void oracle_synth(uint32_t seed, uint32_t patch0, int n, int bands, int H,
                   int W, float *out);
+
+/* v3 ReActNet real-highway engine (csrc/bnn_model_react.c), bnn_oracle_react.c.
+ * Stages: "<block>.proj", ".tap1", ".conv1.P" (enc1: ".conv1.out"), ".h1",
+ * ".tap2", ".conv2.P", then ".skip", ".pool.P", ".poolr", ".down" (encoder)
+ * or ".h2"; decoder blocks start with ".cat"; "logits" last. */
+typedef struct ORModel ORModel;
+ORModel *oracle_react_load_mem(const void *data, size_t n, char *err, int errlen);
+void oracle_react_free(ORModel *m);
+int oracle_react_n_bands(const ORModel *m);
+int oracle_react_n_classes(const ORModel *m);
+int oracle_react_forward(const ORModel *m, const float *input, int H, int W,
+                         float *logits, oracle_stage_cb cb, void *ctx);
+int oracle_react_forward_batch(const ORModel *m, const float *input, int n,
+                               int H, int W, float *logits);
+void oracle_react_proj(const float *x, const float *Wm, float *out, int Cin,
+                       int H, int W, int Cout);
+void oracle_react_conv3(const float *x, const int8_t *wsign, const float *alpha,
+                        float *out, int Cin, int H, int W, int Cout);
 
 #ifdef __cplusplus
 }

@@ -17,6 +17,12 @@ What it records:
     the real conv output and the logits, for seeded synthetic inputs; plus
     the logits of the reference CLI (csrc/main.c) on the same input, which
     must equal the chained logits exactly.
+  * v3 ReActNet models (csrc/bnn_model_react.c): blob bytes against the
+    reference's writer (python/bnn2c/blob_react.py:write_blob_react_from_fold,
+    fed the same folded parameters); every stage from the reference's ReAct
+    kernels chained by oracle/ref_stages_react.c; the chain's logits must equal
+    the reference's own bnn_forward_react (strip-processed enc1/dec1) and the
+    reference CLI csrc/main_react.c (file input, streamed).
   * kernel cases: reference bconv_dispatch P on the edge-shape list of
     csrc/bench_bconv.c:103-107 and on the pad=0 self-test case of
     python/verify/bconv_harness.py:113-118; maxpool_P on the shapes of
@@ -42,6 +48,7 @@ ROOT = os.path.abspath(os.path.join(HERE, "..", ".."))
 sys.path.insert(0, ROOT)
 
 from bnns_to_c_b200 import blob as B  # noqa: E402
+from bnns_to_c_b200 import blob_react as BR  # noqa: E402
 
 STAGE_CB = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int,
                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p)
@@ -61,6 +68,89 @@ STEMS = [
     ("stem_c8_mixed_s3", 8, "mixed", 3, 16, [(32, 32, 12, 2), (37, 23, 13, 1)]),
     ("stem_c16_base_s4", 16, "baseline", 4, 16, [(32, 32, 14, 1), (16, 48, 15, 1)]),
 ]
+
+
+# v3 ReActNet models: (name, base, model seed, [(H, W, synth seed, n patches)])
+REACTS = [
+    ("react_c16_s1", 16, 1, [(32, 32, 21, 1)]),
+    ("react_c8_s3", 8, 3, [(50, 38, 23, 1)]),
+    ("react_c12_s4", 12, 4, [(32, 32, 24, 1)]),
+]
+
+
+def ref_react_blob_bytes(model: dict, ref: str) -> bytes:
+    """The reference's own v3 writer on the same folded parameters."""
+    sys.path.insert(0, os.path.join(ref, "python", "bnn2c"))
+    import blob_react as RR  # the reference's python/bnn2c/blob_react.py
+    fold = {}
+    for name in BR.BLOCKS:
+        b = model["blocks"][name]
+        f = {"input_real": b["input_real"], "conv1_wsign": b["conv1"]["wsign"],
+             "conv1_alpha": b["conv1"].get("alpha"), "proj1_W": b["proj"], "epi1": b["epi1"],
+             "tap1_rsign": b["tap1"], "tap2_rsign": b["tap2"], "conv2_wsign": b["conv2"]["wsign"]}
+        if b["kind"] == "down":
+            f["epi_skip"], f["epi_down"] = b["epi_a"], b["epi_b"]
+        else:
+            f["epi2"] = b["epi_a"]
+        fold[name] = f
+    fold["outc_W"], fold["outc_b"] = model["head"]["W"], model["head"]["bias"]
+    with tempfile.TemporaryDirectory() as d:
+        p = os.path.join(d, "r.blob")
+        RR.write_blob_react_from_fold(fold, p, model["base_channels"], model["n_bands"], model["n_classes"])
+        return open(p, "rb").read()
+
+
+def ref_react_lib():
+    lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_react.so"))
+    lib.ref_react_stages.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_void_p, STAGE_CB, ctypes.c_void_p]
+    lib.ref_react_forward.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_void_p]
+    return lib
+
+
+def react_fixtures(ref, manifest):
+    lib = ref_react_lib()
+    for name, base, seed, runs in REACTS:
+        model = BR.random_react_model(base, 120, 3, seed=seed)
+        data = BR.react_blob_bytes(model)
+        if data != ref_react_blob_bytes(model, ref):
+            raise SystemExit(f"{name}: v3 blob bytes differ from the reference writer's")
+        sha = hashlib.sha256(data).hexdigest()
+        bpath = os.path.join(HERE, name + ".blob")
+        open(bpath, "wb").write(data)
+        for H, W, sseed, n in runs:
+            x = synth(sseed, 0, n, 120, H, W)
+            out = {"H": np.int32(H), "W": np.int32(W), "seed": np.int32(sseed), "n": np.int32(n),
+                   "blob_sha256": np.array(sha)}
+            for p in range(n):
+                xp = np.ascontiguousarray(x[p])
+                stages = {}
+
+                def cb(ctx, nm, kind, C, h, w, d):
+                    k = C * h * w
+                    arr = np.ctypeslib.as_array(ctypes.cast(d, ctypes.POINTER(
+                        {0: ctypes.c_int8, 1: ctypes.c_int32, 2: ctypes.c_float}[kind])), shape=(max(k, 1),))
+                    stages[nm.decode()] = arr[:k].copy().reshape(C, h, w)
+                lg = np.zeros((3, H, W), np.float32)
+                lib.ref_react_stages(bpath.encode(), xp.ctypes.data, H, W, lg.ctypes.data, STAGE_CB(cb), None)
+                fw = np.zeros((3, H, W), np.float32)
+                lib.ref_react_forward(bpath.encode(), xp.ctypes.data, H, W, fw.ctypes.data)
+                if not np.array_equal(fw.view(np.int32), stages["logits"].view(np.int32)):
+                    raise SystemExit(f"{name}: bnn_forward_react logits != chained stage logits")
+                with tempfile.TemporaryDirectory() as d:
+                    inp, o = os.path.join(d, "in.bin"), os.path.join(d, "out.bin")
+                    xp.astype("<f4").tofile(inp)
+                    subprocess.run([os.path.join(ROOT, "oracle", "_ref", "bnn_infer_react"), bpath, inp, o,
+                                    str(H), str(W)], check=True, capture_output=True,
+                                   env=dict(os.environ, OMP_NUM_THREADS="1"))
+                    cli = np.fromfile(o, "<f4").reshape(3, H, W)
+                if not np.array_equal(cli.view(np.int32), stages["logits"].view(np.int32)):
+                    raise SystemExit(f"{name}: bnn_infer_react logits != chained stage logits")
+                for k, v in stages.items():
+                    out[f"p{p}/{k}"] = v
+            np.savez_compressed(os.path.join(HERE, f"{name}_{H}x{W}.npz"), **out)
+            manifest.append(f"{name} {H}x{W} seed={sseed} n={n} blob_sha256={sha}")
 
 
 def ref_blob_bytes(model: dict, ref: str) -> bytes:
@@ -266,6 +356,7 @@ def main():
             np.savez_compressed(os.path.join(HERE, f"{name}_{H}x{W}.npz"), **out)
             manifest.append(f"{name} {H}x{W} seed={sseed} n={n} blob_sha256={sha}")
         os.unlink(tmpb)
+    react_fixtures(args.ref, manifest)
     np.savez_compressed(os.path.join(HERE, "kernels.npz"), **kernel_cases(lib))
     with open(os.path.join(HERE, "MANIFEST.txt"), "w") as f:
         f.write("# generated by tests/golden/make_golden.py from the reference build\n")

@@ -41,6 +41,18 @@ def olib():
         L.oracle_up_cat.argtypes = [vp, ip, ip, ip, vp, ip, ip, ip, vp]
         L.oracle_head.argtypes = [vp, vp, vp, vp, ip, ip, ip, ip]
         L.oracle_synth.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ip, ip, ip, ip, vp]
+        L.oracle_react_load_mem.restype = vp
+        L.oracle_react_load_mem.argtypes = [vp, ctypes.c_size_t, ctypes.c_char_p, ip]
+        L.oracle_react_free.argtypes = [vp]
+        for f in ("oracle_react_n_bands", "oracle_react_n_classes"):
+            getattr(L, f).argtypes = [vp]
+            getattr(L, f).restype = ip
+        L.oracle_react_forward.argtypes = [vp, vp, ip, ip, vp, _CB, vp]
+        L.oracle_react_forward.restype = ip
+        L.oracle_react_forward_batch.argtypes = [vp, vp, ip, ip, ip, vp]
+        L.oracle_react_forward_batch.restype = ip
+        L.oracle_react_proj.argtypes = [vp, vp, vp, ip, ip, ip, ip]
+        L.oracle_react_conv3.argtypes = [vp, vp, vp, vp, ip, ip, ip, ip]
         _lib = L
     return _lib
 
@@ -92,6 +104,51 @@ class OModel:
         rc = olib().oracle_forward_batch(self.h, x.ctypes.data, n, H, W, out.ctypes.data)
         if rc:
             raise ValueError("oracle_forward refused the input")
+        return out
+
+
+def _stage_collector(out):
+    ct = {0: ctypes.c_int8, 1: ctypes.c_int32, 2: ctypes.c_float}
+
+    def cb(ctx, name, kind, C, h, w, data):
+        n = C * h * w
+        arr = np.ctypeslib.as_array(ctypes.cast(data, ctypes.POINTER(ct[kind])), shape=(max(n, 1),))
+        out[name.decode()] = arr[:n].copy().reshape(C, h, w)
+    return _CB(cb)
+
+
+class ORModel:
+    """The v3 ReAct oracle (oracle/bnn_oracle_react.c) on a blob given as bytes."""
+
+    def __init__(self, data: bytes):
+        err = ctypes.create_string_buffer(256)
+        self._buf = ctypes.create_string_buffer(data, len(data))
+        self.h = olib().oracle_react_load_mem(self._buf, len(data), err, 256)
+        if not self.h:
+            raise ValueError(err.value.decode())
+        self.n_bands = olib().oracle_react_n_bands(self.h)
+        self.n_classes = olib().oracle_react_n_classes(self.h)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            olib().oracle_react_free(self.h)
+
+    def stages(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        _, H, W = x.shape
+        logits = np.zeros((self.n_classes, H, W), np.float32)
+        out = {}
+        fn = _stage_collector(out)
+        if olib().oracle_react_forward(self.h, x.ctypes.data, H, W, logits.ctypes.data, fn, None):
+            raise ValueError("oracle_react_forward refused the input")
+        return out
+
+    def forward_batch(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        n, _, H, W = x.shape
+        out = np.zeros((n, self.n_classes, H, W), np.float32)
+        if olib().oracle_react_forward_batch(self.h, x.ctypes.data, n, H, W, out.ctypes.data):
+            raise ValueError("oracle_react_forward refused the input")
         return out
 
 

@@ -10,7 +10,8 @@ import numpy as np
 import pytest
 
 from bnns_to_c_b200 import blob as B
-from oracle_util import OModel, bconv_P, maxpool, synth
+from bnns_to_c_b200 import blob_react as BR
+from oracle_util import OModel, ORModel, bconv_P, maxpool, synth
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -115,3 +116,49 @@ def test_oracle_patched_is_tiles_of_the_forward(H, W, P, tmp_path):
             ph, pw = min(P, H - r * P), min(P, W - c * P)
             want[:, r * P:r * P + ph, c * P:c * P + pw] = lt[r * tx + c, :, :ph, :pw]
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ------------------------------------------------------------------ v3 ReActNet
+def react_fixtures():
+    return [(os.path.basename(f).rsplit("_", 1)[0], f)
+            for f in sorted(glob.glob(os.path.join(GOLD, "react_*_*x*.npz")))]
+
+
+@pytest.mark.parametrize("name,npz", react_fixtures(), ids=[os.path.basename(f) for _, f in react_fixtures()])
+def test_react_oracle_matches_reference_stages(name, npz):
+    """The v3 oracle against the reference's ReAct kernels chained in
+    forward order (whose logits equal the reference's own strip-processed
+    bnn_forward_react and its CLI): every stage, floats included, bit for
+    bit. The blob itself is byte-identical to the reference writer's."""
+    g = np.load(npz)
+    data = open(os.path.join(GOLD, name + ".blob"), "rb").read()
+    assert hashlib.sha256(data).hexdigest() == str(g["blob_sha256"])
+    H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
+    x = synth(seed, 0, n, 120, H, W)
+    m = ORModel(data)
+    for p in range(n):
+        st = m.stages(x[p])
+        keys = [k[len(f"p{p}/"):] for k in g.files if k.startswith(f"p{p}/")]
+        assert set(keys) == set(st), set(keys) ^ set(st)
+        for k in keys:
+            assert st[k].shape == g[f"p{p}/{k}"].shape, k
+            assert np.array_equal(st[k].view(np.uint8), g[f"p{p}/{k}"].view(np.uint8)), k
+
+
+def test_react_blob_roundtrip_and_committed_bytes():
+    for name, base, seed in (("react_c16_s1", 16, 1), ("react_c8_s3", 8, 3), ("react_c12_s4", 12, 4)):
+        data = BR.react_blob_bytes(BR.random_react_model(base, 120, 3, seed=seed))
+        assert data == open(os.path.join(GOLD, name + ".blob"), "rb").read()
+        assert BR.react_blob_bytes(BR.read_react_blob(data)) == data
+
+
+def test_react_oracle_loader_messages():
+    data = open(os.path.join(GOLD, "react_c8_s3.blob"), "rb").read()
+    for bad, msg in ((data[:-1], "short read"), (data + b"x", "trailing bytes in blob"),
+                     (b"XNNC" + data[4:], "bad magic"),
+                     (data[:4] + (1).to_bytes(4, "little") + data[8:],
+                      "blob version 1, this engine reads v3 (ReActNet)"),
+                     (data[:20] + (1).to_bytes(4, "little") + data[24:], "only nearest upsampler supported")):
+        with pytest.raises(ValueError) as e:
+            ORModel(bad)
+        assert str(e.value) == msg
