@@ -99,6 +99,22 @@ def lib():
         "bnn_stem_free": (None, [vp]),
         "bnn_stem_forward": (None, [vp, vp, ip, ip, vp]),
         "bnn_stem_as_model": (vp, [vp]),
+        "bnn_react_load_ex": (ip, [cp, ctypes.POINTER(vp)]),
+        "bnn_react_load_mem": (ip, [vp, ctypes.c_size_t, ctypes.POINTER(vp)]),
+        "bnn_load_react": (vp, [cp]),
+        "bnn_free_react": (None, [vp]),
+        "bnn_forward_react": (None, [vp, vp, ip, ip, vp]),
+        "bnn_forward_react_batch": (ip, [vp, vp, ip, ip, ip, vp]),
+        "bnn_forward_react_device": (ip, [vp, ip, vp, ip, ip, ip, vp, vp]),
+        "bnn_forward_react_patched_ex": (ip, [vp, vp, ip, ip, vp, ip]),
+        "bnn_forward_react_stages": (ip, [vp, vp, ip, ip, vp, STAGE_CB, vp]),
+        "bnn_react_profile_enable": (ip, [vp, ip]),
+        "bnn_react_profile_reset": (None, [vp]),
+        "bnn_react_profile_count": (ip, [vp]),
+        "bnn_react_profile_get": (ip, [vp, ip, ctypes.POINTER(cp), ctypes.POINTER(cp),
+                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                       ctypes.POINTER(ip)]),
+        "bnn_react_forward_launches": (ip, [vp, ip, ip, ip]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -287,6 +303,95 @@ class StemModel(Model):
             lib().bnn_stem_free(self.stem_handle)
         self.stem_handle = None
         self.handle = None
+
+
+class ReactModel:
+    """A loaded v3 ReActNet blob (reference ``ModelR *bnn_load_react(path)``,
+    csrc/bnn_model_react.c)."""
+
+    def __init__(self, path: str | None = None, data: bytes | None = None):
+        L = lib()
+        h = ctypes.c_void_p()
+        if data is not None:
+            buf = ctypes.create_string_buffer(data, len(data))
+            _check(L.bnn_react_load_mem(buf, len(data), ctypes.byref(h)))
+        else:
+            _check(L.bnn_react_load_ex(os.fsencode(path), ctypes.byref(h)))
+        self.handle = h.value
+        hdr = _ModelHeader.from_address(self.handle)
+        self.version, self.base_channels = hdr.version, hdr.base_channels
+        self.n_bands, self.n_classes, self.upsampler = hdr.n_bands, hdr.n_classes, hdr.upsampler
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().bnn_free_react(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        return self.forward_batch(np.asarray(x, np.float32)[None])[0]
+
+    def forward_batch(self, x: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        n, _, H, W = x.shape
+        if out is None:
+            out = np.empty((n, self.n_classes, H, W), np.float32)
+        _check(lib().bnn_forward_react_batch(self.handle, x.ctypes.data, n, H, W, out.ctypes.data))
+        return out
+
+    def forward_device(self, device: int, d_in, n: int, H: int, W: int, d_out, stream=None):
+        s = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+        _check(lib().bnn_forward_react_device(self.handle, device, _ptr(d_in), n, H, W, _ptr(d_out), s))
+
+    def forward_patched(self, cube, P=32, out=None):
+        cube = np.ascontiguousarray(cube, np.float32)
+        _, H, W = cube.shape
+        if out is None:
+            out = np.empty((self.n_classes, H, W), np.float32)
+        _check(lib().bnn_forward_react_patched_ex(self.handle, cube.ctypes.data, H, W, out.ctypes.data, P))
+        return out
+
+    def stages(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32)
+        _, H, W = x.shape
+        logits = np.zeros((self.n_classes, H, W), np.float32)
+        out = {}
+        ct = {0: ctypes.c_int8, 1: ctypes.c_int32, 2: ctypes.c_float}
+
+        def cb(ctx, name, kind, C, h, w, data):
+            k = C * h * w
+            arr = np.ctypeslib.as_array(ctypes.cast(data, ctypes.POINTER(ct[kind])), shape=(max(k, 1),))
+            out[name.decode()] = arr[:k].copy().reshape(C, h, w)
+
+        fn = STAGE_CB(cb)
+        _check(lib().bnn_forward_react_stages(self.handle, x.ctypes.data, H, W, logits.ctypes.data, fn, None))
+        return out
+
+    def launches(self, n, H, W):
+        return lib().bnn_react_forward_launches(self.handle, n, H, W)
+
+    def profile(self, on=True):
+        _check(lib().bnn_react_profile_enable(self.handle, 1 if on else 0))
+
+    def profile_reset(self):
+        lib().bnn_react_profile_reset(self.handle)
+
+    def profile_records(self):
+        L = lib()
+        recs = []
+        for i in range(L.bnn_react_profile_count(self.handle)):
+            lab, op = ctypes.c_char_p(), ctypes.c_char_p()
+            work, ms, calls = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+            _check(L.bnn_react_profile_get(self.handle, i, ctypes.byref(lab), ctypes.byref(op),
+                                           ctypes.byref(work), ctypes.byref(ms), ctypes.byref(calls)))
+            recs.append({"label": lab.value.decode(), "op": op.value.decode(), "work": work.value,
+                         "ms": ms.value, "calls": calls.value})
+        return recs
 
 
 def load_stem(path: str) -> StemModel:

@@ -1,0 +1,763 @@
+// react.cu - the v3 ReActNet real-highway engine (csrc/bnn_model_react.c)
+// behind the drop-in include/bnn_model_react.h.
+//
+// Per patch the forward is the reference's (:395-441) on the whole image
+// (its enc1 / dec1 row strips give the same values): for each block, unit1
+// = projection of the input (+ the input's tap bits), binary conv1 on the
+// tap, epilogue (+ the result's tap bits for conv2); unit2 = binary conv2,
+// then the skip and pooled-down epilogues (encoder) or the block output
+// (bottleneck, decoder); decoders read their concat (skip + nearest
+// upsample) in place. Binary convs run on the v1 engine's tcgen05 kernels
+// through bnn_bconv_layer_* with their exact P written out; the float work
+// is react_kernels.cuh. Activations stay in one device arena per (N, H, W);
+// repeated device forwards replay a captured CUDA graph.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "common.h"
+#include "react_kernels.cuh"
+#include "../../include/bnn_model_react.h"
+
+namespace bnn {
+
+namespace {
+
+#define RCK(call)                                                                                  \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) return set_error(BNN_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
+inline int cw_of(int c) { return (c + 31) >> 5; }
+inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+const char* BN[9] = {"enc1", "enc2", "enc3", "enc4", "bottleneck", "dec4", "dec3", "dec2", "dec1"};
+
+// device copies of one block's float parameters
+struct RBlockDev {
+    float *proj = nullptr;   // [slices][Cin][16]
+    float *tap1 = nullptr, *tap2 = nullptr;
+    float *A1 = nullptr, *Bm1 = nullptr, *pw1 = nullptr;
+    float *Aa = nullptr, *Bma = nullptr, *pwa = nullptr;
+    float *Ab = nullptr, *Bmb = nullptr, *pwb = nullptr;
+    bnn_bconv_layer *conv1 = nullptr, *conv2 = nullptr;
+    int Cin = 0, Cout = 0;
+};
+
+// activations of one block at (N, h, w)
+struct RBuf {
+    float *res = nullptr, *h1 = nullptr, *out = nullptr, *down = nullptr, *c1 = nullptr;
+    uint32_t *t1 = nullptr, *t2 = nullptr;
+    int32_t *P1 = nullptr, *P2 = nullptr;
+    int h = 0, w = 0;
+};
+
+struct GraphKeyR {
+    int N, H, W;
+    const void *in, *out;
+    bool operator<(const GraphKeyR& o) const { return std::tie(N, H, W, in, out) < std::tie(o.N, o.H, o.W, o.in, o.out); }
+};
+
+struct RDev {
+    int device = -1;
+    std::mutex mu;
+    void* wbase = nullptr;
+    RBlockDev blk[9];
+    float *c3w = nullptr, *c3a = nullptr;  // enc1 conv: [Cout/16][Cin][9][16], alpha
+    float *headW = nullptr, *headb = nullptr;
+    // arena
+    void* abase = nullptr;
+    int aN = 0, aH = 0, aW = 0;
+    RBuf buf[9];
+    uint32_t* scratch = nullptr;           // the binary convs' (unused) bit outputs
+    cudaStream_t cs = nullptr;
+    cudaEvent_t ev_last = nullptr;
+    std::map<GraphKeyR, cudaGraphExec_t> graphs;
+};
+
+struct RProfiler {
+    struct Rec {
+        std::string label, optype;
+        double work = 0, ms = 0;
+        int calls = 0;
+    };
+    bool on = false;
+    std::vector<Rec> recs;
+    std::mutex mu;
+};
+
+struct REngine {
+    std::mutex mu;
+    std::map<int, std::unique_ptr<RDev>> devs;
+    RProfiler prof;
+};
+
+const BlockR& block_of(const ModelR* m, int b) { return b < 4 ? m->enc[b] : b == 4 ? m->bott : m->dec[b - 5]; }
+
+void rdev_release(RDev* d) {
+    if (!d || d->device < 0) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->device);
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+    if (d->cs) cudaStreamSynchronize(d->cs);
+    for (auto& b : d->blk) {
+        bnn_bconv_layer_destroy(b.conv1);
+        bnn_bconv_layer_destroy(b.conv2);
+        b.conv1 = b.conv2 = nullptr;
+    }
+    cudaFree(d->wbase);
+    cudaFree(d->abase);
+    if (d->ev_last) cudaEventDestroy(d->ev_last);
+    if (d->cs) cudaStreamDestroy(d->cs);
+    cudaSetDevice(prev);
+}
+
+// upload the model to device d (d->mu held, device current)
+int rdev_init(const ModelR* m, RDev* d) {
+    std::vector<std::pair<std::vector<float>, float**>> up;  // host array -> device slot
+    auto add = [&](std::vector<float> v, float** slot) { up.emplace_back(std::move(v), slot); };
+    auto vec = [](const float* p, int n) { return std::vector<float>(p, p + n); };
+    auto epi = [&](const EpiR& e, float** A, float** Bm, float** pw) {
+        std::vector<float> bm(e.C);
+        for (int c = 0; c < e.C; ++c) bm[c] = e.B[c] + e.move1[c];  // fp32, once per channel (as the reference)
+        add(vec(e.A, e.C), A);
+        add(bm, Bm);
+        add(vec(e.prelu_w, e.C), pw);
+    };
+    for (int b = 0; b < 9; ++b) {
+        const BlockR& B = block_of(m, b);
+        RBlockDev& D = d->blk[b];
+        D.Cin = B.conv1.Cin;
+        D.Cout = B.conv1.Cout;
+        const int sl = cdiv(D.Cout, react::PROJ_CB);
+        std::vector<float> pj((size_t)sl * D.Cin * react::PROJ_CB, 0.0f);
+        for (int co = 0; co < D.Cout; ++co)
+            for (int ci = 0; ci < D.Cin; ++ci)
+                pj[((size_t)(co / react::PROJ_CB) * D.Cin + ci) * react::PROJ_CB + co % react::PROJ_CB] =
+                    B.proj1.W[(size_t)co * D.Cin + ci];
+        add(pj, &D.proj);
+        if (!B.input_real) add(vec(B.tap1.rsign, B.tap1.C), &D.tap1);
+        add(vec(B.tap2.rsign, B.tap2.C), &D.tap2);
+        epi(B.epi1, &D.A1, &D.Bm1, &D.pw1);
+        epi(B.epi_a, &D.Aa, &D.Bma, &D.pwa);
+        if (B.is_down) epi(B.epi_b, &D.Ab, &D.Bmb, &D.pwb);
+    }
+    {
+        const ConvR& c1 = m->enc[0].conv1;
+        const int nb = cdiv(c1.Cout, 16);
+        std::vector<float> w((size_t)nb * c1.Cin * 9 * 16, 0.0f);
+        for (int co = 0; co < c1.Cout; ++co)
+            for (int ci = 0; ci < c1.Cin; ++ci)
+                for (int t = 0; t < 9; ++t)
+                    w[(((size_t)(co / 16) * c1.Cin + ci) * 9 + t) * 16 + co % 16] =
+                        (float)c1.wsign[((size_t)co * c1.Cin + ci) * 9 + t];
+        add(w, &d->c3w);
+        add(vec(c1.alpha, c1.Cout), &d->c3a);
+    }
+    add(vec(m->head_W, m->head_Cout * m->head_Cin), &d->headW);
+    add(vec(m->head_bias, m->head_Cout), &d->headb);
+    size_t total = 0;
+    for (auto& u : up) total += al256(u.first.size() * 4 + 4);
+    if (cudaMalloc(&d->wbase, total) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_OOM, "cudaMalloc ReAct weights (%zu bytes)", total);
+    }
+    char* p = (char*)d->wbase;
+    for (auto& u : up) {
+        RCK(cudaMemcpy(p, u.first.data(), u.first.size() * 4, cudaMemcpyHostToDevice));
+        *u.second = (float*)p;
+        p += al256(u.first.size() * 4 + 4);
+    }
+    // binary convs: the v1 engine's layers, constant folds (their bit output
+    // is not used; P is)
+    for (int b = 0; b < 9; ++b) {
+        const BlockR& B = block_of(m, b);
+        const ConvR* cs[2] = {&B.conv1, &B.conv2};
+        bnn_bconv_layer** slots[2] = {&d->blk[b].conv1, &d->blk[b].conv2};
+        for (int k = 0; k < 2; ++k) {
+            if (k == 0 && B.input_real) continue;
+            const int C = cs[k]->Cout;
+            std::vector<int32_t> zero(C, 0);
+            int rc = bnn_bconv_layer_create(d->device, cs[k]->Cin, C, cs[k]->packed, zero.data(), zero.data(),
+                                            zero.data(), zero.data(), nullptr, nullptr, nullptr, nullptr, slots[k]);
+            if (rc) return rc;
+        }
+    }
+    RCK(cudaFuncSetAttribute(react::proj_tap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             react::PROJ_MAX_CIN * react::PROJ_CB * 4));
+    RCK(cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking));
+    RCK(cudaEventCreateWithFlags(&d->ev_last, cudaEventDisableTiming));
+    RCK(cudaEventRecord(d->ev_last, d->cs));
+    return BNN_OK;
+}
+
+int get_rdev(const ModelR* m, int device, RDev** out) {
+    REngine* E = (REngine*)m->engine;
+    if (!E) return set_error(BNN_ERR_ARG, "model has no engine");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "no CUDA device available");
+    }
+    if (device < 0 || device >= ndev) return set_error(BNN_ERR_ARG, "device %d out of range [0,%d)", device, ndev);
+    RDev* d;
+    {
+        std::lock_guard<std::mutex> g(E->mu);
+        auto& slot = E->devs[device];
+        if (!slot) slot.reset(new RDev());
+        d = slot.get();
+    }
+    std::lock_guard<std::mutex> g(d->mu);
+    if (d->device < 0) {
+        RCK(cudaSetDevice(device));
+        d->device = device;
+        int rc = rdev_init(m, d);
+        if (rc) {
+            rdev_release(d);
+            d->device = -1;
+            d->wbase = d->abase = nullptr;
+            for (auto& b : d->blk) b = RBlockDev();
+            d->cs = nullptr;
+            d->ev_last = nullptr;
+            d->aN = d->aH = d->aW = 0;
+            return rc;
+        }
+    }
+    *out = d;
+    return BNN_OK;
+}
+
+// arena for N patches of H x W (d->mu held)
+int arena(const ModelR* m, RDev* d, int N, int H, int W) {
+    if (d->abase && d->aN >= N && d->aH == H && d->aW == W) return BNN_OK;
+    const int Nn = std::max(N, d->aH == H && d->aW == W ? d->aN : 0);
+    size_t off = 0;
+    std::vector<std::pair<void**, size_t>> plan;
+    auto take = [&](void** slot, size_t bytes) {
+        plan.push_back({slot, off});
+        off += al256(bytes + 16);
+    };
+    size_t scratch = 0;
+    for (int b = 0; b < 9; ++b) {
+        const int l = b < 4 ? b : b == 4 ? 4 : 8 - b;  // resolution level
+        const int h = H >> l, w = W >> l;
+        const size_t px = (size_t)Nn * h * w;
+        const RBlockDev& D = d->blk[b];
+        RBuf& B = d->buf[b];
+        B.h = h;
+        B.w = w;
+        take((void**)&B.res, px * D.Cout * 4);
+        take((void**)&B.h1, px * D.Cout * 4);
+        take((void**)&B.out, px * D.Cout * 4);
+        take((void**)&B.t2, px * cw_of(D.Cout) * 4);
+        take((void**)&B.P2, px * D.Cout * 4);
+        if (b == 0) take((void**)&B.c1, px * D.Cout * 4);
+        else {
+            take((void**)&B.t1, px * cw_of(D.Cin) * 4);
+            take((void**)&B.P1, px * D.Cout * 4);
+        }
+        if (b < 4) take((void**)&B.down, (size_t)Nn * (h / 2) * (w / 2) * D.Cout * 4);
+        scratch = std::max(scratch, px * cw_of(D.Cout) * 4);
+    }
+    take((void**)&d->scratch, scratch);
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+    if (d->abase) {
+        RCK(cudaEventSynchronize(d->ev_last));
+        cudaFree(d->abase);
+        d->abase = nullptr;
+    }
+    if (cudaMalloc(&d->abase, off) != cudaSuccess) {
+        cudaGetLastError();
+        d->aN = 0;
+        return set_error(BNN_ERR_OOM, "cudaMalloc ReAct arena (%zu bytes)", off);
+    }
+    for (auto& pr : plan) *pr.first = (char*)d->abase + pr.second;
+    d->aN = Nn;
+    d->aH = H;
+    d->aW = W;
+    return BNN_OK;
+}
+
+struct RProf {
+    RProfiler* prof = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<std::tuple<std::string, const char*, double, cudaEvent_t, cudaEvent_t>> marks;
+    void begin(const std::string& l, const char* op, double work) {
+        if (!prof) return;
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, st);
+        marks.emplace_back(l, op, work, a, b);
+    }
+    void end() {
+        if (prof) cudaEventRecord(std::get<4>(marks.back()), st);
+    }
+    int finish() {
+        if (!prof) return BNN_OK;
+        RCK(cudaStreamSynchronize(st));
+        std::lock_guard<std::mutex> g(prof->mu);
+        for (auto& mk : marks) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, std::get<3>(mk), std::get<4>(mk));
+            bool found = false;
+            for (auto& r : prof->recs)
+                if (r.label == std::get<0>(mk)) { r.work += std::get<2>(mk); r.ms += ms; r.calls++; found = true; break; }
+            if (!found) prof->recs.push_back({std::get<0>(mk), std::get<1>(mk), std::get<2>(mk), ms, 1});
+            cudaEventDestroy(std::get<3>(mk));
+            cudaEventDestroy(std::get<4>(mk));
+        }
+        marks.clear();
+        return BNN_OK;
+    }
+};
+
+int launched(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+    return BNN_OK;
+}
+
+int run_proj(const RBlockDev& D, const float* x0, int c0, const float* x1, int c1, int h1, int w1, int N, int H,
+             int W, bool blocked, float* out, uint32_t* bits, cudaStream_t st) {
+    react::ProjParams p{};
+    p.x0 = x0; p.x1 = x1; p.c0 = c0; p.c1 = c1; p.h1 = h1; p.w1 = w1;
+    const int upH = 2 * h1, upW = 2 * w1;
+    p.oh = H > upH ? (H - upH) / 2 : 0;
+    p.ow = W > upW ? (W - upW) / 2 : 0;
+    p.cH = std::min(upH, H);
+    p.cW = std::min(upW, W);
+    p.N = N; p.H = H; p.W = W; p.Cin = D.Cin; p.Cout = D.Cout;
+    p.w = D.proj;
+    const int HW = H * W;
+    p.nfull = blocked ? HW - HW % 8 : HW;  // proj_blk's pixel blocks of 8 vs react_proj_1x1
+    p.out = out;
+    p.rsign = bits ? D.tap1 : nullptr;
+    p.bits = bits;
+    const dim3 grid(cdiv((long long)N * HW, 256), cdiv(D.Cout, react::PROJ_CB));
+    react::proj_tap_kernel<<<grid, 256, (size_t)D.Cin * react::PROJ_CB * 4, st>>>(p);
+    return launched("proj");
+}
+
+int run_epi(const int32_t* P, const float* v, const float* res, float* out, const float* A, const float* Bm,
+            const float* pw, const float* rsign, uint32_t* bits, int N, int C, int HW, cudaStream_t st) {
+    react::EpiParams p{P, v, res, out, A, Bm, pw, rsign, bits, N, C, HW};
+    react::epi_kernel<<<cdiv((long long)N * HW, 256), 256, 0, st>>>(p);
+    return launched("epilogue");
+}
+
+int run_bconv(const bnn_bconv_layer* L, const uint32_t* in, int N, int h, int w, int32_t* P, uint32_t* scratch,
+              cudaStream_t st) {
+    return bnn_bconv_layer_run(L, in, N, h, w, scratch, nullptr, P, nullptr, st);
+}
+
+// one forward of N patches (x, logits on the device)
+int forward_launches(const ModelR* m, RDev* d, const float* x, int N, int H, int W, float* logits, cudaStream_t st,
+                     RProf* pc) {
+    int rc;
+    auto beg = [&](int b, const char* what, const char* op, double work) {
+        if (pc && pc->prof) pc->begin(std::string(BN[b]) + "." + what, op, work);
+    };
+    auto end = [&]() { if (pc && pc->prof) pc->end(); };
+    const float* xin = x;  // input of the current block
+    int xc = m->n_bands, xh = H, xw = W;
+    for (int b = 0; b < 9; ++b) {
+        const BlockR& B = block_of(m, b);
+        RBlockDev& D = d->blk[b];
+        RBuf& Q = d->buf[b];
+        const int h = Q.h, w = Q.w, HW = h * w;
+        const double px = (double)N * HW;
+        const bool blocked = D.Cout % 8 == 0;
+        // ---- unit1
+        if (b == 0) {
+            beg(b, "proj", "proj", px * D.Cout * D.Cin);
+            rc = run_proj(D, xin, D.Cin, nullptr, 0, 0, 0, N, h, w, blocked, Q.res, nullptr, st);
+            end();
+            if (rc) return rc;
+            react::Conv3Params c{xin, d->c3w, d->c3a, Q.c1, N, D.Cin, h, w, D.Cout, cdiv(w, react::C3_TC),
+                                 cdiv(h, react::C3_TR)};
+            beg(b, "conv1", "conv_real", px * D.Cout * D.Cin * 9.0);
+            if (blocked)
+                react::conv3_blk_kernel<<<dim3(N * c.tiles_x * c.tiles_y, cdiv(D.Cout, 16)), 256, 0, st>>>(c);
+            else
+                react::conv3_naive_kernel<<<cdiv((long long)N * HW * cdiv(D.Cout, 4), 128), 128, 0, st>>>(c);
+            rc = launched("conv3");
+            end();
+            if (rc) return rc;
+            beg(b, "epi1", "epi", px * D.Cout);
+            rc = run_epi(nullptr, Q.c1, Q.res, Q.h1, D.A1, D.Bm1, D.pw1, D.tap2, Q.t2, N, D.Cout, HW, st);
+            end();
+            if (rc) return rc;
+        } else {
+            const bool dec = b >= 5;
+            const RBuf* skip = dec ? &d->buf[8 - b] : nullptr;  // dec4 <- enc4 (b=5 -> 3) ...
+            beg(b, dec ? "upcat+proj" : "proj", "proj", px * D.Cout * D.Cin);
+            if (dec)
+                rc = run_proj(D, skip->out, d->blk[8 - b].Cout, xin, xc, xh, xw, N, h, w, blocked, Q.res, Q.t1, st);
+            else
+                rc = run_proj(D, xin, D.Cin, nullptr, 0, 0, 0, N, h, w, blocked, Q.res, Q.t1, st);
+            end();
+            if (rc) return rc;
+            beg(b, "conv1", "bconv", px * D.Cout * D.Cin * 9.0);
+            rc = run_bconv(D.conv1, Q.t1, N, h, w, Q.P1, d->scratch, st);
+            end();
+            if (rc) return rc;
+            beg(b, "epi1", "epi", px * D.Cout);
+            rc = run_epi(Q.P1, nullptr, Q.res, Q.h1, D.A1, D.Bm1, D.pw1, D.tap2, Q.t2, N, D.Cout, HW, st);
+            end();
+            if (rc) return rc;
+        }
+        // ---- unit2
+        beg(b, "conv2", "bconv", px * D.Cout * D.Cout * 9.0);
+        rc = run_bconv(D.conv2, Q.t2, N, h, w, Q.P2, d->scratch, st);
+        end();
+        if (rc) return rc;
+        beg(b, b < 4 ? "skip" : "epi2", "epi", px * D.Cout);
+        rc = run_epi(Q.P2, nullptr, Q.h1, Q.out, D.Aa, D.Bma, D.pwa, nullptr, nullptr, N, D.Cout, HW, st);
+        end();
+        if (rc) return rc;
+        if (B.is_down) {
+            react::PoolEpiParams pp{Q.P2, Q.h1, Q.down, D.Ab, D.Bmb, D.pwb, N, D.Cout, h, w};
+            beg(b, "pool+down", "epi", (double)N * (h / 2) * (w / 2) * D.Cout);
+            react::pool_epi_kernel<<<cdiv((long long)N * (h / 2) * (w / 2), 256), 256, 0, st>>>(pp);
+            rc = launched("pool epilogue");
+            end();
+            if (rc) return rc;
+            xin = Q.down; xc = D.Cout; xh = h / 2; xw = w / 2;
+        } else {
+            xin = Q.out; xc = D.Cout; xh = h; xw = w;
+        }
+    }
+    react::HeadParams hp{xin, d->headW, d->headb, logits, N, m->head_Cin, m->head_Cout, H * W};
+    if (pc && pc->prof) pc->begin("head", "head", (double)N * H * W * m->head_Cout * m->head_Cin);
+    react::head_kernel<<<cdiv((long long)N * H * W, 256), 256, 0, st>>>(hp);
+    rc = launched("head");
+    end();
+    return rc;
+}
+
+int check_hw(const ModelR* m, int N, int H, int W) {
+    if (N < 0) return set_error(BNN_ERR_ARG, "N = %d", N);
+    // below 16 a pooled level is empty and the reference's 2x2 max-pools
+    // read past their input (csrc/bnn_react_opt.c:48, (H-2)/2+1 = 1 at H = 1)
+    if (H < 16 || W < 16) return set_error(BNN_ERR_ARG, "H=%d W=%d: the ReAct forward needs H, W >= 16", H, W);
+    if ((long long)N * H * W >= (1ll << 31)) return set_error(BNN_ERR_ARG, "N*H*W too large");
+    if (m->head_Cout > react::HEADR_MAXC) return set_error(BNN_ERR_UNSUPPORTED, "n_classes > %d", react::HEADR_MAXC);
+    return BNN_OK;
+}
+
+int forward_device(const ModelR* m, RDev* d, const float* x, int N, int H, int W, float* logits, cudaStream_t user) {
+    int rc = arena(m, d, N, H, W);
+    if (rc || N == 0) return rc;
+    REngine* E = (REngine*)m->engine;
+    RCK(cudaStreamWaitEvent(user, d->ev_last, 0));
+    if (E->prof.on) {
+        RProf pc;
+        pc.prof = &E->prof;
+        pc.st = user;
+        if ((rc = forward_launches(m, d, x, N, H, W, logits, user, &pc))) return rc;
+        RCK(cudaEventRecord(d->ev_last, user));
+        return pc.finish();
+    }
+    GraphKeyR key{N, H, W, x, logits};
+    auto it = d->graphs.find(key);
+    if (it == d->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        RCK(cudaStreamBeginCapture(d->cs, cudaStreamCaptureModeThreadLocal));
+        rc = forward_launches(m, d, x, N, H, W, logits, d->cs, nullptr);
+        cudaError_t e = cudaStreamEndCapture(d->cs, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+        if (d->graphs.size() > 64) {
+            for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+            d->graphs.clear();
+        }
+        it = d->graphs.emplace(key, ex).first;
+    }
+    RCK(cudaGraphLaunch(it->second, user));
+    RCK(cudaEventRecord(d->ev_last, user));
+    return BNN_OK;
+}
+
+int current_device(int* dev) {
+    if (cudaGetDevice(dev) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "no CUDA device available");
+    }
+    return BNN_OK;
+}
+
+// host batch on the current device: chunks of up to `chunk` patches, copies
+// and compute serialised on one stream (the copies dominate end to end)
+int host_batch(const ModelR* m, const float* in, int N, int H, int W, float* out) {
+    int rc = check_hw(m, N, H, W);
+    if (rc || N == 0) return rc;
+    int dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    RDev* d = nullptr;
+    if ((rc = get_rdev(m, dev, &d))) return rc;
+    std::lock_guard<std::mutex> g(d->mu);
+    RCK(cudaSetDevice(dev));
+    const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
+    const int chunk = std::max(1, std::min(N, 256));
+    float *din = nullptr, *dout = nullptr;
+    if (cudaMalloc(&din, ip * chunk * 4) != cudaSuccess || cudaMalloc(&dout, op * chunk * 4) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(din);
+        return set_error(BNN_ERR_OOM, "cudaMalloc ReAct staging");
+    }
+    for (int s = 0; s < N && !rc; s += chunk) {
+        const int n = std::min(chunk, N - s);
+        if (cudaMemcpyAsync(din, in + ip * s, ip * n * 4, cudaMemcpyHostToDevice, d->cs) != cudaSuccess) {
+            rc = set_error(BNN_ERR_CUDA, "H2D: %s", cudaGetErrorString(cudaGetLastError()));
+            break;
+        }
+        if ((rc = forward_device(m, d, din, n, H, W, dout, d->cs))) break;
+        if (cudaMemcpyAsync(out + op * s, dout, op * n * 4, cudaMemcpyDeviceToHost, d->cs) != cudaSuccess)
+            rc = set_error(BNN_ERR_CUDA, "D2H: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    if (cudaStreamSynchronize(d->cs) != cudaSuccess && !rc)
+        rc = set_error(BNN_ERR_CUDA, "ReAct forward: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaFree(din);
+    cudaFree(dout);
+    return rc;
+}
+
+}  // namespace
+
+void* react_engine_create() { return new (std::nothrow) REngine(); }
+
+void react_engine_destroy(void* e) {
+    REngine* E = (REngine*)e;
+    if (!E) return;
+    for (auto& kv : E->devs) rdev_release(kv.second.get());
+    delete E;
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+BNN_API int bnn_forward_react_batch(const ModelR* m, const float* input, int N, int H, int W, float* logits) {
+    if (!m || !input || !logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    return host_batch(m, input, N, H, W, logits);
+}
+
+BNN_API int bnn_forward_react_device(const ModelR* m, int device, const float* d_input, int N, int H, int W,
+                                     float* d_logits, void* stream) {
+    if (!m || !d_input || !d_logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    int rc = check_hw(m, N, H, W);
+    if (rc) return rc;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_ARG, "cannot select device %d", device);
+    }
+    RDev* d = nullptr;
+    rc = get_rdev(m, device, &d);
+    if (!rc) {
+        std::lock_guard<std::mutex> g(d->mu);
+        rc = forward_device(m, d, d_input, N, H, W, d_logits, (cudaStream_t)stream);
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+BNN_API void bnn_forward_react(const ModelR* m, const float* input, int H, int W, float* logits) {
+    if (bnn_forward_react_batch(m, input, 1, H, W, logits) != BNN_OK) {
+        fprintf(stderr, "%s\n", bnn_last_error());
+        exit(1);
+    }
+}
+
+// the reference's tiler (csrc/bnn_model_react.c:454-476): zero-padded PxP
+// tiles, each a standalone forward, stitched; all tiles in one batch
+BNN_API int bnn_forward_react_patched_ex(const ModelR* m, const float* input, int H, int W, float* logits, int P) {
+    if (!m || !input || !logits) return set_error(BNN_ERR_ARG, "NULL argument");
+    if (P < 16 || P % 16 || H <= 0 || W <= 0)
+        return set_error(BNN_ERR_ARG, "H=%d W=%d P=%d: P must be a multiple of 16", H, W, P);
+    const int nb = m->n_bands, ncl = m->n_classes, ty = cdiv(H, P), tx = cdiv(W, P), nt = ty * tx;
+    std::vector<float> tin((size_t)nt * nb * P * P, 0.0f), tout((size_t)nt * ncl * P * P);
+    for (int a = 0; a < ty; ++a)
+        for (int b = 0; b < tx; ++b) {
+            const int py = a * P, px = b * P, ph = std::min(P, H - py), pw = std::min(P, W - px);
+            float* t = tin.data() + (size_t)(a * tx + b) * nb * P * P;
+            for (int c = 0; c < nb; ++c)
+                for (int y = 0; y < ph; ++y)
+                    memcpy(t + ((size_t)c * P + y) * P, input + ((size_t)c * H + py + y) * W + px, (size_t)pw * 4);
+        }
+    int rc = bnn_forward_react_batch(m, tin.data(), nt, P, P, tout.data());
+    if (rc) return rc;
+    for (int a = 0; a < ty; ++a)
+        for (int b = 0; b < tx; ++b) {
+            const int py = a * P, px = b * P, ph = std::min(P, H - py), pw = std::min(P, W - px);
+            const float* t = tout.data() + (size_t)(a * tx + b) * ncl * P * P;
+            for (int c = 0; c < ncl; ++c)
+                for (int y = 0; y < ph; ++y)
+                    memcpy(logits + ((size_t)c * H + py + y) * W + px, t + ((size_t)c * P + y) * P, (size_t)pw * 4);
+        }
+    return BNN_OK;
+}
+
+BNN_API void bnn_forward_react_patched(const ModelR* m, const float* input, int H, int W, float* logits, int P) {
+    if (bnn_forward_react_patched_ex(m, input, H, W, logits, P) != BNN_OK) {
+        fprintf(stderr, "%s\n", bnn_last_error());
+        exit(1);
+    }
+}
+
+static std::vector<float> read_cube(const ModelR* m, FILE* f, int H, int W) {
+    std::vector<float> x((size_t)m->n_bands * H * W);
+    if (!f || fseek(f, 0, SEEK_SET) != 0 || fread(x.data(), 4, x.size(), f) != x.size()) {
+        fprintf(stderr, "file_reader: short read of the [%d,%d,%d] cube\n", m->n_bands, H, W);
+        exit(1);
+    }
+    return x;
+}
+
+// the file forms read the cube and run the in-memory forwards (the
+// reference streams strips to bound host memory; the values are the same)
+BNN_API void bnn_forward_react_file(const ModelR* m, FILE* in_f, int H, int W, float* logits) {
+    std::vector<float> x = read_cube(m, in_f, H, W);
+    bnn_forward_react(m, x.data(), H, W, logits);
+}
+
+BNN_API void bnn_forward_react_patched_file(const ModelR* m, FILE* f, int H, int W, float* logits, int P) {
+    std::vector<float> x = read_cube(m, f, H, W);
+    bnn_forward_react_patched(m, x.data(), H, W, logits, P);
+}
+
+BNN_API int bnn_forward_react_stages(const ModelR* m, const float* input, int H, int W, float* logits,
+                                     bnn_stage_cb cb, void* ctx) {
+    if (!m || !input || !logits || !cb) return set_error(BNN_ERR_ARG, "NULL argument");
+    int rc = check_hw(m, 1, H, W);
+    if (rc) return rc;
+    int dev = 0;
+    if ((rc = current_device(&dev))) return rc;
+    RDev* d = nullptr;
+    if ((rc = get_rdev(m, dev, &d))) return rc;
+    std::lock_guard<std::mutex> g(d->mu);
+    if ((rc = arena(m, d, 1, H, W))) return rc;
+    const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
+    float *din = nullptr, *dout = nullptr;
+    int8_t* d8 = nullptr;
+    size_t maxc = 0;
+    for (int b = 0; b < 9; ++b) maxc = std::max(maxc, (size_t)std::max(d->blk[b].Cin, d->blk[b].Cout) * d->buf[b].h * d->buf[b].w);
+    if (cudaMalloc(&din, ip * 4) != cudaSuccess || cudaMalloc(&dout, op * 4) != cudaSuccess ||
+        cudaMalloc(&d8, maxc) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(din);
+        cudaFree(dout);
+        return set_error(BNN_ERR_OOM, "cudaMalloc stage buffers");
+    }
+    auto fail = [&](int code) { cudaFree(din); cudaFree(dout); cudaFree(d8); return code; };
+    if (cudaMemcpy(din, input, ip * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(set_error(BNN_ERR_CUDA, "H2D"));
+    if ((rc = forward_launches(m, d, din, 1, H, W, dout, d->cs, nullptr))) return fail(rc);
+    if (cudaStreamSynchronize(d->cs) != cudaSuccess)
+        return fail(set_error(BNN_ERR_CUDA, "ReAct forward: %s", cudaGetErrorString(cudaGetLastError())));
+    std::vector<char> host;
+    auto fl = [&](const char* blk, const char* st, const float* dp, int C, int h, int w) {
+        host.resize((size_t)C * h * w * 4);
+        cudaMemcpy(host.data(), dp, host.size(), cudaMemcpyDeviceToHost);
+        cb(ctx, (std::string(blk) + "." + st).c_str(), 2, C, h, w, host.data());
+    };
+    auto in32 = [&](const char* blk, const char* st, const int32_t* dp, int C, int h, int w) {
+        host.resize((size_t)C * h * w * 4);
+        cudaMemcpy(host.data(), dp, host.size(), cudaMemcpyDeviceToHost);
+        cb(ctx, (std::string(blk) + "." + st).c_str(), 1, C, h, w, host.data());
+    };
+    auto bits = [&](const char* blk, const char* st, const uint32_t* dp, int C, int h, int w) {
+        react::unpack_bits_kernel<<<std::max(1, std::min(cdiv((long long)C * h * w, 256), 148 * 8)), 256, 0, d->cs>>>(
+            dp, 1, C, h * w, d8);
+        cudaStreamSynchronize(d->cs);
+        host.resize((size_t)C * h * w);
+        cudaMemcpy(host.data(), d8, host.size(), cudaMemcpyDeviceToHost);
+        cb(ctx, (std::string(blk) + "." + st).c_str(), 0, C, h, w, host.data());
+    };
+    for (int b = 0; b < 9; ++b) {
+        const RBlockDev& D = d->blk[b];
+        const RBuf& Q = d->buf[b];
+        const int h = Q.h, w = Q.w;
+        fl(BN[b], "proj", Q.res, D.Cout, h, w);
+        if (b == 0) fl(BN[b], "conv1.out", Q.c1, D.Cout, h, w);
+        else {
+            bits(BN[b], "tap1", Q.t1, D.Cin, h, w);
+            in32(BN[b], "conv1.P", Q.P1, D.Cout, h, w);
+        }
+        fl(BN[b], "h1", Q.h1, D.Cout, h, w);
+        bits(BN[b], "tap2", Q.t2, D.Cout, h, w);
+        in32(BN[b], "conv2.P", Q.P2, D.Cout, h, w);
+        if (b < 4) {
+            fl(BN[b], "skip", Q.out, D.Cout, h, w);
+            fl(BN[b], "down", Q.down, D.Cout, h / 2, w / 2);
+        } else {
+            fl(BN[b], "h2", Q.out, D.Cout, h, w);
+        }
+    }
+    cudaMemcpy(logits, dout, op * 4, cudaMemcpyDeviceToHost);
+    cb(ctx, "logits", 2, m->n_classes, H, W, logits);
+    return fail(BNN_OK);
+}
+
+BNN_API int bnn_react_profile_enable(ModelR* m, int on) {
+    if (!m || !m->engine) return set_error(BNN_ERR_ARG, "NULL model");
+    ((REngine*)m->engine)->prof.on = on != 0;
+    return BNN_OK;
+}
+
+BNN_API void bnn_react_profile_reset(ModelR* m) {
+    if (!m || !m->engine) return;
+    REngine* E = (REngine*)m->engine;
+    std::lock_guard<std::mutex> g(E->prof.mu);
+    E->prof.recs.clear();
+}
+
+BNN_API int bnn_react_profile_count(const ModelR* m) {
+    if (!m || !m->engine) return 0;
+    REngine* E = (REngine*)m->engine;
+    std::lock_guard<std::mutex> g(E->prof.mu);
+    return (int)E->prof.recs.size();
+}
+
+BNN_API int bnn_react_profile_get(const ModelR* m, int i, const char** label, const char** optype, double* work,
+                                  double* ms, int* calls) {
+    if (!m || !m->engine) return set_error(BNN_ERR_ARG, "NULL model");
+    REngine* E = (REngine*)m->engine;
+    std::lock_guard<std::mutex> g(E->prof.mu);
+    if (i < 0 || i >= (int)E->prof.recs.size()) return set_error(BNN_ERR_ARG, "record %d out of range", i);
+    const auto& r = E->prof.recs[i];
+    if (label) *label = r.label.c_str();
+    if (optype) *optype = r.optype.c_str();
+    if (work) *work = r.work;
+    if (ms) *ms = r.ms;
+    if (calls) *calls = r.calls;
+    return BNN_OK;
+}
+
+BNN_API int bnn_react_forward_launches(const ModelR* m, int N, int H, int W) {
+    if (!m || N <= 0 || H < 16 || W < 16) return 0;
+    // enc1: proj, conv, epi, conv2, skip, pool; enc2-4: + conv1 - conv; bottleneck
+    // and decoders: proj, conv1, epi, conv2, epi; head
+    return 6 + 3 * 6 + 5 + 4 * 5 + 1;
+}

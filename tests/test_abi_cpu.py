@@ -25,7 +25,7 @@ S8 = os.path.join(GOLD, "stem_c8_mixed_s3.blob")
 
 def declared_functions():
     names = []
-    for h in ("bnn_model.h", "bnn_b200.h", "bnn_model_stem.h"):
+    for h in ("bnn_model.h", "bnn_b200.h", "bnn_model_stem.h", "bnn_model_react.h"):
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(bnn_\w+)\s*\(", src, flags=re.M):
@@ -253,3 +253,50 @@ def test_stem_blob_writer_matches_committed_fixtures():
 def test_stem_cli_usage_matches_reference():
     r = subprocess.run([bn.CLI_STEM_PATH], capture_output=True, text=True)
     assert r.returncode == 1 and "usage:" in r.stderr and "weights_stem.blob" in r.stderr
+
+
+# ------------------------------------------------------------------ v3 ReActNet
+R8 = os.path.join(GOLD, "react_c8_s3.blob")
+
+
+def _react_status(data):
+    L = bn.lib()
+    h = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(data, len(data))
+    rc = L.bnn_react_load_mem(buf, len(data), ctypes.byref(h))
+    if rc == 0:
+        L.bnn_free_react(h.value)
+    return rc, L.bnn_last_error().decode()
+
+
+def test_react_loader_matches_reference():
+    """csrc/bnn_model_react.c:42-135: messages and structural checks."""
+    from bnns_to_c_b200 import blob_react as BR
+    data = open(R8, "rb").read()
+    assert _react_status(data) == (0, "")
+    m = bn.ReactModel(R8)
+    assert (m.version, m.base_channels, m.n_bands, m.n_classes) == (3, 8, 120, 3)
+    m.close()
+    assert _react_status(data[:-1])[1] == "short read"
+    assert _react_status(data + b"\0")[1] == "trailing bytes in blob"
+    assert _react_status(b"XNNC" + data[4:])[1] == "bad magic"
+    assert _react_status(open(C8, "rb").read())[1] == "blob version 1, this engine reads v3 (ReActNet)"
+    assert _react_status(data[:20] + struct.pack("<i", 1) + data[24:])[1] == "only nearest upsampler supported"
+    # enc1's first record is its conv (no tap1): tag 7 there
+    assert _react_status(data[:24] + struct.pack("<i", 7) + data[28:])[1] == "bad conv tag 7"
+    # a tap whose width does not match its conv
+    mdl = BR.random_react_model(8, 120, 3, seed=3)
+    mdl["blocks"]["enc2"]["tap2"] = mdl["blocks"]["enc2"]["tap2"][:5]
+    assert _react_status(BR.react_blob_bytes(mdl))[1] == "blob layout mismatch: tap2 channels"
+    # a channel chain the forward cannot run: refused at load
+    mdl = BR.random_react_model(8, 120, 3, seed=3)
+    mdl["head"]["W"] = mdl["head"]["W"][:, :4]
+    rc, msg = _react_status(BR.react_blob_bytes(mdl))
+    assert rc == bn.BNN_ERR_UNSUPPORTED and "head" in msg
+
+
+def test_react_dropin_load_exits_like_reference(tmp_path):
+    code = ("import ctypes,sys; L=ctypes.CDLL(sys.argv[1]); L.bnn_load_react.restype=ctypes.c_void_p; "
+            "L.bnn_load_react(sys.argv[2].encode()); print('returned')")
+    r = subprocess.run([sys.executable, "-c", code, bn.LIB_PATH, S8], capture_output=True, text=True)
+    assert r.returncode == 1 and "blob version 2, this engine reads v3" in r.stderr and "returned" not in r.stdout

@@ -17,7 +17,8 @@ pytestmark = pytest.mark.gpu
 
 import bnns_to_c_b200 as bn  # noqa: E402
 from bnns_to_c_b200 import blob as B  # noqa: E402
-from oracle_util import OModel, bconv_P, fold_int, maxpool, realin, synth  # noqa: E402
+from bnns_to_c_b200 import blob_react as BR  # noqa: E402
+from oracle_util import OModel, ORModel, bconv_P, fold_int, maxpool, realin, synth  # noqa: E402
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -545,3 +546,90 @@ def test_stem_multi_device(tmp_path):
     one = m.forward_batch(x)
     m.set_devices([0, 1])
     assert same_bits(m.forward_batch(x), one)
+
+
+# ------------------------------------------------------------------ v3 ReActNet
+# stages the GPU engine holds (the oracle also reports pool.P, poolr and the
+# decoders' cat, which the engine never materialises)
+REACT_REQUIRED = ["enc1.proj", "enc1.conv1.out", "enc1.h1", "enc1.tap2", "enc1.conv2.P", "enc1.skip", "enc1.down",
+                  "enc3.tap1", "enc3.conv1.P", "bottleneck.h2", "dec4.proj", "dec4.tap1", "dec1.h2", "logits"]
+
+
+def _react_same_stages(st, ref):
+    for k in REACT_REQUIRED:
+        assert k in st, k
+    for k in st:
+        assert k in ref, k
+        assert same_bits(st[k], ref[k]), k
+
+
+def _react_fixtures():
+    return sorted(glob.glob(os.path.join(GOLD, "react_*_*x*.npz")))
+
+
+@pytest.mark.parametrize("npz", _react_fixtures(), ids=[os.path.basename(f) for f in _react_fixtures()])
+def test_react_stages_match_reference(npz, bconv_kind):
+    """Every intermediate the engine holds (highway maps, taps, P, logits)
+    equals the reference ReAct engine's bit for bit (golden fixtures from the
+    reference's kernels, whose logits equal its own bnn_forward_react)."""
+    g = np.load(npz)
+    name = os.path.basename(npz).rsplit("_", 1)[0]
+    m = bn.ReactModel(os.path.join(GOLD, name + ".blob"))
+    H, W, seed, n = int(g["H"]), int(g["W"]), int(g["seed"]), int(g["n"])
+    x = synth(seed, 0, n, 120, H, W)
+    for p in range(n):
+        ref = {k[len(f"p{p}/"):]: g[k] for k in g.files if k.startswith(f"p{p}/")}
+        _react_same_stages(m.stages(x[p]), ref)
+    lg = m.forward_batch(x)
+    for p in range(n):
+        assert same_bits(lg[p], g[f"p{p}/logits"])
+
+
+@pytest.mark.parametrize("base,H,W", [(16, 64, 64), (16, 44, 60), (8, 50, 38), (24, 32, 32), (12, 33, 47),
+                                      (16, 16, 16), (8, 17, 83)])
+def test_react_sizes_and_widths_vs_oracle(base, H, W):
+    """Odd sizes (floor pools, partly covered upsamples, pixel tails of the
+    blocked projection), widths on both real-conv orders (Cout % 8) and
+    several channel slices; batched logits and every held stage."""
+    mdl = BR.random_react_model(base, 120, 3, seed=base + H)
+    data = BR.react_blob_bytes(mdl)
+    m, om = bn.ReactModel(data=data), ORModel(data)
+    x = synth(base * 7 + W, 0, 3, 120, H, W)
+    _react_same_stages(m.stages(x[0]), om.stages(x[0]))
+    assert same_bits(m.forward_batch(x), om.forward_batch(x))
+
+
+def test_react_device_graph_patched_and_profiler():
+    data = open(os.path.join(GOLD, "react_c8_s3.blob"), "rb").read()
+    m, om = bn.ReactModel(data=data), ORModel(data)
+    x = synth(61, 0, 5, 120, 32, 48)
+    ref = om.forward_batch(x)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((5, 3, 32, 48), dtype=torch.float32, device="cuda")
+    for _ in range(2):  # the second call replays the captured graph
+        dy.zero_()
+        m.forward_device(0, dx, 5, 32, 48, dy)
+        torch.cuda.synchronize()
+        assert same_bits(dy.cpu().numpy(), ref)
+    # the reference's tiler: zero-padded 32x32 tiles, each a standalone forward
+    cube = synth(62, 0, 1, 120, 70, 50)[0]
+    tiles, P = [], 32
+    for y in range(0, 70, P):
+        for xx in range(0, 50, P):
+            t = np.zeros((120, P, P), np.float32)
+            c = cube[:, y:y + P, xx:xx + P]
+            t[:, :c.shape[1], :c.shape[2]] = c
+            tiles.append(t)
+    tl = om.forward_batch(np.stack(tiles))
+    want = np.zeros((3, 70, 50), np.float32)
+    k = 0
+    for y in range(0, 70, P):
+        for xx in range(0, 50, P):
+            want[:, y:y + P, xx:xx + P] = tl[k][:, :min(P, 70 - y), :min(P, 50 - xx)]
+            k += 1
+    assert same_bits(m.forward_patched(cube, P), want)
+    m.profile(True)
+    m.forward_batch(x)
+    recs = m.profile_records()
+    assert len(recs) == m.launches(5, 32, 48) == 50
+    assert sum(r["op"] == "bconv" for r in recs) == 17 and all(r["ms"] > 0 for r in recs)
