@@ -30,6 +30,10 @@ through the patched forward (non-overlapping zero-padded 32x32 tiles,
 fixed 16-cube job); value = tiles/s with the cubes in HBM, e2e = tiles/s
 through bnn_forward_patched from host memory (2 cubes per rank).
 
+--workload react runs BASELINE config 4: the v3 ReAct real-highway UNet
+(base 16) on 1024 patches of 64x64x120 per GPU, against the reference's
+ReAct engine (oracle/_ref/ref_bench_react) as the CPU arm.
+
 --workload stem runs config 2's batch through the v2 spectral-stem variant
 of the network (16-channel 1x1 stem + real fold, enc1.conv1 binary), against
 the reference's stem engine (oracle/_ref/ref_bench_stem) as the CPU arm.
@@ -52,6 +56,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "UNet patches/s (32x32x120)"
 STEM_C = 16                 # v2 stem width: the reference's default (python/bnn2c spectral stem)
+REACT_C = 16                # v3 ReAct base width: the reference's default (python/bnn2c/blob_react.py C0_DEFAULT)
+REACT_METRIC = "ReAct UNet patches/s (64x64x120)"
+FFMA_PER_CLK_SM = 128       # fp32 fused multiply-adds / clock / SM (nominal; probe: 119)
 SEED_MODEL, SEED_INPUT = 0, 1
 POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
 MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (probe-measured on this pool)
@@ -122,10 +129,11 @@ def cpu_info():
     return model, os.cpu_count() or 1
 
 
-def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0, stem=False):
+def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0, stem=False, name=None):
     """Reference engine (compiled from the reference sources) on the host:
-    the v1 engine, or with stem=True the v2 spectral-stem engine."""
-    name = "ref_bench_stem" if stem else "ref_bench"
+    the v1 engine, with stem=True the v2 spectral-stem engine, or the driver
+    `name` (ref_bench_react: the v3 ReAct engine)."""
+    name = name or ("ref_bench_stem" if stem else "ref_bench")
     exe = os.path.join(ROOT, "oracle", "_ref", name)
     if not os.path.exists(exe):
         return None, f"oracle/_ref/{name} not built (needs the reference tree at build time)"
@@ -144,6 +152,12 @@ def model_blob(stem=0):
     return B.blob_bytes(B.random_model(32, 120, 3, seed=SEED_MODEL, rules="baseline", stem_channels=stem))
 
 
+def react_blob():
+    from bnns_to_c_b200 import blob_react as BR
+
+    return BR.react_blob_bytes(BR.random_react_model(REACT_C, 120, 3, seed=SEED_MODEL))
+
+
 def variant(args):
     """(stem channels, metric, workload name) of the network benched."""
     if args.workload == "stem":
@@ -156,6 +170,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.workload == "react":
+        return run_reference_react(args)
     stem, metric, wname = variant(args)
     data = model_blob(stem)
     with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
@@ -473,6 +489,183 @@ def run_scene(args):
     return 0
 
 
+def run_reference_react(args):
+    """Reference arm of BASELINE config 4: the reference's v3 ReAct engine
+    (oracle/_ref/ref_bench_react) on the host cores, 64x64 patches."""
+    H = W = 64
+    with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
+        f.write(react_blob())
+        path = f.name
+    model, cores = cpu_info()
+    n = cores * args.ref_per_core
+    secs, err = ref_bench(path, n, H, W, cores, args.steps, max(0, min(args.warmup, 1)), name="ref_bench_react")
+    os.unlink(path)
+    if secs is None:
+        print(json.dumps({"impl": "reference", "unavailable": err}))
+        return 0
+    v = n * len(secs) / sum(secs)
+    print(json.dumps({
+        "impl": "reference", "metric": REACT_METRIC, "value": round(v, 3), "unit": "patches/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * sum(secs) / len(secs), 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "b1+f32", "data": "synthetic",
+        "config": {"workload": f"react_c{REACT_C}_64x64x120", "base_channels": REACT_C, "H": H, "W": W,
+                   "bands": 120, "classes": 3, "patches_per_step": n},
+        "cpu_baseline": {"value": round(v, 3), "unit": "patches/s", "cores": cores, "kind": "reference",
+                         "sample": f"{n} patches per step, {cores} single-threaded processes, {model}"},
+        "e2e": {"value": round(v, 3), "unit": "patches/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+def run_react(args):
+    """the v3 ReAct UNet (base 16, random weights from
+    seed 0 with the config's distributions) on 1024 patches of 64x64x120 per
+    GPU per step."""
+    import torch
+
+    import bnns_to_c_b200 as bn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def maxall(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    P, H, W = args.react_patches, 64, 64
+    bn.set_bconv_kernel(args.bconv)
+    m = bn.ReactModel(data=react_blob())
+    din = torch.empty((P, 120, H, W), dtype=torch.float32, device="cuda")
+    dout = torch.empty((P, 3, H, W), dtype=torch.float32, device="cuda")
+    bn.synth_device(local, SEED_INPUT, rank * P, P, 120, H, W, din)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    m.profile(True)
+    for _ in range(args.warmup):
+        m.forward_device(local, din, P, H, W, dout, stream)
+    stream.synchronize()
+    m.profile_reset()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.forward_device(local, din, P, H, W, dout, stream)
+        e1.record(stream)
+        stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    dev_ms = maxall(e0.elapsed_time(e1))
+    recs = m.profile_records()
+    m.profile(False)
+    clocks = clk.summary()
+    e2e_s, same = None, None
+    if not args.no_e2e:
+        hin = torch.empty((P, 120, H, W), dtype=torch.float32, pin_memory=True)
+        hin.copy_(din.cpu())
+        hout = torch.empty((P, 3, H, W), dtype=torch.float32, pin_memory=True)
+        for _ in range(max(1, args.warmup)):
+            m.forward_batch(hin.numpy(), out=hout.numpy())
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            m.forward_batch(hin.numpy(), out=hout.numpy())
+        e2e_s = maxall(time.perf_counter() - t0)
+        same = bool(torch.equal(hout.view(torch.int32), dout.cpu().view(torch.int32)))
+    if rank == 0:
+        peaks = read_peaks()
+        props = torch.cuda.get_device_properties(local)
+        sms = props.multi_processor_count
+        max_mhz = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz") or 1965.0
+        by_op = {}
+        for r in recs:
+            o = by_op.setdefault(r["op"], {"ms": 0.0, "work": 0.0})
+            o["ms"] += r["ms"]
+            o["work"] += r["work"]
+        total_ms = sum(o["ms"] for o in by_op.values()) or 1e-9
+        fma_peak = sms * FFMA_PER_CLK_SM * max_mhz * 1e6 / 1e9          # G FMA/s
+        bf16 = peaks.get("bf16_tflops")
+        tensor_i8_peak = bf16 * 1e3 if bf16 else 2.25e6
+        hbm = peaks.get("hbm_gbs") or 6538.9
+
+        def rate(op):
+            o = by_op.get(op, {"ms": 1e-9, "work": 0.0})
+            return o["work"] / (o["ms"] * 1e6), o["ms"] / total_ms
+
+        real_ach, real_share = rate("conv_real")
+        proj_ach, proj_share = rate("proj")
+        bconv_ach, bconv_share = rate("bconv")
+        epi_ach, epi_share = rate("epi")
+        value = P * world * args.steps / (dev_ms / 1e3)
+        model, cores = cpu_info()
+        cpu = None
+        if not args.no_cpu_baseline:
+            with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
+                f.write(react_blob())
+                path = f.name
+            n = cores * args.ref_per_core
+            secs, err = ref_bench(path, n, H, W, cores, 1, 0, name="ref_bench_react")
+            os.unlink(path)
+            cpu = ({"value": round(n / secs[0], 3), "unit": "patches/s", "cores": cores, "kind": "reference",
+                    "sample": f"{n} patches of the same workload, {cores} single-threaded processes of the "
+                              f"reference ReAct engine built from its sources, {model}"} if secs else
+                   {"value": None, "unit": "patches/s", "cores": cores, "kind": "reference", "sample": err})
+        line = {
+            "metric": REACT_METRIC, "value": round(value, 1), "unit": "patches/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "b1+f32",
+            "data": "synthetic",
+            "config": {"workload": f"react_c{REACT_C}_{P}x64x64x120", "base_channels": REACT_C, "bands": 120,
+                       "classes": 3, "H": H, "W": W, "patches_per_gpu": P, "global_batch": P * world,
+                       "parallelism": f"patch-shard x{world}",
+                       "l2": f"inputs > L2 ({P * 120 * H * W * 4 / 1e9:.2f} GB read per step)"},
+            "e2e": {"value": round(P * world * args.steps / e2e_s, 1) if e2e_s else None, "unit": "patches/s",
+                    "h2d_bytes_per_step": P * 120 * H * W * 4, "d2h_bytes_per_step": P * 3 * H * W * 4,
+                    "api": "bnn_forward_react_batch (pinned host buffers)", "matches_device_path": same},
+            "gpu_launches": m.launches(P, H, W) * args.steps,
+            "device_wait_timeouts": bn.device_wait_timeouts(local),
+            "roofline": {"bound": "fp32", "kernel": "conv3_blk_kernel (enc1 real 3x3 conv, exact fp32 order)",
+                         "achieved": round(real_ach, 1), "peak": round(fma_peak, 1),
+                         "unit": "G FMA/s (Cout x Cin x 9 per pixel)", "frac": round(real_ach / fma_peak, 4),
+                         "traffic": None, "time_share": round(real_share, 4),
+                         "peak_source": f"nominal {sms} SMs x {FFMA_PER_CLK_SM} FMA/clk x {max_mhz:.0f} MHz"},
+            "rooflines": {
+                "proj": {"bound": "fp32", "achieved": round(proj_ach, 1), "peak": round(fma_peak, 1),
+                         "unit": "G FMA/s", "frac": round(proj_ach / fma_peak, 4), "time_share": round(proj_share, 4)},
+                "bconv": {"bound": "tensor", "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
+                          "unit": "Gbitop/s", "frac": round(bconv_ach / tensor_i8_peak, 4),
+                          "time_share": round(bconv_share, 4)},
+                "epi": {"bound": "hbm", "time_share": round(epi_share, 4), "peak_gbs": hbm},
+                "hbm_input": {"bytes_per_step": P * 120 * H * W * 4,
+                              "min_ms": round(P * 120 * H * W * 4 / (hbm * 1e6), 4)},
+            },
+            "per_kernel_ms": {r["label"]: round(r["ms"] / max(1, r["calls"]), 4) for r in recs},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -490,15 +683,19 @@ def main():
     ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
                          "mma = mma.sync for every layer")
-    ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem"],
+    ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem", "react"],
                     help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler; "
-                         "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem)")
+                         "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem); "
+                         "react: config 4, the v3 ReAct UNet on 64x64 patches")
+    ap.add_argument("--react-patches", type=int, default=1024, help="react workload: patches per GPU per step")
     ap.add_argument("--cubes", type=int, default=16, help="scene workload: cubes in the job")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "scene":
         return run_scene(args)
+    if args.workload == "react":
+        return run_react(args)
     return run_ours(args)
 
 

@@ -9,13 +9,21 @@
  * one conv's rows).
  *
  * Built with -DREF_STEM (ref_bench_stem) it times the reference's v2
- * spectral-stem engine instead (bnn_stem_load / bnn_stem_forward).
+ * spectral-stem engine instead (bnn_stem_load / bnn_stem_forward), with
+ * -DREF_REACT (ref_bench_react) its v3 ReAct engine (bnn_load_react /
+ * bnn_forward_react).
  *
  * usage: ref_bench blob n_patches H W procs seed steps warmup [first_patch]
  * prints one line per timed step: "step <i> <seconds>", then
  * "checksum <sum of logits of patch 0>" so callers can tie it to the GPU run.
  */
-#ifdef REF_STEM
+#if defined(REF_REACT)
+#include "bnn_model_react.h"
+typedef ModelR RModel;
+#define REF_LOAD bnn_load_react
+#define REF_FORWARD bnn_forward_react
+#define REF_FREE bnn_free_react
+#elif defined(REF_STEM)
 #include "bnn_model_stem.h"
 typedef StemModel RModel;
 #define REF_LOAD bnn_stem_load
