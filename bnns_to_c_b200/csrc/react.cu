@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstdint>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -197,8 +198,14 @@ int rdev_init(const ModelR* m, RDev* d) {
             if (rc) return rc;
         }
     }
-    RCK(cudaFuncSetAttribute(react::proj_tap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             react::PROJ_MAX_CIN * react::PROJ_CB * 4));
+    {
+        const int sm = react::PROJ_MAX_CIN * react::PROJ_CB * 4;
+#define PROJ_ATTR(px, cat, tap) \
+    RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm))
+        PROJ_ATTR(1, false, false); PROJ_ATTR(4, false, false); PROJ_ATTR(1, false, true);
+        PROJ_ATTR(4, false, true); PROJ_ATTR(1, true, true); PROJ_ATTR(4, true, true);
+#undef PROJ_ATTR
+    }
     RCK(cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking));
     RCK(cudaEventCreateWithFlags(&d->ev_last, cudaEventDisableTiming));
     RCK(cudaEventRecord(d->ev_last, d->cs));
@@ -349,15 +356,35 @@ int run_proj(const RBlockDev& D, const float* x0, int c0, const float* x1, int c
     p.out = out;
     p.rsign = bits ? D.tap1 : nullptr;
     p.bits = bits;
-    const dim3 grid(cdiv((long long)N * HW, 256), cdiv(D.Cout, react::PROJ_CB));
-    react::proj_tap_kernel<<<grid, 256, (size_t)D.Cin * react::PROJ_CB * 4, st>>>(p);
+    // 4 pixels of one row per thread when rows split evenly and the plain
+    // input is 16-byte aligned
+    const bool v4 = W % 4 == 0 && ((uintptr_t)x0 & 15) == 0;
+    const int PX = v4 ? 4 : 1;
+    const dim3 grid(cdiv((long long)N * HW / PX, 256), cdiv(D.Cout, react::PROJ_CB));
+    const size_t smem = (size_t)D.Cin * react::PROJ_CB * 4;
+#define PROJ_LAUNCH(px, cat, tap) react::proj_tap_kernel<px, cat, tap><<<grid, 256, smem, st>>>(p)
+    if (x1) {
+        if (v4) PROJ_LAUNCH(4, true, true);
+        else PROJ_LAUNCH(1, true, true);
+    } else if (bits) {
+        if (v4) PROJ_LAUNCH(4, false, true);
+        else PROJ_LAUNCH(1, false, true);
+    } else {
+        if (v4) PROJ_LAUNCH(4, false, false);
+        else PROJ_LAUNCH(1, false, false);
+    }
+#undef PROJ_LAUNCH
     return launched("proj");
 }
 
 int run_epi(const int32_t* P, const float* v, const float* res, float* out, const float* A, const float* Bm,
             const float* pw, const float* rsign, uint32_t* bits, int N, int C, int HW, cudaStream_t st) {
     react::EpiParams p{P, v, res, out, A, Bm, pw, rsign, bits, N, C, HW};
-    react::epi_kernel<<<cdiv((long long)N * HW, 256), 256, 0, st>>>(p);
+    const bool v4 = HW % 4 == 0 && (((uintptr_t)(P ? (const void*)P : (const void*)v) | (uintptr_t)res |
+                                      (uintptr_t)out) & 15) == 0;
+    const unsigned chunks = (unsigned)cdiv(C, 32);
+    if (v4) react::epi_kernel<4><<<dim3(cdiv((long long)N * HW / 4, 256), chunks), 256, 0, st>>>(p);
+    else react::epi_kernel<1><<<dim3(cdiv((long long)N * HW, 256), chunks), 256, 0, st>>>(p);
     return launched("epilogue");
 }
 
@@ -393,7 +420,7 @@ int forward_launches(const ModelR* m, RDev* d, const float* x, int N, int H, int
                                  cdiv(h, react::C3_TR)};
             beg(b, "conv1", "conv_real", px * D.Cout * D.Cin * 9.0);
             if (blocked)
-                react::conv3_blk_kernel<<<dim3(N * c.tiles_x * c.tiles_y, cdiv(D.Cout, 16)), 256, 0, st>>>(c);
+                react::conv3_blk_kernel<<<dim3(N * c.tiles_x * c.tiles_y, cdiv(D.Cout, 16)), 128, 0, st>>>(c);
             else
                 react::conv3_naive_kernel<<<cdiv((long long)N * HW * cdiv(D.Cout, 4), 128), 128, 0, st>>>(c);
             rc = launched("conv3");
@@ -427,25 +454,32 @@ int forward_launches(const ModelR* m, RDev* d, const float* x, int N, int H, int
         rc = run_bconv(D.conv2, Q.t2, N, h, w, Q.P2, d->scratch, st);
         end();
         if (rc) return rc;
-        beg(b, b < 4 ? "skip" : "epi2", "epi", px * D.Cout);
-        rc = run_epi(Q.P2, nullptr, Q.h1, Q.out, D.Aa, D.Bma, D.pwa, nullptr, nullptr, N, D.Cout, HW, st);
-        end();
-        if (rc) return rc;
         if (B.is_down) {
-            react::PoolEpiParams pp{Q.P2, Q.h1, Q.down, D.Ab, D.Bmb, D.pwb, N, D.Cout, h, w};
-            beg(b, "pool+down", "epi", (double)N * (h / 2) * (w / 2) * D.Cout);
-            react::pool_epi_kernel<<<cdiv((long long)N * (h / 2) * (w / 2), 256), 256, 0, st>>>(pp);
-            rc = launched("pool epilogue");
+            react::SkipPoolParams sp{Q.P2, Q.h1, Q.out, Q.down, D.Aa, D.Bma, D.pwa, D.Ab, D.Bmb, D.pwb,
+                                     N, D.Cout, h, w};
+            beg(b, "skip+pool+down", "epi", px * D.Cout);
+            react::skip_pool_kernel<<<dim3(cdiv((long long)N * ((h + 1) / 2) * ((w + 1) / 2), 256),
+                                           (unsigned)cdiv(D.Cout, 16)),
+                                      256, 0, st>>>(sp);
+            rc = launched("skip / pool epilogue");
             end();
             if (rc) return rc;
             xin = Q.down; xc = D.Cout; xh = h / 2; xw = w / 2;
         } else {
+            beg(b, "epi2", "epi", px * D.Cout);
+            rc = run_epi(Q.P2, nullptr, Q.h1, Q.out, D.Aa, D.Bma, D.pwa, nullptr, nullptr, N, D.Cout, HW, st);
+            end();
+            if (rc) return rc;
             xin = Q.out; xc = D.Cout; xh = h; xw = w;
         }
     }
     react::HeadParams hp{xin, d->headW, d->headb, logits, N, m->head_Cin, m->head_Cout, H * W};
     if (pc && pc->prof) pc->begin("head", "head", (double)N * H * W * m->head_Cout * m->head_Cin);
-    react::head_kernel<<<cdiv((long long)N * H * W, 256), 256, 0, st>>>(hp);
+    const bool hv4 = (H * W) % 4 == 0 && (((uintptr_t)xin | (uintptr_t)logits) & 15) == 0;
+    const unsigned hg = (unsigned)cdiv((long long)N * H * W / (hv4 ? 4 : 1), 256);
+    if (hv4 && m->head_Cout == 3) react::head_kernel<4, 3><<<hg, 256, 0, st>>>(hp);
+    else if (hv4) react::head_kernel<4, react::HEADR_MAXC><<<hg, 256, 0, st>>>(hp);
+    else react::head_kernel<1, react::HEADR_MAXC><<<hg, 256, 0, st>>>(hp);
     rc = launched("head");
     end();
     return rc;
@@ -757,7 +791,7 @@ BNN_API int bnn_react_profile_get(const ModelR* m, int i, const char** label, co
 
 BNN_API int bnn_react_forward_launches(const ModelR* m, int N, int H, int W) {
     if (!m || N <= 0 || H < 16 || W < 16) return 0;
-    // enc1: proj, conv, epi, conv2, skip, pool; enc2-4: + conv1 - conv; bottleneck
-    // and decoders: proj, conv1, epi, conv2, epi; head
-    return 6 + 3 * 6 + 5 + 4 * 5 + 1;
+    // every block: proj, conv1 (enc1: the real conv), epi1, conv2, one
+    // closing epilogue (encoder: skip + pooled down in one pass); head
+    return 9 * 5 + 1;
 }

@@ -28,7 +28,7 @@ namespace react {
 // skip map x0, the rest from the half-resolution x1 at (y-oh)/2, (x-ow)/2
 // inside the covered rectangle, 0 outside. With rsign set, slice 0 also
 // writes the input's tap bits: x + rsign > 0 (csrc/bnn_react_ops.c:75-86).
-// Thread = one pixel x CB output channels (blockIdx.y = channel slice).
+// Thread = PX pixels x CB output channels (blockIdx.y = channel slice).
 // ---------------------------------------------------------------------
 struct ProjParams {
     const float* x0;
@@ -52,7 +52,117 @@ __device__ __forceinline__ float cat_value(const ProjParams& p, int n, int ci, i
     return __ldg(p.x1 + (((size_t)n * p.c1 + (ci - p.c0)) * p.h1 + (yy >> 1)) * p.w1 + (xx >> 1));
 }
 
-__global__ void __launch_bounds__(256) proj_tap_kernel(const ProjParams p) {
+// PX pixels of one row per thread (PX = 4 when W % 4 == 0: 16-byte loads of
+// the plain input); channel pairs in fp32x2 FMAs (two independent FMAs each).
+// CAT: the input is a decoder's concat; TAP: write the input's tap bits;
+// FUSED: fused multiply-adds (else the rounded-product-then-add tail form).
+template <int PX, bool TAP, bool FUSED>
+__device__ __forceinline__ void proj_step(float2 (&acc)[PX][PROJ_CB / 2], const float (&xv)[PX], const float* sw,
+                                          int ci, const ProjParams& p, uint32_t (&word)[PX], long long pix) {
+    constexpr int CB = PROJ_CB;
+    if constexpr (TAP) {
+        const float rs = __ldg(p.rsign + ci);
+#pragma unroll
+        for (int j = 0; j < PX; ++j) word[j] |= (__fadd_rn(xv[j], rs) > 0.0f ? 1u : 0u) << (ci & 31);
+        if ((ci & 31) == 31 || ci == p.Cin - 1) {
+            const int cw = (p.Cin + 31) >> 5;
+#pragma unroll
+            for (int j = 0; j < PX; ++j) {
+                p.bits[(size_t)(pix + j) * cw + (ci >> 5)] = word[j];
+                word[j] = 0u;
+            }
+        }
+    }
+    const float4* wr = reinterpret_cast<const float4*>(sw + ci * CB);
+#pragma unroll
+    for (int c4 = 0; c4 < CB / 4; ++c4) {
+        const float4 w4 = wr[c4];
+        if constexpr (FUSED) {
+            const float2 wa = make_float2(w4.x, w4.y), wb = make_float2(w4.z, w4.w);
+#pragma unroll
+            for (int j = 0; j < PX; ++j) {
+                const float2 xx2 = make_float2(xv[j], xv[j]);
+                acc[j][2 * c4] = __ffma2_rn(wa, xx2, acc[j][2 * c4]);
+                acc[j][2 * c4 + 1] = __ffma2_rn(wb, xx2, acc[j][2 * c4 + 1]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < PX; ++j) {
+                acc[j][2 * c4].x = __fadd_rn(acc[j][2 * c4].x, __fmul_rn(w4.x, xv[j]));
+                acc[j][2 * c4].y = __fadd_rn(acc[j][2 * c4].y, __fmul_rn(w4.y, xv[j]));
+                acc[j][2 * c4 + 1].x = __fadd_rn(acc[j][2 * c4 + 1].x, __fmul_rn(w4.z, xv[j]));
+                acc[j][2 * c4 + 1].y = __fadd_rn(acc[j][2 * c4 + 1].y, __fmul_rn(w4.w, xv[j]));
+            }
+        }
+    }
+}
+
+template <int PX, bool CAT, bool TAP, bool FUSED>
+__device__ __forceinline__ void proj_body(const ProjParams& p, const float* sw, int n, int q, int y, int x,
+                                          long long pix) {
+    constexpr int CB = PROJ_CB;
+    const int HW = p.H * p.W;
+    float2 acc[PX][CB / 2];
+#pragma unroll
+    for (int j = 0; j < PX; ++j)
+#pragma unroll
+        for (int c = 0; c < CB / 2; ++c) acc[j][c] = make_float2(0.0f, 0.0f);
+    uint32_t word[PX];
+#pragma unroll
+    for (int j = 0; j < PX; ++j) word[j] = 0u;
+    const float* x0p = p.x0 + (size_t)n * p.c0 * HW + q;
+#pragma unroll 2
+    for (int ci = 0; ci < p.c0; ++ci) {
+        float xv[PX];
+        if constexpr (PX == 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x0p + (size_t)ci * HW));
+            xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
+        } else {
+            xv[0] = __ldg(x0p + (size_t)ci * HW);
+        }
+        proj_step<PX, TAP, FUSED>(acc, xv, sw, ci, p, word, pix);
+    }
+    if constexpr (CAT) {
+        // the upsampled channels: each pixel's source offset and cover, once
+        const int yy = y - p.oh;
+        const bool yin = (unsigned)yy < (unsigned)p.cH;
+        int off[PX];
+        bool in[PX];
+#pragma unroll
+        for (int j = 0; j < PX; ++j) {
+            const int xx = x + j - p.ow;
+            in[j] = yin && (unsigned)xx < (unsigned)p.cW;
+            off[j] = in[j] ? (yy >> 1) * p.w1 + (xx >> 1) : 0;
+        }
+        const int hw1 = p.h1 * p.w1;
+        const float* x1p = p.x1 + (size_t)n * p.c1 * hw1;
+#pragma unroll 2
+        for (int ci = p.c0; ci < p.Cin; ++ci) {
+            const float* src = x1p + (size_t)(ci - p.c0) * hw1;
+            float xv[PX];
+#pragma unroll
+            for (int j = 0; j < PX; ++j) xv[j] = in[j] ? __ldg(src + off[j]) : 0.0f;
+            proj_step<PX, TAP, FUSED>(acc, xv, sw, ci, p, word, pix);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CB; ++c) {
+        const int co = blockIdx.y * CB + c;
+        if (co >= p.Cout) break;
+        float* o = p.out + ((size_t)n * p.Cout + co) * HW + q;
+        if constexpr (PX == 4) {
+            *reinterpret_cast<float4*>(o) = (c & 1) ? make_float4(acc[0][c >> 1].y, acc[1][c >> 1].y, acc[2][c >> 1].y,
+                                                                  acc[3][c >> 1].y)
+                                                    : make_float4(acc[0][c >> 1].x, acc[1][c >> 1].x, acc[2][c >> 1].x,
+                                                                  acc[3][c >> 1].x);
+        } else {
+            o[0] = (c & 1) ? acc[0][c >> 1].y : acc[0][c >> 1].x;
+        }
+    }
+}
+
+template <int PX, bool CAT, bool TAP>
+__global__ void __launch_bounds__(256, 2) proj_tap_kernel(const ProjParams p) {
     constexpr int CB = PROJ_CB;
     extern __shared__ __align__(16) float sw[];  // [Cin][CB]
     {
@@ -63,51 +173,20 @@ __global__ void __launch_bounds__(256) proj_tap_kernel(const ProjParams p) {
     __syncthreads();
     const int HW = p.H * p.W;
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= (long long)p.N * HW) return;
-    const int n = (int)(g / HW), q = (int)(g - (long long)n * HW);
+    if (g * PX >= (long long)p.N * HW) return;
+    const long long pix = g * PX;
+    const int n = (int)(pix / HW), q = (int)(pix - (long long)n * HW);
     const int y = q / p.W, x = q - y * p.W;
-    float acc[CB];
-#pragma unroll
-    for (int c = 0; c < CB; ++c) acc[c] = 0.0f;
-    const bool tap = p.rsign != nullptr && blockIdx.y == 0;
-    const int cw = (p.Cin + 31) >> 5;
-    uint32_t word = 0u;
-    const bool fused = q < p.nfull;
-    for (int ci = 0; ci < p.Cin; ++ci) {
-        const float xv = cat_value(p, n, ci, y, x);
-        if (tap) {
-            word |= (__fadd_rn(xv, __ldg(p.rsign + ci)) > 0.0f ? 1u : 0u) << (ci & 31);
-            if ((ci & 31) == 31 || ci == p.Cin - 1) {
-                p.bits[(size_t)g * cw + (ci >> 5)] = word;
-                word = 0u;
-            }
-        }
-        const float4* wr = reinterpret_cast<const float4*>(sw + ci * CB);
-        if (fused) {
-#pragma unroll
-            for (int c4 = 0; c4 < CB / 4; ++c4) {
-                const float4 w4 = wr[c4];
-                acc[4 * c4 + 0] = __fmaf_rn(xv, w4.x, acc[4 * c4 + 0]);
-                acc[4 * c4 + 1] = __fmaf_rn(xv, w4.y, acc[4 * c4 + 1]);
-                acc[4 * c4 + 2] = __fmaf_rn(xv, w4.z, acc[4 * c4 + 2]);
-                acc[4 * c4 + 3] = __fmaf_rn(xv, w4.w, acc[4 * c4 + 3]);
-            }
-        } else {
-#pragma unroll
-            for (int c4 = 0; c4 < CB / 4; ++c4) {
-                const float4 w4 = wr[c4];
-                acc[4 * c4 + 0] = __fadd_rn(acc[4 * c4 + 0], __fmul_rn(w4.x, xv));
-                acc[4 * c4 + 1] = __fadd_rn(acc[4 * c4 + 1], __fmul_rn(w4.y, xv));
-                acc[4 * c4 + 2] = __fadd_rn(acc[4 * c4 + 2], __fmul_rn(w4.z, xv));
-                acc[4 * c4 + 3] = __fadd_rn(acc[4 * c4 + 3], __fmul_rn(w4.w, xv));
-            }
+    const bool fused = q < p.nfull;  // a group never straddles nfull (both multiples of PX)
+    if constexpr (TAP) {
+        if (blockIdx.y == 0) {
+            if (fused) proj_body<PX, CAT, true, true>(p, sw, n, q, y, x, pix);
+            else proj_body<PX, CAT, true, false>(p, sw, n, q, y, x, pix);
+            return;
         }
     }
-#pragma unroll
-    for (int c = 0; c < CB; ++c) {
-        const int co = blockIdx.y * CB + c;
-        if (co < p.Cout) p.out[((size_t)n * p.Cout + co) * HW + q] = acc[c];
-    }
+    if (fused) proj_body<PX, CAT, false, true>(p, sw, n, q, y, x, pix);
+    else proj_body<PX, CAT, false, false>(p, sw, n, q, y, x, pix);
 }
 
 // ---------------------------------------------------------------------
@@ -117,7 +196,7 @@ __global__ void __launch_bounds__(256) proj_tap_kernel(const ProjParams p) {
 // fused multiply-add per tap (exact products; out-of-image taps read staged
 // zeros, and adding a zero product leaves a sum that is never -0 unchanged,
 // as skipping the tap does); out = sum * alpha. CTA tile: 16 rows x 32
-// columns of one patch x 16 channels; thread: 4 consecutive pixels x 8
+// columns of one patch x 16 channels; thread: 4 consecutive pixels x 16
 // channels; bands staged 8 at a time with their weights in shared memory.
 // ---------------------------------------------------------------------
 struct Conv3Params {
@@ -131,7 +210,10 @@ struct Conv3Params {
 // row stride 35 (odd): the 4 rows x 8 column groups a warp reads hit 32 banks
 constexpr int C3_TR = 16, C3_TC = 32, C3_CK = 8, C3_SR = C3_TR + 2, C3_SC = C3_TC + 2, C3_SCP = 35;
 
-__global__ void __launch_bounds__(256) conv3_blk_kernel(const Conv3Params p) {
+// thread: 4 pixels x 16 channels, the channels in pairs for fp32x2 FMAs
+// (two independent FMAs, bit-identical to scalar ones) - half the issue
+// slots of scalar FMAs, which bound this kernel
+__global__ void __launch_bounds__(128, 4) conv3_blk_kernel(const Conv3Params p) {
     __shared__ __align__(16) float sx[C3_CK][C3_SR][C3_SCP];
     __shared__ __align__(16) float sw[C3_CK][9][16];
     const int tid = threadIdx.x;
@@ -139,19 +221,18 @@ __global__ void __launch_bounds__(256) conv3_blk_kernel(const Conv3Params p) {
     const int n = blockIdx.x / per, r = blockIdx.x - n * per;
     const int y0 = (r / p.tiles_x) * C3_TR, x0 = (r % p.tiles_x) * C3_TC;
     const int cb = blockIdx.y;
-    const int g = tid >> 7, rest = tid & 127;     // channel group (8 channels), row, column group
-    const int row = rest >> 3, cg = rest & 7;
-    float acc[4][8];
+    const int row = tid >> 3, cg = tid & 7;
+    float2 acc[4][8];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc[j][c] = 0.0f;
+        for (int c = 0; c < 8; ++c) acc[j][c] = make_float2(0.0f, 0.0f);
     const size_t plane = (size_t)p.H * p.W;
     const float* xn = p.x + (size_t)n * p.Cin * plane;
     for (int c0 = 0; c0 < p.Cin; c0 += C3_CK) {
         const int nc = min(C3_CK, p.Cin - c0);
         __syncthreads();
-        for (int e = tid; e < C3_CK * C3_SR * C3_SC; e += 256) {
+        for (int e = tid; e < C3_CK * C3_SR * C3_SC; e += 128) {
             const int ci = e / (C3_SR * C3_SC), rr = e - ci * (C3_SR * C3_SC);
             const int sy = rr / C3_SC, sxx = rr - sy * C3_SC;
             const int yy = y0 + sy - 1, xx = x0 + sxx - 1;
@@ -160,7 +241,7 @@ __global__ void __launch_bounds__(256) conv3_blk_kernel(const Conv3Params p) {
                 v = __ldg(xn + (size_t)(c0 + ci) * plane + (size_t)yy * p.W + xx);
             sx[ci][sy][sxx] = v;
         }
-        for (int e = tid; e < C3_CK * 9 * 16; e += 256) {
+        for (int e = tid; e < C3_CK * 9 * 16; e += 128) {
             const int ci = e / 144, rr = e - ci * 144;
             sw[ci][rr / 16][rr % 16] =
                 ci < nc ? __ldg(p.w + (((size_t)cb * p.Cin + c0 + ci) * 9) * 16 + rr) : 0.0f;
@@ -169,32 +250,41 @@ __global__ void __launch_bounds__(256) conv3_blk_kernel(const Conv3Params p) {
         for (int ci = 0; ci < nc; ++ci)
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky) {
-                float xr[6];
+                float2 xx2[6];
 #pragma unroll
-                for (int k = 0; k < 6; ++k) xr[k] = sx[ci][row + ky][4 * cg + k];
+                for (int k = 0; k < 6; ++k) {
+                    const float v = sx[ci][row + ky][4 * cg + k];
+                    xx2[k] = make_float2(v, v);
+                }
 #pragma unroll
                 for (int kx = 0; kx < 3; ++kx) {
-                    const float4 wa = *reinterpret_cast<const float4*>(&sw[ci][ky * 3 + kx][8 * g]);
-                    const float4 wb = *reinterpret_cast<const float4*>(&sw[ci][ky * 3 + kx][8 * g + 4]);
-                    const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                    const float4* wq = reinterpret_cast<const float4*>(&sw[ci][ky * 3 + kx][0]);
+                    float2 wp[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float4 w4 = wq[k];
+                        wp[2 * k] = make_float2(w4.x, w4.y);
+                        wp[2 * k + 1] = make_float2(w4.z, w4.w);
+                    }
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
 #pragma unroll
-                        for (int c = 0; c < 8; ++c) acc[j][c] = __fmaf_rn(xr[j + kx], w8[c], acc[j][c]);
+                        for (int c = 0; c < 8; ++c) acc[j][c] = __ffma2_rn(wp[c], xx2[j + kx], acc[j][c]);
                 }
             }
     }
     const int y = y0 + row;
     if (y >= p.H) return;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const int co = cb * 16 + 8 * g + c;
+    for (int c = 0; c < 16; ++c) {
+        const int co = cb * 16 + c;
         if (co >= p.Cout) break;
         const float a = __ldg(p.alpha + co);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int x = x0 + 4 * cg + j;
-            if (x < p.W) p.out[((size_t)n * p.Cout + co) * plane + (size_t)y * p.W + x] = __fmul_rn(acc[j][c], a);
+            const float v = (c & 1) ? acc[j][c >> 1].y : acc[j][c >> 1].x;
+            if (x < p.W) p.out[((size_t)n * p.Cout + co) * plane + (size_t)y * p.W + x] = __fmul_rn(v, a);
         }
     }
 }
@@ -267,65 +357,110 @@ __device__ __forceinline__ float rprelu(float A, float v, float Bm, float r, flo
     return t >= 0.0f ? t : __fmul_rn(pw, t);
 }
 
+// PX pixels per thread (PX = 4 when H*W % 4 == 0: 16-byte accesses) and one
+// 32-channel chunk (blockIdx.y; one tap word per pixel), so small maps with
+// many channels still fill the GPU
+template <int PX>
 __global__ void __launch_bounds__(256) epi_kernel(const EpiParams p) {
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= (long long)p.N * p.HW) return;
-    const int n = (int)(g / p.HW), q = (int)(g - (long long)n * p.HW);
+    if (g * PX >= (long long)p.N * p.HW) return;
+    const long long pix = g * PX;
+    const int n = (int)(pix / p.HW), q = (int)(pix - (long long)n * p.HW);
     const int cw = (p.C + 31) >> 5;
-    uint32_t word = 0u;
-    for (int c = 0; c < p.C; ++c) {
+    const int c0 = blockIdx.y * 32, c1 = min(p.C, c0 + 32);
+    uint32_t word[PX];
+#pragma unroll
+    for (int j = 0; j < PX; ++j) word[j] = 0u;
+#pragma unroll 4
+    for (int c = c0; c < c1; ++c) {
         const size_t i = ((size_t)n * p.C + c) * p.HW + q;
-        const float v = p.P ? (float)__ldg(p.P + i) : __ldg(p.v + i);
-        const float o = rprelu(__ldg(p.A + c), v, __ldg(p.Bm + c), __ldg(p.res + i), __ldg(p.pw + c));
-        p.out[i] = o;
-        if (p.rsign) {
-            word |= (__fadd_rn(o, __ldg(p.rsign + c)) > 0.0f ? 1u : 0u) << (c & 31);
-            if ((c & 31) == 31 || c == p.C - 1) {
-                p.bits[(size_t)g * cw + (c >> 5)] = word;
-                word = 0u;
+        float v[PX], r[PX], o[PX];
+        if constexpr (PX == 4) {
+            if (p.P) {
+                const int4 t = __ldg(reinterpret_cast<const int4*>(p.P + i));
+                v[0] = (float)t.x; v[1] = (float)t.y; v[2] = (float)t.z; v[3] = (float)t.w;
+            } else {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(p.v + i));
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
             }
+            const float4 t = __ldg(reinterpret_cast<const float4*>(p.res + i));
+            r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+        } else {
+            v[0] = p.P ? (float)__ldg(p.P + i) : __ldg(p.v + i);
+            r[0] = __ldg(p.res + i);
         }
+        const float A = __ldg(p.A + c), Bm = __ldg(p.Bm + c), pw = __ldg(p.pw + c);
+#pragma unroll
+        for (int j = 0; j < PX; ++j) o[j] = rprelu(A, v[j], Bm, r[j], pw);
+        if constexpr (PX == 4) *reinterpret_cast<float4*>(p.out + i) = make_float4(o[0], o[1], o[2], o[3]);
+        else p.out[i] = o[0];
+        if (p.rsign) {
+            const float rs = __ldg(p.rsign + c);
+#pragma unroll
+            for (int j = 0; j < PX; ++j) word[j] |= (__fadd_rn(o[j], rs) > 0.0f ? 1u : 0u) << (c & 31);
+        }
+    }
+    if (p.rsign) {
+#pragma unroll
+        for (int j = 0; j < PX; ++j) p.bits[(size_t)(pix + j) * cw + blockIdx.y] = word[j];
     }
 }
 
-// Pooled branch of a DownBlock (csrc/bnn_model_react.c:245-258): Pd = 2x2
-// max of P, hd = 2x2 max of h1 (compare chains of csrc/bnn_react_opt.c:
-// 46-85: first element, then each strictly greater one), down = epilogue(Pd,
-// hd). Floor dims. Thread = one half-resolution pixel, all channels.
-struct PoolEpiParams {
+// unit2 epilogues of a DownBlock in one pass (csrc/bnn_model_react.c:238-258):
+// skip = epilogue_a(P, h1) at full resolution, and the pooled branch
+// down = epilogue_b(Pd, hd) with Pd / hd the 2x2 maxima of P / h1 (compare
+// chains of csrc/bnn_react_opt.c:46-85: first element, then each strictly
+// greater one), floor dims. Thread = one 2x2 quad (ceil dims), all channels;
+// an odd last row or column gets its skip values only.
+struct SkipPoolParams {
     const int32_t* P;    // [N][C][H][W]
     const float* h1;     // [N][C][H][W]
-    float* out;          // [N][C][H/2][W/2]
-    const float* A;
-    const float* Bm;
-    const float* pw;
+    float* skip;         // [N][C][H][W]
+    float* down;         // [N][C][H/2][W/2]
+    const float *Aa, *Bma, *pwa, *Ab, *Bmb, *pwb;
     int N, C, H, W;
 };
 
-__global__ void __launch_bounds__(256) pool_epi_kernel(const PoolEpiParams p) {
-    const int Ho = p.H / 2, Wo = p.W / 2;
+// blockIdx.y: 16-channel chunk
+__global__ void __launch_bounds__(256) skip_pool_kernel(const SkipPoolParams p) {
+    const int Hq = (p.H + 1) / 2, Wq = (p.W + 1) / 2, Ho = p.H / 2, Wo = p.W / 2;
+    const int cbeg = blockIdx.y * 16, cend = min(p.C, cbeg + 16);
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= (long long)p.N * Ho * Wo) return;
-    const int HWo = Ho * Wo;
-    const int n = (int)(g / HWo), q = (int)(g - (long long)n * HWo);
-    const int oy = q / Wo, ox = q - oy * Wo;
-    for (int c = 0; c < p.C; ++c) {
-        const size_t b = (((size_t)n * p.C + c) * p.H + 2 * oy) * p.W + 2 * ox;
-        int32_t m = __ldg(p.P + b), v1 = __ldg(p.P + b + 1), v2 = __ldg(p.P + b + p.W), v3 = __ldg(p.P + b + p.W + 1);
-        if (v1 > m) m = v1;
-        if (v2 > m) m = v2;
-        if (v3 > m) m = v3;
-        float f = __ldg(p.h1 + b), f1 = __ldg(p.h1 + b + 1), f2 = __ldg(p.h1 + b + p.W), f3 = __ldg(p.h1 + b + p.W + 1);
-        if (f1 > f) f = f1;
-        if (f2 > f) f = f2;
-        if (f3 > f) f = f3;
-        p.out[((size_t)n * p.C + c) * HWo + q] =
-            rprelu(__ldg(p.A + c), (float)m, __ldg(p.Bm + c), f, __ldg(p.pw + c));
+    if (g >= (long long)p.N * Hq * Wq) return;
+    const int n = (int)(g / ((long long)Hq * Wq)), qq = (int)(g - (long long)n * Hq * Wq);
+    const int qy = qq / Wq, qx = qq - qy * Wq;
+    const int y0 = 2 * qy, x0 = 2 * qx;
+    const bool hy = y0 + 1 < p.H, hx = x0 + 1 < p.W, full = qy < Ho && qx < Wo;
+#pragma unroll 2
+    for (int c = cbeg; c < cend; ++c) {
+        const size_t b = (((size_t)n * p.C + c) * p.H + y0) * p.W + x0;
+        const int32_t P00 = __ldg(p.P + b), P01 = hx ? __ldg(p.P + b + 1) : 0, P10 = hy ? __ldg(p.P + b + p.W) : 0,
+                      P11 = hx && hy ? __ldg(p.P + b + p.W + 1) : 0;
+        const float f00 = __ldg(p.h1 + b), f01 = hx ? __ldg(p.h1 + b + 1) : 0.0f,
+                    f10 = hy ? __ldg(p.h1 + b + p.W) : 0.0f, f11 = hx && hy ? __ldg(p.h1 + b + p.W + 1) : 0.0f;
+        const float A = __ldg(p.Aa + c), Bm = __ldg(p.Bma + c), pw = __ldg(p.pwa + c);
+        p.skip[b] = rprelu(A, (float)P00, Bm, f00, pw);
+        if (hx) p.skip[b + 1] = rprelu(A, (float)P01, Bm, f01, pw);
+        if (hy) p.skip[b + p.W] = rprelu(A, (float)P10, Bm, f10, pw);
+        if (hx && hy) p.skip[b + p.W + 1] = rprelu(A, (float)P11, Bm, f11, pw);
+        if (full) {
+            int32_t m = P00;
+            if (P01 > m) m = P01;
+            if (P10 > m) m = P10;
+            if (P11 > m) m = P11;
+            float f = f00;
+            if (f01 > f) f = f01;
+            if (f10 > f) f = f10;
+            if (f11 > f) f = f11;
+            p.down[((size_t)n * p.C + c) * Ho * Wo + (size_t)qy * Wo + qx] =
+                rprelu(__ldg(p.Ab + c), (float)m, __ldg(p.Bmb + c), f, __ldg(p.pwb + c));
+        }
     }
 }
 
 // fp32 1x1 head (head_1x1_v2, csrc/bnn_react_opt.c:26-43): each logit starts
 // at the bias and takes one fused multiply-add per input channel, in order.
+// Thread = PX pixels, all classes.
 constexpr int HEADR_MAXC = 16;
 struct HeadParams {
     const float* a;      // [N][Cin][HW]
@@ -335,22 +470,43 @@ struct HeadParams {
     int N, Cin, Cout, HW;
 };
 
+template <int PX, int NC>  // NC: the class count, or HEADR_MAXC for any count up to it
 __global__ void __launch_bounds__(256) head_kernel(const HeadParams p) {
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= (long long)p.N * p.HW) return;
-    const int n = (int)(g / p.HW), q = (int)(g - (long long)n * p.HW);
-    float v[HEADR_MAXC];
+    if (g * PX >= (long long)p.N * p.HW) return;
+    const long long pix = g * PX;
+    const int n = (int)(pix / p.HW), q = (int)(pix - (long long)n * p.HW);
+    const int nc = NC == HEADR_MAXC ? p.Cout : NC;
+    float v[NC][PX];
 #pragma unroll
-    for (int o = 0; o < HEADR_MAXC; ++o) v[o] = o < p.Cout ? __ldg(p.bias + o) : 0.0f;
+    for (int o = 0; o < NC; ++o)
+#pragma unroll
+        for (int j = 0; j < PX; ++j) v[o][j] = o < nc ? __ldg(p.bias + o) : 0.0f;
+#pragma unroll 4
     for (int c = 0; c < p.Cin; ++c) {
-        const float a = __ldg(p.a + ((size_t)n * p.Cin + c) * p.HW + q);
+        const float* src = p.a + ((size_t)n * p.Cin + c) * p.HW + q;
+        float a[PX];
+        if constexpr (PX == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+            a[0] = t.x; a[1] = t.y; a[2] = t.z; a[3] = t.w;
+        } else {
+            a[0] = __ldg(src);
+        }
 #pragma unroll
-        for (int o = 0; o < HEADR_MAXC; ++o)
-            if (o < p.Cout) v[o] = __fmaf_rn(__ldg(p.W + o * p.Cin + c), a, v[o]);
+        for (int o = 0; o < NC; ++o)
+            if (o < nc) {
+                const float w = __ldg(p.W + o * p.Cin + c);
+#pragma unroll
+                for (int j = 0; j < PX; ++j) v[o][j] = __fmaf_rn(w, a[j], v[o][j]);
+            }
     }
 #pragma unroll
-    for (int o = 0; o < HEADR_MAXC; ++o)
-        if (o < p.Cout) p.out[((size_t)n * p.Cout + o) * p.HW + q] = v[o];
+    for (int o = 0; o < NC; ++o)
+        if (o < nc) {
+            float* dst = p.out + ((size_t)n * p.Cout + o) * p.HW + q;
+            if constexpr (PX == 4) *reinterpret_cast<float4*>(dst) = make_float4(v[o][0], v[o][1], v[o][2], v[o][3]);
+            else dst[0] = v[o][0];
+        }
 }
 
 // bit plane [N][HW][cw] -> int8 +-1 [N][C][HW] (stage dumps)

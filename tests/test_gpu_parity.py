@@ -631,5 +631,5 @@ def test_react_device_graph_patched_and_profiler():
     m.profile(True)
     m.forward_batch(x)
     recs = m.profile_records()
-    assert len(recs) == m.launches(5, 32, 48) == 50
+    assert len(recs) == m.launches(5, 32, 48) == 46
     assert sum(r["op"] == "bconv" for r in recs) == 17 and all(r["ms"] > 0 for r in recs)
