@@ -115,6 +115,8 @@ def lib():
                                        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(ip)]),
         "bnn_react_forward_launches": (ip, [vp, ip, ip, ip]),
+        "bnn_react_set_conv_kernel": (ip, [ip]),
+        "bnn_react_device_error": (ip, [ip, ctypes.POINTER(ctypes.c_uint)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -392,6 +394,17 @@ class ReactModel:
             recs.append({"label": lab.value.decode(), "op": op.value.decode(), "work": work.value,
                          "ms": ms.value, "calls": calls.value})
         return recs
+
+
+def set_react_conv_kernel(kind: str):
+    """enc1 real-conv kernel of the ReAct engine: 'tma' (default) or 'plain'."""
+    _check(lib().bnn_react_set_conv_kernel({"tma": 0, "plain": 1}[kind]))
+
+
+def react_wait_timeouts(device=0):
+    n = ctypes.c_uint()
+    _check(lib().bnn_react_device_error(device, ctypes.byref(n)))
+    return n.value
 
 
 def load_stem(path: str) -> StemModel:

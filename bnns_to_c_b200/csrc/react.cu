@@ -86,6 +86,11 @@ struct RDev {
     cudaStream_t cs = nullptr;
     cudaEvent_t ev_last = nullptr;
     std::map<GraphKeyR, cudaGraphExec_t> graphs;
+    // host batches: two device staging slots, copies on their own streams
+    float *pin[2] = {nullptr, nullptr}, *pout[2] = {nullptr, nullptr};
+    size_t pcap = 0, pin_floats = 0, pout_floats = 0;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_comp[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
 };
 
 struct RProfiler {
@@ -120,10 +125,21 @@ void rdev_release(RDev* d) {
         bnn_bconv_layer_destroy(b.conv2);
         b.conv1 = b.conv2 = nullptr;
     }
+    if (d->h2d) cudaStreamSynchronize(d->h2d);
+    if (d->d2h) cudaStreamSynchronize(d->d2h);
     cudaFree(d->wbase);
     cudaFree(d->abase);
+    for (int k = 0; k < 2; ++k) {
+        cudaFree(d->pin[k]);
+        cudaFree(d->pout[k]);
+        if (d->ev_in[k]) cudaEventDestroy(d->ev_in[k]);
+        if (d->ev_comp[k]) cudaEventDestroy(d->ev_comp[k]);
+        if (d->ev_out[k]) cudaEventDestroy(d->ev_out[k]);
+    }
     if (d->ev_last) cudaEventDestroy(d->ev_last);
     if (d->cs) cudaStreamDestroy(d->cs);
+    if (d->h2d) cudaStreamDestroy(d->h2d);
+    if (d->d2h) cudaStreamDestroy(d->d2h);
     cudaSetDevice(prev);
 }
 
@@ -198,6 +214,10 @@ int rdev_init(const ModelR* m, RDev* d) {
             if (rc) return rc;
         }
     }
+    RCK(cudaFuncSetAttribute(react::conv3_tma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)react::C4Cfg<64>::SMEM));
+    RCK(cudaFuncSetAttribute(react::conv3_tma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)react::C4Cfg<32>::SMEM));
     {
         const int sm = react::PROJ_MAX_CIN * react::PROJ_CB * 4;
 #define PROJ_ATTR(px, cat, tap) \
@@ -207,6 +227,15 @@ int rdev_init(const ModelR* m, RDev* d) {
 #undef PROJ_ATTR
     }
     RCK(cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking));
+    RCK(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+    RCK(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+    for (int k = 0; k < 2; ++k) {
+        RCK(cudaEventCreateWithFlags(&d->ev_in[k], cudaEventDisableTiming));
+        RCK(cudaEventCreateWithFlags(&d->ev_comp[k], cudaEventDisableTiming));
+        RCK(cudaEventCreateWithFlags(&d->ev_out[k], cudaEventDisableTiming));
+        RCK(cudaEventRecord(d->ev_comp[k], d->cs));
+        RCK(cudaEventRecord(d->ev_out[k], d->cs));
+    }
     RCK(cudaEventCreateWithFlags(&d->ev_last, cudaEventDisableTiming));
     RCK(cudaEventRecord(d->ev_last, d->cs));
     return BNN_OK;
@@ -334,6 +363,44 @@ struct RProf {
     }
 };
 
+typedef CUresult (*EncodeTiledFnR)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point
+EncodeTiledFnR encode_tiled_r() {
+    static EncodeTiledFnR fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFnR)f;
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// the enc1 input as a 4-D map (W, H, bands, patches), box = one stage of
+// conv3_tma_kernel<TC>; false where TMA cannot address it (W % 4, alignment)
+bool conv3_tmap(const float* x, int N, int C, int H, int W, int TC, CUtensorMap* tm) {
+    EncodeTiledFnR fn = encode_tiled_r();
+    if (!fn || W % 4 || ((uintptr_t)x & 15)) return false;
+    const int bx = TC + 8, by = 128 / (TC / 4) + 2;
+    const cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)C, (cuuint64_t)N};
+    const cuuint64_t strides[3] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4, (cuuint64_t)C * H * W * 4};
+    const cuuint32_t box[4] = {(cuuint32_t)bx, (cuuint32_t)by, (cuuint32_t)react::C4_CK, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)x, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// conv kernel choice (A/B): 0 = TMA-staged where it applies, 1 = the
+// thread-staged kernel
+int g_conv3_kind = 0;
+
 int launched(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
@@ -419,10 +486,22 @@ int forward_launches(const ModelR* m, RDev* d, const float* x, int N, int H, int
             react::Conv3Params c{xin, d->c3w, d->c3a, Q.c1, N, D.Cin, h, w, D.Cout, cdiv(w, react::C3_TC),
                                  cdiv(h, react::C3_TR)};
             beg(b, "conv1", "conv_real", px * D.Cout * D.Cin * 9.0);
-            if (blocked)
+            const int TC = w >= 64 ? 64 : 32;
+            CUtensorMap tm;
+            if (blocked && g_conv3_kind == 0 && conv3_tmap(xin, N, D.Cin, h, w, TC, &tm)) {
+                react::Conv3Params c4 = c;
+                c4.tiles_x = cdiv(w, TC);
+                c4.tiles_y = cdiv(h, 512 / TC);
+                const dim3 grid(N * c4.tiles_x * c4.tiles_y, cdiv(D.Cout, 16));
+                if (TC == 64)
+                    react::conv3_tma_kernel<64><<<grid, 128, react::C4Cfg<64>::SMEM, st>>>(tm, c4);
+                else
+                    react::conv3_tma_kernel<32><<<grid, 128, react::C4Cfg<32>::SMEM, st>>>(tm, c4);
+            } else if (blocked) {
                 react::conv3_blk_kernel<<<dim3(N * c.tiles_x * c.tiles_y, cdiv(D.Cout, 16)), 128, 0, st>>>(c);
-            else
+            } else {
                 react::conv3_naive_kernel<<<cdiv((long long)N * HW * cdiv(D.Cout, 4), 128), 128, 0, st>>>(c);
+            }
             rc = launched("conv3");
             end();
             if (rc) return rc;
@@ -540,8 +619,10 @@ int current_device(int* dev) {
     return BNN_OK;
 }
 
-// host batch on the current device: chunks of up to `chunk` patches, copies
-// and compute serialised on one stream (the copies dominate end to end)
+// host batch on the current device: chunks through two device staging
+// slots, host->device copies on one stream, forwards on the compute stream,
+// device->host copies on a third, so chunk i's compute overlaps chunk i+1's
+// upload and chunk i-1's download (end to end this is bound by the host link)
 int host_batch(const ModelR* m, const float* in, int N, int H, int W, float* out) {
     int rc = check_hw(m, N, H, W);
     if (rc || N == 0) return rc;
@@ -552,27 +633,51 @@ int host_batch(const ModelR* m, const float* in, int N, int H, int W, float* out
     std::lock_guard<std::mutex> g(d->mu);
     RCK(cudaSetDevice(dev));
     const size_t ip = (size_t)m->n_bands * H * W, op = (size_t)m->n_classes * H * W;
-    const int chunk = std::max(1, std::min(N, 256));
-    float *din = nullptr, *dout = nullptr;
-    if (cudaMalloc(&din, ip * chunk * 4) != cudaSuccess || cudaMalloc(&dout, op * chunk * 4) != cudaSuccess) {
-        cudaGetLastError();
-        cudaFree(din);
-        return set_error(BNN_ERR_OOM, "cudaMalloc ReAct staging");
+    // chunk: about 64 MB of input, at least 1 patch, at most N
+    const int chunk = (int)std::max<size_t>(1, std::min<size_t>((size_t)N, ((size_t)64 << 20) / (ip * 4)));
+    if (d->pcap < (size_t)chunk || d->pin_floats != ip || d->pout_floats != op) {
+        RCK(cudaStreamSynchronize(d->h2d));
+        RCK(cudaStreamSynchronize(d->d2h));
+        RCK(cudaStreamSynchronize(d->cs));
+        for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+        d->graphs.clear();
+        for (int k = 0; k < 2; ++k) {
+            cudaFree(d->pin[k]);
+            cudaFree(d->pout[k]);
+            d->pin[k] = d->pout[k] = nullptr;
+        }
+        d->pcap = 0;
+        for (int k = 0; k < 2; ++k)
+            if (cudaMalloc(&d->pin[k], ip * chunk * 4) != cudaSuccess ||
+                cudaMalloc(&d->pout[k], op * chunk * 4) != cudaSuccess) {
+                cudaGetLastError();
+                return set_error(BNN_ERR_OOM, "cudaMalloc ReAct staging");
+            }
+        d->pcap = chunk;
+        d->pin_floats = ip;
+        d->pout_floats = op;
     }
-    for (int s = 0; s < N && !rc; s += chunk) {
-        const int n = std::min(chunk, N - s);
-        if (cudaMemcpyAsync(din, in + ip * s, ip * n * 4, cudaMemcpyHostToDevice, d->cs) != cudaSuccess) {
+    int i = 0;
+    for (int s0 = 0; s0 < N && !rc; s0 += chunk, ++i) {
+        const int n = std::min(chunk, N - s0), k = i & 1;
+        // slot k's input is free once its previous forward ran; its output
+        // once its previous download ran
+        if (cudaStreamWaitEvent(d->h2d, d->ev_comp[k], 0) != cudaSuccess ||
+            cudaMemcpyAsync(d->pin[k], in + ip * s0, ip * n * 4, cudaMemcpyHostToDevice, d->h2d) != cudaSuccess ||
+            cudaEventRecord(d->ev_in[k], d->h2d) != cudaSuccess || cudaStreamWaitEvent(d->cs, d->ev_in[k], 0) != cudaSuccess ||
+            cudaStreamWaitEvent(d->cs, d->ev_out[k], 0) != cudaSuccess) {
             rc = set_error(BNN_ERR_CUDA, "H2D: %s", cudaGetErrorString(cudaGetLastError()));
             break;
         }
-        if ((rc = forward_device(m, d, din, n, H, W, dout, d->cs))) break;
-        if (cudaMemcpyAsync(out + op * s, dout, op * n * 4, cudaMemcpyDeviceToHost, d->cs) != cudaSuccess)
+        if ((rc = forward_device(m, d, d->pin[k], n, H, W, d->pout[k], d->cs))) break;
+        if (cudaEventRecord(d->ev_comp[k], d->cs) != cudaSuccess || cudaStreamWaitEvent(d->d2h, d->ev_comp[k], 0) != cudaSuccess ||
+            cudaMemcpyAsync(out + op * s0, d->pout[k], op * n * 4, cudaMemcpyDeviceToHost, d->d2h) != cudaSuccess ||
+            cudaEventRecord(d->ev_out[k], d->d2h) != cudaSuccess)
             rc = set_error(BNN_ERR_CUDA, "D2H: %s", cudaGetErrorString(cudaGetLastError()));
     }
-    if (cudaStreamSynchronize(d->cs) != cudaSuccess && !rc)
+    cudaError_t e1 = cudaStreamSynchronize(d->d2h), e2 = cudaStreamSynchronize(d->cs), e3 = cudaStreamSynchronize(d->h2d);
+    if (!rc && (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess))
         rc = set_error(BNN_ERR_CUDA, "ReAct forward: %s", cudaGetErrorString(cudaGetLastError()));
-    cudaFree(din);
-    cudaFree(dout);
     return rc;
 }
 
@@ -786,6 +891,26 @@ BNN_API int bnn_react_profile_get(const ModelR* m, int i, const char** label, co
     if (work) *work = r.work;
     if (ms) *ms = r.ms;
     if (calls) *calls = r.calls;
+    return BNN_OK;
+}
+
+BNN_API int bnn_react_set_conv_kernel(int kind) {
+    if (kind != 0 && kind != 1) return set_error(BNN_ERR_ARG, "ReAct conv kernel kind %d (0 = TMA, 1 = plain)", kind);
+    g_conv3_kind = kind;
+    return BNN_OK;
+}
+
+BNN_API int bnn_react_device_error(int device, unsigned int* wait_timeouts) {
+    if (!wait_timeouts) return set_error(BNN_ERR_ARG, "NULL argument");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_ARG, "cannot select device %d", device);
+    }
+    cudaError_t e = cudaMemcpyFromSymbol(wait_timeouts, react::g_react_wait_timeouts, sizeof(unsigned int));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "read wait counter: %s", cudaGetErrorString(e));
     return BNN_OK;
 }
 

@@ -107,6 +107,13 @@ void bnn_react_profile_reset(ModelR *m);
 int bnn_react_profile_count(const ModelR *m);
 int bnn_react_profile_get(const ModelR *m, int i, const char **label, const char **optype, double *work, double *ms,
                           int *calls);
+/* A/B choice of the enc1 real-conv kernel: 0 = input staged by TMA through
+ * a shared-memory ring (default where W % 4 == 0), 1 = thread-staged. Both
+ * keep the reference's order, so both give its bits. */
+int bnn_react_set_conv_kernel(int kind);
+/* Bounded device waits of the ReAct kernels that gave up on `device` since
+ * the library was loaded (expected to stay 0). */
+int bnn_react_device_error(int device, unsigned int *wait_timeouts);
 /* Kernel launches of one device forward of N patches of H x W. */
 int bnn_react_forward_launches(const ModelR *m, int N, int H, int W);
 

@@ -633,3 +633,25 @@ def test_react_device_graph_patched_and_profiler():
     recs = m.profile_records()
     assert len(recs) == m.launches(5, 32, 48) == 46
     assert sum(r["op"] == "bconv" for r in recs) == 17 and all(r["ms"] > 0 for r in recs)
+
+
+@pytest.mark.parametrize("H,W", [(64, 64), (32, 32), (48, 72), (20, 36), (64, 96)])
+def test_react_conv_kernels_agree(H, W):
+    """enc1's real conv: the TMA-staged kernel (both tile widths, edge tiles,
+    rows past the patch) equals the thread-staged one and the oracle; no
+    bounded wait gives up."""
+    data = open(os.path.join(GOLD, "react_c16_s1.blob"), "rb").read()
+    m, om = bn.ReactModel(data=data), ORModel(data)
+    x = synth(70 + H, 0, 2, 120, H, W)
+    before = bn.react_wait_timeouts(0)
+    st = m.stages(x[0])
+    bn.set_react_conv_kernel("plain")
+    try:
+        st2 = m.stages(x[0])
+    finally:
+        bn.set_react_conv_kernel("tma")
+    ref = om.stages(x[0])
+    assert same_bits(st["enc1.conv1.out"], ref["enc1.conv1.out"])
+    assert same_bits(st2["enc1.conv1.out"], ref["enc1.conv1.out"])
+    assert same_bits(m.forward_batch(x), om.forward_batch(x))
+    assert bn.react_wait_timeouts(0) == before
