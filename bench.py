@@ -641,7 +641,7 @@ def run_react(args):
                     "api": "bnn_forward_react_batch (pinned host buffers)", "matches_device_path": same},
             "gpu_launches": m.launches(P, H, W) * args.steps,
             "device_wait_timeouts": bn.device_wait_timeouts(local),
-            "roofline": {"bound": "fp32", "kernel": "conv3_blk_kernel (enc1 real 3x3 conv, exact fp32 order)",
+            "roofline": {"bound": "fp32", "kernel": "conv3_tma_kernel (enc1 real 3x3 conv, TMA-staged, exact fp32 order)",
                          "achieved": round(real_ach, 1), "peak": round(fma_peak, 1),
                          "unit": "G FMA/s (Cout x Cin x 9 per pixel)", "frac": round(real_ach / fma_peak, 4),
                          "traffic": None, "time_share": round(real_share, 4),

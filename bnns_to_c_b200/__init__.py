@@ -24,6 +24,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libbnn_b200.so")
 CLI_PATH = os.path.join(HERE, "lib", "bnn_infer")
 CLI_STEM_PATH = os.path.join(HERE, "lib", "bnn_infer_stem")
+CLI_REACT_PATH = os.path.join(HERE, "lib", "bnn_infer_react")
 
 BNN_OK, BNN_ERR_IO, BNN_ERR_FORMAT, BNN_ERR_UNSUPPORTED, BNN_ERR_ARG, BNN_ERR_CUDA, BNN_ERR_OOM = range(7)
 

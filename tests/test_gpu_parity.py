@@ -655,3 +655,23 @@ def test_react_conv_kernels_agree(H, W):
     assert same_bits(st2["enc1.conv1.out"], ref["enc1.conv1.out"])
     assert same_bits(m.forward_batch(x), om.forward_batch(x))
     assert bn.react_wait_timeouts(0) == before
+
+
+def test_react_cli_matches_reference_binary(tmp_path):
+    """bnn_infer_react against the reference's own CLI (csrc/main_react.c,
+    built from its sources into oracle/_ref when the tree was present): the
+    same `rand` cube, whole-image and patch-wise, identical logits."""
+    ref_cli = os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref", "bnn_infer_react")
+    if not os.path.exists(ref_cli):
+        pytest.skip("reference ReAct CLI not built")
+    blob = os.path.join(GOLD, "react_c8_s3.blob")
+    for spec, H, W in (("rand", 48, 40), ("patch16:rand", 40, 56)):
+        ours, theirs = tmp_path / "o.bin", tmp_path / "t.bin"
+        r = subprocess.run([bn.CLI_REACT_PATH, blob, spec, str(ours), str(H), str(W), "2"], capture_output=True,
+                           text=True)
+        assert r.returncode == 0, r.stderr
+        assert f"# forward {H}x{W} reps=2" in r.stdout
+        r2 = subprocess.run([ref_cli, blob, spec, str(theirs), str(H), str(W)], capture_output=True, text=True,
+                            env=dict(os.environ, OMP_NUM_THREADS="1"))
+        assert r2.returncode == 0, r2.stderr
+        assert same_bits(np.fromfile(ours, "<f4"), np.fromfile(theirs, "<f4")), spec
