@@ -919,7 +919,9 @@ __device__ float realin_exact_acc(const float* x, const float* wf, int Cin, int 
 
 // Undecided outputs of the tensor-core first convs, recomputed exactly. One
 // warp per listed (pixel, channel group): the 3x3 x Cin input window is
-// loaded once into shared memory (every load independent), then lanes
+// loaded once into shared memory (every load independent, a window row's
+// three taps by adjacent lanes: the reads are scattered over the input's
+// band planes, so sectors, not bytes, are what they cost), then lanes
 // 9c + t (three channels at a time) run tap t of channel c as the
 // reference's sequential fp32 chain over the bands, and lane 9c sums the
 // in-image taps in order. If the list overflowed, every output of the batch
@@ -951,11 +953,15 @@ __global__ void __launch_bounds__(FIX_WARPS * 32) realin_fixup_kernel(const Real
             const int xx = (int)(pix % p.W), y = (int)((pix / p.W) % p.H), n = (int)(pix / ((size_t)p.W * p.H));
             const float* xn = p.x + (size_t)n * p.Cin * plane;
             __syncwarp();
+            // element e = (ky, band, kx), kx fastest: the three taps of a
+            // window row are adjacent floats, read by adjacent lanes (one
+            // sector), instead of one sector per lane
             for (int e = lane; e < 9 * p.Cin; e += 32) {
-                const int t = e / p.Cin, ci = e - t * p.Cin;
-                const int iy = y + t / 3 - 1, ix = xx + t % 3 - 1;
-                wv[t][ci] = ((unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W)
-                                ? __ldg(xn + (size_t)ci * plane + (size_t)iy * p.W + ix) : 0.0f;
+                const int ky = e / (3 * p.Cin), r3 = e - ky * 3 * p.Cin;
+                const int ci = r3 / 3, kx = r3 - ci * 3;
+                const int iy = y + ky - 1, ix = xx + kx - 1;
+                wv[ky * 3 + kx][ci] = ((unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W)
+                                          ? __ldg(xn + (size_t)ci * plane + (size_t)iy * p.W + ix) : 0.0f;
             }
             __syncwarp();
             uint32_t bits = 0u;
