@@ -382,8 +382,10 @@ def run_ours(args):
                                             / peaks["hbm_gbs"], 4) if peaks.get("hbm_gbs") else None,
                               "time_share": frac_split.get("conv_real")} if stem else
                 {"bound": "tensor",
-                              "kernel": ("realin_ws_kernel (tcgen05)" if args.first == "tc" else
-                                         "realin_mma_kernel (mma.sync)") + " + realin_fixup_kernel",
+                              "kernel": {"tc": "realin_ws_kernel (tcgen05, nine shifted taps)",
+                                         "tcn": "realin_dxn_kernel (tcgen05, column taps in N)",
+                                         "mma": "realin_mma_kernel (mma.sync)"}[args.first]
+                              + " + realin_fixup_kernel",
                               "achieved": round(real_ach, 1), "peak": round(tensor_i8_peak, 1),
                               "unit": "G int8 MAC/s executed (3 planes x 128 bands x 9 taps x 32 ch per pixel)",
                               "frac": round(real_ach / tensor_i8_peak, 4),
@@ -690,7 +692,7 @@ def main():
     ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
-    ap.add_argument("--first", default="tc", choices=["tc", "mma"],
+    ap.add_argument("--first", default="tc", choices=["tc", "mma", "tcn"],
                     help="first conv kernel: tcgen05 (default) or mma.sync")
     ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "

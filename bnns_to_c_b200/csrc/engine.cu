@@ -99,6 +99,7 @@ struct DevState {
     uint4* rm_wfrag = nullptr;  // first conv +-1 int8 weights in mma B-fragment order
     int* rm_exact = nullptr;    // per channel: fold not monotone -> exact path
     int8_t* rw_wu = nullptr;    // first conv +-1 int8 weights for realin_ws_kernel (Cin <= 128, Cout <= 32)
+    int8_t* rx_wu = nullptr;    // the same for realin_dxn_kernel (column taps stacked in N)
     std::vector<RwThr> rw_thr;  // first conv fold thresholds for realin_ws_kernel (host copy, 32 entries)
     float* st_w = nullptr;      // v2 stem weights [slice][band][st_CB] (+-1, 0)
     float* st_fold = nullptr;   // v2 stem [channel][5]: alpha, A, B, slope, rsign
@@ -341,6 +342,8 @@ static int set_kernel_attrs(int device) {
             cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
             cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_dxn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
+            cudaSuccess ||
         (e = attr_stem<8>()) != cudaSuccess || (e = attr_stem<16>()) != cudaSuccess ||
         (e = attr_stem<32>()) != cudaSuccess)
         return set_error(BNN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -413,7 +416,7 @@ static int dev_init(const Model* m, DevState* d) {
     std::vector<float> wf, rfold;
     std::vector<uint32_t> wfrag;
     std::vector<int> rexact;
-    std::vector<int8_t> rwu;
+    std::vector<int8_t> rwu, rxu;
     std::vector<RwThr> rthr;
     // stem of a v2 model: [slice][band][CB] weights and [channel][5] folds
     std::vector<float> sw, sfold;
@@ -493,6 +496,17 @@ static int dev_init(const Model* m, DevState* d) {
                                         c1->wsign[((size_t)co * Cin + ci) * 9 + t];
                             }
         }
+        // and for realin_dxn_kernel: [chunk][kernel row][16-band half][column tap * 32 + channel][16 bands]
+        if (!rwu.empty()) {
+            rxu.assign(RX_WBYTES, (int8_t)0);
+            for (int kc = 0; kc < 4; ++kc)
+                for (int t = 0; t < 9; ++t)
+                    for (int h = 0; h < 2; ++h)
+                        for (int co = 0; co < CoutR; ++co)
+                            for (int i = 0; i < 16; ++i)
+                                rxu[((((size_t)kc * 3 + t / 3) * 2 + h) * 96 + (t % 3) * 32 + co) * 16 + i] =
+                                    rwu[((((size_t)kc * 9 + t) * 2 + h) * 32 + co) * 16 + i];
+        }
         if (!rwu.empty()) rthr.assign(32, RwThr{1ll << 62, 1, 0});
         for (int co = 0; co < CoutR; ++co) {
             const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
@@ -525,7 +539,7 @@ static int dev_init(const Model* m, DevState* d) {
         items.push_back({&d->dec2[i], &m->dec_conv2[i], &m->dec_act2[i], nullptr, m->dec_conv2[i].Cin, {}});
     }
     size_t total = align256(wf.size() * 4) + align256(rfold.size() * 4) + align256(wfrag.size() * 4) +
-                   align256(rexact.size() * 4) + align256(rwu.size()) + align256(sw.size() * 4) +
+                   align256(rexact.size() * 4) + align256(rwu.size()) + align256(rxu.size()) + align256(sw.size() * 4) +
                    align256(sfold.size() * 4);
     for (auto& it : items) {
         relayout_bin(it.c->packed, it.c->nwords, it.c->Cin, it.c->Cout, it.sC, *it.L, it.h, it.a2 != nullptr);
@@ -555,6 +569,7 @@ static int dev_init(const Model* m, DevState* d) {
     d->rm_wfrag = (uint4*)put(wfrag.data(), wfrag.size() * 4);
     d->rm_exact = (int*)put(rexact.data(), rexact.size() * 4);
     d->rw_wu = rwu.empty() ? nullptr : (int8_t*)put(rwu.data(), rwu.size());
+    d->rx_wu = rxu.empty() ? nullptr : (int8_t*)put(rxu.data(), rxu.size());
     d->rw_thr = rthr;
     d->st_w = sw.empty() ? nullptr : (float*)put(sw.data(), sw.size() * 4);
     d->st_fold = sfold.empty() ? nullptr : (float*)put(sfold.data(), sfold.size() * 4);
@@ -934,23 +949,40 @@ static bool first_conv_tmap(const float* x, int N, int C, int H, int W, CUtensor
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D map over the flattened image (H*W, C, N) for realin_dxn_kernel: box
+// (npos, 32, 1), an item's staged rows as one contiguous run per band
+static bool first_conv_tmap3(const float* x, int N, int C, int H, int W, int npos, CUtensorMap* tm) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || (W % 4) != 0 || ((uintptr_t)x & 15) || npos > 256) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)H * W, (cuuint64_t)C, (cuuint64_t)N};
+    const cuuint64_t strides[2] = {(cuuint64_t)H * W * 4, (cuuint64_t)C * H * W * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)npos, 32, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)x, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool first_conv_fast_ok(const Model* m, int N, int H, int W) {
     return m->enc_conv1[0].Cin <= RM_CINP && (W % 4) == 0 && (size_t)N * H * W < ((size_t)1 << 31) &&
            encode_tiled() != nullptr;
 }
 
-// first conv implementation: 0 = tcgen05 where the shape allows (default),
-// 1 = mma.sync
+// first conv implementation: 0 = tcgen05 realin_ws_kernel where the shape
+// allows (default), 1 = mma.sync, 2 = tcgen05 realin_dxn_kernel (column taps
+// in N) where W divides 32, realin_ws_kernel for other widths. Measured on
+// 4096 32x32 patches: realin_ws 1.29 ms, realin_dxn 1.35 ms (with the fix-up).
 static int g_first_kind = 0;
 
 // realin_ws_kernel geometry for (H, W); false if the shape does not fit it
 struct RwGeo {
-    int R, Wp, SP, NS;
+    int R, Wp, SP, NS, NB;
     size_t smem;
 };
 static bool rw_geometry(int H, int W, RwGeo* g) {
     if ((W % 4) != 0 || W > RW_MT * 128 - 1) return false;
     g->Wp = W + 1;
+    g->NB = RW_NB;
     g->R = std::min(H, (RW_MT * 128 - W) / g->Wp + 1);  // every output row of the item inside the tiles
     g->SP = (RW_MT * 128 + 2 * g->Wp + 2 + 7) & ~7;
     if (g->R < 1 || g->SP > RW_MAX_SP || g->R + 2 > 256) return false;
@@ -958,6 +990,28 @@ static bool rw_geometry(int H, int W, RwGeo* g) {
     if (fixed + 2 * rw_stage_bytes(g->SP) > RW_MAX_SMEM) return false;
     g->NS = (int)std::min<size_t>(4, (RW_MAX_SMEM - fixed) / rw_stage_bytes(g->SP));
     g->smem = std::max<size_t>(fixed + (size_t)g->NS * rw_stage_bytes(g->SP), (size_t)116 * 1024);
+    return true;
+}
+
+#ifndef BNN_RX_MINNS
+#define BNN_RX_MINNS 2  // stages kept before input boxes are added
+#endif
+// realin_dxn_kernel geometry: W divides 32, an item = 128 / W whole rows;
+// two stages, then as many input boxes as fit (5 at W = 32, 6 below), then
+// stages again up to 4
+static bool rx_geometry(int W, RwGeo* g) {
+    if (W < 4 || W > 32 || (32 % W) != 0) return false;
+    g->R = 128 / W;
+    g->Wp = W;
+    g->SP = rx_sp(W);
+    const size_t stage = rx_stage_bytes(W);
+    int nb = RX_MAXNB;
+    while (nb > 2 && rx_fixed_bytes(W, nb) + BNN_RX_MINNS * stage > RW_MAX_SMEM) --nb;
+    const size_t fixed = rx_fixed_bytes(W, nb);
+    if (fixed + 2 * stage > RW_MAX_SMEM) return false;
+    g->NB = nb;
+    g->NS = (int)std::min<size_t>(4, (RW_MAX_SMEM - fixed) / stage);
+    g->smem = std::max<size_t>(fixed + (size_t)g->NS * stage, (size_t)116 * 1024);
     return true;
 }
 
@@ -970,11 +1024,13 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     CUtensorMap tm;
     RwGeo geo;
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
-    if (g_first_kind == 0 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP && rw_geometry(H, W, &geo) &&
-        first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32)) {
+    const bool dxn = g_first_kind == 2 && d->rx_wu && rx_geometry(W, &geo);
+    if (g_first_kind != 1 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP &&
+        (dxn || rw_geometry(H, W, &geo)) &&
+        (dxn ? first_conv_tmap3(x, N, Cin, H, W, rx_npos(W), &tm) : first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32))) {
         CK(cudaMemsetAsync(a.rm_ctl, 0, 3 * sizeof(unsigned int), st));
         RealinWsParams p{};
-        p.wu = d->rw_wu; p.out = out;
+        p.wu = dxn ? d->rx_wu : d->rw_wu; p.out = out;
         for (int c = 0; c < 32; ++c) {
             p.thrC[c] = d->rw_thr[c].C;
             p.thr_neg |= (uint32_t)(d->rw_thr[c].sgn < 0) << c;
@@ -982,12 +1038,13 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         }
         p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
         p.N = N; p.Cin = Cin; p.H = H; p.W = W; p.Cout = Cout; p.cwo = cw_of(Cout);
-        p.R = geo.R; p.Wp = geo.Wp; p.SP = geo.SP; p.NS = geo.NS; p.KC = cdiv(Cin, 32);
+        p.R = geo.R; p.Wp = geo.Wp; p.SP = geo.SP; p.NS = geo.NS; p.NB = geo.NB; p.KC = cdiv(Cin, 32);
         p.ipi = cdiv(H, geo.R);
         p.n_items = N * p.ipi;
         p.c9 = first_conv_c9(Cin);
         const int grid = std::min(p.n_items, sm_count());
-        realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);
+        if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
+        else realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
@@ -1040,7 +1097,7 @@ static int run_stem(DevState* d, const Model* m, const float* x, int N, int H, i
     // 16 ch: 0.44 ms), wider ones the bulk-copy kernel (32 ch: 0.93 ms vs
     // 1.25 ms) where rows are 16-byte aligned and its ring fits;
     // set_first_conv_kernel(1) swaps the two
-    const bool want_bulk = (CB == 32) == (g_first_kind == 0);
+    const bool want_bulk = (CB == 32) == (g_first_kind != 1);
     {
         const int PXb = CB == 32 ? 2 : 4;
         const int nst = sb_stages(p.Cin, CB, PXb);
@@ -1542,8 +1599,9 @@ BNN_API int bnn_set_bconv_kernel(int kind) {
 }
 
 BNN_API int bnn_set_first_conv_kernel(int kind) {
-    if (kind != 0 && kind != 1)
-        return set_error(BNN_ERR_ARG, "first conv kernel kind %d (0 = tcgen05, 1 = mma.sync)", kind);
+    if (kind < 0 || kind > 2)
+        return set_error(BNN_ERR_ARG,
+                         "first conv kernel kind %d (0 = tcgen05, 1 = mma.sync, 2 = tcgen05 column taps in N)", kind);
     g_first_kind = kind;
     return BNN_OK;
 }

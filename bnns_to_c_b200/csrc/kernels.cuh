@@ -666,6 +666,14 @@ __device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int c0, int c1
                  : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int c0, int c1, int c2, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];\n" ::"r"(dst),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
     asm volatile(
@@ -2192,6 +2200,7 @@ struct RealinWsParams {
     unsigned int* ctl;     // [0] = entries, [1] = overflow / wait failure, [2] = outputs
     int cap, N, Cin, H, W, Cout, cwo;
     int R, Wp, SP, ipi, n_items, NS, KC;  // rows per item, staged width, staged positions, items per image
+    int NB;                // input box buffers (realin_dxn_kernel)
     float c9;              // e2 / T for a full 3x3 window, rounded up
 };
 
@@ -2487,6 +2496,389 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         }
     }
     if (warp == RW_NT / 32 - 1) {
+        tc_fence_after();
+        tc_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------
+// First conv on tcgen05 with the column taps in N, for W dividing 32. The
+// numerics are those of realin_ws_kernel (three int8 planes of
+// q = rint(x*2^18), the same error bound, thresholds and undecided list);
+// what changes is how often an operand tile crosses shared memory. An item
+// is 128 output pixels = RI = 128/W whole rows; its staged rows
+// y0-1 .. y0+RI are kept W wide (no zero column): staged position
+// s = 1 + row*W + col, with s = 0 and the tail as zero margins.
+// Planes 0 and 1: per kernel row dy ONE MMA, A = the plane from
+// s = 1 + dy*W (tile row i = staged pixel i + dy*W), B = the row's three
+// column taps stacked in N (N = 96, B row dx*32 + co), so TMEM column
+// dx*32 + co of lane i holds sum_dy x[i + dy*W] * w[dy][dx][co]; output o
+// takes dx = 0 from lane o-1, dx = 1 from lane o and dx = 2 from lane o+1
+// (warp shuffles: W divides 32, so a warp holds whole rows, and the taps
+// past a row's ends are left out). Plane 2 keeps the nine shifted MMAs
+// (N = 32), into two output-aligned blocks (taps 0-4 and 5-8, one per
+// issuer); its dx = 0 taps read a copy of the plane with column W-1
+// zeroed and its dx = 2 taps a copy with column 0 zeroed, so a shift never
+// wraps into the neighbouring row. An A tile thus crosses shared memory
+// 3 + 3 + 9 times per 32-band chunk, not 27. TMEM per item: 96 + 96 + 32
+// + 32 columns, two items in flight (columns 0 and 256).
+// Warps (16, so 128 registers a thread): 0-7 epilogue (warp w: TMEM lanes
+// 32*(w%4).., channels 16*(w/4)..; each writes its 16-bit half of the
+// output word), 8-13 producers (one staged pixel each), 14 and 15 MMA
+// issue (plane 0 + plane-2 taps 0-4 / plane 1 + taps 5-8: 8 and 7 MMAs a
+// chunk, each accumulator with one issuer). The second issuer also runs
+// the input stream: the boxes go through a ring of NB buffers, each
+// refilled as soon as the producers are done with it (NB - 1 boxes in
+// flight; an extra L2 prefetch further ahead measured slower); box
+// coordinates advance incrementally (no divisions on that path). The
+// tensor map is 3-D over the flattened image (H*W, bands, images): an
+// item's RI+2 rows are one contiguous run of NPOS floats per band, so a box
+// is 32 runs of NPOS*4 bytes (768 at W = 32) rather than 32*(RI+2) rows of
+// W*4 bytes; rows above or below the image fall outside the flattened
+// extent and read as zeros, and the box start (y0-1)*W*4 bytes is a
+// multiple of 16. Every wait is bounded as in
+// realin_ws_kernel.
+// ---------------------------------------------------------------------
+constexpr int RX_NEPI = 256;   // warps 0-7
+constexpr int RX_PROD0 = 8;    // first producer warp
+constexpr int RX_NPROD = 192;  // warps 8-13
+constexpr int RX_ISS0 = 14;    // warps 14-15 (15 also streams the input and allocates TMEM)
+constexpr int RX_NT = 512;
+constexpr int RX_NSLAB = 5;  // plane 0, plane 1, plane 2, plane 2 without column W-1, plane 2 without column 0
+constexpr size_t RX_WBYTES = (size_t)4 * 3 * 2 * 96 * 16;  // [chunk][dy][half][dx*32 + co][16 bands]
+constexpr int RX_MAXNB = 6;  // input box buffers, at most
+
+__host__ __device__ inline int rx_npos(int W) { return 128 + 2 * W; }  // staged pixels of an item
+__host__ __device__ inline int rx_sp(int W) { return (rx_npos(W) + 2 + 7) & ~7; }
+__host__ __device__ inline size_t rx_box_bytes(int W) { return (size_t)rx_npos(W) * 32 * 4; }
+__host__ __device__ inline size_t rx_stage_bytes(int W) { return (size_t)RX_NSLAB * 2 * rx_sp(W) * 16; }
+__host__ __device__ inline size_t rx_fixed_bytes(int W, int NB) {
+    return RX_WBYTES + NB * rx_box_bytes(W) + (size_t)2 * rx_npos(W) * 4;
+}
+
+// position of an input stream: chunk kc of this CTA's it-th item (items
+// blockIdx.x + it * gridDim.x, R rows each), advanced without divisions
+// except one per item
+struct RxCursor {
+    int it, kc, n, y0;
+    __device__ void set_item(const RealinWsParams& p, int it_) {
+        it = it_;
+        kc = 0;
+        const int item = (int)blockIdx.x + it * (int)gridDim.x;
+        n = item / p.ipi;
+        y0 = (item - n * p.ipi) * p.R;
+    }
+    __device__ void next(const RealinWsParams& p) {
+        if (++kc == p.KC) set_item(p, it + 1);
+    }
+};
+
+__global__ void __launch_bounds__(RX_NT, 1) realin_dxn_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                            const RealinWsParams p) {
+    extern __shared__ __align__(1024) unsigned char rx_smem[];
+    __shared__ __align__(8) unsigned long long boxf_b[RX_MAXNB], boxe_b[RX_MAXNB], full_b[4], empty_b[4], accf_b[2],
+        acce_b[2], bpxf_b[2], wrdy_b;
+    __shared__ uint32_t tmem_s;
+    __shared__ int abort_s;
+    volatile int* abort_v = &abort_s;
+
+    const int W = p.W, RI = p.R, SP = p.SP, NS = p.NS, KC = p.KC, NB = p.NB;
+    const int NPOS = rx_npos(W);
+    const size_t box_bytes = rx_box_bytes(W), stage_bytes = rx_stage_bytes(W);
+    unsigned char* boxes = rx_smem + RX_WBYTES;                        // [NB][32 bands][NPOS] f32
+    unsigned char* stages = boxes + NB * box_bytes;                    // [NS][5 slabs][2 halves][SP][16]
+    float* bpx = reinterpret_cast<float*>(stages + NS * stage_bytes);  // [2][NPOS] error bound per pixel
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int my_items = (int)blockIdx.x < p.n_items ? (p.n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    {
+        // the margins of every stage stay zero from here on
+        uint4* z = reinterpret_cast<uint4*>(stages);
+        const int nz = (int)(NS * stage_bytes / 16);
+        for (int i = tid; i < nz; i += RX_NT) z[i] = make_uint4(0u, 0u, 0u, 0u);
+        fence_async_smem();
+    }
+    if (warp == RX_ISS0 + 1) {
+        tc_alloc(smem_u32(&tmem_s), 512);
+        tc_relinquish();
+    }
+    if (tid == 0) {
+        abort_s = 0;
+        // one arrival per warp (lane 0, after the warp's writes): a per-thread
+        // arrival costs a shared-memory atomic on the same word per thread
+        for (int b = 0; b < NB; ++b) {
+            mbar_init(smem_u32(&boxf_b[b]), 1);
+            mbar_init(smem_u32(&boxe_b[b]), RX_NPROD / 32);
+        }
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_b[s]), RX_NPROD / 32);
+            mbar_init(smem_u32(&empty_b[s]), 2);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&accf_b[b]), 2);
+            mbar_init(smem_u32(&acce_b[b]), RX_NEPI / 32);
+            mbar_init(smem_u32(&bpxf_b[b]), RX_NPROD / 32);
+        }
+        mbar_init(smem_u32(&wrdy_b), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    const uint32_t sm0 = smem_u32(rx_smem);
+
+    if (warp >= RX_PROD0 && warp < RX_ISS0) {
+        // ------------------------------------------------------------ producers
+        const int pt = tid - RX_PROD0 * 32;  // staged pixel (row pt / W of the item's rows y0-1 .., column pt % W)
+        const bool live = pt < NPOS;
+        const int col = pt % W;
+        int stage = 0, seq = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        // warp-uniform control flow throughout (the arrivals follow a __syncwarp)
+        for (int it = 0; it < my_items && ok; ++it) {
+            float tsum = 0.0f, amax = 0.0f;
+            for (int kc = 0; kc < KC; ++kc, ++seq) {
+                const int bb = seq % NB;
+                bool go = mbar_wait_ab(smem_u32(&boxf_b[bb]), (uint32_t)(seq / NB) & 1u, abort_v);
+                if (go) go = mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v);
+                if (!__all_sync(0xffffffffu, go)) { ok = false; break; }
+                if (live) {
+                    const float* src = reinterpret_cast<const float*>(boxes + bb * box_bytes) + pt;  // band b: src[b*NPOS]
+                    // plane 0 = byte 2 (signed), plane 1 = byte 1, plane 2 = byte 0; word k = bands 4k..4k+3
+                    uint32_t w[3][8];
+#pragma unroll
+                    for (int g2 = 0; g2 < 4; g2 += 2) {  // 16 bands loaded at once
+                        float xv[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) xv[i] = src[(g2 * 8 + i) * NPOS];
+                        // sum |x| in two rounded-up chains (any order bounds the sum from above)
+                        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            s0 = __fadd_ru(s0, fabsf(xv[i]));
+                            s1 = __fadd_ru(s1, fabsf(xv[i + 1]));
+                            amax = fmaxf(amax, fmaxf(fabsf(xv[i]), fabsf(xv[i + 1])));
+                        }
+                        tsum = __fadd_ru(tsum, __fadd_ru(s0, s1));
+#pragma unroll
+                        for (int g = g2; g < g2 + 2; ++g) {
+                            uint32_t qv[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                // x * 2^18 is exact, so this single rounding is rint(x * 2^18) (rm_fix)
+                                qv[i] = (uint32_t)(__float_as_int(__fmaf_rn(xv[(g - g2) * 8 + i], (float)(1 << RM_FIX),
+                                                                           12582912.0f)) -
+                                                   0x4B400000);
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t lo0 = __byte_perm(qv[h * 4 + 0], qv[h * 4 + 1], 0x5140);
+                                const uint32_t hi0 = __byte_perm(qv[h * 4 + 2], qv[h * 4 + 3], 0x5140);
+                                w[2][g * 2 + h] = __byte_perm(lo0, hi0, 0x5410);  // bytes 0
+                                w[1][g * 2 + h] = __byte_perm(lo0, hi0, 0x7632);  // bytes 1
+                                w[0][g * 2 + h] = __byte_perm(__byte_perm(qv[h * 4 + 0], qv[h * 4 + 1], 0x6262),
+                                                              __byte_perm(qv[h * 4 + 2], qv[h * 4 + 3], 0x6262),
+                                                              0x5410);  // bytes 2
+                            }
+                        }
+                    }
+                    unsigned char* st = stages + stage * stage_bytes + (size_t)(1 + pt) * 16;
+                    const size_t half = (size_t)SP * 16;  // bytes between the two 16-band halves of a slab
+#pragma unroll
+                    for (int pl = 0; pl < 3; ++pl) {
+                        *reinterpret_cast<uint4*>(st + (2 * pl) * half) = make_uint4(w[pl][0], w[pl][1], w[pl][2], w[pl][3]);
+                        *reinterpret_cast<uint4*>(st + (2 * pl + 1) * half) =
+                            make_uint4(w[pl][4], w[pl][5], w[pl][6], w[pl][7]);
+                    }
+                    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                    const uint4 lo = make_uint4(w[2][0], w[2][1], w[2][2], w[2][3]);
+                    const uint4 hi = make_uint4(w[2][4], w[2][5], w[2][6], w[2][7]);
+                    const bool last = col == W - 1, first = col == 0;
+                    *reinterpret_cast<uint4*>(st + 6 * half) = last ? z : lo;
+                    *reinterpret_cast<uint4*>(st + 7 * half) = last ? z : hi;
+                    *reinterpret_cast<uint4*>(st + 8 * half) = first ? z : lo;
+                    *reinterpret_cast<uint4*>(st + 9 * half) = first ? z : hi;
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(&full_b[stage]));
+                    mbar_arrive(smem_u32(&boxe_b[bb]));
+                }
+                if (++stage == NS) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            // error bounds of this item's staged pixels, once the epilogue is
+            // done with the item that used this table two items ago
+            const int buf = it & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_ab(smem_u32(&acce_b[buf]), (uint32_t)((it >> 1) & 1) ^ 1u, abort_v)))
+                break;
+            const float rnd = __fmul_ru((float)p.Cin, 1.0f / (float)(1 << (RM_FIX + 1)));
+            // NaN inputs: tsum is NaN, and so is the bound
+            if (live) bpx[buf * NPOS + pt] = amax < 16.0f ? __fmaf_ru(p.c9, tsum, rnd) : __int_as_float(0x7f800000);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bpxf_b[buf]));
+        }
+    } else if (warp >= RX_ISS0) {
+        // ------------------------------------------------------------ MMA issuers
+        const int u = warp - RX_ISS0;
+        const int nseq = my_items * KC;
+        RxCursor cur;  // input stream (issuer 1): the next box to load
+        auto load_box = [&](int seq) {  // chunk seq (the cursor's) into buffer seq % NB
+            const uint32_t bar = smem_u32(&boxf_b[seq % NB]);
+            mbar_expect_tx(bar, (uint32_t)box_bytes);
+            // rows y0-1 .. y0+RI of the flattened image: one (NPOS, 32, 1) box
+            tma_load_3d(sm0 + (uint32_t)(RX_WBYTES + (seq % NB) * box_bytes), &tmap, (cur.y0 - 1) * W, cur.kc * 32,
+                        cur.n, bar);
+            cur.next(p);
+        };
+        if (u == 1 && lane == 0) {
+            mbar_expect_tx(smem_u32(&wrdy_b), (uint32_t)RX_WBYTES);
+            bulk_g2s(sm0, p.wu, (uint32_t)RX_WBYTES, smem_u32(&wrdy_b));
+            cur.set_item(p, 0);
+            for (int s2 = 0; s2 < NB && s2 < nseq; ++s2) load_box(s2);
+        }
+        if (lane == 0 && mbar_wait_ab(smem_u32(&wrdy_b), 0u, abort_v)) {
+            // A: plane 0 signed, planes 1-2 unsigned; B signed; D s32; M = 128
+            const uint32_t id_s96 = (2u << 4) | (1u << 7) | (1u << 10) | ((96u >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t id_u96 = (2u << 4) | (0u << 7) | (1u << 10) | ((96u >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t id_u32 = (2u << 4) | (0u << 7) | (1u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t sbase0 = sm0 + (uint32_t)(RX_WBYTES + NB * box_bytes);
+            int stage = 0, seq = 0;
+            uint32_t phase = 0;
+            for (int it = 0; it < my_items && !*abort_v; ++it) {
+                const int buf = it & 1;
+                if (!mbar_wait_ab(smem_u32(&acce_b[buf]), (uint32_t)((it >> 1) & 1) ^ 1u, abort_v)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * 256);
+                bool ok = true;
+                for (int kc = 0; kc < KC; ++kc, ++seq) {
+                    if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
+                    tc_fence_after();
+                    if (u == 1 && seq + NB < nseq) {
+                        // the producers arrive on the box right after the stage: refill its buffer
+                        // (measured: refilling after this chunk's MMAs instead is slower)
+                        if (!mbar_wait_ab(smem_u32(&boxe_b[seq % NB]), (uint32_t)(seq / NB) & 1u, abort_v)) {
+                            ok = false;
+                            break;
+                        }
+                        load_box(seq + NB);
+                    }
+                    const uint32_t sb = sbase0 + (uint32_t)(stage * stage_bytes);
+                    const uint32_t wb = sm0 + (uint32_t)(kc * 3 * 3072);
+                    // plane u: one N = 96 MMA per kernel row
+#pragma unroll
+                    for (int dy = 0; dy < 3; ++dy)
+                        tc_mma_i8(d + u * 96, tc_desc(sb + (uint32_t)(u * 2 * SP + 1 + dy * W) * 16, (uint32_t)SP * 16),
+                                  tc_desc(wb + dy * 3072, 1536), u == 0 ? id_s96 : id_u96, (kc > 0 || dy > 0) ? 1u : 0u);
+                    // plane 2: taps 0-4 (issuer 0) or 5-8 (issuer 1), shifted N = 32 MMAs
+                    // (dx = 0 from slab 3, dx = 2 from slab 4)
+                    const int t0 = u == 0 ? 0 : 5, t1 = u == 0 ? 5 : 9;
+#pragma unroll 1
+                    for (int t = t0; t < t1; ++t) {
+                        const int dy = t / 3, dx = t % 3, slab = dx == 0 ? 3 : (dx == 2 ? 4 : 2);
+                        tc_mma_i8(d + 192 + u * 32,
+                                  tc_desc(sb + (uint32_t)((2 * slab) * SP + dy * W + dx) * 16, (uint32_t)SP * 16),
+                                  tc_desc(wb + dy * 3072 + dx * 512, 1536), id_u32, (kc > 0 || t > t0) ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(&empty_b[stage]));
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(smem_u32(&accf_b[buf]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // warp w: TMEM lanes 32*(w%4).. = outputs 32*(w%4).. of the item
+        // (whole rows), channels c0 .. c0+15 with c0 = 16*(w/4)
+        const int quad = warp & 3, c0 = (warp >> 2) * 16, o = quad * 32 + lane;
+        const int orow = o / W, ocol = o - orow * W;
+        const bool has_l = ocol > 0, has_r = ocol < W - 1;
+        for (int it = 0; it < my_items; ++it) {
+            const int buf = it & 1;
+            const int item = (int)blockIdx.x + it * (int)gridDim.x;
+            const int n = item / p.ipi, y = (item - n * p.ipi) * RI + orow;
+            // warp-uniform exit: the TMEM loads and shuffles below need the whole warp
+            bool go = !*abort_v;
+            if (go) go = mbar_wait_ab(smem_u32(&accf_b[buf]), (uint32_t)(it >> 1) & 1u, abort_v);
+            if (go) go = mbar_wait_ab(smem_u32(&bpxf_b[buf]), (uint32_t)(it >> 1) & 1u, abort_v);
+            if (!__all_sync(0xffffffffu, go)) break;
+            tc_fence_after();
+            const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + c0);
+            // planes 0-1 of the column taps 0 and 1 (issued before the bound is summed)
+            uint32_t a[4][16];
+            tc_ld16(ta, a[0]);
+            tc_ld16(ta + 96, a[1]);
+            tc_ld16(ta + 32, a[2]);
+            tc_ld16(ta + 128, a[3]);
+            const bool valid = y < p.H;
+            const float* bt = bpx + buf * NPOS;
+            float ef = 0.0f;
+            if (valid) {
+                // staged pixel of tap (dy, dx) = o + dy*W + dx - 1
+#pragma unroll
+                for (int dy = 0; dy < 3; ++dy) {
+                    if (has_l) ef = __fadd_ru(ef, bt[o + dy * W - 1]);
+                    ef = __fadd_ru(ef, bt[o + dy * W]);
+                    if (has_r) ef = __fadd_ru(ef, bt[o + dy * W + 1]);
+                }
+            }
+            // E = ceil(e * 2^18) (exact scaling); e past 2^40, inf or NaN: nothing is decided
+            const bool finite = ef <= 1.0995116e12f;
+            const long long E = finite ? __float2ll_ru(ef * 262144.0f) : 0ll;
+            tc_wait_ld();
+            // v = 2^8 * S0 + S1 of the three column taps at this output
+            int v[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int s = __shfl_up_sync(0xffffffffu, (int)a[0][k] * 256 + (int)a[1][k], 1);
+                v[k] = (has_l ? s : 0) + (int)a[2][k] * 256 + (int)a[3][k];
+            }
+            tc_ld16(ta + 64, a[0]);
+            tc_ld16(ta + 160, a[1]);
+            tc_ld16(ta + 192, a[2]);  // plane 2, output-aligned: taps 0-4
+            tc_ld16(ta + 224, a[3]);  // and 5-8
+            tc_wait_ld();
+            uint32_t bits = 0u, und = 0u;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int s = __shfl_down_sync(0xffffffffu, (int)a[0][k] * 256 + (int)a[1][k], 1);
+                const int co = c0 + k;
+                if (co >= p.Cout) continue;
+                const long long Q =
+                    (long long)(v[k] + (has_r ? s : 0)) * 256 + (long long)((int)a[2][k] + (int)a[3][k]);
+                const long long Qs = (p.thr_neg >> co) & 1u ? -Q : Q;
+                const long long C = p.thrC[co];
+                const bool ok = finite && !((p.thr_exact >> co) & 1u);
+                if (ok && Qs - E >= C) bits |= 1u << k;
+                else if (!(ok && Qs + E < C)) und |= 1u << co;
+            }
+            if (valid) {
+                // this warp's 16-bit half of the pixel's output word (cwo = 1)
+                const size_t pix = ((size_t)n * p.H + y) * W + ocol;
+                reinterpret_cast<uint16_t*>(p.out + pix)[c0 >> 4] = (uint16_t)bits;
+                if (und) realin_list(p.list, p.ctl, p.cap, pix, 0, und);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce_b[buf]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
+        // let any MMA or copy still in flight land before TMEM and shared
+        // memory are released; the fix-up then recomputes the batch exactly
+        for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
+        if (tid == 0) {
+            atomicExch(p.ctl + 1, 1u);
+            atomicAdd(&g_bnn_wait_timeouts, 1u);
+        }
+    }
+    if (warp == RX_ISS0 + 1) {
         tc_fence_after();
         tc_dealloc(tmem, 512);
     }

@@ -220,8 +220,10 @@ int rdev_init(const ModelR* m, RDev* d) {
                              (int)react::C4Cfg<32>::SMEM));
     {
         const int sm = react::PROJ_MAX_CIN * react::PROJ_CB * 4;
-#define PROJ_ATTR(px, cat, tap) \
-    RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm))
+#define PROJ_ATTR(px, cat, tap)                                                                             \
+    RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             sm));                                                                                  \
+    RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm))
         PROJ_ATTR(1, false, false); PROJ_ATTR(4, false, false); PROJ_ATTR(1, false, true);
         PROJ_ATTR(4, false, true); PROJ_ATTR(1, true, true); PROJ_ATTR(4, true, true);
 #undef PROJ_ATTR
@@ -429,7 +431,12 @@ int run_proj(const RBlockDev& D, const float* x0, int c0, const float* x1, int c
     const int PX = v4 ? 4 : 1;
     const dim3 grid(cdiv((long long)N * HW / PX, 256), cdiv(D.Cout, react::PROJ_CB));
     const size_t smem = (size_t)D.Cin * react::PROJ_CB * 4;
-#define PROJ_LAUNCH(px, cat, tap) react::proj_tap_kernel<px, cat, tap><<<grid, 256, smem, st>>>(p)
+    const bool all_fused = p.nfull == HW;
+#define PROJ_LAUNCH(px, cat, tap)                                                          \
+    do {                                                                                   \
+        if (all_fused) react::proj_tap_kernel<px, cat, tap, 1><<<grid, 256, smem, st>>>(p); \
+        else react::proj_tap_kernel<px, cat, tap, 0><<<grid, 256, smem, st>>>(p);          \
+    } while (0)
     if (x1) {
         if (v4) PROJ_LAUNCH(4, true, true);
         else PROJ_LAUNCH(1, true, true);

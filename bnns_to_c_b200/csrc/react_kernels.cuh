@@ -162,7 +162,8 @@ __device__ __forceinline__ void proj_body(const ProjParams& p, const float* sw, 
     }
 }
 
-template <int PX, bool CAT, bool TAP>
+// MODE 1: every pixel fused (nfull = H*W); MODE 0: per pixel, fused below nfull
+template <int PX, bool CAT, bool TAP, int MODE>
 __global__ void __launch_bounds__(256, 2) proj_tap_kernel(const ProjParams p) {
     constexpr int CB = PROJ_CB;
     extern __shared__ __align__(16) float sw[];  // [Cin][CB]
@@ -178,16 +179,16 @@ __global__ void __launch_bounds__(256, 2) proj_tap_kernel(const ProjParams p) {
     const long long pix = g * PX;
     const int n = (int)(pix / HW), q = (int)(pix - (long long)n * HW);
     const int y = q / p.W, x = q - y * p.W;
-    const bool fused = q < p.nfull;  // a group never straddles nfull (both multiples of PX)
+    const bool fused = MODE == 1 || q < p.nfull;  // a group never straddles nfull (both multiples of PX)
     if constexpr (TAP) {
         if (blockIdx.y == 0) {
             if (fused) proj_body<PX, CAT, true, true>(p, sw, n, q, y, x, pix);
-            else proj_body<PX, CAT, true, false>(p, sw, n, q, y, x, pix);
+            else if constexpr (MODE == 0) proj_body<PX, CAT, true, false>(p, sw, n, q, y, x, pix);
             return;
         }
     }
     if (fused) proj_body<PX, CAT, false, true>(p, sw, n, q, y, x, pix);
-    else proj_body<PX, CAT, false, false>(p, sw, n, q, y, x, pix);
+    else if constexpr (MODE == 0) proj_body<PX, CAT, false, false>(p, sw, n, q, y, x, pix);
 }
 
 // ---------------------------------------------------------------------

@@ -83,7 +83,10 @@ int bnn_forward_patched_device(const Model *m, int device, const float *d_cube,
 int bnn_set_bconv_kernel(int kind);
 
 /* Process-wide choice of the first conv's tensor-core kernel (A/B testing):
- * 0 = tcgen05 (default; shapes it cannot stage fall back to 1), 1 = mma.sync.
+ * 0 = tcgen05, nine shifted taps (default; shapes it cannot stage fall back
+ * to 1), 1 = mma.sync, 2 = tcgen05 with the three column taps of a kernel
+ * row stacked in the MMA's N where the width divides 32 (kind 0 for other
+ * widths).
  * Both decide every output by the same error bound and fix up the rest in
  * the reference's fp32 order, so both give the reference's bits. For a v2
  * model's stem: 0 = the measured-faster of its two exact-order kernels for

@@ -260,9 +260,10 @@ def test_multi_device_shards_match_single():
 
 
 # ------------------------------------------------------------------ first conv: tensor-core path
-@pytest.fixture(params=["tc", "mma"])
+@pytest.fixture(params=["tc", "mma", "tcn"])
 def first_kind(request):
-    """Both first-conv tensor-core kernels (tcgen05, mma.sync); no bounded
+    """Every first-conv tensor-core kernel (tcgen05 nine-tap, mma.sync,
+    tcgen05 with the column taps in N where W divides 32); no bounded
     device wait may have given up while it ran."""
     bn.set_first_conv_kernel(request.param)
     before = bn.device_wait_timeouts(0)
@@ -356,12 +357,13 @@ def test_first_conv_nonfinite_and_extreme_inputs(first_kind):
 
 
 @pytest.mark.parametrize("H,W", [(17, 40), (33, 33), (64, 16), (16, 16), (16, 100), (40, 64), (21, 252),
-                                 (16, 124)])
+                                 (16, 124), (17, 16), (21, 16), (31, 32), (18, 32)])
 def test_first_conv_tensor_path_odd_sizes(H, W, first_kind):
-    """Sizes that exercise the tcgen05 kernel's row items (several per
-    image, a short last one, one image per item, wide rows) and the shapes
-    it hands back to the mma.sync kernel (W not a multiple of 4, boxes too
-    big for shared memory)."""
+    """Sizes that exercise the tcgen05 kernels' row items (several per
+    image, a short last one, one image per item, wide rows; the column-taps
+    kernel's items of 8 rows at W = 16 and 4 rows at W = 32 with 1 to 3 rows
+    left for the last) and the shapes handed back to the mma.sync kernel
+    (W not a multiple of 4, boxes too big for shared memory)."""
     m = _model(base=16, seed=3)
     x = synth(46, 0, 3, 120, H, W)
     fast, _ = _first_conv_bits(m, x, False)
