@@ -224,9 +224,15 @@ int rdev_init(const ModelR* m, RDev* d) {
     RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                              sm));                                                                                  \
     RCK(cudaFuncSetAttribute(react::proj_tap_kernel<px, cat, tap, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm))
-        PROJ_ATTR(1, false, false); PROJ_ATTR(4, false, false); PROJ_ATTR(1, false, true);
-        PROJ_ATTR(4, false, true); PROJ_ATTR(1, true, true); PROJ_ATTR(4, true, true);
+        PROJ_ATTR(1, false, false); PROJ_ATTR(1, false, true); PROJ_ATTR(1, true, true);
 #undef PROJ_ATTR
+        const int sa = sm + react::PROJ_D * 256 * 16;
+#define PROJ_ATTR_A(cat, tap)                                                                                  \
+    RCK(cudaFuncSetAttribute(react::proj_async_kernel<cat, tap, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             sa));                                                                             \
+    RCK(cudaFuncSetAttribute(react::proj_async_kernel<cat, tap, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sa))
+        PROJ_ATTR_A(false, false); PROJ_ATTR_A(false, true); PROJ_ATTR_A(true, true);
+#undef PROJ_ATTR_A
     }
     RCK(cudaStreamCreateWithFlags(&d->cs, cudaStreamNonBlocking));
     RCK(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
@@ -431,22 +437,21 @@ int run_proj(const RBlockDev& D, const float* x0, int c0, const float* x1, int c
     const int PX = v4 ? 4 : 1;
     const dim3 grid(cdiv((long long)N * HW / PX, 256), cdiv(D.Cout, react::PROJ_CB));
     const size_t smem = (size_t)D.Cin * react::PROJ_CB * 4;
+    const size_t smem_a = smem + (size_t)react::PROJ_D * 256 * 16;  // + the cp.async slots
     const bool all_fused = p.nfull == HW;
-#define PROJ_LAUNCH(px, cat, tap)                                                          \
-    do {                                                                                   \
-        if (all_fused) react::proj_tap_kernel<px, cat, tap, 1><<<grid, 256, smem, st>>>(p); \
-        else react::proj_tap_kernel<px, cat, tap, 0><<<grid, 256, smem, st>>>(p);          \
+#define PROJ_LAUNCH(cat, tap)                                                                              \
+    do {                                                                                                   \
+        if (v4) {                                                                                          \
+            if (all_fused) react::proj_async_kernel<cat, tap, 1><<<grid, 256, smem_a, st>>>(p);             \
+            else react::proj_async_kernel<cat, tap, 0><<<grid, 256, smem_a, st>>>(p);                      \
+        } else {                                                                                           \
+            if (all_fused) react::proj_tap_kernel<1, cat, tap, 1><<<grid, 256, smem, st>>>(p);              \
+            else react::proj_tap_kernel<1, cat, tap, 0><<<grid, 256, smem, st>>>(p);                       \
+        }                                                                                                  \
     } while (0)
-    if (x1) {
-        if (v4) PROJ_LAUNCH(4, true, true);
-        else PROJ_LAUNCH(1, true, true);
-    } else if (bits) {
-        if (v4) PROJ_LAUNCH(4, false, true);
-        else PROJ_LAUNCH(1, false, true);
-    } else {
-        if (v4) PROJ_LAUNCH(4, false, false);
-        else PROJ_LAUNCH(1, false, false);
-    }
+    if (x1) PROJ_LAUNCH(true, true);
+    else if (bits) PROJ_LAUNCH(false, true);
+    else PROJ_LAUNCH(false, false);
 #undef PROJ_LAUNCH
     return launched("proj");
 }

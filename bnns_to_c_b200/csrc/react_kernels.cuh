@@ -192,6 +192,138 @@ __global__ void __launch_bounds__(256, 2) proj_tap_kernel(const ProjParams p) {
 }
 
 // ---------------------------------------------------------------------
+// The same projection with its input streamed by cp.async (4 pixels per
+// thread, W % 4 == 0): each thread copies its own 16 bytes of channel
+// ci + PROJ_D into a private ring of PROJ_D shared-memory slots while it
+// multiplies channel ci, so PROJ_D channels of loads are in flight per
+// thread without holding registers (the register-fed kernel keeps one or two
+// and is latency-bound). A thread only reads slots it filled, so the waits
+// are per thread (cp.async.wait_group), no block barrier. The upsampled
+// channels of a decoder's concat are one 8-byte copy of the two source
+// pixels when the 4-pixel group is covered and 8-byte aligned, else four
+// 4-byte copies with zero fill outside the covered rectangle. The
+// multiply-adds and their order are proj_step's.
+// ---------------------------------------------------------------------
+constexpr int PROJ_D = 8;
+
+__device__ __forceinline__ void cpa16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
+}
+// 4 bytes, or 4 zero bytes when !valid (src-size 0 reads nothing)
+__device__ __forceinline__ void cpa4z(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <bool CAT, bool TAP, int MODE>
+__global__ void __launch_bounds__(256, 2) proj_async_kernel(const ProjParams p) {
+    constexpr int CB = PROJ_CB, PX = 4, D = PROJ_D;
+    extern __shared__ __align__(16) float sw[];  // [Cin][CB], then the slots [D][256] x 16 bytes
+    {
+        const float4* src = reinterpret_cast<const float4*>(p.w + (size_t)blockIdx.y * p.Cin * CB);
+        float4* dst = reinterpret_cast<float4*>(sw);
+        for (int i = threadIdx.x; i < p.Cin * CB / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    const int HW = p.H * p.W;
+    const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g * PX >= (long long)p.N * HW) return;
+    const long long pix = g * PX;
+    const int n = (int)(pix / HW), q = (int)(pix - (long long)n * HW);
+    const int y = q / p.W, x = q - y * p.W;
+    const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(sw + p.Cin * CB) + threadIdx.x * 16u;
+    const float* x0p = p.x0 + (size_t)n * p.c0 * HW + q;
+    // the upsampled channels' sources (CAT)
+    int off[PX] = {0, 0, 0, 0};
+    bool in[PX] = {false, false, false, false};
+    bool pair = false;
+    const float* x1p = nullptr;
+    int hw1 = 0;
+    if constexpr (CAT) {
+        const int yy = y - p.oh;
+        const bool yin = (unsigned)yy < (unsigned)p.cH;
+#pragma unroll
+        for (int j = 0; j < PX; ++j) {
+            const int xx = x + j - p.ow;
+            in[j] = yin && (unsigned)xx < (unsigned)p.cW;
+            off[j] = in[j] ? (yy >> 1) * p.w1 + (xx >> 1) : 0;
+        }
+        hw1 = p.h1 * p.w1;
+        x1p = p.x1 + (size_t)n * p.c1 * hw1;
+        pair = in[0] && in[3] && ((x - p.ow) & 3) == 0 && (hw1 & 1) == 0 &&
+               ((reinterpret_cast<uintptr_t>(x1p + off[0]) & 7) == 0);
+    }
+    auto issue = [&](int ci) {  // channel ci into slot ci % D (one commit group per call)
+        if (ci < p.Cin) {
+            const uint32_t dst = slot0 + (uint32_t)(ci % D) * (256u * 16u);
+            if (!CAT || ci < p.c0) {
+                cpa16(dst, x0p + (size_t)ci * HW);
+            } else {
+                const float* src = x1p + (size_t)(ci - p.c0) * hw1;
+                if (pair) {
+                    cpa8(dst, src + off[0]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < PX; ++j) cpa4z(dst + 4u * j, src + off[j], in[j]);
+                }
+            }
+        }
+        cpa_commit();
+    };
+    float2 acc[PX][CB / 2];
+#pragma unroll
+    for (int j = 0; j < PX; ++j)
+#pragma unroll
+        for (int c = 0; c < CB / 2; ++c) acc[j][c] = make_float2(0.0f, 0.0f);
+    uint32_t word[PX];
+#pragma unroll
+    for (int j = 0; j < PX; ++j) word[j] = 0u;
+#pragma unroll
+    for (int k = 0; k < D; ++k) issue(k);
+    const bool fused = MODE == 1 || q < p.nfull;  // a group never straddles nfull (both multiples of 4)
+    for (int ci = 0; ci < p.Cin; ++ci) {
+        cpa_wait<D - 1>();  // channel ci has landed
+        const float* sl = sw + p.Cin * CB + (size_t)(ci % D) * 256 * 4 + threadIdx.x * 4;
+        float xv[PX];
+        if (CAT && ci >= p.c0 && pair) {
+            const float2 t = *reinterpret_cast<const float2*>(sl);
+            xv[0] = t.x; xv[1] = t.x; xv[2] = t.y; xv[3] = t.y;
+        } else {
+            const float4 t = *reinterpret_cast<const float4*>(sl);
+            xv[0] = t.x; xv[1] = t.y; xv[2] = t.z; xv[3] = t.w;
+        }
+        const bool tap = TAP && blockIdx.y == 0;
+        if (fused) {
+            if (tap) proj_step<PX, TAP, true>(acc, xv, sw, ci, p, word, pix);
+            else proj_step<PX, false, true>(acc, xv, sw, ci, p, word, pix);
+        } else if constexpr (MODE == 0) {
+            if (tap) proj_step<PX, TAP, false>(acc, xv, sw, ci, p, word, pix);
+            else proj_step<PX, false, false>(acc, xv, sw, ci, p, word, pix);
+        }
+        issue(ci + D);  // into the slot just read (its value is in xv, already used)
+    }
+    cpa_wait<0>();
+#pragma unroll
+    for (int c = 0; c < CB; ++c) {
+        const int co = blockIdx.y * CB + c;
+        if (co >= p.Cout) break;
+        float* o = p.out + ((size_t)n * p.Cout + co) * HW + q;
+        *reinterpret_cast<float4*>(o) = (c & 1) ? make_float4(acc[0][c >> 1].y, acc[1][c >> 1].y, acc[2][c >> 1].y,
+                                                              acc[3][c >> 1].y)
+                                                : make_float4(acc[0][c >> 1].x, acc[1][c >> 1].x, acc[2][c >> 1].x,
+                                                              acc[3][c >> 1].x);
+    }
+}
+
+// ---------------------------------------------------------------------
 // enc1.conv1: real input, +-1 weights, 3x3 pad 1, register-blocked order
 // (csrc/bnn_realin_blk.h:90-150, Cout % 8 == 0): each output's sum runs band
 // by band and, inside a band, over the taps row by row (ky, then kx), one
