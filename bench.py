@@ -61,6 +61,14 @@ REACT_METRIC = "ReAct UNet patches/s (64x64x120)"
 FFMA_PER_CLK_SM = 128       # fp32 fused multiply-adds / clock / SM (nominal; probe: 119)
 SEED_MODEL, SEED_INPUT = 0, 1
 POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 17 binary-conv
+# launches of one forward of the default workload, from one ncu launch list of a
+# 512-patch forward (profiles/unet_c32_512x32x32_dram_launches.md); scaled by
+# patches in the bench line
+BCONV_DRAM_BYTES_PER_512 = 24.14e6
+# bit planes the 17 binary convs read and write per 32x32 patch at base 32
+# (inputs, concat halves, outputs and pooled outputs)
+BCONV_ALGO_BYTES_PER_PATCH = 58112
 MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (probe-measured on this pool)
 
 
@@ -358,16 +366,21 @@ def run_ours(args):
             "roofline": (
                 {"bound": "tensor",
                  "kernel": ("bconv_ws_kernel + bconv_ws_pool_kernel (17 fused binary convs, tcgen05 int8, "
-                            "persistent warp-specialised)") if args.bconv == "tc" else
+                            "persistent warp-specialised)") if args.bconv in ("tc", "tcx") else
                            "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
                  "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
                  "unit": "Gbitop/s (1 bitop = 1 binary MAC, run as one int8 MAC)",
-                 "frac": round(bconv_ach / tensor_i8_peak, 4), "traffic": None,
+                 "frac": round(bconv_ach / tensor_i8_peak, 4),
+                 "traffic": round(BCONV_DRAM_BYTES_PER_512 * P / 512) if (H, W) == (32, 32) and not stem else None,
+                 "traffic_scope": "DRAM bytes of the 17 binary-conv launches of one forward (ncu, 512-patch "
+                                  "capture scaled by patches); their bit planes stay mostly in L2",
+                 "algorithmic_bytes": BCONV_ALGO_BYTES_PER_PATCH * P if (H, W) == (32, 32) and not stem else None,
                  "peak_source": "int8 dense tensor rate = 2x the measured cuBLAS bf16 rate in MEASURED_PEAKS.json"
                  if bf16 else "fallback 2.25 P int8 MAC/s",
                  "frac_of_mma_sync_measured": round(bconv_ach / mma_sync_peak, 4),
+                 "frac_of_popc_peak": round(bconv_ach / popc_peak, 4),
                  "time_share": frac_split.get("bconv")}
-                if args.bconv in ("tc", "mma") else
+                if args.bconv in ("tc", "tcx", "mma") else
                 {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
                  "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
                  "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
@@ -694,9 +707,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
     ap.add_argument("--first", default="tc", choices=["tc", "mma", "tcn"],
                     help="first conv kernel: tcgen05 (default) or mma.sync")
-    ap.add_argument("--bconv", default="tc", choices=["tc", "popc", "mma"],
-                    help="binary-conv kernels: tc = tcgen05 + mma.sync (default), popc = XOR + POPC, "
-                         "mma = mma.sync for every layer")
+    ap.add_argument("--bconv", default="tc", choices=["tc", "tcx", "popc", "mma"],
+                    help="binary-conv kernels: tc = tcgen05 + mma.sync (default), tcx = the same with the "
+                         "column taps in N at 32 channels, popc = XOR + POPC, mma = mma.sync for every layer")
     ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem", "react"],
                     help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler; "
                          "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem); "

@@ -478,9 +478,10 @@ class BconvLayer:
 
 
 def set_bconv_kernel(kind: str):
-    """'tc' (tcgen05 + mma.sync, default), 'popc' (XOR + POPC) or 'mma'
-    (mma.sync for every layer)."""
-    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2}[kind]))
+    """'tc' (tcgen05 with nine shifted taps + mma.sync, default), 'popc'
+    (XOR + POPC), 'mma' (mma.sync for every layer) or 'tcx' (as 'tc', with
+    the column taps in N for the non-pooled layers of at most 32 channels)."""
+    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2, "tcx": 3}[kind]))
 
 
 def set_first_conv_kernel(kind):

@@ -48,6 +48,7 @@ struct BinLayer {
     int8_t* w8 = nullptr;     // mma.sync kernel weights [Kw][9][CoutP][32]
     int8_t* wu = nullptr;     // tcgen05 kernel weights [Cout/ubn][Kw][9][2][ubn][16]
     int ubn = 0;              // tcgen05 channel block (N of one MMA)
+    int8_t* wx = nullptr;     // ubn == 32: the same weights for bconv_wsx_kernel [Kw][3 dy][2][3 dx][32][16]
     FoldIv* fold = nullptr;
     FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
 };
@@ -207,7 +208,7 @@ static FoldIv to_iv(int type, int t, int lo, int hi) {
 
 struct HostBin {
     std::vector<uint32_t> wt;
-    std::vector<int8_t> w8, wu;
+    std::vector<int8_t> w8, wu, wx;
     std::vector<int> wpop;
     std::vector<FoldIv> fold, fold2;
 };
@@ -269,6 +270,19 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
                     for (int c = 0; c < bn && cb * bn + c < Cout; ++c)
                         memcpy(&h.wu[((((size_t)cb * L.Kw + kw) * 9 + t) * 2 + hh) * bn * 16 + (size_t)c * 16],
                                &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32 + hh * 16], 16);
+    // 32-channel layers: the column taps of a kernel row stacked in N for
+    // bconv_wsx_kernel ([word][dy][16-byte K half][dx][channel][16 bytes])
+    h.wx.clear();
+    if (bn == 32) {
+        h.wx.assign((size_t)L.Kw * 3 * 2 * 3 * 32 * 16, (int8_t)0);
+        for (int kw = 0; kw < L.Kw; ++kw)
+            for (int dy = 0; dy < 3; ++dy)
+                for (int hh = 0; hh < 2; ++hh)
+                    for (int dx = 0; dx < 3; ++dx)
+                        for (int c = 0; c < Cout; ++c)
+                            memcpy(&h.wx[((((size_t)kw * 3 + dy) * 2 + hh) * 3 + dx) * 32 * 16 + (size_t)c * 16],
+                                   &h.w8[(((size_t)kw * 9 + dy * 3 + dx) * L.CoutP + c) * 32 + hh * 16], 16);
+    }
 }
 
 static void folds_of(const Act* a, int CoutP, std::vector<FoldIv>& v) {
@@ -294,6 +308,11 @@ template <int BN, int MT>
 static cudaError_t attr_ws() {
     return cudaFuncSetAttribute(bconv_ws_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)WsCfg<BN, MT>::max_smem);
+}
+template <int MT>
+static cudaError_t attr_wsx() {
+    return cudaFuncSetAttribute(bconv_wsx_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)WsxCfg<MT>::max_smem);
 }
 template <int BN>
 static cudaError_t attr_bmma() {
@@ -335,7 +354,7 @@ static int set_kernel_attrs(int device) {
         (e = attr_ws<32, 8>()) != cudaSuccess || (e = attr_ws<64, 4>()) != cudaSuccess ||
         (e = attr_ws<128, BNN_WS128_MT>()) != cudaSuccess || (e = attr_ws<256, BNN_WS256_MT>()) != cudaSuccess ||
         (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
-        (e = attr_ws_pool<128, 1>()) != cudaSuccess ||
+        (e = attr_ws_pool<128, 1>()) != cudaSuccess || (e = attr_wsx<2>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -546,6 +565,7 @@ static int dev_init(const Model* m, DevState* d) {
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
         total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wu.size()) +
+                 align256(it.h.wx.size()) +
                  align256(it.h.wpop.size() * 4) +
                  align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
     }
@@ -577,6 +597,7 @@ static int dev_init(const Model* m, DevState* d) {
         it.L->wt = (uint32_t*)put(it.h.wt.data(), it.h.wt.size() * 4);
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
         it.L->wu = (int8_t*)put(it.h.wu.data(), it.h.wu.size());
+        it.L->wx = it.h.wx.empty() ? nullptr : (int8_t*)put(it.h.wx.data(), it.h.wx.size());
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
         it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
         it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -804,6 +825,34 @@ static int launch_ws(BconvParams p, int N, cudaStream_t st) {
     return BNN_OK;
 }
 
+// 32-channel non-pooled layers with the column taps in N (bconv_wsx_kernel);
+// BNN_ERR_UNSUPPORTED (nothing launched) when the staging does not fit
+template <int MT>
+static int launch_wsx(BconvParams p, int N, cudaStream_t st) {
+    using Cfg = WsxCfg<MT>;
+    if (!p.wx || p.Cout > 32) return BNN_ERR_UNSUPPORTED;
+    const long gk = std::max(1, 64 / (p.W + 1));
+    const long Gw = gk * (p.W + 1) + 1;
+    const long rows = (long)cdiv(N, gk) * (p.H + 1) + 1;
+    const long ptot = (rows - 2) * Gw;  // output positions: grid rows 1 .. rows-2
+    const long sp = Cfg::sp_of((int)std::min<long>(Gw, 1L << 20));
+    const long groups = (ptot + Cfg::PIV - 1) / Cfg::PIV;
+    if (sp > Cfg::MAX_SP || groups * Cfg::PIV + 2 * Gw + 130 >= (1L << 31) || groups >= (1L << 31))
+        return BNN_ERR_UNSUPPORTED;
+    const int ns = Cfg::stages((int)sp, (int)Gw, p.Cout);
+    if (ns < 2) return BNN_ERR_UNSUPPORTED;
+    p.gk = (int)gk; p.Gw = (int)Gw; p.HP = (int)sp;
+    p.TR = (int)groups; p.TC = 1; p.TNI = ns;
+    p.wu = p.wx;
+    const size_t smem = std::max<size_t>(
+        (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
+    const int grid = (int)std::min<long>(groups, sm_count());
+    bconv_wsx_kernel<MT><<<grid, Cfg::NT, smem, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 (taps in N) launch: %s", cudaGetErrorString(e));
+    return BNN_OK;
+}
+
 // the pooled layers' polyphase kernel (even H and W, no concat input)
 template <int BN, int MT>
 static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
@@ -834,7 +883,8 @@ static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
 }
 
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
-    if (g_bconv_kind == 0 && p.out2 && p.wu) {
+    const bool tc = g_bconv_kind == 0 || g_bconv_kind == 3;
+    if (tc && p.out2 && p.wu) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
             case 32: rc = launch_ws_pool<32, 2>(p, N, st); break;
@@ -843,17 +893,20 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
         }
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }
-    if (g_bconv_kind == 0 && !p.out2 && p.wu) {
+    if (tc && !p.out2 && p.wu) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
-            case 32: rc = launch_ws<32, 8>(p, N, st); break;
+            case 32:
+                if (g_bconv_kind == 3) rc = launch_wsx<2>(p, N, st);
+                if (rc == BNN_ERR_UNSUPPORTED) rc = launch_ws<32, 8>(p, N, st);
+                break;
             case 64: rc = launch_ws<64, 4>(p, N, st); break;
             case 128: rc = launch_ws<128, BNN_WS128_MT>(p, N, st); break;
             case 256: rc = launch_ws<256, BNN_WS256_MT>(p, N, st); break;
         }
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }
-    if (g_bconv_kind == 0 || g_bconv_kind == 2) {
+    if (tc || g_bconv_kind == 2) {
         if (p.Cout <= 32) return launch_bmma<32>(p, N, st);
         if (p.Cout <= 64) return launch_bmma<64>(p, N, st);
         return launch_bmma<128>(p, N, st);
@@ -879,7 +932,7 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     p.cW = std::min(upW, W);
     p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
     p.wt = L.wt; p.wpop = L.wpop; p.w8 = L.w8; p.CoutP = L.CoutP; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
-    p.wu = L.wu; p.ubn = L.ubn;
+    p.wu = L.wu; p.ubn = L.ubn; p.wx = L.wx;
     if ((g_bconv_kind != 1 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
         return set_error(BNN_ERR_ARG, "binary conv layer has no weights for the selected kernel");
     p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
@@ -1592,8 +1645,10 @@ BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float
 }
 
 BNN_API int bnn_set_bconv_kernel(int kind) {
-    if (kind < 0 || kind > 2)
-        return set_error(BNN_ERR_ARG, "bconv kernel kind %d (0 = tcgen05 + mma.sync, 1 = popc, 2 = mma.sync)", kind);
+    if (kind < 0 || kind > 3)
+        return set_error(BNN_ERR_ARG,
+                         "bconv kernel kind %d (0 = tcgen05 + mma.sync, 1 = popc, 2 = mma.sync, "
+                         "3 = as 0 with the column taps in N at 32 channels)", kind);
     g_bconv_kind = kind;
     return BNN_OK;
 }
@@ -1929,7 +1984,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         folds_of(&a2, Lh->L.CoutP, h.fold2);
     }
     size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wu.size()) +
-                   align256(h.wpop.size() * 4) +
+                   align256(h.wx.size()) + align256(h.wpop.size() * 4) +
                    2 * align256(h.fold.size() * sizeof(FoldIv));
     if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
@@ -1947,6 +2002,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     Lh->L.wt = (uint32_t*)put(h.wt.data(), h.wt.size() * 4);
     Lh->L.w8 = (int8_t*)put(h.w8.data(), h.w8.size());
     Lh->L.wu = (int8_t*)put(h.wu.data(), h.wu.size());
+    Lh->L.wx = h.wx.empty() ? nullptr : (int8_t*)put(h.wx.data(), h.wx.size());
     Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
     Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
     Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;

@@ -55,6 +55,7 @@ struct BconvParams {
     int gk, Gw;           // tcgen05 kernel: images per grid row, grid width
     const int8_t* wu;     // tcgen05 kernel weights [Cout/BN][Kw][9][2][BN][16]
     int ubn;              // BN of wu
+    const int8_t* wx;     // 32-channel blocks, column taps in N: [Cout/32][Kw][3 dy][2][3 dx][32][16], or nullptr
 };
 
 // set by a kernel whose bounded wait on an mbarrier gave up (never expected;
@@ -1730,6 +1731,402 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     if (abort_s) {
         // let any MMA or bulk copy still in flight land before TMEM and shared
         // memory are released (bounded; the result is flagged as untrustworthy)
+        for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
+        if (tid == 0) atomicAdd(&g_bnn_wait_timeouts, 1u);
+    }
+    if (warp == 15) {
+        tc_fence_after();
+        tc_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------
+// 32-channel binary convs on tcgen05 with the column taps in N.
+// At N = 32 an MMA of bconv_ws_kernel reads a 4 KB A tile for a 1 KB B
+// tile, and the nine shifted MMAs per tile and word are bound by how fast
+// they can be issued. Here one MMA per kernel row dy takes the A tile
+// shifted by dy rows only and B = the row's three column taps stacked
+// (N = 96, B row dx*32 + c), so TMEM column dx*32 + c of lane i holds
+// sum_dy x[i + (dy-1)*Gw] . w[dy][dx][c]; the output at lane i takes the
+// dx = 0 block from lane i-1, dx = 1 from lane i and dx = 2 from lane i+1:
+// 3 MMAs of N = 96 per tile and word instead of 9 of N = 32. A 128-lane
+// tile yields the 126 outputs of lanes 1..126 (consecutive tiles overlap by
+// two positions), so no lane needs a neighbour outside its tile; inside a
+// tile the neighbours are warp shuffles, and across the 32-lane TMEM
+// quarters an exchange through shared memory (the boundary lanes' 16
+// values, an mbarrier per epilogue half, double-buffered, every wait
+// bounded). The accumulators start from zero (the first MMA of an item
+// overwrites) and the epilogue adds the fold's start value. Grid, staging,
+// producers and folds are those of bconv_ws_kernel; the weights come in
+// the order [channel block][word][dy][16-byte K half][dx][32 ch][16 bytes].
+// Warps: 0-7 epilogue (half h takes the tiles mt = h mod 2, quarter
+// w % 4), 8-13 producers, 14-15 MMA issue (issuer u: tiles mt = u mod 2;
+// warp 15 allocates TMEM).
+// Opt-in (bnn_set_bconv_kernel(3)): measured on 4096 32x32 patches it is
+// slower than bconv_ws_kernel<32, 8> (dec1.conv1 0.53 vs 0.27 ms, dec1.conv2
+// 0.35 vs 0.13 ms): with 96 TMEM columns a tile, two items of 252 outputs
+// fill TMEM, and the per-item epilogue (three TMEM loads, 32 shuffles and
+// an exchange round per 16 channels) bounds it, not the MMA issue.
+// ---------------------------------------------------------------------
+template <int MT>
+struct WsxCfg {
+    static constexpr int BN = 32;
+    static constexpr int NX = 3 * BN;      // N of one MMA
+    static constexpr int TV = 126;         // outputs per 128-lane tile (lanes 1..126)
+    static constexpr int PIV = TV * MT;    // outputs per item
+    static constexpr int NBUF = 2;
+    static constexpr int NEPI = 256, NPROD = 192, NT = 512;
+    static constexpr int MAX_SP = 128 * MT + 648;  // Gw up to 320
+    static constexpr int NQ = (MAX_SP + NPROD - 1) / NPROD;
+    static constexpr size_t b_bytes = (size_t)9 * 2 * BN * 16;
+    static constexpr size_t max_smem = (size_t)224 * 1024;
+    static constexpr size_t xch_bytes = (size_t)2 * 2 * 4 * 2 * 16 * 4;  // [half][parity][quarter][side][16]
+    __host__ __device__ static int sp_of(int Gw) { return ((MT - 1) * TV + 128 + 2 * Gw + 7) & ~7; }
+    __host__ __device__ static size_t a_bytes(int SP) { return (size_t)2 * SP * 16; }
+    __host__ __device__ static size_t stage_bytes(int SP) { return (a_bytes(SP) + b_bytes + 127) & ~(size_t)127; }
+    __host__ __device__ static size_t fold_bytes(int Cout) {
+        return (size_t)((Cout + 31) & ~31) * (sizeof(int2) + 4) + (size_t)((Cout + 31) / 32) * 12;
+    }
+    __host__ __device__ static size_t fixed_bytes(int SP, int Gw, int Cout) {
+        return (size_t)2 * SP * sizeof(int2) + (((size_t)Gw * 4 + 15) & ~(size_t)15) + fold_bytes(Cout) + 16 +
+               xch_bytes;
+    }
+    static int stages(int SP, int Gw, int Cout) {
+        const size_t n = (max_smem - fixed_bytes(SP, Gw, Cout)) / stage_bytes(SP);
+        return n > 8 ? 8 : (int)n;
+    }
+    static_assert(NBUF * MT * NX <= 512, "TMEM holds the item's accumulators twice");
+    static_assert(MT % 2 == 0, "the two issuers and the two epilogue halves take alternate tiles");
+};
+
+// 16 consecutive TMEM columns of this thread's lane, no wait
+__device__ __forceinline__ void tc_ld16_nw(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// p.HP = staged positions per item (SP); p.TR = items; p.TC = channel blocks;
+// p.TNI = pipeline stages; p.wu = weights in the dy-stacked order above
+template <int MT>
+__global__ void __launch_bounds__(512, 1) bconv_wsx_kernel(const BconvParams p) {
+    using C = WsxCfg<MT>;
+    constexpr int NBUF = C::NBUF, PIV = C::PIV, NQ = C::NQ, NPROD = C::NPROD, NEPI = C::NEPI, NX = C::NX;
+    extern __shared__ __align__(1024) unsigned char wsx_smem[];
+    __shared__ __align__(8) unsigned long long full_b[8], empty_b[8], accf_b[2], acce_b[2], xch_b[2];
+    __shared__ uint32_t tmem_s;
+    __shared__ int abort_s;
+    volatile int* abort_v = &abort_s;
+
+    const int SP = p.HP, n_items = p.TR, ncb = p.TC, NS = p.TNI;
+    const size_t SB = C::stage_bytes(SP);
+    int2* pxu = reinterpret_cast<int2*>(wsx_smem + (size_t)NS * SB);  // [2][SP] (pixel, upsampled pixel)
+    int* colmap = reinterpret_cast<int*>(pxu + 2 * SP);               // [Gw]
+    const int CoutR = (p.Cout + 31) & ~31, nwo = CoutR / 32;
+    int2* fu = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(colmap) + ((p.Gw * 4 + 15) & ~15));
+    int* fstart = reinterpret_cast<int*>(fu + CoutR);                 // [CoutR] -T (threshold words) or 0
+    uint32_t* finv_t = reinterpret_cast<uint32_t*>(fstart + CoutR);
+    uint32_t* finv_b = finv_t + nwo;
+    uint32_t* fband = finv_b + nwo;
+    int* xch = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(fband + nwo) + 15) & ~(uintptr_t)15);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 15) {
+        tc_alloc(smem_u32(&tmem_s), 512);
+        tc_relinquish();
+    }
+    if (tid == 0) {
+        abort_s = 0;
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_b[s]), NPROD);
+            mbar_init(smem_u32(&empty_b[s]), 2);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(smem_u32(&accf_b[b]), 2);
+            mbar_init(smem_u32(&acce_b[b]), NEPI);
+        }
+        for (int h = 0; h < 2; ++h) mbar_init(smem_u32(&xch_b[h]), NEPI / 2);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    for (int c = tid; c < p.Gw; c += C::NT) {
+        int cm = -1;
+        if (c > 0) {
+            const int jb = (c - 1) / (p.W + 1), xx = (c - 1) - jb * (p.W + 1);
+            if (xx < p.W && jb < p.gk) cm = (jb << 16) | xx;
+        }
+        colmap[c] = cm;
+    }
+    for (int w = warp; w < nwo; w += C::NT / 32) {  // the folds of bconv_ws_kernel
+        const int c = w * 32 + lane;
+        int T = -(1 << 30), inv_t = 0, inv = 0;
+        bool band = false;
+        int2 e = make_int2(0, 0);
+        if (c < p.Cout) {
+            const FoldIv f = p.fold[c];
+            const bool lo_open = f.lo == INT_MIN, hi_open = f.hi == INT_MAX;
+            if (f.lo >= f.hi) {
+                inv_t = f.inv;
+            } else if (lo_open && hi_open) {
+                inv_t = f.inv ^ 1;
+            } else if (lo_open) {
+                T = f.hi; inv_t = f.inv;
+            } else if (hi_open) {
+                T = f.lo; inv_t = f.inv ^ 1;
+            } else {
+                band = true;
+            }
+            e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
+            inv = f.inv & 1;
+        }
+        T = max(-(1 << 30), min(1 << 30, T));
+        const uint32_t bw = __ballot_sync(0xffffffffu, band);
+        fu[c] = e;
+        fstart[c] = bw ? 0 : -T;
+        const uint32_t it = __ballot_sync(0xffffffffu, inv_t & 1), ib = __ballot_sync(0xffffffffu, inv);
+        if (lane == 0) {
+            finv_t[w] = it;
+            finv_b[w] = ib;
+            fband[w] = bw ? 1u : 0u;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    const uint32_t sm0 = smem_u32(wsx_smem);
+
+    if (warp >= 8 && warp < 14) {
+        // ------------------------------------------------------------ producers
+        const int pt = tid - NEPI;
+        // staged position q of item pg = grid position pg*PIV - 1 + q
+        auto map_item = [&](int item, int2* tb) {
+            const int pg = item / ncb;
+            const GridGeo geo = grid_geo(p);
+            GridWalk g;
+            g.init(geo, pg * PIV - 1 + pt, NPROD);
+            for (int q = pt; q < SP; q += NPROD, g.step(geo)) {
+                int n = 0, x = 0, up = -1;
+                const int px = g.pixel(geo, colmap, n, x);
+                if (px >= 0 && p.cw1 > 0) {
+                    const int uy = g.yy - p.oh, ux = x - p.ow;
+                    if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
+                        up = (n * p.h1 + (uy >> 1)) * p.w1 + (ux >> 1);
+                }
+                tb[q] = make_int2(px, up);
+            }
+        };
+        auto load_words = [&](const int2* tb, int kw, uint32_t* v) {
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                const int q = pt + NPROD * j;
+                v[j] = 0u;
+                if (q < SP) {
+                    const int2 e = tb[q];
+                    if (e.x >= 0) {
+                        if (kw < p.cw0) v[j] = __ldg(p.in0 + (size_t)e.x * p.cw0 + kw);
+                        else if (e.y >= 0) v[j] = __ldg(p.in1 + (size_t)e.y * p.cw1 + (kw - p.cw0));
+                    }
+                }
+            }
+        };
+        int stage = 0, tb = 0;
+        uint32_t phase = 0;
+        int item = blockIdx.x;
+        uint32_t vn[NQ];
+        if (item < n_items) {
+            map_item(item, pxu);
+            load_words(pxu, 0, vn);
+        }
+        while (item < n_items && !*abort_v) {
+            const int cb = item % ncb;
+            const int2* cur = pxu + tb * SP;
+            bool ok = true;
+            for (int kw = 0; kw < p.Kw; ++kw) {
+                uint32_t v[NQ];
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) v[j] = vn[j];
+                if (kw + 1 < p.Kw) {
+                    load_words(cur, kw + 1, vn);
+                } else if (item + (int)gridDim.x < n_items) {
+                    int2* nxt = pxu + (tb ^ 1) * SP;
+                    map_item(item + gridDim.x, nxt);
+                    load_words(nxt, 0, vn);
+                }
+                const uint32_t fb = smem_u32(&full_b[stage]);
+                if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
+                unsigned char* As = wsx_smem + (size_t)stage * SB;
+                if (pt == 0) {
+                    mbar_expect_tx_only(fb, (uint32_t)C::b_bytes);
+                    bulk_g2s(sm0 + (uint32_t)(stage * SB + C::a_bytes(SP)),
+                             p.wu + ((size_t)cb * p.Kw + kw) * C::b_bytes, (uint32_t)C::b_bytes, fb);
+                }
+#pragma unroll
+                for (int j = 0; j < NQ; ++j) {
+                    const int q = pt + NPROD * j;
+                    if (q < SP) {
+                        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                        if (cur[q].x >= 0) expand32(v[j], lo, hi);
+                        *reinterpret_cast<uint4*>(As + (size_t)q * 16) = lo;
+                        *reinterpret_cast<uint4*>(As + ((size_t)SP + q) * 16) = hi;
+                    }
+                }
+                fence_async_smem();
+                mbar_arrive(fb);
+                if (++stage == NS) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            tb ^= 1;
+            item += gridDim.x;
+        }
+    } else if (warp >= 14) {
+        // ------------------------------------------------------------ MMA issuers
+        const int u = warp - 14;
+        if (lane == 0) {
+            const uint32_t idesc =
+                (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NX >> 3) << 17) | ((128u >> 4) << 24);
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+                const int buf = it & 1;
+                const uint32_t use = (uint32_t)(it >> 1);
+                if (!mbar_wait_ab(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, abort_v)) break;
+                tc_fence_after();
+                const uint32_t dcol = tmem + (uint32_t)(buf * MT * NX);
+                bool ok = true;
+                for (int kw = 0; kw < p.Kw; ++kw) {
+                    if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_s = sm0 + (uint32_t)(stage * SB);
+                    const uint32_t b_s = a_s + (uint32_t)C::a_bytes(SP);
+                    const uint64_t a0 = tc_desc(a_s, (uint32_t)SP * 16), b0 = tc_desc(b_s, NX * 16);
+#pragma unroll 1
+                    for (int mt = u; mt < MT; mt += 2) {
+#pragma unroll
+                        for (int dy = 0; dy < 3; ++dy) {
+                            // descriptor start addresses are in 16-byte units in the low bits
+                            const uint64_t ad = a0 + (uint64_t)(mt * C::TV + dy * p.Gw);
+                            const uint64_t bd = b0 + (uint64_t)(dy * 2 * NX);
+                            tc_mma_i8(dcol + mt * NX, ad, bd, idesc, (kw > 0 || dy > 0) ? 1u : 0u);
+                        }
+                    }
+                    tc_commit(smem_u32(&empty_b[stage]));
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(smem_u32(&accf_b[buf]));
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp & 3, half = warp >> 2;
+        const int r = quad * 32 + lane;  // TMEM lane = tile lane
+        int it = 0;
+        uint32_t xph = 0u;  // parity of this half's exchange barrier
+        int xr = 0;         // exchange rounds so far (selects the buffer)
+        int* xh = xch + half * (2 * 4 * 2 * 16);
+        for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
+            const int buf = it & 1;
+            const uint32_t use = (uint32_t)(it >> 1);
+            const int cb = item % ncb, pg = item / ncb, cout0 = cb * 32;
+            if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
+            tc_fence_after();
+            const GridGeo geo = grid_geo(p);
+            bool ok = true;
+#pragma unroll 1
+            for (int mt = half; mt < MT; mt += 2) {
+                // this lane's output: grid position p.Gw + pg*PIV + mt*TV + r - 1 (lanes 1..126)
+                GridWalk g;
+                g.init(geo, p.Gw + pg * PIV + mt * C::TV + r - 1, 1);
+                int n = 0, x = 0;
+                const int px = (r >= 1 && r <= C::TV) ? g.pixel(geo, colmap, n, x) : -1;
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * MT * NX + mt * NX);
+                uint32_t bits = 0u;
+                const bool band = fband[cout0 >> 5] != 0u;
+#pragma unroll 1
+                for (int c0 = 0; c0 < 32; c0 += 16) {
+                    uint32_t v0[16], v1[16], v2[16];
+                    tc_ld16_nw(ta + (uint32_t)c0, v0);
+                    tc_ld16_nw(ta + 32u + (uint32_t)c0, v1);
+                    tc_ld16_nw(ta + 64u + (uint32_t)c0, v2);
+                    tc_wait_ld();
+                    // quarter boundaries: lane 31 hands its dx = 0 block to the
+                    // next quarter's lane 0, lane 0 its dx = 2 block to the
+                    // previous quarter's lane 31
+                    int* xb = xh + (xr & 1) * (4 * 2 * 16);
+                    if (lane == 31) {
+#pragma unroll
+                        for (int k = 0; k < 16; k += 4)
+                            *reinterpret_cast<int4*>(xb + (quad * 2 + 0) * 16 + k) =
+                                make_int4((int)v0[k], (int)v0[k + 1], (int)v0[k + 2], (int)v0[k + 3]);
+                    }
+                    if (lane == 0) {
+#pragma unroll
+                        for (int k = 0; k < 16; k += 4)
+                            *reinterpret_cast<int4*>(xb + (quad * 2 + 1) * 16 + k) =
+                                make_int4((int)v2[k], (int)v2[k + 1], (int)v2[k + 2], (int)v2[k + 3]);
+                    }
+                    // dx = 0 block of lane - 1, dx = 2 block of lane + 1
+                    int a0[16], a2[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        a0[k] = __shfl_up_sync(0xffffffffu, (int)v0[k], 1);
+                        a2[k] = __shfl_down_sync(0xffffffffu, (int)v2[k], 1);
+                    }
+                    mbar_arrive(smem_u32(&xch_b[half]));
+                    if (!mbar_wait_ab(smem_u32(&xch_b[half]), xph, abort_v)) { ok = false; break; }
+                    xph ^= 1u;
+                    ++xr;
+                    if (lane == 0) {  // tile lane 0 (quarter 0) has no output
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) a0[k] = quad > 0 ? xb[((quad - 1) * 2 + 0) * 16 + k] : 0;
+                    }
+                    if (lane == 31) {  // tile lane 127 (quarter 3) has no output
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) a2[k] = quad < 3 ? xb[((quad + 1) * 2 + 1) * 16 + k] : 0;
+                    }
+                    int s[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) s[k] = a0[k] + (int)v1[k] + a2[k];
+                    // s = P of channels cout0 + c0 .. +15 at this lane's output
+                    uint32_t hb = 0u;
+                    if (!band) {
+#pragma unroll
+                        for (int k = 15; k >= 0; --k)
+                            hb = __funnelshift_l((uint32_t)(s[k] + fstart[cout0 + c0 + k]), hb, 1);
+                    } else {
+                        const int2* f = fu + cout0 + c0;
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) hb |= (uint32_t)((unsigned)(s[k] - f[k].x) < (unsigned)f[k].y) << k;
+                    }
+                    bits |= (hb & 0xFFFFu) << c0;
+                    if (p.P && px >= 0) {  // debug: the accumulators themselves, [N][Cout][H][W]
+                        const int lim = p.Cout - cout0 - c0;
+                        int* Pp = p.P + (((size_t)n * p.Cout + cout0 + c0) * p.H + g.yy) * p.W + x;
+                        const int hw = p.H * p.W;
+#pragma unroll
+                        for (int k = 0; k < 16; ++k)
+                            if (k < lim) Pp[(size_t)k * hw] = s[k];
+                    }
+                }
+                if (!ok) break;
+                if (px >= 0 && cout0 < p.Cout) {
+                    const int cw = cout0 >> 5, lim = p.Cout - cout0;
+                    bits ^= band ? finv_b[cw] : finv_t[cw];
+                    if (lim < 32) bits &= (1u << lim) - 1u;
+                    p.out[(size_t)px * p.cwo + cw] = bits;
+                }
+            }
+            if (!ok) break;
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce_b[buf]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
         for (int i = 0; i < (1 << 16); ++i) __nanosleep(1000);
         if (tid == 0) atomicAdd(&g_bnn_wait_timeouts, 1u);
     }

@@ -75,9 +75,11 @@ int bnn_forward_patched_device(const Model *m, int device, const float *d_cube,
                                void *stream);
 
 /* Process-wide choice of the binary-conv kernel, for measurement and A/B
- * parity tests: 0 = tcgen05 int8 MMAs for the non-pooled layers and
- * mma.sync int8 for the pooled encoder convs (default), 1 = XOR + POPC on
- * the integer pipe, 2 = mma.sync int8 for every layer. All compute the
+ * parity tests: 0 = tcgen05 int8 MMAs with nine shifted taps (default;
+ * mma.sync int8 where the staging does not fit), 1 = XOR + POPC on the
+ * integer pipe, 2 = mma.sync int8 for every layer, 3 = as 0, but layers of
+ * at most 32 channels without a pool take the tcgen05 kernel with a kernel
+ * row's three column taps stacked in N (measured slower). All compute the
  * reference's P exactly; set it before the forwards to compare (captured
  * graphs keep the kernels they captured). */
 int bnn_set_bconv_kernel(int kind);
