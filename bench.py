@@ -366,7 +366,7 @@ def run_ours(args):
             "roofline": (
                 {"bound": "tensor",
                  "kernel": ("bconv_ws_kernel + bconv_ws_pool_kernel (17 fused binary convs, tcgen05 int8, "
-                            "persistent warp-specialised)") if args.bconv in ("tc", "tcx") else
+                            "persistent warp-specialised)") if args.bconv in ("tc", "tc8", "tc4", "tcx") else
                            "bconv_mma_kernel (17 fused binary convs, int8 mma.sync)",
                  "achieved": round(bconv_ach, 1), "peak": round(tensor_i8_peak, 1),
                  "unit": "Gbitop/s (1 bitop = 1 binary MAC, run as one int8 MAC)",
@@ -380,7 +380,7 @@ def run_ours(args):
                  "frac_of_mma_sync_measured": round(bconv_ach / mma_sync_peak, 4),
                  "frac_of_popc_peak": round(bconv_ach / popc_peak, 4),
                  "time_share": frac_split.get("bconv")}
-                if args.bconv in ("tc", "tcx", "mma") else
+                if args.bconv in ("tc", "tc8", "tc4", "tcx", "mma") else
                 {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
                  "achieved": round(bconv_ach, 1), "peak": round(popc_peak, 1), "unit": "Gbitop/s",
                  "frac": round(bconv_ach / popc_peak, 4), "traffic": None,
@@ -707,9 +707,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
     ap.add_argument("--first", default="tc", choices=["tc", "mma", "tcn"],
                     help="first conv kernel: tcgen05 (default) or mma.sync")
-    ap.add_argument("--bconv", default="tc", choices=["tc", "tcx", "popc", "mma"],
-                    help="binary-conv kernels: tc = tcgen05 + mma.sync (default), tcx = the same with the "
-                         "column taps in N at 32 channels, popc = XOR + POPC, mma = mma.sync for every layer")
+    ap.add_argument("--bconv", default="tc", choices=["tc", "tc8", "tc4", "tcx", "popc", "mma"],
+                    help="binary-conv kernels: tc = tcgen05 int8, e2m1 where measured faster (default), "
+                         "tc8 = tcgen05 int8 throughout, tc4 = tcgen05 e2m1 for every non-pooled layer, "
+                         "tcx = tc8 with the column taps in N at 32 channels, popc = XOR + POPC, "
+                         "mma = mma.sync for every layer")
     ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem", "react"],
                     help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler; "
                          "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem); "

@@ -478,10 +478,13 @@ class BconvLayer:
 
 
 def set_bconv_kernel(kind: str):
-    """'tc' (tcgen05 with nine shifted taps + mma.sync, default), 'popc'
-    (XOR + POPC), 'mma' (mma.sync for every layer) or 'tcx' (as 'tc', with
-    the column taps in N for the non-pooled layers of at most 32 channels)."""
-    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2, "tcx": 3}[kind]))
+    """'tc' (default: tcgen05, int8 operands, e2m1 for the 64- and 128-channel
+    non-pooled layers with at least 4 input words, mma.sync where the
+    staging does not fit), 'tc8' (tcgen05 int8 throughout), 'tcx' (as
+    'tc8', with the column taps in N for the non-pooled layers of at most 32
+    channels), 'tc4' (tcgen05 e2m1 for every non-pooled layer), 'popc'
+    (XOR + POPC) or 'mma' (mma.sync for every layer)."""
+    _check(lib().bnn_set_bconv_kernel({"tc": 0, "popc": 1, "mma": 2, "tcx": 3, "tc8": 4, "tc4": 5}[kind]))
 
 
 def set_first_conv_kernel(kind):

@@ -49,6 +49,7 @@ struct BinLayer {
     int8_t* wu = nullptr;     // tcgen05 kernel weights [Cout/ubn][Kw][9][2][ubn][16]
     int ubn = 0;              // tcgen05 channel block (N of one MMA)
     int8_t* wx = nullptr;     // ubn == 32: the same weights for bconv_wsx_kernel [Kw][3 dy][2][3 dx][32][16]
+    int8_t* w4 = nullptr;     // the same weights as e2m1 nibbles for the kind::mxf4 kernel (layout of wu, two words a step)
     FoldIv* fold = nullptr;
     FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
 };
@@ -208,7 +209,7 @@ static FoldIv to_iv(int type, int t, int lo, int hi) {
 
 struct HostBin {
     std::vector<uint32_t> wt;
-    std::vector<int8_t> w8, wu, wx;
+    std::vector<int8_t> w8, wu, wx, w4;
     std::vector<int> wpop;
     std::vector<FoldIv> fold, fold2;
 };
@@ -223,6 +224,24 @@ struct HostBin {
 #endif
 #ifndef BNN_WS256_MT
 #define BNN_WS256_MT 2
+#endif
+// epilogue warps of the pooled tcgen05 kernel (4 or 8; the producers take the other 14 - EW)
+#ifndef BNN_POOL_EPI_WARPS
+#define BNN_POOL_EPI_WARPS 8
+#endif
+// tiles per work item of the kind::mxf4 (e2m1) kernel: 32 TMEM columns hold
+// the block scales, so the item shapes that filled all 512 columns shrink
+#ifndef BNN_F4_MT32
+#define BNN_F4_MT32 7
+#endif
+#ifndef BNN_F4_MT64
+#define BNN_F4_MT64 3
+#endif
+#ifndef BNN_F4_MT128
+#define BNN_F4_MT128 3
+#endif
+#ifndef BNN_F4_MT256
+#define BNN_F4_MT256 1
 #endif
 
 // tcgen05 channel block for a layer of Cout channels: the whole layer up to
@@ -270,6 +289,26 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
                     for (int c = 0; c < bn && cb * bn + c < Cout; ++c)
                         memcpy(&h.wu[((((size_t)cb * L.Kw + kw) * 9 + t) * 2 + hh) * bn * 16 + (size_t)c * 16],
                                &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32 + hh * 16], 16);
+    // the kind::mxf4 kernel: per (channel block, K step of two words) the 9
+    // taps' B operands [tap][word of the step][channel][16 bytes], each
+    // 16 bytes = 32 e2m1 nibbles (channel j of the word in byte j/2, low
+    // nibble for even j: +1 -> 0x2, -1 -> 0xA, absent -> 0)
+    {
+        const int KS = (L.Kw + 1) / 2;
+        h.w4.assign((size_t)ncb * KS * 9 * 2 * bn * 16, (int8_t)0);
+        for (int cb = 0; cb < ncb; ++cb)
+            for (int kw = 0; kw < L.Kw; ++kw)
+                for (int t = 0; t < 9; ++t)
+                    for (int c = 0; c < bn && cb * bn + c < Cout; ++c) {
+                        const int8_t* src = &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32];
+                        int8_t* dst = &h.w4[((((size_t)cb * KS + kw / 2) * 9 + t) * 2 + (kw & 1)) * bn * 16 +
+                                            (size_t)c * 16];
+                        for (int j = 0; j < 32; ++j) {
+                            const uint8_t nib = src[j] > 0 ? 0x2 : src[j] < 0 ? 0xA : 0x0;
+                            dst[j >> 1] = (int8_t)((uint8_t)dst[j >> 1] | (uint8_t)(nib << ((j & 1) * 4)));
+                        }
+                    }
+    }
     // 32-channel layers: the column taps of a kernel row stacked in N for
     // bconv_wsx_kernel ([word][dy][16-byte K half][dx][channel][16 bytes])
     h.wx.clear();
@@ -299,15 +338,15 @@ static cudaError_t attr_bconv() {
     return cudaFuncSetAttribute(bconv3x3_kernel<BN, TM, TN, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)BconvCfg<BN, TM, TN, KC>::smem_bytes(512));
 }
-template <int BN, int MT>
+template <int BN, int MT, int EW = BNN_POOL_EPI_WARPS>
 static cudaError_t attr_ws_pool() {
-    return cudaFuncSetAttribute(bconv_ws_pool_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)WsPoolCfg<BN, MT>::max_smem);
+    return cudaFuncSetAttribute(bconv_ws_pool_kernel<BN, MT, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)WsPoolCfg<BN, MT, EW>::max_smem);
 }
-template <int BN, int MT>
+template <int BN, int MT, bool F4 = false, int EW = 8>
 static cudaError_t attr_ws() {
-    return cudaFuncSetAttribute(bconv_ws_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)WsCfg<BN, MT>::max_smem);
+    return cudaFuncSetAttribute(bconv_ws_kernel<BN, MT, F4, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)WsCfg<BN, MT, F4, EW>::max_smem);
 }
 template <int MT>
 static cudaError_t attr_wsx() {
@@ -353,8 +392,13 @@ static int set_kernel_attrs(int device) {
         (e = attr_bmma<64>()) != cudaSuccess || (e = attr_bmma<128>()) != cudaSuccess ||
         (e = attr_ws<32, 8>()) != cudaSuccess || (e = attr_ws<64, 4>()) != cudaSuccess ||
         (e = attr_ws<128, BNN_WS128_MT>()) != cudaSuccess || (e = attr_ws<256, BNN_WS256_MT>()) != cudaSuccess ||
+        (e = attr_ws<32, BNN_F4_MT32, true>()) != cudaSuccess || (e = attr_ws<64, BNN_F4_MT64, true>()) != cudaSuccess ||
+        (e = attr_ws<128, BNN_F4_MT128, true>()) != cudaSuccess ||
+        (e = attr_ws<256, BNN_F4_MT256, true>()) != cudaSuccess || (e = attr_ws<32, 8, false, 4>()) != cudaSuccess ||
+        (e = attr_ws<64, BNN_F4_MT64, true, 4>()) != cudaSuccess ||
         (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
         (e = attr_ws_pool<128, 1>()) != cudaSuccess || (e = attr_wsx<2>()) != cudaSuccess ||
+        (e = attr_ws_pool<64, 1, 4>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -565,7 +609,7 @@ static int dev_init(const Model* m, DevState* d) {
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
         total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wu.size()) +
-                 align256(it.h.wx.size()) +
+                 align256(it.h.wx.size()) + align256(it.h.w4.size()) +
                  align256(it.h.wpop.size() * 4) +
                  align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
     }
@@ -598,6 +642,7 @@ static int dev_init(const Model* m, DevState* d) {
         it.L->w8 = (int8_t*)put(it.h.w8.data(), it.h.w8.size());
         it.L->wu = (int8_t*)put(it.h.wu.data(), it.h.wu.size());
         it.L->wx = it.h.wx.empty() ? nullptr : (int8_t*)put(it.h.wx.data(), it.h.wx.size());
+        it.L->w4 = it.h.w4.empty() ? nullptr : (int8_t*)put(it.h.w4.data(), it.h.w4.size());
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
         it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
         it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -799,9 +844,13 @@ static int sm_count() {
 
 // persistent tcgen05 kernel on the padded grid (non-pooled layers); returns
 // BNN_ERR_UNSUPPORTED (and launches nothing) when the staging does not fit
-template <int BN, int MT>
+template <int BN, int MT, bool F4 = false, int EW = 8>
 static int launch_ws(BconvParams p, int N, cudaStream_t st) {
-    using Cfg = WsCfg<BN, MT>;
+    using Cfg = WsCfg<BN, MT, F4, EW>;
+    if (F4) {
+        if (!p.w4) return BNN_ERR_UNSUPPORTED;
+        p.wu = p.w4;
+    }
     const long gk = std::max(1, 64 / (p.W + 1));
     const long Gw = gk * (p.W + 1) + 1;
     const long rows = (long)cdiv(N, gk) * (p.H + 1) + 1;
@@ -819,7 +868,7 @@ static int launch_ws(BconvParams p, int N, cudaStream_t st) {
     const size_t smem = std::max<size_t>(
         (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
     const int grid = (int)std::min<long>(groups * ncb, sm_count());
-    bconv_ws_kernel<BN, MT><<<grid, Cfg::NT, smem, st>>>(p);
+    bconv_ws_kernel<BN, MT, F4, EW><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 launch: %s", cudaGetErrorString(e));
     return BNN_OK;
@@ -854,9 +903,9 @@ static int launch_wsx(BconvParams p, int N, cudaStream_t st) {
 }
 
 // the pooled layers' polyphase kernel (even H and W, no concat input)
-template <int BN, int MT>
+template <int BN, int MT, int EW = BNN_POOL_EPI_WARPS>
 static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
-    using Cfg = WsPoolCfg<BN, MT>;
+    using Cfg = WsPoolCfg<BN, MT, EW>;
     if ((p.H & 1) || (p.W & 1) || p.cw1 != 0 || !p.fold2) return BNN_ERR_UNSUPPORTED;
     const long H2 = p.H / 2, W2 = p.W / 2;
     const long gk = std::max(1L, 64 / (W2 + 1));
@@ -876,20 +925,38 @@ static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
     const size_t smem = std::max<size_t>(
         (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
     const int grid = (int)std::min<long>(groups * ncb, sm_count());
-    bconv_ws_pool_kernel<BN, MT><<<grid, Cfg::NT, smem, st>>>(p);
+    bconv_ws_pool_kernel<BN, MT, EW><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 pooled launch: %s", cudaGetErrorString(e));
     return BNN_OK;
 }
 
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
-    const bool tc = g_bconv_kind == 0 || g_bconv_kind == 3;
+    const bool tc = g_bconv_kind == 0 || g_bconv_kind >= 3;
     if (tc && p.out2 && p.wu) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
             case 32: rc = launch_ws_pool<32, 2>(p, N, st); break;
-            case 64: rc = launch_ws_pool<64, 1>(p, N, st); break;
+            // 10 producer warps at 64 channels (enc2.conv2 0.138 vs 0.155 ms); 6 at 32 and 128 (faster there)
+            case 64: rc = launch_ws_pool<64, 1, 4>(p, N, st); break;
             case 128: rc = launch_ws_pool<128, 1>(p, N, st); break;
+        }
+        if (rc != BNN_ERR_UNSUPPORTED) return rc;
+    }
+    // e2m1 MMAs where they measured faster than int8 (4096 32x32 patches):
+    // 64- and 128-channel layers with at least 4 input words (dec3.conv1
+    // 0.090 vs 0.117 ms, dec2.conv1 0.162 vs 0.175, dec3.conv2 0.058 vs
+    // 0.060); kind 5 takes them for every non-pooled layer
+    const bool f4 = (g_bconv_kind == 0 && (p.ubn == 64 || p.ubn == 128) && p.Kw >= 4) || g_bconv_kind == 5;
+    if (f4 && !p.out2 && p.w4) {
+        int rc = BNN_ERR_UNSUPPORTED;
+        switch (p.ubn) {
+            case 32: rc = launch_ws<32, BNN_F4_MT32, true>(p, N, st); break;
+            case 64:
+                rc = p.cw1 > 0 ? launch_ws<64, BNN_F4_MT64, true, 4>(p, N, st) : launch_ws<64, BNN_F4_MT64, true>(p, N, st);
+                break;
+            case 128: rc = launch_ws<128, BNN_F4_MT128, true>(p, N, st); break;
+            case 256: rc = launch_ws<256, BNN_F4_MT256, true>(p, N, st); break;
         }
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }
@@ -898,7 +965,10 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
         switch (p.ubn) {
             case 32:
                 if (g_bconv_kind == 3) rc = launch_wsx<2>(p, N, st);
-                if (rc == BNN_ERR_UNSUPPORTED) rc = launch_ws<32, 8>(p, N, st);
+                // a decoder conv1 (concat input) stages two sources: 10 producer warps
+                // (dec1.conv1 0.22 vs 0.27 ms); 6 elsewhere (4 epilogue warps measured slower there)
+                if (rc == BNN_ERR_UNSUPPORTED)
+                    rc = p.cw1 > 0 ? launch_ws<32, 8, false, 4>(p, N, st) : launch_ws<32, 8>(p, N, st);
                 break;
             case 64: rc = launch_ws<64, 4>(p, N, st); break;
             case 128: rc = launch_ws<128, BNN_WS128_MT>(p, N, st); break;
@@ -932,7 +1002,7 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     p.cW = std::min(upW, W);
     p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
     p.wt = L.wt; p.wpop = L.wpop; p.w8 = L.w8; p.CoutP = L.CoutP; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
-    p.wu = L.wu; p.ubn = L.ubn; p.wx = L.wx;
+    p.wu = L.wu; p.ubn = L.ubn; p.wx = L.wx; p.w4 = L.w4;
     if ((g_bconv_kind != 1 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
         return set_error(BNN_ERR_ARG, "binary conv layer has no weights for the selected kernel");
     p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
@@ -1645,10 +1715,11 @@ BNN_API void bnn_forward(const Model* m, const float* input, int H, int W, float
 }
 
 BNN_API int bnn_set_bconv_kernel(int kind) {
-    if (kind < 0 || kind > 3)
+    if (kind < 0 || kind > 5)
         return set_error(BNN_ERR_ARG,
-                         "bconv kernel kind %d (0 = tcgen05 + mma.sync, 1 = popc, 2 = mma.sync, "
-                         "3 = as 0 with the column taps in N at 32 channels)", kind);
+                         "bconv kernel kind %d (0 = tcgen05 int8 + e2m1 where faster, 1 = popc, 2 = mma.sync, "
+                         "3 = tcgen05 int8 with the column taps in N at 32 channels, 4 = tcgen05 int8, "
+                         "5 = tcgen05 e2m1 for every non-pooled layer)", kind);
     g_bconv_kind = kind;
     return BNN_OK;
 }
@@ -1984,7 +2055,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         folds_of(&a2, Lh->L.CoutP, h.fold2);
     }
     size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wu.size()) +
-                   align256(h.wx.size()) + align256(h.wpop.size() * 4) +
+                   align256(h.wx.size()) + align256(h.w4.size()) + align256(h.wpop.size() * 4) +
                    2 * align256(h.fold.size() * sizeof(FoldIv));
     if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
@@ -2003,6 +2074,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     Lh->L.w8 = (int8_t*)put(h.w8.data(), h.w8.size());
     Lh->L.wu = (int8_t*)put(h.wu.data(), h.wu.size());
     Lh->L.wx = h.wx.empty() ? nullptr : (int8_t*)put(h.wx.data(), h.wx.size());
+    Lh->L.w4 = h.w4.empty() ? nullptr : (int8_t*)put(h.w4.data(), h.w4.size());
     Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
     Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
     Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;

@@ -56,6 +56,7 @@ struct BconvParams {
     const int8_t* wu;     // tcgen05 kernel weights [Cout/BN][Kw][9][2][BN][16]
     int ubn;              // BN of wu
     const int8_t* wx;     // 32-channel blocks, column taps in N: [Cout/32][Kw][3 dy][2][3 dx][32][16], or nullptr
+    const int8_t* w4;     // e2m1 weights for the kind::mxf4 kernel: [Cout/BN][ceil(Kw/2)][9][2 words][BN][16], or nullptr
 };
 
 // set by a kernel whose bounded wait on an mbarrier gave up (never expected;
@@ -1211,13 +1212,18 @@ __global__ void __launch_bounds__(BmmaCfg<BN>::NT, 512 / BmmaCfg<BN>::NT) bconv_
 // straddle items). Every wait is bounded; a wait that gives up aborts the
 // whole CTA (all later waits return at once) and bumps g_bnn_wait_timeouts.
 // ---------------------------------------------------------------------
-template <int BN, int MT>
+// EW: epilogue warps (4 or 8); the producers take the other 14 - EW
+template <int BN, int MT, bool F4 = false, int EW_ = 8>
 struct WsCfg {
-    static constexpr int NBUF = 512 / (BN * MT);
+    // F4: the top 32 TMEM columns hold the MMAs' block scales
+    static constexpr int TCOLS = F4 ? 512 - 32 : 512;
+    static constexpr int NBUF = TCOLS / (BN * MT) >= 2 ? 2 : TCOLS / (BN * MT);
     static constexpr int PI = 128 * MT;  // output positions per item
-    static constexpr int NEPI = 256;     // warps 0-7: epilogue (two per TMEM lane quarter)
-    static constexpr int NPROD = 192;    // warps 8-13: producers
+    static constexpr int EW = EW_;       // warps 0..EW-1: epilogue (EW / 4 per TMEM lane quarter)
+    static constexpr int NEPI = 32 * EW;
+    static constexpr int NPROD = 32 * (14 - EW);  // warps EW-13: producers
     static constexpr int NT = 512;       // + warps 14, 15: MMA issue (warp 15 also allocates TMEM)
+    static_assert(EW == 4 || EW == 8, "the epilogue covers the four TMEM lane quarters once or twice");
     static constexpr int MAX_SP = PI + 648;  // Gw up to 320
     static constexpr int NQ = (MAX_SP + NPROD - 1) / NPROD;  // staged positions per producer thread
     static constexpr size_t b_bytes = (size_t)9 * 2 * BN * 16;
@@ -1239,6 +1245,12 @@ struct WsCfg {
     }
     static_assert(NBUF == 1 || NBUF == 2, "TMEM holds one or two accumulators");
 };
+
+// first TMEM column of the block scales of the kind::mxf4 MMAs: A's at
+// F4_SF, B's at F4_SF + 16, all 32 columns x 128 lanes 0x7F7F7F7F (UE8M0
+// 1.0 in every byte), so the MMA reads a scale of 1.0 whatever the byte it
+// selects
+constexpr uint32_t F4_SF = 512 - 32;
 
 __device__ __forceinline__ void tc_alloc(uint32_t smem_dst, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_dst), "r"(ncols)
@@ -1263,6 +1275,36 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t adesc, uint64_t b
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z)
         : "memory");
 }
+// D[tmem] (+)= A(smem desc) x B(smem desc), e2m1 x e2m1 -> fp32, K = 64
+// (32 bytes of packed nibbles per row), block scales (one per 32 elements)
+// read from TMEM at sfa / sfb
+__device__ __forceinline__ void tc_mma_f4(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc,
+                                          uint32_t sfa, uint32_t sfb) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+// instruction descriptor of kind::mxf4: A and B E2M1, UE8M0 scales, K = 64, M = 128
+__host__ __device__ constexpr uint32_t f4_idesc(int N) {
+    return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24);
+}
+// 32 activation bits -> 32 e2m1 nibbles (16 bytes): bit 1 -> +1.0 (0x2),
+// bit 0 -> -1.0 (0xA); channel j in byte j/2, low nibble for even j. The
+// shifts spread bit k of each byte to bit 4k (no carries), and
+// 0xA ^ (bit << 3) gives the nibble.
+__device__ __forceinline__ uint32_t nib8(uint32_t b) {
+    uint32_t t = b & 0xFFu;
+    t = (t | (t << 12)) & 0x000F000Fu;
+    t = (t | (t << 6)) & 0x03030303u;
+    t = (t | (t << 3)) & 0x11111111u;
+    return 0xAAAAAAAAu ^ (t << 3);
+}
+__device__ __forceinline__ uint4 nib32(uint32_t w) {
+    return make_uint4(nib8(w), nib8(w >> 8), nib8(w >> 16), nib8(w >> 24));
+}
+
 __device__ __forceinline__ void tc_commit(uint32_t mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar)
                  : "memory");
@@ -1417,9 +1459,9 @@ struct GridWalk {
 
 // p.HP = staged positions per item (SP); p.TR = items; p.TC = channel blocks;
 // p.TNI = pipeline stages
-template <int BN, int MT>
+template <int BN, int MT, bool F4, int EW>
 __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
-    using C = WsCfg<BN, MT>;
+    using C = WsCfg<BN, MT, F4, EW>;
     constexpr int NBUF = C::NBUF, PI = C::PI, NQ = C::NQ, NPROD = C::NPROD, NEPI = C::NEPI;
     constexpr int NCH = BN / 32, NPAIR = MT * NCH;  // epilogue units: (tile, 32-column chunk)
     extern __shared__ __align__(1024) unsigned char ws_smem[];
@@ -1429,6 +1471,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     volatile int* abort_v = &abort_s;
 
     const int SP = p.HP, n_items = p.TR, ncb = p.TC, NS = p.TNI;
+    const int KS = F4 ? (p.Kw + 1) >> 1 : p.Kw;  // K steps: one word (int8) or two words (e2m1) each
     const size_t SB = C::stage_bytes(SP);
     int2* pxu = reinterpret_cast<int2*>(ws_smem + (size_t)NS * SB);  // [2][SP] (pixel, upsampled pixel)
     int* colmap = reinterpret_cast<int*>(pxu + 2 * SP);              // [Gw]
@@ -1471,7 +1514,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     }
     for (int w = warp; w < nwo; w += C::NT / 32) {  // one warp per 32-channel word, lane = channel
         const int c = w * 32 + lane;
-        int T = -(1 << 30), inv_t = 0, inv = 0;  // channels past Cout: bit 0
+        int T = -(1 << 22), inv_t = 0, inv = 0;  // channels past Cout: bit 0
         bool band = false;
         int2 e = make_int2(0, 0);
         if (c < p.Cout) {
@@ -1491,7 +1534,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
             e = make_int2(f.lo, f.hi > f.lo ? (int)((unsigned)f.hi - (unsigned)f.lo) : 0);
             inv = f.inv & 1;
         }
-        T = max(-(1 << 30), min(1 << 30, T));  // |P| < 2^24: clamping keeps every comparison
+        // |P| < 2^22: clamping keeps every comparison, and P - T stays an
+        // integer an fp32 accumulator holds exactly
+        T = max(-(1 << 22), min(1 << 22, T));
         const uint32_t bw = __ballot_sync(0xffffffffu, band);
         fu[c] = e;
         fstart[c] = bw ? 0 : -T;  // a band word starts at 0
@@ -1510,18 +1555,23 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
 
     // epilogue geometry: warp w reads TMEM lanes 32*(w%4).. and takes every
     // other (tile, chunk) of an item
-    const int quad = warp & 3, half = (warp >> 2) & 1;
+    constexpr int EH = C::EW / 4;  // epilogue warps per TMEM lane quarter
+    const int quad = warp & 3, half = (warp >> 2) % EH;
     auto start_vals = [&](int c, uint32_t* v) {  // accumulator start values of channels c..c+31
 #pragma unroll
         for (int k = 0; k < 32; k += 4) {
             const int4 q = *reinterpret_cast<const int4*>(fstart + c + k);
             v[k] = (uint32_t)q.x; v[k + 1] = (uint32_t)q.y; v[k + 2] = (uint32_t)q.z; v[k + 3] = (uint32_t)q.w;
         }
+        if (F4) {  // fp32 accumulators: the same integers as floats (exact, |start| <= 2^22)
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = __float_as_uint((float)(int)v[k]);
+        }
     };
-    if (warp < 8) {
+    if (warp < C::EW) {
         // every accumulator starts at its channels' start values
         for (int b = 0; b < NBUF; ++b)
-            for (int i = half; i < NPAIR; i += 2) {
+            for (int i = half; i < NPAIR; i += EH) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
                 // channel block of the first item that uses accumulator b
                 const int cs = (int)((blockIdx.x + (unsigned)b * gridDim.x) % (unsigned)ncb) * BN + c0;
@@ -1529,13 +1579,19 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 start_vals(cs < CoutR ? cs : 0, v);
                 tc_st32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN * MT + mt * BN + c0), v);
             }
+        if (F4 && half == 0) {  // the block scales: 1.0 in every byte of columns F4_SF..F4_SF+31
+            uint32_t v[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = 0x7F7F7F7Fu;
+            tc_st32(tmem + ((uint32_t)(quad * 32) << 16) + F4_SF, v);
+        }
         tc_wait_st();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
-    if (warp >= 8 && warp < 14) {
+    if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
         const int pt = tid - NEPI;
         // map the staged positions q = pt + NPROD*j of `item` into table `tb`
@@ -1569,29 +1625,40 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 }
             }
         };
+        // the words of K step ks: ks (int8) or 2ks and 2ks+1 (e2m1)
+        auto load_step = [&](const int2* tb, int ks, uint32_t* v, uint32_t* v2) {
+            if (F4) {
+                load_words(tb, 2 * ks, v);
+                if (2 * ks + 1 < p.Kw) load_words(tb, 2 * ks + 1, v2);
+            } else {
+                load_words(tb, ks, v);
+            }
+        };
         int stage = 0, tb = 0;
         uint32_t phase = 0;
         int item = blockIdx.x;
-        uint32_t vn[NQ];
+        uint32_t vn[NQ], vn2[NQ];
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) vn2[j] = 0u;
         if (item < n_items) {
             map_item(item, pxu);
-            load_words(pxu, 0, vn);
+            load_step(pxu, 0, vn, vn2);
         }
         while (item < n_items && !*abort_v) {
             const int cb = item % ncb;
             const int2* cur = pxu + tb * SP;
             bool ok = true;
-            for (int kw = 0; kw < p.Kw; ++kw) {
-                uint32_t v[NQ];
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t v[NQ], v2[NQ];
 #pragma unroll
-                for (int j = 0; j < NQ; ++j) v[j] = vn[j];
+                for (int j = 0; j < NQ; ++j) { v[j] = vn[j]; v2[j] = vn2[j]; }
                 // issue the next stage's loads before this stage's wait and stores
-                if (kw + 1 < p.Kw) {
-                    load_words(cur, kw + 1, vn);
+                if (ks + 1 < KS) {
+                    load_step(cur, ks + 1, vn, vn2);
                 } else if (item + (int)gridDim.x < n_items) {
                     int2* nxt = pxu + (tb ^ 1) * SP;
                     map_item(item + gridDim.x, nxt);
-                    load_words(nxt, 0, vn);
+                    load_step(nxt, 0, vn, vn2);
                 }
                 const uint32_t fb = smem_u32(&full_b[stage]);
                 if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
@@ -1599,14 +1666,22 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 if (pt == 0) {
                     mbar_expect_tx_only(fb, (uint32_t)C::b_bytes);
                     bulk_g2s(sm0 + (uint32_t)(stage * SB + C::a_bytes(SP)),
-                             p.wu + ((size_t)cb * p.Kw + kw) * C::b_bytes, (uint32_t)C::b_bytes, fb);
+                             p.wu + ((size_t)cb * KS + ks) * C::b_bytes, (uint32_t)C::b_bytes, fb);
                 }
+                const bool odd_last = F4 && 2 * ks + 1 >= p.Kw;  // no second word: zeros
 #pragma unroll
                 for (int j = 0; j < NQ; ++j) {
                     const int q = pt + NPROD * j;
                     if (q < SP) {
                         uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                        if (cur[q].x >= 0) expand32(v[j], lo, hi);  // a pixel (an uncovered concat word: -1s)
+                        if (cur[q].x >= 0) {  // a pixel (an uncovered concat word: -1s)
+                            if (F4) {
+                                lo = nib32(v[j]);  // K half 0: word 2ks, K half 1: word 2ks+1
+                                if (!odd_last) hi = nib32(v2[j]);
+                            } else {
+                                expand32(v[j], lo, hi);
+                            }
+                        }
                         *reinterpret_cast<uint4*>(As + (size_t)q * 16) = lo;
                         *reinterpret_cast<uint4*>(As + ((size_t)SP + q) * 16) = hi;
                     }
@@ -1626,8 +1701,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         const int u = warp - 14;
         if (lane == 0) {
             constexpr int NI = MT > 1 ? BN : BN / 2;
-            const uint32_t idesc =
-                (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NI >> 3) << 17) | ((128u >> 4) << 24);
+            const uint32_t idesc = F4 ? f4_idesc(NI)
+                                      : (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NI >> 3) << 17) |
+                                            ((128u >> 4) << 24);
             int stage = 0, it = 0;
             uint32_t phase = 0;
             for (int item = blockIdx.x; item < n_items && !*abort_v; item += gridDim.x, ++it) {
@@ -1637,7 +1713,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 tc_fence_after();
                 const uint32_t dcol = tmem + (uint32_t)(buf * BN * MT) + (MT > 1 ? 0u : (uint32_t)(u * NI));
                 bool ok = true;
-                for (int kw = 0; kw < p.Kw; ++kw) {
+                for (int ks = 0; ks < KS; ++ks) {
                     if (!mbar_wait_ab(smem_u32(&full_b[stage]), phase, abort_v)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_s = sm0 + (uint32_t)(stage * SB);
@@ -1650,7 +1726,8 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                             // descriptor start addresses are in 16-byte units in the low bits
                             const uint64_t ad = a0 + (uint64_t)(mt * 128 + (t / 3) * p.Gw + t % 3);
                             const uint64_t bd = b0 + (uint64_t)(t * 2 * BN);
-                            tc_mma_i8(dcol + mt * BN, ad, bd, idesc, 1u);
+                            if (F4) tc_mma_f4(dcol + mt * BN, ad, bd, idesc, 1u, tmem + F4_SF, tmem + F4_SF + 16);
+                            else tc_mma_i8(dcol + mt * BN, ad, bd, idesc, 1u);
                         }
                     }
                     tc_commit(smem_u32(&empty_b[stage]));
@@ -1679,13 +1756,17 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
             g.init(geo, p.Gw + pg * PI + r, 128);
             int gmt = 0;
 #pragma unroll 1
-            for (int i = half; i < NPAIR; i += 2) {
+            for (int i = half; i < NPAIR; i += EH) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
                 for (; gmt < mt; ++gmt) g.step(geo);
                 const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN * MT + mt * BN + c0);
                 uint32_t v[32];
                 tc_ld32_nw(ta, v);
                 tc_wait_ld();
+                if (F4) {  // fp32 accumulators hold integers below 2^23: exact
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) v[k] = (uint32_t)__float2int_rn(__uint_as_float(v[k]));
+                }
                 int n = 0, x = 0;
                 const int px = g.pixel(geo, colmap, n, x);
                 if (px >= 0 && cout0 + c0 < p.Cout) {
@@ -2152,12 +2233,13 @@ __global__ void __launch_bounds__(512, 1) bconv_wsx_kernel(const BconvParams p) 
 // bconv_ws_kernel; fold2 adds the per-channel difference to its own
 // threshold. Issuer u takes the phases with px = u.
 // ---------------------------------------------------------------------
-template <int BN, int MT>
+template <int BN, int MT, int EW_ = 8>
 struct WsPoolCfg {
     static constexpr int NPH = 4;
     static constexpr int NBUF = 512 / (NPH * BN * MT);
     static constexpr int PI = 128 * MT;   // half-res positions per item
-    static constexpr int NEPI = 256, NPROD = 192, NT = 512;
+    static constexpr int EW = EW_;  // epilogue warps 0..EW-1 (4 or 8), producers EW..13
+    static constexpr int NEPI = 32 * EW, NPROD = 32 * (14 - EW), NT = 512;
     static constexpr int MAX_GW = 128;
     static constexpr int MAX_SP = PI + 2 * MAX_GW + 8;  // per phase
     static constexpr int NQP = (MAX_SP + NPROD - 1) / NPROD;
@@ -2181,9 +2263,9 @@ struct WsPoolCfg {
 
 // p.HP = staged positions per phase (SP); p.TR = items; p.TC = channel
 // blocks; p.TNI = pipeline stages; p.gk / p.Gw: the half-res grid
-template <int BN, int MT>
+template <int BN, int MT, int EW>
 __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams p) {
-    using C = WsPoolCfg<BN, MT>;
+    using C = WsPoolCfg<BN, MT, EW>;
     constexpr int NPH = C::NPH, NBUF = C::NBUF, PI = C::PI, NQP = C::NQP, NPROD = C::NPROD, NEPI = C::NEPI;
     constexpr int NCH = BN / 32, NPAIR = MT * NCH;
     constexpr int ACC = NPH * MT * BN;  // TMEM columns of one accumulator set
@@ -2274,7 +2356,8 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
     const uint32_t tmem = tmem_s;
     const uint32_t sm0 = smem_u32(wp_smem);
 
-    const int quad = warp & 3, half = (warp >> 2) & 1;
+    constexpr int EH = C::EW / 4;  // epilogue warps per TMEM lane quarter
+    const int quad = warp & 3, half = (warp >> 2) % EH;
     auto start_vals = [&](int c, uint32_t* v) {
 #pragma unroll
         for (int k = 0; k < 32; k += 4) {
@@ -2282,9 +2365,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
             v[k] = (uint32_t)q.x; v[k + 1] = (uint32_t)q.y; v[k + 2] = (uint32_t)q.z; v[k + 3] = (uint32_t)q.w;
         }
     };
-    if (warp < 8) {
+    if (warp < C::EW) {
         for (int b = 0; b < NBUF; ++b)
-            for (int i = half; i < NPAIR; i += 2) {
+            for (int i = half; i < NPAIR; i += EH) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
                 const int cs = (int)((blockIdx.x + (unsigned)b * gridDim.x) % (unsigned)ncb) * BN + c0;
                 uint32_t v[32];
@@ -2299,7 +2382,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
     __syncthreads();
     tc_fence_after();
 
-    if (warp >= 8 && warp < 14) {
+    if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
         const int pt = tid - NEPI;
         auto map_item = [&](int item, int* tb) {
@@ -2443,7 +2526,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
             g.init(geo, p.Gw + pg * PI + r, 128);
             int gmt = 0;
 #pragma unroll 1
-            for (int i = half; i < NPAIR; i += 2) {
+            for (int i = half; i < NPAIR; i += EH) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
                 for (; gmt < mt; ++gmt) g.step(geo);
                 int n = 0, hi = 0, hj = 0;

@@ -75,13 +75,17 @@ int bnn_forward_patched_device(const Model *m, int device, const float *d_cube,
                                void *stream);
 
 /* Process-wide choice of the binary-conv kernel, for measurement and A/B
- * parity tests: 0 = tcgen05 int8 MMAs with nine shifted taps (default;
- * mma.sync int8 where the staging does not fit), 1 = XOR + POPC on the
- * integer pipe, 2 = mma.sync int8 for every layer, 3 = as 0, but layers of
- * at most 32 channels without a pool take the tcgen05 kernel with a kernel
- * row's three column taps stacked in N (measured slower). All compute the
- * reference's P exactly; set it before the forwards to compare (captured
- * graphs keep the kernels they captured). */
+ * parity tests: 0 = tcgen05 (default): int8 MMAs, and e2m1 MMAs
+ * (kind::mxf4: +-1 exact in 4 bits, 64 channels per instruction, fp32
+ * accumulators holding exact integers) for the non-pooled 64- and
+ * 128-channel layers with at least 4 input words, where they measured
+ * faster; mma.sync int8 where the staging does not fit; 1 = XOR + POPC on
+ * the integer pipe; 2 = mma.sync int8 for every layer; 3 = as 4, but layers
+ * of at most 32 channels without a pool take the kernel with a kernel row's
+ * three column taps stacked in N (measured slower); 4 = tcgen05 int8 MMAs
+ * for every layer; 5 = e2m1 MMAs for every non-pooled layer. All compute
+ * the reference's P exactly; set it before the forwards to compare
+ * (captured graphs keep the kernels they captured). */
 int bnn_set_bconv_kernel(int kind);
 
 /* Process-wide choice of the first conv's tensor-core kernel (A/B testing):

@@ -34,13 +34,14 @@ def same_bits(a, b):
                                                  np.ascontiguousarray(b).view(np.uint8))
 
 
-@pytest.fixture(params=["tc", "tcx", "popc", "mma"])
+@pytest.fixture(params=["tc", "tc8", "tc4", "tcx", "popc", "mma"])
 def bconv_kind(request):
-    """Every binary-conv implementation: the default (tcgen05 with nine
-    shifted taps, mma.sync where the staging does not fit), the same with
-    the column taps in N for the non-pooled layers of at most 32 channels,
-    XOR + POPC, and mma.sync throughout. No bounded device wait may have
-    given up while it ran."""
+    """Every binary-conv implementation: the default (tcgen05, int8 with
+    e2m1 for the deeper 64/128-channel layers, mma.sync where the staging
+    does not fit), tcgen05 int8 throughout, tcgen05 e2m1 for every
+    non-pooled layer, int8 with the column taps in N at 32 channels, XOR +
+    POPC, and mma.sync throughout. No bounded device wait may have given up
+    while it ran."""
     bn.set_bconv_kernel(request.param)
     before = bn.device_wait_timeouts(0)
     yield request.param
