@@ -1038,6 +1038,27 @@ static float first_conv_c9(int Cin) {
     return f;
 }
 
+// Coefficients of the tighter per-position bound of realin_ws_kernel. The
+// reference sums a tap's bands sequentially (csrc/bnn_conv_realin.c:66-116):
+// s_1 = y_1 exactly, s_k = fl(s_{k-1} + y_k), y = x*w exact (w = +-1 or 0),
+// so its error is at most sum_{k>=2} u |s_{k-1} + y_k| with
+// |s_{k-1} + y_k| <= (1 + gamma(n)) sum_{i<=k} |y_i|: at most
+// u (1 + gamma(n)) sum_b (n - b)|x_b| over bands b = 0..n-1 (band b enters
+// n - b of the partial sums at most). The nine tap sums add gamma(8) times
+// sum_t |s_t| <= gamma(8) (1 + gamma(n)) sum_t sum_b |x_b|. Both rounded up,
+// with the same 2^-30 margin as first_conv_c9.
+static void first_conv_cab(int Cin, float* ca, float* cb) {
+    const double u = std::ldexp(1.0, -24);
+    auto g = [&](int n) { return n * u / (1.0 - n * u); };
+    const double m = 1.0 + std::ldexp(1.0, -30);
+    const double a = u * (1.0 + g(Cin)) * m, b = g(8) * (1.0 + g(Cin)) * m;
+    float fa = (float)a, fb = (float)b;
+    if ((double)fa < a) fa = std::nextafter(fa, 1.0f);
+    if ((double)fb < b) fb = std::nextafter(fb, 1.0f);
+    *ca = fa;
+    *cb = fb;
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // link-time dependency on libcuda)
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1165,6 +1186,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         p.ipi = cdiv(H, geo.R);
         p.n_items = N * p.ipi;
         p.c9 = first_conv_c9(Cin);
+        first_conv_cab(Cin, &p.ca, &p.cb);
         const int grid = std::min(p.n_items, sm_count());
         if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
         else realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);

@@ -2681,7 +2681,11 @@ struct RealinWsParams {
     int cap, N, Cin, H, W, Cout, cwo;
     int R, Wp, SP, ipi, n_items, NS, KC;  // rows per item, staged width, staged positions, items per image
     int NB;                // input box buffers (realin_dxn_kernel)
-    float c9;              // e2 / T for a full 3x3 window, rounded up
+    float c9;              // e2 / T for a full 3x3 window, rounded up (realin_dxn_kernel)
+    // realin_ws_kernel: the reference's fp32 rounding at a window position
+    // is bounded by ca * sum_b (Cin - b)|x_b| (its sequential band sum) plus
+    // cb * sum_b |x_b| (its share of the nine-tap sum), both rounded up
+    float ca, cb;
 };
 
 __host__ __device__ inline size_t rw_box_bytes(int W, int R) { return (size_t)W * (R + 2) * 32 * 4; }
@@ -2764,9 +2768,10 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         uint32_t phase = 0;
         bool ok = true;
         for (int it = 0; it < my_items && ok && !*abort_v; ++it) {
-            float tsum[RW_NQ], amax[RW_NQ];
+            // per staged position: sum |x| and sum (Cin - band) |x| (both rounded up)
+            float tsum[RW_NQ], wsum[RW_NQ], amax[RW_NQ];
 #pragma unroll
-            for (int j = 0; j < RW_NQ; ++j) { tsum[j] = 0.0f; amax[j] = 0.0f; }
+            for (int j = 0; j < RW_NQ; ++j) { tsum[j] = 0.0f; wsum[j] = 0.0f; amax[j] = 0.0f; }
             for (int kc = 0; kc < KC; ++kc, ++seq) {
                 const int bb = seq % RW_NB;
                 if (pt == 0 && seq >= 1 && seq + 1 < nseq) {
@@ -2796,7 +2801,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                                 float xv[16];
 #pragma unroll
                                 for (int i = 0; i < 16; ++i) xv[i] = src[(size_t)(g2 * 8 + i) * bstride];
-                                // sum |x| in two rounded-up chains (any order bounds the sum from above)
+                                // sum |x| in two rounded-up chains (any order bounds the sum
+                                // from above); the band-weighted sum takes the 16 bands at the
+                                // weight of the first, Cin - (kc*32 + g2*8), the largest
                                 float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
                                 for (int i = 0; i < 16; i += 2) {
@@ -2804,7 +2811,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                                     s1 = __fadd_ru(s1, fabsf(xv[i + 1]));
                                     amax[j] = fmaxf(amax[j], fmaxf(fabsf(xv[i]), fabsf(xv[i + 1])));
                                 }
-                                tsum[j] = __fadd_ru(tsum[j], __fadd_ru(s0, s1));
+                                const float s01 = __fadd_ru(s0, s1);
+                                tsum[j] = __fadd_ru(tsum[j], s01);
+                                wsum[j] = __fmaf_ru(fmaxf((float)(p.Cin - kc * 32 - g2 * 8), 0.0f), s01, wsum[j]);
 #pragma unroll
                             for (int g = g2; g < g2 + 2; ++g) {
                                 uint32_t qv[8];
@@ -2857,8 +2866,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                     const int row = q / Wp, col = q - row * Wp;
                     float e = 0.0f;  // zero columns and positions past the box are exact zeros
                     if (col >= 1 && row < R + 2)
-                        e = amax[j] < 16.0f ? __fmaf_ru(p.c9, tsum[j], rnd) : __int_as_float(0x7f800000);
-                    bt[q] = e;  // NaN inputs: tsum is NaN, and so is e
+                        e = amax[j] < 16.0f ? __fmaf_ru(p.ca, wsum[j], __fmaf_ru(p.cb, tsum[j], rnd))
+                                            : __int_as_float(0x7f800000);
+                    bt[q] = e;  // NaN inputs: the sums are NaN, and so is e
                 }
             }
             mbar_arrive(smem_u32(&bpxf_b[buf]));
