@@ -478,9 +478,9 @@ class BconvLayer:
 
 
 def set_bconv_kernel(kind: str):
-    """'tc' (default: tcgen05, int8 operands, e2m1 for the 64- and 128-channel
-    non-pooled layers with at least 4 input words, mma.sync where the
-    staging does not fit), 'tc8' (tcgen05 int8 throughout), 'tcx' (as
+    """'tc' (default: tcgen05, int8 operands, e2m1 for the deeper non-pooled
+    layers: 64/128 channels with at least 4 input words, 256 with at least
+    16; mma.sync where the staging does not fit), 'tc8' (tcgen05 int8 throughout), 'tcx' (as
     'tc8', with the column taps in N for the non-pooled layers of at most 32
     channels), 'tc4' (tcgen05 e2m1 for every non-pooled layer), 'popc'
     (XOR + POPC) or 'mma' (mma.sync for every layer)."""

@@ -240,9 +240,6 @@ struct HostBin {
 #ifndef BNN_F4_MT128
 #define BNN_F4_MT128 3
 #endif
-#ifndef BNN_F4_MT256
-#define BNN_F4_MT256 1
-#endif
 
 // tcgen05 channel block for a layer of Cout channels: the whole layer up to
 // 256 channels (N of one MMA), 256-channel blocks beyond
@@ -292,16 +289,17 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
     // the kind::mxf4 kernel: per (channel block, K step of two words) the 9
     // taps' B operands [tap][word of the step][channel][16 bytes], each
     // 16 bytes = 32 e2m1 nibbles (channel j of the word in byte j/2, low
-    // nibble for even j: +1 -> 0x2, -1 -> 0xA, absent -> 0)
+    // nibble for even j: +1 -> 0x2, -1 -> 0xA, absent -> 0); channel blocks
+    // of at most 128 (a 256-wide block leaves room for one tile per item)
     {
-        const int KS = (L.Kw + 1) / 2;
-        h.w4.assign((size_t)ncb * KS * 9 * 2 * bn * 16, (int8_t)0);
-        for (int cb = 0; cb < ncb; ++cb)
+        const int KS = (L.Kw + 1) / 2, bn4 = std::min(bn, 128), ncb4 = cdiv(Cout, bn4);
+        h.w4.assign((size_t)ncb4 * KS * 9 * 2 * bn4 * 16, (int8_t)0);
+        for (int cb = 0; cb < ncb4; ++cb)
             for (int kw = 0; kw < L.Kw; ++kw)
                 for (int t = 0; t < 9; ++t)
-                    for (int c = 0; c < bn && cb * bn + c < Cout; ++c) {
-                        const int8_t* src = &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32];
-                        int8_t* dst = &h.w4[((((size_t)cb * KS + kw / 2) * 9 + t) * 2 + (kw & 1)) * bn * 16 +
+                    for (int c = 0; c < bn4 && cb * bn4 + c < Cout; ++c) {
+                        const int8_t* src = &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn4 + c) * 32];
+                        int8_t* dst = &h.w4[((((size_t)cb * KS + kw / 2) * 9 + t) * 2 + (kw & 1)) * bn4 * 16 +
                                             (size_t)c * 16];
                         for (int j = 0; j < 32; ++j) {
                             const uint8_t nib = src[j] > 0 ? 0x2 : src[j] < 0 ? 0xA : 0x0;
@@ -394,7 +392,7 @@ static int set_kernel_attrs(int device) {
         (e = attr_ws<128, BNN_WS128_MT>()) != cudaSuccess || (e = attr_ws<256, BNN_WS256_MT>()) != cudaSuccess ||
         (e = attr_ws<32, BNN_F4_MT32, true>()) != cudaSuccess || (e = attr_ws<64, BNN_F4_MT64, true>()) != cudaSuccess ||
         (e = attr_ws<128, BNN_F4_MT128, true>()) != cudaSuccess ||
-        (e = attr_ws<256, BNN_F4_MT256, true>()) != cudaSuccess || (e = attr_ws<32, 8, false, 4>()) != cudaSuccess ||
+        (e = attr_ws<32, 8, false, 4>()) != cudaSuccess ||
         (e = attr_ws<64, BNN_F4_MT64, true, 4>()) != cudaSuccess ||
         (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
         (e = attr_ws_pool<128, 1>()) != cudaSuccess || (e = attr_wsx<2>()) != cudaSuccess ||
@@ -946,8 +944,11 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
     // e2m1 MMAs where they measured faster than int8 (4096 32x32 patches):
     // 64- and 128-channel layers with at least 4 input words (dec3.conv1
     // 0.090 vs 0.117 ms, dec2.conv1 0.162 vs 0.175, dec3.conv2 0.058 vs
-    // 0.060); kind 5 takes them for every non-pooled layer
-    const bool f4 = (g_bconv_kind == 0 && (p.ubn == 64 || p.ubn == 128) && p.Kw >= 4) || g_bconv_kind == 5;
+    // 0.060), 256-channel layers with at least 16, in 128-channel blocks
+    // (dec4.conv1 0.105 vs 0.120, bott.conv2 0.060 vs 0.062; shallower ones
+    // are slower that way); kind 5 takes them for every non-pooled layer
+    const bool f4 = (g_bconv_kind == 0 && (p.ubn == 64 || p.ubn == 128) && p.Kw >= 4) ||
+                    (g_bconv_kind == 0 && p.ubn == 256 && p.Kw >= 16) || g_bconv_kind == 5;
     if (f4 && !p.out2 && p.w4) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
@@ -956,7 +957,7 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
                 rc = p.cw1 > 0 ? launch_ws<64, BNN_F4_MT64, true, 4>(p, N, st) : launch_ws<64, BNN_F4_MT64, true>(p, N, st);
                 break;
             case 128: rc = launch_ws<128, BNN_F4_MT128, true>(p, N, st); break;
-            case 256: rc = launch_ws<256, BNN_F4_MT256, true>(p, N, st); break;
+            case 256: rc = launch_ws<128, BNN_F4_MT128, true>(p, N, st); break;  // 128-channel blocks
         }
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }

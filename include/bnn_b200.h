@@ -78,8 +78,9 @@ int bnn_forward_patched_device(const Model *m, int device, const float *d_cube,
  * parity tests: 0 = tcgen05 (default): int8 MMAs, and e2m1 MMAs
  * (kind::mxf4: +-1 exact in 4 bits, 64 channels per instruction, fp32
  * accumulators holding exact integers) for the non-pooled 64- and
- * 128-channel layers with at least 4 input words, where they measured
- * faster; mma.sync int8 where the staging does not fit; 1 = XOR + POPC on
+ * 128-channel layers with at least 4 input words and the 256-channel ones
+ * with at least 16, where they measured faster; mma.sync int8 where the
+ * staging does not fit; 1 = XOR + POPC on
  * the integer pipe; 2 = mma.sync int8 for every layer; 3 = as 4, but layers
  * of at most 32 channels without a pool take the kernel with a kernel row's
  * three column taps stacked in N (measured slower); 4 = tcgen05 int8 MMAs
