@@ -3445,8 +3445,10 @@ struct HeadParams {
 
 // Two pixels per thread and every class at once: 2*ncls independent
 // sequential chains (the order within each chain is the reference's), the
-// +-1 products as sign selects of weights held in shared memory. 32-bit
-// indexing (the forward keeps N*H*W < 2^31).
+// +-1 products as sign flips of weights held in shared memory (one mask per
+// pixel and channel, shared by the classes), the two pixels' chains of a
+// class advanced by one fp32x2 add. 32-bit indexing (the forward keeps
+// N*H*W < 2^31).
 constexpr int HEAD_MAXC = 8;        // classes handled per pass
 constexpr int HEAD_MAXW = 64 * 32;  // weights held in shared memory (ncls*Cin)
 __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
@@ -3463,21 +3465,27 @@ __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
         const bool two = g0 + 1 < total;
         if (in_smem) {
             for (int o0 = 0; o0 < p.ncls; o0 += 4) {
-                float acc[2][4];
+                // acc[k] = the chains of class o0 + k at pixels g0 (.x) and g0 + 1 (.y),
+                // advanced together by one fp32x2 add (two round-to-nearest adds)
+                float2 acc[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc[0][k] = acc[1][k] = o0 + k < p.ncls ? bs[o0 + k] : 0.0f;
+                for (int k = 0; k < 4; ++k) {
+                    const float b0 = o0 + k < p.ncls ? bs[o0 + k] : 0.0f;
+                    acc[k] = make_float2(b0, b0);
+                }
                 for (int cw = 0; cw < p.cwi; ++cw) {
-                    const uint32_t w0 = __ldg(p.in + (size_t)g0 * p.cwi + cw);
-                    const uint32_t w1 = two ? __ldg(p.in + (size_t)(g0 + 1) * p.cwi + cw) : 0u;
+                    // bit 0 (-1) flips the weight's sign bit: the same bits as -w
+                    const uint32_t n0 = ~__ldg(p.in + (size_t)g0 * p.cwi + cw);
+                    const uint32_t n1 = two ? ~__ldg(p.in + (size_t)(g0 + 1) * p.cwi + cw) : 0u;
                     const int cn = min(32, p.Cin - cw * 32);
                     auto step = [&](int b) {
                         const int c = cw * 32 + b;
+                        const uint32_t s0 = (n0 << (31 - b)) & 0x80000000u, s1 = (n1 << (31 - b)) & 0x80000000u;
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             if (o0 + k < p.ncls) {
-                                const float wv = ws[(o0 + k) * p.Cin + c];
-                                acc[0][k] = __fadd_rn(acc[0][k], ((w0 >> b) & 1u) ? wv : -wv);
-                                acc[1][k] = __fadd_rn(acc[1][k], ((w1 >> b) & 1u) ? wv : -wv);
+                                const uint32_t wv = __float_as_uint(ws[(o0 + k) * p.Cin + c]);
+                                acc[k] = __fadd2_rn(acc[k], make_float2(__uint_as_float(wv ^ s0), __uint_as_float(wv ^ s1)));
                             }
                         }
                     };
@@ -3494,7 +3502,7 @@ __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
                     const unsigned g = g0 + h, n = g / HW, px = g - n * HW;
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                        if (o0 + k < p.ncls) p.out[(size_t)(n * p.ncls + o0 + k) * HW + px] = acc[h][k];
+                        if (o0 + k < p.ncls) p.out[(size_t)(n * p.ncls + o0 + k) * HW + px] = h ? acc[k].y : acc[k].x;
                 }
             }
         } else {
