@@ -379,6 +379,8 @@ def run_ours(args):
                  if bf16 else "fallback 2.25 P int8 MAC/s",
                  "frac_of_mma_sync_measured": round(bconv_ach / mma_sync_peak, 4),
                  "frac_of_popc_peak": round(bconv_ach / popc_peak, 4),
+                 # the e2m1 layers (default: the deeper 64/128/256-channel ones) have twice the int8 rate
+                 "frac_of_e2m1_peak": round(bconv_ach / (2 * tensor_i8_peak), 4),
                  "time_share": frac_split.get("bconv")}
                 if args.bconv in ("tc", "tc8", "tc4", "tcx", "mma") else
                 {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
