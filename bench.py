@@ -137,21 +137,248 @@ def cpu_info():
     return model, os.cpu_count() or 1
 
 
+REF_BUILD = {"march": None}  # which reference build ran (set by run_ref)
+
+
+def run_ref(name, argv, threads):
+    """Run a reference timing driver built from the reference sources: the
+    -march=native build (the reference Makefile's flags, csrc/Makefile:9-11)
+    when it runs on this host, else the portable -march=x86-64-v3 one. Returns
+    (CompletedProcess, None) or (None, reason)."""
+    last = None
+    for sub, march in (("native", "native"), ("", "x86-64-v3")):
+        exe = os.path.join(ROOT, "oracle", "_ref", sub, name)
+        if not os.path.exists(exe):
+            continue
+        r = subprocess.run([exe] + [str(a) for a in argv], capture_output=True, text=True,
+                           env=dict(os.environ, OMP_NUM_THREADS=str(threads)))
+        if r.returncode < 0:  # killed by a signal: an instruction this host lacks
+            last = f"{name} ({march}) died with signal {-r.returncode}"
+            continue
+        if r.returncode != 0:
+            return None, f"{name} failed: {r.stderr.strip()[-200:]}"
+        REF_BUILD["march"] = march
+        return r, None
+    return None, last or f"oracle/_ref/{name} not built (needs the reference tree at build time)"
+
+
 def ref_bench(blob_path, n, H, W, procs, steps, warm, first=0, stem=False, name=None):
     """Reference engine (compiled from the reference sources) on the host:
     the v1 engine, with stem=True the v2 spectral-stem engine, or the driver
     `name` (ref_bench_react: the v3 ReAct engine)."""
     name = name or ("ref_bench_stem" if stem else "ref_bench")
-    exe = os.path.join(ROOT, "oracle", "_ref", name)
-    if not os.path.exists(exe):
-        return None, f"oracle/_ref/{name} not built (needs the reference tree at build time)"
-    r = subprocess.run([exe, blob_path, str(n), str(H), str(W), str(procs), str(SEED_INPUT), str(steps),
-                        str(warm), str(first)], capture_output=True, text=True,
-                       env=dict(os.environ, OMP_NUM_THREADS="1"))
-    if r.returncode != 0:
-        return None, f"ref_bench failed: {r.stderr.strip()[-200:]}"
+    r, err = run_ref(name, [blob_path, n, H, W, procs, SEED_INPUT, steps, warm, first], 1)
+    if r is None:
+        return None, err
     secs = [float(ln.split()[2]) for ln in r.stdout.splitlines() if ln.startswith("step ")]
     return secs, None
+
+
+# ---------------------------------------------------------------- config 1
+SWEEP_C = (64, 128, 256, 512)
+SWEEP_H = (128, 64, 32, 16)
+SWEEP_N = 64
+SEED_SWEEP = 11
+
+
+def sweep_layer(C, seed, pool):
+    """Random weights (uniform bits, kidx-packed as in the blob) and folds
+    (rule P >= t, t uniform in [-2C, 2C]) of one sweep layer."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    nw = (9 * C + 63) // 64
+    packed = np.frombuffer(rng.bytes(C * nw * 8), np.uint64).reshape(C, nw).copy()
+    if (9 * C) % 64:
+        packed[:, -1] &= np.uint64((1 << ((9 * C) % 64)) - 1)
+
+    def fold():
+        return {"type": np.ones(C, np.int32), "t": rng.integers(-2 * C, 2 * C + 1, C).astype(np.int32),
+                "lo": np.zeros(C, np.int32), "hi": np.zeros(C, np.int32)}
+
+    return packed, fold(), (fold() if pool else None)
+
+
+def ref_sweep_point(C, H, pool, budget):
+    """Seconds per image of the reference's own layer (bconv_dispatch +
+    apply_fold_int [+ maxpool_P + apply_fold_int]), all host cores."""
+    _, cores = cpu_info()
+    r, err = run_ref("ref_bench_bconv", [C, H, int(pool), budget], cores)
+    if r is None:
+        return None, err
+    kv = dict(ln.split(None, 1) for ln in r.stdout.splitlines() if " " in ln)
+    return float(kv["image_s"]), int(kv["images"])
+
+
+def run_sweep(local, reps=10, warm=3, ref_budget=0.3, cpu=True):
+    """the isolated fused binary conv layer (3x3, pad 1,
+    stride 1, Cin = Cout = C) over C in {64,128,256,512} x H = W in
+    {128,64,32,16}, batch 64, without and with the 2x2 max-pool of P, through
+    bnn_bconv_layer_run on device buffers. Each timed run is one launch,
+    bracketed by CUDA events on its stream, after an L2 flush (a 256 MB
+    write); the median of `reps` runs is reported. 1 bitop = 1 binary MAC =
+    Cout*H*W*Cin*9 per image (the reference profiler's work unit)."""
+    import numpy as np
+    import torch
+
+    import bnns_to_c_b200 as bn
+
+    peaks = read_peaks()
+    bf16 = peaks.get("bf16_tflops")
+    i8 = bf16 * 1e3 if bf16 else 2.25e6          # G int8 MAC/s: 2x the bf16 MAC rate
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    props = torch.cuda.get_device_properties(local)
+    popc = props.multi_processor_count * POPC_PER_CLK_SM * 32 * (peaks.get("sm_max_mhz") or 1965.0) * 1e6 / 1e9
+    stream = torch.cuda.Stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    model, cores = cpu_info()
+    shapes, tot_mac, tot_ms, tot_ref = [], 0.0, 0.0, 0.0
+    for C in SWEEP_C:
+        for pool in (False, True):
+            packed, f1, f2 = sweep_layer(C, SEED_SWEEP + C + int(pool), pool)
+            L = bn.BconvLayer(local, C, C, packed, f1, f2)
+            for H in SWEEP_H:
+                N, W, cw = SWEEP_N, H, C // 32
+                din = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, H, W, cw), dtype=torch.int32, device="cuda")
+                dout = torch.empty((N, H, W, cw), dtype=torch.int32, device="cuda")
+                dpool = torch.empty((N, H // 2, W // 2, cw), dtype=torch.int32, device="cuda") if pool else None
+                torch.cuda.synchronize()
+                with torch.cuda.stream(stream):
+                    for _ in range(warm):
+                        L.run(din, N, H, W, dout, dpool, stream=stream)
+                    kern = bn.bconv_last_kernel()
+                    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                          for _ in range(reps)]
+                    for r in range(reps):
+                        flush.fill_(r & 0xFF)
+                        ev[r][0].record(stream)
+                        L.run(din, N, H, W, dout, dpool, stream=stream)
+                        ev[r][1].record(stream)
+                stream.synchronize()
+                ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+                mac = float(N) * H * W * C * C * 9
+                nbytes = N * H * W * C // 8 * 2 + (N * (H // 2) * (W // 2) * C // 8 if pool else 0) + C * C * 9 // 8
+                g = mac / (ms * 1e6)
+                row = {"C": C, "H": H, "pool": pool, "ms": round(ms, 5), "gbitops": round(g, 1),
+                       "frac_int8": round(g / i8, 4), "frac_e2m1": round(g / (2 * i8), 4),
+                       "frac_popc": round(g / popc, 3), "hbm_gbs": round(nbytes / (ms * 1e6), 1),
+                       "kernel": kern}
+                if cpu:
+                    per, err = ref_sweep_point(C, H, pool, ref_budget)
+                    if per is not None:
+                        row["ref_ms_per_batch"] = round(per * N * 1e3, 3)
+                        row["ref_gbitops"] = round(mac / (per * N) / 1e9, 2)
+                        row["speedup"] = round(per * N * 1e3 / ms, 1)
+                        tot_ref += per * N * 1e3
+                    else:
+                        row["ref_error"] = err
+                shapes.append(row)
+                tot_mac += mac
+                tot_ms += ms
+                del din, dout, dpool
+            L.close()
+    del flush
+    g_all = tot_mac / (tot_ms * 1e6)
+    out = {
+        "metric": "binary-conv Gbitop/s (config 1 sweep, 1 bitop = 1 binary MAC)",
+        "gbitops": round(g_all, 1), "ms_total": round(tot_ms, 3),
+        "frac_int8": round(g_all / i8, 4), "frac_e2m1": round(g_all / (2 * i8), 4),
+        "peak_int8_gmacs": round(i8, 1), "peak_source": "int8 dense tensor rate = 2x the measured cuBLAS bf16 rate "
+        "(MEASURED_PEAKS.json)" if bf16 else "fallback", "popc_peak_gbitops": round(popc, 1),
+        "config": {"C": list(SWEEP_C), "H=W": list(SWEEP_H), "batch": SWEEP_N, "pool": [False, True],
+                   "thresholds": "P >= t, t ~ U[-2C, 2C]", "timing": f"median of {reps} single launches, "
+                   "CUDA events, L2 flushed (256 MB write) before each", "data": "uniform random bits"},
+        "shapes": shapes,
+    }
+    if cpu and tot_ref:
+        out["reference"] = {"ms_total": round(tot_ref, 1), "gbitops": round(tot_mac / (tot_ref * 1e6), 2),
+                            "speedup": round(tot_ref / tot_ms, 1), "cores": cores, "march": REF_BUILD["march"],
+                            "sample": f"images of each shape timed for up to {ref_budget} s after one untimed image "
+                                      f"(at most 64), scaled to the batch of {SWEEP_N}; OpenMP on {cores} threads, "
+                                      f"{model}"}
+    return out
+
+
+# ---------------------------------------------------------------- config 0
+def cli_forward_ms(exe, blob_path, out_path, reps, threads):
+    """Median forward ms that a csrc/main.c-style CLI reports for one 32x32
+    'rand' patch (srand(1234) uniform [-1, 1] input, `reps` timed forwards)."""
+    r = subprocess.run([exe, blob_path, "rand", out_path, "32", "32", str(reps)], capture_output=True, text=True,
+                       env=dict(os.environ, OMP_NUM_THREADS=str(threads)))
+    if r.returncode != 0:
+        return None, f"{os.path.basename(exe)} rc {r.returncode}: {r.stderr.strip()[-160:]}"
+    for ln in r.stderr.splitlines():
+        if ln.startswith("# forward"):
+            return float(ln.split(":", 1)[1].split()[0]), None
+    return None, "no forward line"
+
+
+def run_single(m, local, reps=50, ref_reps=5, cpu=True):
+    """one 32x32x120 patch, batch 1 (latency).
+    cli: this engine's bnn_infer (csrc/main.c semantics: bnn_forward on host
+    buffers, median of `reps`), the call an existing caller of main.c makes;
+    device: bnn_forward_device with N = 1 from HBM (graph replay, CUDA events);
+    reference: its own CLI built from its sources, 1 thread and all cores."""
+    import numpy as np
+    import torch
+
+    import bnns_to_c_b200 as bn
+
+    out = {"metric": "single-patch forward latency (32x32x120, batch 1)", "unit": "us/patch"}
+    with tempfile.TemporaryDirectory() as td:
+        blob = os.path.join(td, "m.blob")
+        with open(blob, "wb") as f:
+            f.write(model_blob())
+        mine, err = cli_forward_ms(bn.CLI_PATH, blob, os.path.join(td, "ours.bin"), reps, 1)
+        out["cli_us"] = round(mine * 1e3, 1) if mine is not None else None
+        if err:
+            out["cli_error"] = err
+        # the same call in-process (ctypes), pageable host buffers
+        x = np.random.default_rng(3).standard_normal((120, 32, 32)).astype(np.float32)
+        y = np.empty((3, 32, 32), np.float32)
+        L = bn.lib()
+        for _ in range(5):
+            L.bnn_forward(m.handle, x.ctypes.data, 32, 32, y.ctypes.data)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            L.bnn_forward(m.handle, x.ctypes.data, 32, 32, y.ctypes.data)
+            ts.append(time.perf_counter() - t0)
+        out["bnn_forward_us"] = round(statistics.median(ts) * 1e6, 1)
+        din = torch.from_numpy(x[None]).cuda()
+        dout = torch.empty((1, 3, 32, 32), dtype=torch.float32, device="cuda")
+        st = torch.cuda.Stream()
+        for _ in range(5):
+            m.forward_device(local, din, 1, 32, 32, dout, st)
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            m.forward_device(local, din, 1, 32, 32, dout, st)
+        e1.record(st)
+        st.synchronize()
+        out["device_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 1)
+        if cpu:
+            _, cores = cpu_info()
+            ref = {}
+            for th in (1, cores):
+                r, err = run_ref("bnn_infer", [blob, "rand", os.path.join(td, "ref.bin"), 32, 32, ref_reps], th)
+                ms = None
+                if r is not None:
+                    for ln in r.stderr.splitlines():
+                        if ln.startswith("# forward"):
+                            ms = float(ln.split(":", 1)[1].split()[0])
+                ref[f"threads_{th}_us"] = round(ms * 1e3, 1) if ms is not None else err
+            ref["march"] = REF_BUILD["march"]
+            out["reference"] = ref
+            if mine is not None and os.path.exists(os.path.join(td, "ref.bin")):
+                a = np.fromfile(os.path.join(td, "ours.bin"), np.float32)
+                b = np.fromfile(os.path.join(td, "ref.bin"), np.float32)
+                out["cli_logits_identical"] = bool(a.shape == b.shape and np.array_equal(a.view(np.uint32),
+                                                                                         b.view(np.uint32)))
+            if mine is not None and isinstance(ref.get("threads_1_us"), float):
+                out["speedup_vs_reference_1_thread"] = round(ref["threads_1_us"] / out["cli_us"], 1)
+    return out
 
 
 def model_blob(stem=0):
@@ -208,6 +435,29 @@ def run_reference(args):
     return 0
 
 
+def gpu_affinity(local):
+    """Pin this process to the host CPUs local to its GPU (the PCI device's
+    local_cpulist), before any pinned host buffer is touched, so the staging
+    pages and copy threads sit on the GPU's NUMA node. Returns what was done."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(local)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        base = f"/sys/bus/pci/devices/{bus}"
+        cpus = set()
+        for part in open(f"{base}/local_cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        node = open(f"{base}/numa_node").read().strip()
+        if cpus and cpus != set(os.sched_getaffinity(0)):
+            os.sched_setaffinity(0, cpus)
+            return {"pci": bus, "numa_node": node, "cpus": len(cpus), "pinned": True}
+        return {"pci": bus, "numa_node": node, "cpus": len(cpus), "pinned": False}
+    except Exception as e:  # no sysfs entry (containers), keep the default
+        return {"error": str(e)[:120]}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -238,6 +488,7 @@ def run_ours(args):
 
     P, H, W = args.patches, args.H, args.W
     stem, metric, wname = variant(args)
+    affinity = gpu_affinity(local)
     bn.set_bconv_kernel(args.bconv)
     bn.set_first_conv_kernel(args.first)
     m = (bn.StemModel if stem else bn.Model)(data=model_blob(stem))
@@ -267,6 +518,17 @@ def run_ours(args):
     torch.cuda.synchronize()
     dev_ms = maxall(e0.elapsed_time(e1))
     clocks = clk.summary()
+    # the same K-step region repeated (run-to-run spread of the headline; not the headline itself)
+    reps_ms = []
+    for _ in range(args.repeats):
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            m.forward_device(local, din, P, H, W, dout, stream)
+        f1.record(stream)
+        stream.synchronize()
+        reps_ms.append(maxall(f0.elapsed_time(f1)))
     # ---------------- per-kernel CUDA events: separate profiled steps (eager launches) ----------------
     m.profile(True)
     m.forward_device(local, din, P, H, W, dout, stream)
@@ -279,7 +541,7 @@ def run_ours(args):
     m.profile(False)
 
     # ---------------- end to end through the public host API ----------------
-    e2e_s, same, h2d_gbs = None, None, None
+    e2e_s, same, h2d_gbs, h2d_agg_gbs = None, None, None, None
     if not args.no_e2e:
         hin = torch.empty((P, 120, H, W), dtype=torch.float32, pin_memory=True)
         hin.copy_(din.cpu())
@@ -298,11 +560,21 @@ def run_ours(args):
         # the host link by itself: one pinned 2 GB host->device copy, CUDA events
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         din.copy_(hin, non_blocking=True)
+        torch.cuda.synchronize()
         c0.record()
         din.copy_(hin, non_blocking=True)
         c1.record()
         torch.cuda.synchronize()
         h2d_gbs = hin.numel() * 4 / (c0.elapsed_time(c1) * 1e6)
+        # the box's aggregate host->device ceiling: every rank copies its 2 GB at
+        # the same moment (after a barrier); time = the slowest rank's copy
+        barrier()
+        c0.record()
+        din.copy_(hin, non_blocking=True)
+        c1.record()
+        torch.cuda.synchronize()
+        agg_s = maxall(c0.elapsed_time(c1) / 1e3)
+        h2d_agg_gbs = world * hin.numel() * 4 / agg_s / 1e9
 
     if rank == 0:
         peaks = read_peaks()
@@ -359,8 +631,15 @@ def run_ours(args):
                     "d2h_bytes_per_step": P * 3 * H * W * 4, "api": "bnn_forward_batch (pinned host buffers)",
                     "matches_device_path": same,
                     "h2d_link_gbs": round(h2d_gbs, 2) if h2d_gbs else None,
-                    "frac_of_h2d_link": round(e2e * P * 120 * H * W * 4 / P / (h2d_gbs * 1e9), 4)
-                    if (e2e and h2d_gbs) else None},
+                    # per GPU: this rank's share of the e2e rate against its own link
+                    "frac_of_h2d_link": round(e2e / world * 120 * H * W * 4 / (h2d_gbs * 1e9), 4)
+                    if (e2e and h2d_gbs) else None,
+                    "h2d_aggregate_gbs": round(h2d_agg_gbs, 2) if h2d_agg_gbs else None,
+                    "frac_of_h2d_aggregate": round(e2e * 120 * H * W * 4 / (h2d_agg_gbs * 1e9), 4)
+                    if (e2e and h2d_agg_gbs) else None,
+                    "h2d_aggregate_how": "all ranks copy their pinned 2 GB input at once after a barrier; "
+                                         "world x bytes / the slowest rank's copy time",
+                    "affinity": affinity},
             "gpu_launches": launches_per_fwd * args.steps * (1 + (0 if args.no_e2e else chunks)),
             "device_wait_timeouts": bn.device_wait_timeouts(local),
             "roofline": (
@@ -410,12 +689,49 @@ def run_ours(args):
                               "min_ms": round(P * 120 * H * W * 4 / (peaks.get("hbm_gbs", 6538.9) * 1e6), 4)},
             },
             "per_kernel_ms": {r["label"]: round(r["ms"] / r["calls"], 4) for r in recs},
+            "per_layer_frac": {r["label"]: round(r["work"] / (r["ms"] * 1e6) / tensor_i8_peak, 4)
+                               for r in recs if r["op"] == "bconv"},
+            "per_kernel_source": "CUDA events around each launch in separate eager (non-graph) steps after "
+                                 "the timed region; their sum runs ~3% above the graph-replayed step, so the "
+                                 "per-kernel fractions are slightly pessimistic",
+            "repeats_ms_per_step": [round(t / args.steps, 4) for t in reps_ms],
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if world == 1 and not args.no_single:
+            line["single"] = run_single(m, local, cpu=not args.no_cpu_baseline)
+        if world == 1 and not args.no_sweep:
+            line["sweep"] = run_sweep(local, cpu=not args.no_cpu_baseline)
         print(json.dumps(line))
     if dist:
         dist.destroy_process_group()
+    return 0
+
+
+def run_sweep_line(args):
+    """--workload sweep: BASELINE config 1 alone, as its own JSON line
+    (rank 0 of a one-GPU run)."""
+    import torch
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    import bnns_to_c_b200 as bn
+
+    bn.set_bconv_kernel(args.bconv)
+    with ClockSampler(local) as clk:
+        sw = run_sweep(local, reps=max(3, args.steps), warm=args.warmup, cpu=not args.no_cpu_baseline)
+    line = {"metric": sw["metric"], "value": sw["gbitops"], "unit": "Gbitop/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": sw["ms_total"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "b1", "data": "synthetic",
+            "config": dict(sw["config"], workload="bconv_sweep_C64-512_H16-128_b64"),
+            "roofline": {"bound": "tensor", "achieved": sw["gbitops"], "peak": sw["peak_int8_gmacs"],
+                         "unit": "Gbitop/s (1 binary MAC run as one int8 or e2m1 MAC)", "frac": sw["frac_int8"],
+                         "frac_of_e2m1_peak": sw["frac_e2m1"], "traffic": None},
+            "cpu_baseline": ({"value": sw["reference"]["gbitops"], "unit": "Gbitop/s",
+                              "cores": sw["reference"]["cores"], "kind": "reference",
+                              "sample": sw["reference"]["sample"]} if "reference" in sw else None),
+            "clocks": clk.summary(), "sweep": sw}
+    print(json.dumps(line))
     return 0
 
 
@@ -714,7 +1030,11 @@ def main():
                          "tc8 = tcgen05 int8 throughout, tc4 = tcgen05 e2m1 for every non-pooled layer, "
                          "tcx = tc8 with the column taps in N at 32 channels, popc = XOR + POPC, "
                          "mma = mma.sync for every layer")
-    ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem", "react"],
+    ap.add_argument("--no-sweep", action="store_true", help="leave the config-1 binary-conv sweep out of the line")
+    ap.add_argument("--no-single", action="store_true", help="leave the config-0 single-patch latency out")
+    ap.add_argument("--repeats", type=int, default=4,
+                    help="extra repeats of the K-step device region (spread only; the headline is the first)")
+    ap.add_argument("--workload", default="unet", choices=["unet", "scene", "stem", "react", "sweep"],
                     help="unet: BASELINE config 2 (default); scene: config 3, whole cubes through the tiler; "
                          "stem: config 2's batch through the v2 spectral-stem variant (16-channel stem); "
                          "react: config 4, the v3 ReAct UNet on 64x64 patches")
@@ -729,6 +1049,8 @@ def main():
         return run_scene(args)
     if args.workload == "react":
         return run_react(args)
+    if args.workload == "sweep":
+        return run_sweep_line(args)
     return run_ours(args)
 
 

@@ -118,6 +118,9 @@ def lib():
         "bnn_react_forward_launches": (ip, [vp, ip, ip, ip]),
         "bnn_react_set_conv_kernel": (ip, [ip]),
         "bnn_react_device_error": (ip, [ip, ctypes.POINTER(ctypes.c_uint)]),
+        "bnn_wait_probe": (ip, [ip, ip, ctypes.POINTER(ip), ctypes.POINTER(ctypes.c_uint)]),
+        "bnn_debug_inject_fault": (ip, [ip, ip]),
+        "bnn_bconv_last_kernel": (cp, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -498,6 +501,28 @@ def device_wait_timeouts(device=0):
     n = ctypes.c_uint()
     _check(lib().bnn_device_error(device, ctypes.byref(n)))
     return n.value
+
+
+def wait_probe(device=0, rounds=4096):
+    """Run the bounded-wait self-test kernel (an mbarrier phase nothing
+    completes). Returns (gave_up, device counter afterwards)."""
+    g, n = ctypes.c_int(), ctypes.c_uint()
+    _check(lib().bnn_wait_probe(device, rounds, ctypes.byref(g), ctypes.byref(n)))
+    return bool(g.value), n.value
+
+
+FAULT_ALLOC, FAULT_WAIT, FAULT_SHARD = 1, 2, 3
+
+
+def inject_fault(kind: int, arg: int = 0):
+    """Host-side fault injection (bnn_debug_inject_fault); kind 0 clears."""
+    _check(lib().bnn_debug_inject_fault(kind, arg))
+
+
+def bconv_last_kernel() -> str:
+    """Name and template parameters of the last binary-conv kernel this
+    thread launched."""
+    return lib().bnn_bconv_last_kernel().decode()
 
 
 def synth_device(device, seed, first, n, bands, H, W, d_out, stream=None):

@@ -11,7 +11,9 @@
 // The forward order is the reference's (csrc/bnn_model.c:150-253): 19
 // kernel launches (first conv, 17 fused binary convs, head).
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
+#include <cstdarg>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -37,6 +39,39 @@ namespace bnn {
 
 static inline int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
 static inline int cw_of(int c) { return (c + 31) >> 5; }
+
+// -------------------------------------------------------------------
+// host-side fault injection (bnn_debug_inject_fault; tests of the failure
+// paths, no GPU fault involved)
+// -------------------------------------------------------------------
+static std::atomic<int> g_fail_alloc{0};   // the k-th next device allocation fails
+static std::atomic<int> g_fail_wait{0};    // the next synchronous call meets a wait that gives up
+static std::atomic<int> g_fail_shard{-1};  // this shard of the next multi-device batch fails
+
+// every device allocation of the engine goes through here
+template <class T>
+static cudaError_t dev_malloc(T** p, size_t bytes) {
+    int k = g_fail_alloc.load();
+    while (k > 0 && !g_fail_alloc.compare_exchange_weak(k, k - 1)) {
+    }
+    if (k == 1) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc((void**)p, bytes);
+}
+
+// name of the last binary-conv kernel this thread launched (with its
+// template parameters), for benchmarks and tests that must know which
+// implementation ran
+static thread_local char g_last_kernel[96];
+static void note_kernel(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
+static void note_kernel(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_kernel, sizeof g_last_kernel, fmt, ap);
+    va_end(ap);
+}
 
 // -------------------------------------------------------------------
 // device-side layer descriptions
@@ -119,6 +154,7 @@ struct DevState {
     cudaEvent_t ev_in[2], ev_comp[2], ev_out[2];
     cudaEvent_t ev_last;  // completion of the last forward enqueued on this device
     bool events = false;
+    unsigned int* wt_host = nullptr;  // pinned: the device wait give-up counter at a call's start and end
     // patched (scene) forward: a chunk of tiles in and out, and a scene slab
     float *tin = nullptr, *tout = nullptr;
     size_t tcap = 0;  // floats of tin / tout
@@ -182,6 +218,8 @@ static void dev_release(DevState* d) {
     if (d->cs) cudaStreamDestroy(d->cs);
     if (d->h2d) cudaStreamDestroy(d->h2d);
     if (d->d2h) cudaStreamDestroy(d->d2h);
+    if (d->wt_host) cudaFreeHost(d->wt_host);
+    d->wt_host = nullptr;
     cudaSetDevice(prev);
 }
 
@@ -614,7 +652,7 @@ static int dev_init(const Model* m, DevState* d) {
     const size_t hw = (size_t)m->head_Cout * m->head_Cin;
     total += align256(hw * 4) + align256((size_t)m->head_Cout * 4);
     void* base = nullptr;
-    if (cudaMalloc(&base, total) != cudaSuccess) {
+    if (dev_malloc(&base, total) != cudaSuccess) {
         cudaGetLastError();
         return set_error(BNN_ERR_OOM, "cudaMalloc weights (%zu bytes) on device %d", total, d->device);
     }
@@ -659,6 +697,8 @@ static int dev_init(const Model* m, DevState* d) {
     CK(cudaEventCreateWithFlags(&d->ev_last, cudaEventDisableTiming));
     CK(cudaEventRecord(d->ev_last, d->cs));
     d->events = true;
+    CK(cudaMallocHost((void**)&d->wt_host, 2 * sizeof(unsigned int)));
+    d->wt_host[0] = d->wt_host[1] = 0u;
     return BNN_OK;
 }
 
@@ -742,7 +782,7 @@ static int arena_reserve(const Model* m, DevState* d, int N, int H, int W) {
         a.base = nullptr;
     }
     void* base = nullptr;
-    if (cudaMalloc(&base, off) != cudaSuccess) {
+    if (dev_malloc(&base, off) != cudaSuccess) {
         cudaGetLastError();
         a.N = 0;
         return set_error(BNN_ERR_OOM, "cudaMalloc activation arena (%zu bytes)", off);
@@ -802,6 +842,7 @@ static int launch_bconv_t(BconvParams p, int N, cudaStream_t st) {
     bconv3x3_kernel<BN, TM, TN, KC><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv launch: %s", cudaGetErrorString(e));
+    note_kernel("bconv3x3_kernel<%d,%d,%d,%d> (XOR+POPC)", BN, TM, TN, KC);
     return BNN_OK;
 }
 
@@ -823,6 +864,7 @@ static int launch_bmma(BconvParams p, int N, cudaStream_t st) {
     bconv_mma_kernel<BN><<<grid, Cfg::NT, Cfg::smem_bytes(g.HP), st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv mma launch: %s", cudaGetErrorString(e));
+    note_kernel("bconv_mma_kernel<%d> (mma.sync int8)", BN);
     return BNN_OK;
 }
 
@@ -869,6 +911,8 @@ static int launch_ws(BconvParams p, int N, cudaStream_t st) {
     bconv_ws_kernel<BN, MT, F4, EW><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 launch: %s", cudaGetErrorString(e));
+    note_kernel("bconv_ws_kernel<%d,%d,%s,%d> (tcgen05 %s)", BN, MT, F4 ? "e2m1" : "i8", EW,
+                F4 ? "kind::mxf4" : "kind::i8");
     return BNN_OK;
 }
 
@@ -897,6 +941,7 @@ static int launch_wsx(BconvParams p, int N, cudaStream_t st) {
     bconv_wsx_kernel<MT><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 (taps in N) launch: %s", cudaGetErrorString(e));
+    note_kernel("bconv_wsx_kernel<%d> (tcgen05 kind::i8, column taps in N)", MT);
     return BNN_OK;
 }
 
@@ -926,6 +971,7 @@ static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
     bconv_ws_pool_kernel<BN, MT, EW><<<grid, Cfg::NT, smem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 pooled launch: %s", cudaGetErrorString(e));
+    note_kernel("bconv_ws_pool_kernel<%d,%d,%d> (tcgen05 kind::i8, polyphase 2x2 pool)", BN, MT, EW);
     return BNN_OK;
 }
 
@@ -1483,6 +1529,33 @@ static int current_device(int* dev) {
     return BNN_OK;
 }
 
+// Bounded device waits that gave up during a synchronous call. The device
+// counter (g_bnn_wait_timeouts) is read on the call's stream before its
+// first launch (slot 0) and after its last (slot 1) into pinned host words:
+// no extra synchronisation, and work queued by other calls before this one
+// is not counted against it.
+static int wait_mark(DevState* d, cudaStream_t s, int slot) {
+    CK(cudaMemcpyFromSymbolAsync(&d->wt_host[slot], g_bnn_wait_timeouts, sizeof(unsigned int), 0,
+                                 cudaMemcpyDeviceToHost, s));
+    return BNN_OK;
+}
+// test hook (BNN_FAULT_WAIT): a wait that gives up, queued on stream s
+static int inject_wait(cudaStream_t s) {
+    if (g_fail_wait.exchange(0) == 0) return BNN_OK;
+    wait_probe_kernel<<<1, 1, 0, s>>>(1 << 12, nullptr);
+    CK(cudaGetLastError());
+    return BNN_OK;
+}
+// once the stream that carried both marks has been synchronised
+static int wait_verdict(const DevState* d) {
+    const unsigned int n = d->wt_host[1] - d->wt_host[0];
+    if (n)
+        return set_error(BNN_ERR_CUDA,
+                         "%u bounded device wait(s) gave up on device %d during this call: its outputs are not valid",
+                         n, d->device);
+    return BNN_OK;
+}
+
 // pipelined host batch on one device: chunks of `chunk` patches, H2D of the
 // next chunk and D2H of the previous one overlap the current forward
 static int host_batch_on(const Model* m, int device, const float* in, int N, int H, int W, float* out, int chunk) {
@@ -1501,8 +1574,8 @@ static int host_batch_on(const Model* m, int device, const float* in, int N, int
         }
         d->pcap = 0;
         for (int s = 0; s < 2; ++s) {
-            if (cudaMalloc(&d->pin[s], (size_t)C * ip * 4) != cudaSuccess ||
-                cudaMalloc(&d->pout[s], (size_t)C * op * 4) != cudaSuccess) {
+            if (dev_malloc(&d->pin[s], (size_t)C * ip * 4) != cudaSuccess ||
+                dev_malloc(&d->pout[s], (size_t)C * op * 4) != cudaSuccess) {
                 cudaGetLastError();
                 return set_error(BNN_ERR_OOM, "cudaMalloc staging (%d patches)", C);
             }
@@ -1510,6 +1583,20 @@ static int host_batch_on(const Model* m, int device, const float* in, int N, int
         d->pcap = (size_t)C; d->pbands = m->n_bands; d->pclasses = m->n_classes; d->pH = H; d->pW = W;
     }
     const int nch = cdiv(N, C);
+    // on an error after work was queued, let the queued copies finish before
+    // returning: the caller may release its host buffers at once
+    struct Drain {
+        DevState* d;
+        bool armed = true;
+        ~Drain() {
+            if (!armed) return;
+            cudaStreamSynchronize(d->h2d);
+            cudaStreamSynchronize(d->cs);
+            cudaStreamSynchronize(d->d2h);
+            cudaGetLastError();
+        }
+    } drain{d};
+    if ((rc = wait_mark(d, d->cs, 0))) return rc;
     for (int k = 0; k < nch; ++k) {
         const int s = k & 1;
         const int lo = k * C, n = std::min(C, N - lo);
@@ -1525,9 +1612,11 @@ static int host_batch_on(const Model* m, int device, const float* in, int N, int
         CK(cudaMemcpyAsync(out + (size_t)lo * op, d->pout[s], (size_t)n * op * 4, cudaMemcpyDeviceToHost, d->d2h));
         CK(cudaEventRecord(d->ev_out[s], d->d2h));
     }
+    if ((rc = inject_wait(d->cs)) || (rc = wait_mark(d, d->cs, 1))) return rc;
+    drain.armed = false;
     CK(cudaStreamSynchronize(d->d2h));
     CK(cudaStreamSynchronize(d->cs));
-    return BNN_OK;
+    return wait_verdict(d);
 }
 
 // device buffer of at least `n` floats, kept in *buf / *cap across calls
@@ -1536,7 +1625,7 @@ static int grow(float** buf, size_t* cap, size_t n, const char* what) {
     cudaFree(*buf);
     *buf = nullptr;
     *cap = 0;
-    if (cudaMalloc(buf, n * sizeof(float)) != cudaSuccess) {
+    if (dev_malloc(buf, n * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         return set_error(BNN_ERR_OOM, "cudaMalloc %s (%zu bytes)", what, n * sizeof(float));
     }
@@ -1586,13 +1675,15 @@ static int scene_host_on(const Model* m, int device, const float* in, int H, int
     const size_t plane = (size_t)Hs * W;
     if ((rc = grow(&d->scube, &d->scube_cap, (size_t)m->n_bands * plane, "scene slab"))) return rc;
     if ((rc = grow(&d->slog, &d->slog_cap, (size_t)m->n_classes * plane, "scene logits"))) return rc;
+    if ((rc = wait_mark(d, d->cs, 0))) return rc;
     CK(cudaMemcpy2DAsync(d->scube, plane * 4, in + (size_t)y0 * W, (size_t)H * W * 4, plane * 4, m->n_bands,
                          cudaMemcpyHostToDevice, d->cs));
     if ((rc = scene_device(m, d, d->scube, Hs, W, P, d->slog, d->cs))) return rc;
     CK(cudaMemcpy2DAsync(out + (size_t)y0 * W, (size_t)H * W * 4, d->slog, plane * 4, plane * 4, m->n_classes,
                          cudaMemcpyDeviceToHost, d->cs));
+    if ((rc = inject_wait(d->cs)) || (rc = wait_mark(d, d->cs, 1))) return rc;
     CK(cudaStreamSynchronize(d->cs));
-    return BNN_OK;
+    return wait_verdict(d);
 }
 
 }  // namespace bnn
@@ -1651,11 +1742,15 @@ BNN_API int bnn_forward_batch(const Model* m, const float* input, int N, int H, 
     std::vector<int> st(nd, BNN_OK);
     std::vector<std::string> msg(nd);
     std::vector<std::thread> th;
+    const int fail = g_fail_shard.exchange(-1);  // test hook (BNN_FAULT_SHARD)
     for (int r = 0; r < nd; ++r) {
         const int lo = (int)((long)N * r / nd), hi = (int)((long)N * (r + 1) / nd);
         th.emplace_back([&, r, lo, hi]() {
-            if (hi > lo) st[r] = host_batch_on(m, devs[r], input + (size_t)lo * ip, hi - lo, H, W,
-                                               logits + (size_t)lo * op, E->chunk);
+            if (r == fail)
+                st[r] = set_error(BNN_ERR_CUDA, "shard %d: injected host-thread failure", r);
+            else if (hi > lo)
+                st[r] = host_batch_on(m, devs[r], input + (size_t)lo * ip, hi - lo, H, W, logits + (size_t)lo * op,
+                                      E->chunk);
             if (st[r]) msg[r] = bnn_last_error();
         });
     }
@@ -1765,6 +1860,54 @@ BNN_API int bnn_device_error(int device, unsigned int* wait_timeouts) {
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "read device error counter: %s", cudaGetErrorString(e));
     return BNN_OK;
 }
+
+BNN_API int bnn_wait_probe(int device, int rounds, int* gave_up, unsigned int* timeouts) {
+    if (rounds < 1 || rounds > (1 << 22)) return set_error(BNN_ERR_ARG, "rounds %d outside [1, 2^22]", rounds);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    CK(cudaSetDevice(device));
+    int* d = nullptr;
+    int h[2] = {0, 0};
+    int rc = BNN_OK;
+    if (cudaMalloc(&d, 2 * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        rc = set_error(BNN_ERR_OOM, "cudaMalloc probe flags");
+    }
+    if (!rc) {
+        wait_probe_kernel<<<1, 1>>>(rounds, d);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpy(h, d, sizeof h, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "wait probe: %s", cudaGetErrorString(e));
+        cudaFree(d);
+    }
+    if (!rc && timeouts && cudaMemcpyFromSymbol(timeouts, g_bnn_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
+        rc = set_error(BNN_ERR_CUDA, "read device error counter");
+    if (!rc && gave_up) *gave_up = h[0] && h[1];
+    cudaSetDevice(prev);
+    return rc;
+}
+
+BNN_API int bnn_debug_inject_fault(int kind, int arg) {
+    switch (kind) {
+        case 0:
+            g_fail_alloc = 0; g_fail_wait = 0; g_fail_shard = -1;
+            return BNN_OK;
+        case BNN_FAULT_ALLOC:
+            if (arg < 1) return set_error(BNN_ERR_ARG, "allocation index %d (1 = the next one)", arg);
+            g_fail_alloc = arg;
+            return BNN_OK;
+        case BNN_FAULT_WAIT:
+            g_fail_wait = 1;
+            return BNN_OK;
+        case BNN_FAULT_SHARD:
+            if (arg < 0) return set_error(BNN_ERR_ARG, "shard %d", arg);
+            g_fail_shard = arg;
+            return BNN_OK;
+    }
+    return set_error(BNN_ERR_ARG, "fault kind %d", kind);
+}
+
+BNN_API const char* bnn_bconv_last_kernel(void) { return g_last_kernel; }
 
 BNN_API int bnn_set_devices(Model* m, const int* devices, int n) {
     if (!m || n < 0 || (n > 0 && !devices)) return set_error(BNN_ERR_ARG, "bad arguments");
@@ -1944,7 +2087,7 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     const size_t ri_words = (size_t)(stc ? stc : m->enc_conv1[0].Cout) * H * W;
     const size_t rb_words = (size_t)H * W * cw_of(m->enc_conv1[0].Cout);
     void* buf = nullptr;
-    if (cudaMalloc(&buf, (words + ri_words + ip + op + rb_words) * 4) != cudaSuccess) {
+    if (dev_malloc(&buf, (words + ri_words + ip + op + rb_words) * 4) != cudaSuccess) {
         cudaGetLastError();
         return set_error(BNN_ERR_OOM, "cudaMalloc stage buffers");
     }
@@ -2080,7 +2223,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wu.size()) +
                    align256(h.wx.size()) + align256(h.w4.size()) + align256(h.wpop.size() * 4) +
                    2 * align256(h.fold.size() * sizeof(FoldIv));
-    if (cudaMalloc(&Lh->base, total) != cudaSuccess) {
+    if (dev_malloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
         delete Lh;
         cudaSetDevice(prev);
@@ -2167,6 +2310,26 @@ BNN_API int bnn_unpack_act_device(const uint32_t* d_bits, int N, int C, int H, i
 }
 
 // ---------------- host-pointer kernel shims ----------------
+namespace bnn {
+// the device give-up counter read synchronously (the host-pointer shims
+// synchronise the device anyway)
+static int read_wait_counter(unsigned int* v) {
+    CK(cudaMemcpyFromSymbol(v, g_bnn_wait_timeouts, sizeof(unsigned int)));
+    return BNN_OK;
+}
+// after the device was synchronised: the call's verdict from the counter
+// read before it (w0)
+static int sync_wait_verdict(unsigned int w0) {
+    unsigned int w1 = w0;
+    int rc = read_wait_counter(&w1);
+    if (rc) return rc;
+    if (w1 != w0)
+        return set_error(BNN_ERR_CUDA, "%u bounded device wait(s) gave up during this call: its outputs are not valid",
+                         w1 - w0);
+    return BNN_OK;
+}
+}  // namespace bnn
+
 BNN_API int bnn_gpu_bconv_dispatch(const int8_t* a, const uint64_t* packed_w, int32_t* P, int Cin, int H, int W,
                                    int Cout, int kh, int kw, int pad, int stride) {
     if (kh != 3 || kw != 3 || stride != 1 || (pad != 0 && pad != 1))
@@ -2186,7 +2349,7 @@ BNN_API int bnn_gpu_bconv_dispatch(const int8_t* a, const uint64_t* packed_w, in
     const int cw = cw_of(Cin);
     const size_t na = (size_t)Cin * H * W, nbits = (size_t)H * W * cw, nP = (size_t)Cout * H * W;
     void* buf = nullptr;
-    if (cudaMalloc(&buf, na + 16 + nbits * 4 + (size_t)H * W * cw_of(Cout) * 4 + nP * 4) != cudaSuccess) {
+    if (dev_malloc(&buf, na + 16 + nbits * 4 + (size_t)H * W * cw_of(Cout) * 4 + nP * 4) != cudaSuccess) {
         cudaGetLastError();
         bnn_bconv_layer_destroy(L);
         return set_error(BNN_ERR_OOM, "cudaMalloc");
@@ -2195,12 +2358,15 @@ BNN_API int bnn_gpu_bconv_dispatch(const int8_t* a, const uint64_t* packed_w, in
     uint32_t* dbits = (uint32_t*)((char*)buf + ((na + 15) & ~(size_t)15));
     uint32_t* dout = dbits + nbits;
     int32_t* dP = (int32_t*)(dout + (size_t)H * W * cw_of(Cout));
-    rc = BNN_OK;
-    if (cudaMemcpy(da, a, na, cudaMemcpyHostToDevice) != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "H2D");
+    unsigned int w0 = 0;
+    rc = read_wait_counter(&w0);
+    if (!rc && cudaMemcpy(da, a, na, cudaMemcpyHostToDevice) != cudaSuccess) rc = set_error(BNN_ERR_CUDA, "H2D");
     if (!rc) rc = bnn_pack_act_device(da, 1, Cin, H, W, dbits, nullptr);
     if (!rc) rc = bnn_bconv_layer_run(L, dbits, 1, H, W, dout, nullptr, dP, nullptr, nullptr);
+    if (!rc) rc = inject_wait(nullptr);
     if (!rc && cudaDeviceSynchronize() != cudaSuccess)
         rc = set_error(BNN_ERR_CUDA, "bconv: %s", cudaGetErrorString(cudaGetLastError()));
+    if (!rc) rc = sync_wait_verdict(w0);
     if (!rc) {
         std::vector<int32_t> full(nP);
         cudaMemcpy(full.data(), dP, nP * 4, cudaMemcpyDeviceToHost);
@@ -2244,7 +2410,7 @@ BNN_API int bnn_gpu_conv_realin(const float* x, const int8_t* wsign, const float
     const size_t nx = (size_t)Cin * H * W, no = (size_t)Cout * H * W, nb = (size_t)H * W * cw_of(Cout);
     void* buf = nullptr;
     const size_t bytes = (wf.size() + fold.size() + nx + no + nb) * 4;
-    if (cudaMalloc(&buf, bytes) != cudaSuccess) {
+    if (dev_malloc(&buf, bytes) != cudaSuccess) {
         cudaGetLastError();
         return set_error(BNN_ERR_OOM, "cudaMalloc");
     }
@@ -2285,24 +2451,28 @@ static constexpr size_t kNoAllocScratch = BNN_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch];
 
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[64];  // device address of g_noalloc_scratch, per device
+static bool g_noalloc_attrs[64];  // kernel attributes set on this device
 
-// Once per device, with that device current: the array's name in host code
-// is only a host-side stand-in, so its device address comes from
-// cudaGetSymbolAddress.
+// On every call, with the call's device current: the array's name in host
+// code is only a host-side stand-in, so its device address comes from
+// cudaGetSymbolAddress (looked up each time, so a device reset or a new
+// primary context never leaves a stale address behind). The kernels'
+// shared-memory attributes are set once per device, on its first call.
 static int noalloc_scratch(int dev, unsigned char** out) {
     std::lock_guard<std::mutex> g(g_noalloc_mu);
     if (dev < 0 || dev >= 64) return set_error(BNN_ERR_ARG, "device %d out of range for the static scratch", dev);
-    if (!g_noalloc_addr[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return set_error(BNN_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+        cudaGetLastError();
+        return set_error(BNN_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    }
+    if (!g_noalloc_attrs[dev]) {
         int rc = set_kernel_attrs(dev);
         if (rc) return rc;
-        g_noalloc_addr[dev] = p;
+        g_noalloc_attrs[dev] = true;
     }
-    *out = (unsigned char*)g_noalloc_addr[dev];
+    *out = (unsigned char*)p;
     return BNN_OK;
 }
 
@@ -2356,7 +2526,6 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
     const int Ho = H + 2 * pad - 2, Wo = W + 2 * pad - 2;
     if (Ho <= 0 || Wo <= 0) return BNN_OK;
     int rc, dev = 0;
-    if ((rc = current_device(&dev))) return rc;
     // layout of the static scratch for this call (256-byte aligned regions)
     const int nwords = (9 * Cin + 63) / 64, Kw = cw_of(Cin), CoutP = cdiv(Cout, 128) * 128;
     const size_t n_a = (size_t)Cin * H * W, n_pk = (size_t)Cout * nwords * 8, n_bits = (size_t)H * W * Kw * 4,
@@ -2371,6 +2540,7 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
         return set_error(BNN_ERR_ARG,
                          "bconv Cin=%d H=%d W=%d Cout=%d needs %zu bytes of scratch, above the %zu-byte static array",
                          Cin, H, W, Cout, need, kNoAllocScratch);
+    if ((rc = current_device(&dev))) return rc;
     unsigned char* base = nullptr;
     if ((rc = noalloc_scratch(dev, &base))) return rc;
     unsigned char* p = base;
@@ -2389,6 +2559,8 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
     int32_t* dP = (int32_t*)take(n_P);
     int32_t* dcrop = (int32_t*)take(n_crop);
     // every region below is fully rewritten by this call before it is read
+    unsigned int w0 = 0;
+    if ((rc = read_wait_counter(&w0))) return rc;
     CK(cudaMemcpy(da, a, n_a, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(dpk, packed_w, n_pk, cudaMemcpyHostToDevice));
     noalloc_relayout_kernel<<<cdiv((long)CoutP * 9, 128), 128>>>(dpk, nwords, Cin, Cout, CoutP, Kw, L.wt, L.w8, L.wpop,
@@ -2404,5 +2576,5 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
         src = dcrop;
     }
     CK(cudaMemcpy(P, src, (size_t)Cout * Ho * Wo * 4, cudaMemcpyDeviceToHost));
-    return BNN_OK;
+    return sync_wait_verdict(w0);
 }

@@ -1385,8 +1385,12 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 #ifndef BNN_WAIT_HINT_NS
 #define BNN_WAIT_HINT_NS 0
 #endif
-__device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-    for (int it = 0; it < (BNN_WAIT_HINT_NS > 0 ? (1 << 16) : (1 << 22)); ++it) {
+// try_wait rounds before a pipeline wait gives up (each round returns after
+// at most a short hardware-defined time): seconds in total, far above any
+// legitimate hand-off, which takes well under a microsecond
+constexpr int kWaitRounds = BNN_WAIT_HINT_NS > 0 ? (1 << 16) : (1 << 22);
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort_flag, int rounds) {
+    for (int it = 0; it < rounds; ++it) {
         uint32_t done;
 #if BNN_WAIT_HINT_NS > 0
         asm volatile(
@@ -1406,6 +1410,28 @@ __device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, vola
     }
     *abort_flag = 1;
     return false;
+}
+__device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    return mbar_wait_limit(bar, parity, abort_flag, kWaitRounds);
+}
+
+// Self-test of the bounded wait and of the give-up accounting (one thread):
+// waits on an mbarrier phase that nothing completes, with `rounds` try_wait
+// rounds, and records the give-up exactly as a pipeline CTA does (the
+// device counter read by bnn_device_error). out[0] = 1 if the wait gave up,
+// out[1] = 1 if the abort flag was set (out may be null).
+__global__ void wait_probe_kernel(int rounds, int* out) {
+    __shared__ __align__(8) unsigned long long bar;
+    __shared__ int abort_s;
+    abort_s = 0;
+    mbar_init(smem_u32(&bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    const bool done = mbar_wait_limit(smem_u32(&bar), 0, &abort_s, rounds);
+    if (!done) atomicAdd(&g_bnn_wait_timeouts, 1u);
+    if (out) {
+        out[0] = done ? 0 : 1;
+        out[1] = abort_s;
+    }
 }
 
 // Walks grid positions in steps of a fixed stride without divisions: row gr,

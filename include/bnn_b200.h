@@ -107,6 +107,42 @@ int bnn_set_first_conv_kernel(int kind);
  * Expected to stay 0. */
 int bnn_device_error(int device, unsigned int *wait_timeouts);
 
+/* Synchronous calls (bnn_forward, bnn_forward_batch, bnn_forward_patched,
+ * bnn_gpu_bconv_dispatch and its allocation-free twin) compare that count
+ * before and after their own launches and return BNN_ERR_CUDA (bnn_forward:
+ * print + exit(1)) when it went up. The asynchronous device-pointer calls
+ * leave it to the caller to poll bnn_device_error. */
+
+/* Self-test of the bounded device wait (no reference counterpart): one
+ * thread waits on an mbarrier phase that nothing completes, for `rounds`
+ * try_wait rounds (1 .. 2^22; the pipelines use 2^22, seconds in total),
+ * gives up and records it exactly as a pipeline CTA does. *gave_up = 1 when
+ * the wait returned "not completed" and set its abort flag; *timeouts gets
+ * the device counter afterwards. The context stays usable. */
+int bnn_wait_probe(int device, int rounds, int *gave_up, unsigned int *timeouts);
+
+/* Host-side fault injection for tests of the failure paths (no reference
+ * counterpart; nothing faults or stalls a GPU):
+ *   BNN_FAULT_ALLOC: the arg-th next device allocation made by the engine
+ *     (weights, activation arena, staging) fails as an out-of-memory
+ *     cudaMalloc would (BNN_ERR_OOM);
+ *   BNN_FAULT_WAIT: the next synchronous call queues, after its own
+ *     launches, one bounded wait that gives up (bnn_wait_probe's kernel with
+ *     a short limit), so the call must report BNN_ERR_CUDA;
+ *   BNN_FAULT_SHARD: host thread `arg` of the next multi-device
+ *     bnn_forward_batch fails before it launches anything; the others run,
+ *     and the error is returned after every thread has been joined.
+ * kind 0 clears every pending injection. Each injection fires once. */
+#define BNN_FAULT_ALLOC 1
+#define BNN_FAULT_WAIT 2
+#define BNN_FAULT_SHARD 3
+int bnn_debug_inject_fault(int kind, int arg);
+
+/* Name and template parameters of the last binary-conv kernel the calling
+ * thread launched (bnn_bconv_layer_run, a forward, the dispatch shims),
+ * e.g. "bconv_ws_kernel<64,4,i8,8> (tcgen05 kind::i8)"; "" before any. */
+const char *bnn_bconv_last_kernel(void);
+
 /* Devices used by bnn_forward_batch, in shard order. n = 0 restores the
  * default: the calling thread's current device. */
 int bnn_set_devices(Model *m, const int *devices, int n);
@@ -158,10 +194,14 @@ int bnn_gpu_bconv_dispatch(const int8_t *a, const uint64_t *packed_w, int32_t *P
  * the process exits; a call whose buffers do not fit returns BNN_ERR_ARG
  * before touching the GPU (it needs about 1.2*Cin*H*W + 8*Cout*H*W +
  * 11.3*CoutP*Cin bytes with CoutP = Cout rounded up to 128, each buffer
- * rounded up to 256).
- * The first call on a device looks up that array's device address (once per
- * device, with the device current); make that first call before any stream
- * capture. All calls share the one array and it keeps the last call's
+ * rounded up to 256). The weights it stages are those of the mma.sync
+ * kernel (bconv_mma_kernel), so this path always runs that kernel (or the
+ * XOR/POPC one under bnn_set_bconv_kernel(1)), never the tcgen05 kernels
+ * of the allocating twin: same result bit for bit, lower throughput.
+ * Every call looks up that array's device address with the device current;
+ * the first call on a device also sets the kernels' shared-memory
+ * attributes, so make that first call before any stream capture. All calls
+ * share the one array and it keeps the last call's
  * contents: calls that overlap on the GPU (from several host threads on one
  * device) race, so serialise them. Runs on the current device and returns
  * when P is in host memory. */

@@ -253,6 +253,51 @@ void oracle_bconv_P(const int8_t *a, const uint64_t *pw, int32_t *P, int Cin,
     }
 }
 
+/* bconv_xnor_packed: csrc/bnn_conv.c:145-213, on an input that is already
+ * channel-packed per pixel (the reference packs a[Cin][H][W] into
+ * apack[H*W][Wc] first, :156-164; here the words are 32 channels wide,
+ * bits [H][W][ceil(Cin/32)], channel c -> bit c&31 of word c>>5). The
+ * weights are repacked from kidx order to [Cout][9][cw] (:166-180); per
+ * output, over the in-bounds taps only, P = 2 * (equal bits) - valid, the
+ * last word masked to the Cin tail (:183-208). 3x3, pad 1, stride 1.
+ * Same integers as oracle_bconv_P, fast enough for the 512-channel,
+ * 128x128 sweep shapes. */
+__attribute__((target("popcnt")))
+void oracle_bconv_P_bits(const uint32_t *bits, const uint64_t *pw, int32_t *P,
+                         int Cin, int H, int W, int Cout) {
+    int cw = (Cin + 31) / 32, nwords = (9 * Cin + 63) / 64;
+    uint32_t tail = (Cin & 31) ? ((1u << (Cin & 31)) - 1u) : 0xFFFFFFFFu;
+    uint32_t *wp = calloc((size_t)Cout * 9 * cw, sizeof(uint32_t));
+    if (!wp) return;
+    for (int co = 0; co < Cout; ++co)
+        for (int ci = 0; ci < Cin; ++ci)
+            for (int t = 0; t < 9; ++t) {
+                int k = ci * 9 + t;
+                if ((pw[(size_t)co * nwords + (k >> 6)] >> (k & 63)) & 1)
+                    wp[((size_t)co * 9 + t) * cw + (ci >> 5)] |= 1u << (ci & 31);
+            }
+    for (int y = 0; y < H; ++y)
+        for (int x = 0; x < W; ++x) {
+            int ky0 = y == 0 ? 1 : 0, ky1 = y == H - 1 ? 2 : 3;
+            int kx0 = x == 0 ? 1 : 0, kx1 = x == W - 1 ? 2 : 3;
+            int valid = (ky1 - ky0) * (kx1 - kx0) * Cin;
+            for (int co = 0; co < Cout; ++co) {
+                int eq = 0;
+                for (int ky = ky0; ky < ky1; ++ky)
+                    for (int kx = kx0; kx < kx1; ++kx) {
+                        const uint32_t *a = bits + ((size_t)(y + ky - 1) * W + (x + kx - 1)) * cw;
+                        const uint32_t *w = wp + ((size_t)co * 9 + ky * 3 + kx) * cw;
+                        for (int j = 0; j < cw; ++j) {
+                            uint32_t m = j == cw - 1 ? tail : 0xFFFFFFFFu;
+                            eq += __builtin_popcount(~(a[j] ^ w[j]) & m);
+                        }
+                    }
+                P[((size_t)co * H + y) * W + x] = 2 * eq - valid;
+            }
+        }
+    free(wp);
+}
+
 /* conv_realin_general: csrc/bnn_conv_realin.c:66-116. Per output: for each
  * in-bounds tap in row-major (ky,kx) order, s = sequential fp32 sum over ci
  * of x*w (w = +-1, product exact), acc += s; out = alpha*acc. */

@@ -51,6 +51,10 @@ void oracle_bconv_P(const int8_t *a, const uint64_t *packed_w, int32_t *P,
 void oracle_realin(const float *x, const int8_t *wsign, const float *alpha,
                    float *out, int Cin, int H, int W, int Cout, int kh,
                    int kw, int pad, int stride);
+/* bconv_xnor_packed (csrc/bnn_conv.c:145-213) on channel-packed bits
+ * [H][W][ceil(Cin/32)] (32 channels per word): P [Cout][H][W], 3x3 pad 1. */
+void oracle_bconv_P_bits(const uint32_t *bits, const uint64_t *packed_w,
+                         int32_t *P, int Cin, int H, int W, int Cout);
 void oracle_fold_int(const int32_t *P, int8_t *out, int C, int H, int W,
                      const int32_t *type, const int32_t *t, const int32_t *lo,
                      const int32_t *hi);

@@ -1,6 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the REFERENCE itself.
 
-Run in a container that has the reference tree (default /root/reference) and
+Run in a container that has the reference tree (--ref, or the BNN_REFERENCE
+environment variable) and
 the reference build from ``make -C oracle`` (oracle/_ref/). The GPU box has
 neither; it only reads the committed outputs of this script.
 
@@ -28,7 +29,7 @@ What it records:
     python/verify/bconv_harness.py:113-118; maxpool_P on the shapes of
     python/verify/maxpool_harness.py:77.
 
-usage: python tests/golden/make_golden.py [--ref /root/reference]
+usage: python tests/golden/make_golden.py --ref <reference tree>
 """
 
 from __future__ import annotations
@@ -329,8 +330,11 @@ def kernel_cases(lib):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BNN_REFERENCE"),
+                    help="the reference project's root (default: $BNN_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref or not os.path.isdir(os.path.join(args.ref, "csrc")):
+        ap.error("the reference tree is needed: pass --ref or set BNN_REFERENCE")
     lib, slib = ref_lib(), ref_stem_lib()
     manifest = []
     models = [(n, b, r, s, 0, runs) for n, b, r, s, runs in MODELS + [C32]] + STEMS

@@ -34,6 +34,7 @@ def olib():
         L.oracle_forward_patched.restype = ip
         L.oracle_pack_weights.argtypes = [vp, vp, ip, ip, ip, ip]
         L.oracle_bconv_P.argtypes = [vp, vp, vp] + [ip] * 8
+        L.oracle_bconv_P_bits.argtypes = [vp, vp, vp] + [ip] * 4
         L.oracle_realin.argtypes = [vp, vp, vp, vp] + [ip] * 8
         L.oracle_fold_int.argtypes = [vp, vp, ip, ip, ip, vp, vp, vp, vp]
         L.oracle_fold_real.argtypes = [vp, vp, ip, ip, ip, vp, vp, vp, vp]
@@ -164,6 +165,28 @@ def bconv_P(a, packed, cout, pad=1):
     cin, H, W = a.shape
     P = np.zeros((cout, H + 2 * pad - 2, W + 2 * pad - 2), np.int32)
     olib().oracle_bconv_P(a.ctypes.data, packed.ctypes.data, P.ctypes.data, cin, H, W, cout, 3, 3, pad, 1)
+    return P
+
+
+def pack_bits(a):
+    """int8 +-1 [C][H][W] -> uint32 [H][W][ceil(C/32)] (channel c -> bit c&31
+    of word c>>5, +1 -> 1), the engine's bit-plane layout."""
+    C, H, W = a.shape
+    cw = (C + 31) // 32
+    b = np.zeros((H, W, cw * 32), np.uint64)
+    b[:, :, :C] = (np.transpose(a, (1, 2, 0)) > 0)
+    w = (b.reshape(H, W, cw, 32) << np.arange(32, dtype=np.uint64)).sum(-1)
+    return w.astype(np.uint32)
+
+
+def bconv_P_bits(bits, packed, cin, cout):
+    """P [cout][H][W] of a 3x3 pad-1 binary conv on channel-packed bits
+    [H][W][ceil(cin/32)] (the reference's packed kernel)."""
+    bits = np.ascontiguousarray(bits, np.uint32)
+    packed = np.ascontiguousarray(packed, np.uint64)
+    H, W, _ = bits.shape
+    P = np.zeros((cout, H, W), np.int32)
+    olib().oracle_bconv_P_bits(bits.ctypes.data, packed.ctypes.data, P.ctypes.data, cin, H, W, cout)
     return P
 
 

@@ -11,7 +11,7 @@ import pytest
 
 from bnns_to_c_b200 import blob as B
 from bnns_to_c_b200 import blob_react as BR
-from oracle_util import OModel, ORModel, bconv_P, maxpool, synth
+from oracle_util import OModel, ORModel, bconv_P, bconv_P_bits, maxpool, pack_bits, synth
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -68,6 +68,30 @@ def test_oracle_bconv_edge_shapes():
         assert np.array_equal(P, g[f"bconv{i}_P"]), (cin, h, w, cout, pad)
         i += 1
     assert i == 14
+
+
+def test_oracle_packed_bconv_matches_fixtures_and_scalar():
+    """The packed-word checker (used for the large sweep shapes) gives the
+    reference's P: on every pad-1 fixture of the reference's edge-shape list,
+    and against the scalar restatement on Cin tails and sweep widths."""
+    g = np.load(os.path.join(GOLD, "kernels.npz"))
+    i, seen = 0, 0
+    while f"bconv{i}_a" in g.files:
+        cin, h, w, cout, pad = (int(v) for v in g[f"bconv{i}_shape"])
+        if pad == 1:
+            a = g[f"bconv{i}_a"]
+            P = bconv_P_bits(pack_bits(a), g[f"bconv{i}_w"], cin, cout)
+            assert np.array_equal(P, g[f"bconv{i}_P"]), (cin, h, w, cout)
+            seen += 1
+        i += 1
+    assert seen >= 12
+    rng = np.random.default_rng(5)
+    for cin, cout, H, W in [(1, 3, 1, 1), (31, 5, 2, 7), (33, 8, 6, 1), (64, 16, 5, 5), (96, 7, 4, 9),
+                            (512, 4, 3, 3), (130, 9, 7, 4)]:
+        a = np.where(rng.random((cin, H, W)) < 0.5, 1, -1).astype(np.int8)
+        ws = np.where(rng.random((cout, cin, 3, 3)) < 0.5, 1, -1).astype(np.int8)
+        packed = B.pack_kidx(ws)
+        assert np.array_equal(bconv_P_bits(pack_bits(a), packed, cin, cout), bconv_P(a, packed, cout)), (cin, H, W)
 
 
 def test_oracle_maxpool():
