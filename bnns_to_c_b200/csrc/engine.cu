@@ -2575,6 +2575,7 @@ BNN_API int bnn_gpu_bconv_dispatch_noalloc(const int8_t* a, const uint64_t* pack
         CK(cudaGetLastError());
         src = dcrop;
     }
+    if ((rc = inject_wait(nullptr))) return rc;
     CK(cudaMemcpy(P, src, (size_t)Cout * Ho * Wo * 4, cudaMemcpyDeviceToHost));
     return sync_wait_verdict(w0);
 }

@@ -31,6 +31,14 @@ def need_gpu():
     bn.inject_fault(0)
 
 
+@pytest.fixture(autouse=True)
+def no_pending_injection():
+    """An injection that a failing test left pending must not fire in the next."""
+    bn.inject_fault(0)
+    yield
+    bn.inject_fault(0)
+
+
 @pytest.fixture(scope="module")
 def ref():
     x = synth(31, 0, 3, 120, 32, 32)
