@@ -1304,6 +1304,26 @@ __device__ __forceinline__ uint32_t nib8(uint32_t b) {
 __device__ __forceinline__ uint4 nib32(uint32_t w) {
     return make_uint4(nib8(w), nib8(w >> 8), nib8(w >> 16), nib8(w >> 24));
 }
+// an fp32 accumulator holding an integer |v| < 2^22 -> that int32: adding
+// 1.5*2^23 puts the integer in the low mantissa bits exactly (one add and
+// one integer subtract, full rate, where cvt.rni.s32.f32 is quarter rate);
+// -0.0 gives 0
+__device__ __forceinline__ int f32_exact_int(uint32_t f) {
+    return __float_as_int(__fadd_rn(__uint_as_float(f), 12582912.0f)) - 0x4B400000;
+}
+// sign bits of v[k] + off[k], k = 0..31 -> bit k: four independent
+// funnel-shift chains of eight channels (ILP), then merged
+__device__ __forceinline__ uint32_t pack_signs(const uint32_t* v, const int* off) {
+    uint32_t b0 = 0u, b1 = 0u, b2 = 0u, b3 = 0u;
+#pragma unroll
+    for (int k = 7; k >= 0; --k) {
+        b0 = __funnelshift_l((uint32_t)((int)v[k] + off[k]), b0, 1);
+        b1 = __funnelshift_l((uint32_t)((int)v[k + 8] + off[k + 8]), b1, 1);
+        b2 = __funnelshift_l((uint32_t)((int)v[k + 16] + off[k + 16]), b2, 1);
+        b3 = __funnelshift_l((uint32_t)((int)v[k + 24] + off[k + 24]), b3, 1);
+    }
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
 
 __device__ __forceinline__ void tc_commit(uint32_t mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar)
@@ -1502,10 +1522,11 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     int2* pxu = reinterpret_cast<int2*>(ws_smem + (size_t)NS * SB);  // [2][SP] (pixel, upsampled pixel)
     int* colmap = reinterpret_cast<int*>(pxu + 2 * SP);              // [Gw]
     // Folds. A word of 32 channels whose folds are all one-sided (ge, lt,
-    // const, empty) is a "threshold word": bit = sign(P - T) ^ inv, and the
-    // accumulator starts at -T so that it ends at P - T and one funnel shift
-    // per channel packs the signs. A word with a band fold starts at 0 and
-    // takes bit = ((unsigned)(P - lo) < span) ^ inv per channel.
+    // const, empty) is a "threshold word": bit = sign(P - T) ^ inv, one
+    // funnel shift per channel of P + fstart (fstart = -T). A word with a
+    // band fold (fstart = 0) takes bit = ((unsigned)(P - lo) < span) ^ inv
+    // per channel. The accumulators hold P itself: the first MMA of an item
+    // overwrites them.
     const int CoutR = (p.Cout + 31) & ~31, nwo = CoutR / 32;
     int2* fu = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(colmap) + ((p.Gw * 4 + 15) & ~15));
     int* fstart = reinterpret_cast<int*>(fu + CoutR);            // [CoutR] accumulator start (-T or 0)
@@ -1565,7 +1586,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         T = max(-(1 << 22), min(1 << 22, T));
         const uint32_t bw = __ballot_sync(0xffffffffu, band);
         fu[c] = e;
-        fstart[c] = bw ? 0 : -T;  // a band word starts at 0
+        fstart[c] = bw ? 0 : -T;  // a band word has no offset
         const uint32_t it = __ballot_sync(0xffffffffu, inv_t & 1), ib = __ballot_sync(0xffffffffu, inv);
         if (lane == 0) {
             finv_t[w] = it;
@@ -1583,28 +1604,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
     // other (tile, chunk) of an item
     constexpr int EH = C::EW / 4;  // epilogue warps per TMEM lane quarter
     const int quad = warp & 3, half = (warp >> 2) % EH;
-    auto start_vals = [&](int c, uint32_t* v) {  // accumulator start values of channels c..c+31
-#pragma unroll
-        for (int k = 0; k < 32; k += 4) {
-            const int4 q = *reinterpret_cast<const int4*>(fstart + c + k);
-            v[k] = (uint32_t)q.x; v[k + 1] = (uint32_t)q.y; v[k + 2] = (uint32_t)q.z; v[k + 3] = (uint32_t)q.w;
-        }
-        if (F4) {  // fp32 accumulators: the same integers as floats (exact, |start| <= 2^22)
-#pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] = __float_as_uint((float)(int)v[k]);
-        }
-    };
     if (warp < C::EW) {
-        // every accumulator starts at its channels' start values
-        for (int b = 0; b < NBUF; ++b)
-            for (int i = half; i < NPAIR; i += EH) {
-                const int mt = i / NCH, c0 = (i % NCH) * 32;
-                // channel block of the first item that uses accumulator b
-                const int cs = (int)((blockIdx.x + (unsigned)b * gridDim.x) % (unsigned)ncb) * BN + c0;
-                uint32_t v[32];
-                start_vals(cs < CoutR ? cs : 0, v);
-                tc_st32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN * MT + mt * BN + c0), v);
-            }
         if (F4 && half == 0) {  // the block scales: 1.0 in every byte of columns F4_SF..F4_SF+31
             uint32_t v[32];
 #pragma unroll
@@ -1752,8 +1752,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                             // descriptor start addresses are in 16-byte units in the low bits
                             const uint64_t ad = a0 + (uint64_t)(mt * 128 + (t / 3) * p.Gw + t % 3);
                             const uint64_t bd = b0 + (uint64_t)(t * 2 * BN);
-                            if (F4) tc_mma_f4(dcol + mt * BN, ad, bd, idesc, 1u, tmem + F4_SF, tmem + F4_SF + 16);
-                            else tc_mma_i8(dcol + mt * BN, ad, bd, idesc, 1u);
+                            const uint32_t acc = (ks | t) ? 1u : 0u;  // an item's first MMA overwrites
+                            if (F4) tc_mma_f4(dcol + mt * BN, ad, bd, idesc, acc, tmem + F4_SF, tmem + F4_SF + 16);
+                            else tc_mma_i8(dcol + mt * BN, ad, bd, idesc, acc);
                         }
                     }
                     tc_commit(smem_u32(&empty_b[stage]));
@@ -1772,9 +1773,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
             const int buf = NBUF == 2 ? (it & 1) : 0;
             const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
             const int cb = item % ncb, pg = item / ncb, cout0 = cb * BN;
-            // the channel block of the item that reuses this accumulator
-            const int nitem = item + NBUF * (int)gridDim.x;
-            const int ncout0 = (nitem % ncb) * BN;
             if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
             tc_fence_after();
             const GridGeo geo = grid_geo(p);
@@ -1791,7 +1789,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 tc_wait_ld();
                 if (F4) {  // fp32 accumulators hold integers below 2^23: exact
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) v[k] = (uint32_t)__float2int_rn(__uint_as_float(v[k]));
+                    for (int k = 0; k < 32; ++k) v[k] = (uint32_t)f32_exact_int(v[k]);
                 }
                 int n = 0, x = 0;
                 const int px = g.pixel(geo, colmap, n, x);
@@ -1799,10 +1797,8 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                     const int cw = (cout0 + c0) >> 5, lim = p.Cout - cout0 - c0;
                     uint32_t bits = 0u;
                     if (!fband[cw]) {
-                        // accumulator = P - T: pack the sign bits, channel 31 first
-#pragma unroll
-                        for (int k = 31; k >= 0; --k) bits = __funnelshift_l(v[k], bits, 1);
-                        bits ^= finv_t[cw];
+                        // sign bits of P - T
+                        bits = pack_signs(v, fstart + cout0 + c0) ^ finv_t[cw];
                     } else {
                         const int2* f = fu + cout0 + c0;
 #pragma unroll
@@ -1815,20 +1811,12 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                     if (p.P) {  // debug: the accumulators themselves, [N][Cout][H][W]
                         int* Pp = p.P + (((size_t)n * p.Cout + cout0 + c0) * p.H + g.yy) * p.W + x;
                         const int hw = p.H * p.W;
-                        const int* st = fstart + cout0 + c0;
 #pragma unroll
                         for (int k = 0; k < 32; ++k)
-                            if (k < lim) Pp[(size_t)k * hw] = (int)v[k] - st[k];
+                            if (k < lim) Pp[(size_t)k * hw] = (int)v[k];
                     }
                 }
-                // restart this accumulator chunk for its next item
-                if (nitem < n_items) {
-                    const int cs = ncout0 + c0;
-                    start_vals(cs < CoutR ? cs : 0, v);
-                    tc_st32(ta, v);
-                }
             }
-            tc_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_b[buf]));
         }
@@ -2310,7 +2298,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
     const int CoutR = (p.Cout + 31) & ~31, nwo = CoutR / 32;
     int2* fu1 = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(colmap) + ((p.Gw * 4 + 15) & ~15));
     int2* fu2 = fu1 + CoutR;
-    int* fstart = reinterpret_cast<int*>(fu2 + CoutR);  // accumulator start (-T1 or 0)
+    int* fstart = reinterpret_cast<int*>(fu2 + CoutR);  // fold offset: P + fstart = P - T1 (or P)
     int* fd2 = fstart + CoutR;                          // fold2 offset: max + fd2 = maxP - T2 (or maxP)
     uint32_t* fm = reinterpret_cast<uint32_t*>(fd2 + CoutR);  // [6][nwo]: inv1_t inv1_b band1 inv2_t inv2_b band2
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -2368,10 +2356,9 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
         m[5] = __ballot_sync(0xffffffffu, bd2) ? 1u : 0u;
         fu1[c] = e1;
         fu2[c] = e2;
-        // band words start at 0; fold2 offset = -start - T2 (threshold words) or -start
-        const int st = m[2] ? 0 : -T1;
-        fstart[c] = st;
-        fd2[c] = m[5] ? -st : -st - T2;
+        // offsets of the threshold words (0 for band words); the accumulators hold P
+        fstart[c] = m[2] ? 0 : -T1;
+        fd2[c] = m[5] ? 0 : -T2;
         if (lane == 0)
 #pragma unroll
             for (int k = 0; k < 6; ++k) fm[k * nwo + w] = m[k];
@@ -2384,29 +2371,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 
     constexpr int EH = C::EW / 4;  // epilogue warps per TMEM lane quarter
     const int quad = warp & 3, half = (warp >> 2) % EH;
-    auto start_vals = [&](int c, uint32_t* v) {
-#pragma unroll
-        for (int k = 0; k < 32; k += 4) {
-            const int4 q = *reinterpret_cast<const int4*>(fstart + c + k);
-            v[k] = (uint32_t)q.x; v[k + 1] = (uint32_t)q.y; v[k + 2] = (uint32_t)q.z; v[k + 3] = (uint32_t)q.w;
-        }
-    };
-    if (warp < C::EW) {
-        for (int b = 0; b < NBUF; ++b)
-            for (int i = half; i < NPAIR; i += EH) {
-                const int mt = i / NCH, c0 = (i % NCH) * 32;
-                const int cs = (int)((blockIdx.x + (unsigned)b * gridDim.x) % (unsigned)ncb) * BN + c0;
-                uint32_t v[32];
-                start_vals(cs < CoutR ? cs : 0, v);
-#pragma unroll 1
-                for (int ph = 0; ph < NPH; ++ph)
-                    tc_st32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * ACC + (ph * MT + mt) * BN + c0), v);
-            }
-        tc_wait_st();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
 
     if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
@@ -2523,7 +2487,8 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                                 const int oy = (sy + 2) / 2 - 1, ox = (sx + 2) / 2 - 1;  // floor(s / 2)
                                 const uint64_t ad =
                                     a0 + (uint64_t)(qph * 2 * SP + mt * 128 + (oy + 1) * p.Gw + (ox + 1));
-                                tc_mma_i8(d, ad, b0 + (uint64_t)(t * 2 * BN), idesc, 1u);
+                                // an item's first MMA into each accumulator overwrites it
+                                tc_mma_i8(d, ad, b0 + (uint64_t)(t * 2 * BN), idesc, (kw | t) ? 1u : 0u);
                             }
                         }
                     }
@@ -2544,8 +2509,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
             const int buf = NBUF == 2 ? (it & 1) : 0;
             const uint32_t use = NBUF == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
             const int cb = item % ncb, pg = item / ncb, cout0 = cb * BN;
-            const int nitem = item + NBUF * (int)gridDim.x;
-            const int ncout0 = (nitem % ncb) * BN;
             if (!mbar_wait_ab(smem_u32(&accf_b[buf]), use & 1u, abort_v)) break;
             tc_fence_after();
             GridWalk g;
@@ -2560,8 +2523,6 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                 const int cw = (cout0 + c0) >> 5, lim = p.Cout - cout0 - c0;
                 const uint32_t lmask = lim < 32 ? (1u << lim) - 1u : 0xFFFFFFFFu;
                 uint32_t mx[32];
-                const bool restart = nitem < n_items;
-                const int cs = ncout0 + c0 < CoutR ? ncout0 + c0 : 0;
 #pragma unroll 1
                 for (int ph = 0; ph < NPH; ++ph) {
                     const uint32_t ta =
@@ -2574,9 +2535,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                     if (valid) {
                         uint32_t bits = 0u;
                         if (!fm[2 * nwo + cw]) {
-#pragma unroll
-                            for (int k = 31; k >= 0; --k) bits = __funnelshift_l(v[k], bits, 1);
-                            bits ^= fm[cw];
+                            bits = pack_signs(v, fstart + cout0 + c0) ^ fm[cw];
                         } else {
                             const int2* f = fu1 + cout0 + c0;
 #pragma unroll
@@ -2590,25 +2549,17 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                         if (p.P) {
                             int* Pp = p.P + (((size_t)n * p.Cout + cout0 + c0) * p.H + y) * p.W + x;
                             const int hw = p.H * p.W;
-                            const int* st = fstart + cout0 + c0;
 #pragma unroll
                             for (int k = 0; k < 32; ++k)
-                                if (k < lim) Pp[(size_t)k * hw] = (int)v[k] - st[k];
+                                if (k < lim) Pp[(size_t)k * hw] = (int)v[k];
                         }
-                    }
-                    // restart this phase's accumulator chunk for its next item
-                    if (restart) {
-                        start_vals(cs, v);
-                        tc_st32(ta, v);
                     }
                 }
                 if (valid) {
                     const int* d2 = fd2 + cout0 + c0;
                     uint32_t bits = 0u;
                     if (!fm[5 * nwo + cw]) {
-#pragma unroll
-                        for (int k = 31; k >= 0; --k) bits = __funnelshift_l((uint32_t)((int)mx[k] + d2[k]), bits, 1);
-                        bits ^= fm[3 * nwo + cw];
+                        bits = pack_signs(mx, d2) ^ fm[3 * nwo + cw];
                     } else {
                         const int2* f = fu2 + cout0 + c0;
 #pragma unroll
@@ -2621,14 +2572,12 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
                     if (p.P2) {
                         int* Pp = p.P2 + (((size_t)n * p.Cout + cout0 + c0) * H2 + hi) * W2 + hj;
                         const int hw = H2 * W2;
-                        const int* st = fstart + cout0 + c0;
 #pragma unroll
                         for (int k = 0; k < 32; ++k)
-                            if (k < lim) Pp[(size_t)k * hw] = (int)mx[k] - st[k];
+                            if (k < lim) Pp[(size_t)k * hw] = (int)mx[k];
                     }
                 }
             }
-            tc_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_b[buf]));
         }
