@@ -1454,6 +1454,18 @@ __global__ void wait_probe_kernel(int rounds, int* out) {
     }
 }
 
+// n / d and n % d for n < 2^32 and d >= 2 with m = magic_u32(d) = ceil(2^32 / d):
+// umulhi(n, m) is floor(n / d) or one more (n*m/2^32 = n/d + n*e/(d*2^32) with
+// e = m*d - 2^32 < d, so the excess is below 1); one correction step
+__host__ __device__ inline uint32_t magic_u32(uint32_t d) { return (uint32_t)((0x100000000ull + d - 1) / d); }
+__device__ __forceinline__ void divmod_u32(uint32_t n, uint32_t d, uint32_t m, uint32_t& q, uint32_t& r) {
+    q = __umulhi(n, m);
+    r = n - q * d;
+    if ((int)r < 0) {
+        --q;
+        r += d;
+    }
+}
 // Walks grid positions in steps of a fixed stride without divisions: row gr,
 // column gc, image-block row ib and row yy within it (gr = 1 + ib*(H+1) + yy).
 // colmap[gc] = (image slot << 16) | x for image columns, -1 for separators.
@@ -1462,6 +1474,25 @@ struct GridGeo {
     int N, H, W, gk, Gw;
 };
 __device__ __forceinline__ GridGeo grid_geo(const BconvParams& p) { return GridGeo{p.N, p.H, p.W, p.gk, p.Gw}; }
+
+// Image (n, y, x) of grid position gp (gp >= -1) of the padded grid: false
+// for the zero rows and columns and for slots past the last image. Every
+// position is independent (no walk), so a thread maps its positions in
+// parallel. mG = magic_u32(Gw), mH = magic_u32(H + 1).
+__device__ __forceinline__ bool grid_pixel(const GridGeo& g, const int* colmap, int gp, uint32_t mG, uint32_t mH,
+                                           int& n, int& y, int& x) {
+    if (gp < g.Gw) return false;  // grid row 0 (and position -1): zeros
+    uint32_t gr, gc, ib, yy;
+    divmod_u32((uint32_t)gp, (uint32_t)g.Gw, mG, gr, gc);
+    divmod_u32(gr - 1u, (uint32_t)(g.H + 1), mH, ib, yy);
+    const int cm = colmap[gc];
+    if ((int)yy >= g.H || cm < 0) return false;
+    n = (int)ib * g.gk + (cm >> 16);
+    y = (int)yy;
+    x = cm & 0xFFFF;
+    return n < g.N;
+}
+
 
 struct GridWalk {
     int gr, gc, ib, yy;
@@ -1621,20 +1652,26 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         // ------------------------------------------------------------ producers
         const int pt = tid - NEPI;
         // map the staged positions q = pt + NPROD*j of `item` into table `tb`
+        // (staged position 0 = first output - Gw - 1)
+        const GridGeo geo = grid_geo(p);
+        const uint32_t mG = magic_u32((uint32_t)p.Gw), mH = magic_u32((uint32_t)(p.H + 1));
         auto map_item = [&](int item, int2* tb) {
-            const int pg = item / ncb;
-            const GridGeo geo = grid_geo(p);
-            GridWalk g;
-            g.init(geo, pg * PI - 1 + pt, NPROD);  // staged position 0 = first output - Gw - 1
-            for (int q = pt; q < SP; q += NPROD, g.step(geo)) {
-                int n = 0, x = 0, up = -1;
-                const int px = g.pixel(geo, colmap, n, x);
-                if (px >= 0 && p.cw1 > 0) {
-                    const int uy = g.yy - p.oh, ux = x - p.ow;
-                    if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
-                        up = (n * p.h1 + (uy >> 1)) * p.w1 + (ux >> 1);
+            const int base = (item / ncb) * PI - 1;
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                const int q = pt + NPROD * j;
+                if (q < SP) {
+                    int n = 0, y = 0, x = 0, px = -1, up = -1;
+                    if (grid_pixel(geo, colmap, base + q, mG, mH, n, y, x)) {
+                        px = (n * p.H + y) * p.W + x;
+                        if (p.cw1 > 0) {
+                            const int uy = y - p.oh, ux = x - p.ow;
+                            if ((unsigned)uy < (unsigned)p.cH && (unsigned)ux < (unsigned)p.cW)
+                                up = (n * p.h1 + (uy >> 1)) * p.w1 + (ux >> 1);
+                        }
+                    }
+                    tb[q] = make_int2(px, up);
                 }
-                tb[q] = make_int2(px, up);
             }
         };
         auto load_words = [&](const int2* tb, int kw, uint32_t* v) {
@@ -2375,15 +2412,20 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
     if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
         const int pt = tid - NEPI;
+        // one half-res grid position per staged q; its four full-res pixels
+        // are the phases (row parity, column parity)
+        const uint32_t mG = magic_u32((uint32_t)p.Gw), mH = magic_u32((uint32_t)(H2 + 1));
         auto map_item = [&](int item, int* tb) {
-            const int pg = item / ncb;
-            for (int ph = 0; ph < NPH; ++ph) {
-                const int py = ph >> 1, pxp = ph & 1;
-                GridWalk g;
-                g.init(geo, pg * PI - 1 + pt, NPROD);
-                for (int q = pt; q < SP; q += NPROD, g.step(geo)) {
-                    int n, i, j;
-                    tb[ph * SP + q] = g.at(geo, colmap, n, i, j) ? (n * p.H + 2 * i + py) * p.W + 2 * j + pxp : -1;
+            const int base = (item / ncb) * PI - 1;
+#pragma unroll
+            for (int j = 0; j < NQP; ++j) {
+                const int q = pt + NPROD * j;
+                if (q < SP) {
+                    int n = 0, hy = 0, hx = 0, px = -1;
+                    if (grid_pixel(geo, colmap, base + q, mG, mH, n, hy, hx)) px = (n * p.H + 2 * hy) * p.W + 2 * hx;
+#pragma unroll
+                    for (int ph = 0; ph < NPH; ++ph)
+                        tb[ph * SP + q] = px >= 0 ? px + (ph >> 1) * p.W + (ph & 1) : -1;
                 }
             }
         };
