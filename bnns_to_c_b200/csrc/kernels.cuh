@@ -948,6 +948,7 @@ struct RealinFixParams {
 
 constexpr int FIX_WARPS = 4;
 constexpr int FIX_MAXC = 128;  // bands staged per window (the fast paths take Cin <= 128)
+constexpr int FIX_PER_LANE = (9 * FIX_MAXC + 31) / 32;  // window elements a lane loads
 
 __global__ void __launch_bounds__(FIX_WARPS * 32) realin_fixup_kernel(const RealinFixParams p) {
     __shared__ float win[FIX_WARPS][9][FIX_MAXC];
@@ -965,14 +966,28 @@ __global__ void __launch_bounds__(FIX_WARPS * 32) realin_fixup_kernel(const Real
             __syncwarp();
             // element e = (ky, band, kx), kx fastest: the three taps of a
             // window row are adjacent floats, read by adjacent lanes (one
-            // sector), instead of one sector per lane
-            for (int e = lane; e < 9 * p.Cin; e += 32) {
-                const int ky = e / (3 * p.Cin), r3 = e - ky * 3 * p.Cin;
-                const int ci = r3 / 3, kx = r3 - ci * 3;
-                const int iy = y + ky - 1, ix = xx + kx - 1;
-                wv[ky * 3 + kx][ci] = ((unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W)
-                                          ? __ldg(xn + (size_t)ci * plane + (size_t)iy * p.W + ix) : 0.0f;
+            // sector), instead of one sector per lane. Every load of the
+            // window is issued before the first is stored (one memory
+            // latency per window instead of one per element).
+            float ev[FIX_PER_LANE];
+            int ed[FIX_PER_LANE];
+#pragma unroll
+            for (int k = 0; k < FIX_PER_LANE; ++k) {
+                const int e = lane + 32 * k;
+                ev[k] = 0.0f;
+                ed[k] = -1;
+                if (e < 9 * p.Cin) {
+                    const int ky = e / (3 * p.Cin), r3 = e - ky * 3 * p.Cin;
+                    const int ci = r3 / 3, kx = r3 - ci * 3;
+                    const int iy = y + ky - 1, ix = xx + kx - 1;
+                    ed[k] = (ky * 3 + kx) * FIX_MAXC + ci;
+                    if ((unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W)
+                        ev[k] = __ldg(xn + (size_t)ci * plane + (size_t)iy * p.W + ix);
+                }
             }
+#pragma unroll
+            for (int k = 0; k < FIX_PER_LANE; ++k)
+                if (ed[k] >= 0) (&wv[0][0])[ed[k]] = ev[k];
             __syncwarp();
             uint32_t bits = 0u;
             while (mask) {
@@ -1353,6 +1368,18 @@ __device__ __forceinline__ void tc_ld32_nw(uint32_t taddr, uint32_t* r) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+// the same wait, with the 32 registers of an earlier tc_ld32_nw as operands,
+// so that no use of them can be scheduled before it
+__device__ __forceinline__ void tc_wait_ld32(uint32_t* r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
 // 32 consecutive TMEM columns of this thread's lane <- r
 __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t* r) {
     asm volatile(
@@ -1655,7 +1682,15 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         // (staged position 0 = first output - Gw - 1)
         const GridGeo geo = grid_geo(p);
         const uint32_t mG = magic_u32((uint32_t)p.Gw), mH = magic_u32((uint32_t)(p.H + 1));
-        auto map_item = [&](int item, int2* tb) {
+        // word kw of the position whose (pixel, upsampled pixel) is (px, up)
+        auto word_at = [&](int px, int up, int kw) -> uint32_t {
+            if (px < 0) return 0u;
+            if (kw < p.cw0) return __ldg(p.in0 + (size_t)px * p.cw0 + kw);
+            return up >= 0 ? __ldg(p.in1 + (size_t)up * p.cw1 + (kw - p.cw0)) : 0u;
+        };
+        // map `item` into table `tb` and load the words of its first K step
+        // (the loads go out as soon as each pixel index is known)
+        auto map_item = [&](int item, int2* tb, uint32_t* v, uint32_t* v2) {
             const int base = (item / ncb) * PI - 1;
 #pragma unroll
             for (int j = 0; j < NQ; ++j) {
@@ -1671,6 +1706,10 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                         }
                     }
                     tb[q] = make_int2(px, up);
+                    v[j] = word_at(px, up, 0);
+                    if (F4 && p.Kw > 1) v2[j] = word_at(px, up, 1);
+                } else {
+                    v[j] = 0u;
                 }
             }
         };
@@ -1703,10 +1742,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
         uint32_t vn[NQ], vn2[NQ];
 #pragma unroll
         for (int j = 0; j < NQ; ++j) vn2[j] = 0u;
-        if (item < n_items) {
-            map_item(item, pxu);
-            load_step(pxu, 0, vn, vn2);
-        }
+        if (item < n_items) map_item(item, pxu, vn, vn2);
         while (item < n_items && !*abort_v) {
             const int cb = item % ncb;
             const int2* cur = pxu + tb * SP;
@@ -1719,9 +1755,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                 if (ks + 1 < KS) {
                     load_step(cur, ks + 1, vn, vn2);
                 } else if (item + (int)gridDim.x < n_items) {
-                    int2* nxt = pxu + (tb ^ 1) * SP;
-                    map_item(item + gridDim.x, nxt);
-                    load_step(nxt, 0, vn, vn2);
+                    map_item(item + gridDim.x, pxu + (tb ^ 1) * SP, vn, vn2);
                 }
                 const uint32_t fb = smem_u32(&full_b[stage]);
                 if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
@@ -1816,14 +1850,14 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
             GridWalk g;
             g.init(geo, p.Gw + pg * PI + r, 128);
             int gmt = 0;
-#pragma unroll 1
-            for (int i = half; i < NPAIR; i += EH) {
+            auto taddr = [&](int i) {
+                return tmem + ((uint32_t)(quad * 32) << 16) +
+                       (uint32_t)(buf * BN * MT + (i / NCH) * BN + (i % NCH) * 32);
+            };
+            // fold, pack and store unit i (tile i / NCH, 32-channel chunk i % NCH)
+            auto unit = [&](uint32_t* v, int i) {
                 const int mt = i / NCH, c0 = (i % NCH) * 32;
                 for (; gmt < mt; ++gmt) g.step(geo);
-                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN * MT + mt * BN + c0);
-                uint32_t v[32];
-                tc_ld32_nw(ta, v);
-                tc_wait_ld();
                 if (F4) {  // fp32 accumulators hold integers below 2^23: exact
 #pragma unroll
                     for (int k = 0; k < 32; ++k) v[k] = (uint32_t)f32_exact_int(v[k]);
@@ -1853,6 +1887,24 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
                             if (k < lim) Pp[(size_t)k * hw] = (int)v[k];
                     }
                 }
+            };
+            // this warp's units i = half, half + EH, ...: the next unit's TMEM
+            // load is in flight while the current one is folded
+            uint32_t va[32], vb[32];
+            int i = half;
+            if (i < NPAIR) tc_ld32_nw(taddr(i), va);
+#pragma unroll 1
+            while (i < NPAIR) {
+                const int i2 = i + EH;
+                tc_wait_ld32(va);
+                if (i2 < NPAIR) tc_ld32_nw(taddr(i2), vb);
+                unit(va, i);
+                if (i2 >= NPAIR) break;
+                const int i3 = i2 + EH;
+                tc_wait_ld32(vb);
+                if (i3 < NPAIR) tc_ld32_nw(taddr(i3), va);
+                unit(vb, i2);
+                i = i3;
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_b[buf]));
