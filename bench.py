@@ -62,14 +62,16 @@ FFMA_PER_CLK_SM = 128       # fp32 fused multiply-adds / clock / SM (nominal; pr
 SEED_MODEL, SEED_INPUT = 0, 1
 POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 17 binary-conv
-# launches of one forward of the default workload, from one ncu launch list of a
-# 512-patch forward (profiles/unet_c32_512x32x32_dram_launches.md); scaled by
-# patches in the bench line
-BCONV_DRAM_BYTES_PER_512 = 24.14e6
+# launches of one forward of the default workload at 512 patches, summed over one
+# ncu capture per kernel instance (commit ab0ffc7 kernels); scaled by patches in
+# the bench line
+BCONV_DRAM_BYTES_PER_512 = 21.5e6
+# the same for the first conv's main kernel (its 251.66 MB input read once)
+REALIN_DRAM_BYTES_PER_512 = 253.0e6
 # bit planes the 17 binary convs read and write per 32x32 patch at base 32
 # (inputs, concat halves, outputs and pooled outputs)
 BCONV_ALGO_BYTES_PER_PATCH = 58112
-MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (probe-measured on this pool)
+MMA_SYNC_I8_PER_CLK_SM = 1951  # int8 MACs / clock / SM of mma.sync m16n8k32 (measured by a probe kernel)
 
 
 def read_peaks():
@@ -684,6 +686,12 @@ def run_ours(args):
                               "unit": "G int8 MAC/s executed (3 planes x 128 bands x 9 taps x 32 ch per pixel)",
                               "frac": round(real_ach / tensor_i8_peak, 4),
                               "frac_of_mma_sync_measured": round(real_ach / mma_sync_peak, 4),
+                              # the same kernels as an input-read (HBM) roofline
+                              "hbm_gbs": round(P * 120 * H * W * 4 * args.prof_steps / (r_["ms"] * 1e6), 1),
+                              "frac_of_hbm": round(P * 120 * H * W * 4 * args.prof_steps / (r_["ms"] * 1e6)
+                                                   / peaks["hbm_gbs"], 4) if peaks.get("hbm_gbs") else None,
+                              "traffic": round(REALIN_DRAM_BYTES_PER_512 * P / 512)
+                              if (H, W) == (32, 32) and not stem else None,
                               "time_share": frac_split.get("conv_real")},
                 "hbm_input": {"bytes_per_step": P * 120 * H * W * 4, "peak_gbs": peaks.get("hbm_gbs"),
                               "min_ms": round(P * 120 * H * W * 4 / (peaks.get("hbm_gbs", 6538.9) * 1e6), 4)},
