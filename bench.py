@@ -680,6 +680,7 @@ def run_ours(args):
                 {"bound": "tensor",
                               "kernel": {"tc": "realin_ws_kernel (tcgen05, nine shifted taps)",
                                          "tcn": "realin_dxn_kernel (tcgen05, column taps in N)",
+                                         "tx": "realin_tx_kernel (tcgen05, weights in M, positions in N)",
                                          "mma": "realin_mma_kernel (mma.sync)"}[args.first]
                               + " + realin_fixup_kernel",
                               "achieved": round(real_ach, 1), "peak": round(tensor_i8_peak, 1),
@@ -1031,7 +1032,7 @@ def main():
     ap.add_argument("--ref-per-core", type=int, default=4, help="reference sample: patches per host core")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-pointer leg (profiling runs)")
-    ap.add_argument("--first", default="tc", choices=["tc", "mma", "tcn"],
+    ap.add_argument("--first", default="tc", choices=["tc", "mma", "tcn", "tx"],
                     help="first conv kernel: tcgen05 (default) or mma.sync")
     ap.add_argument("--bconv", default="tc", choices=["tc", "tc8", "tc4", "tcx", "popc", "mma"],
                     help="binary-conv kernels: tc = tcgen05 int8, e2m1 where measured faster (default), "

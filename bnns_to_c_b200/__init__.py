@@ -492,9 +492,10 @@ def set_bconv_kernel(kind: str):
 
 def set_first_conv_kernel(kind):
     """'tc' (tcgen05, nine shifted taps; default), 'mma' (mma.sync) or
-    'tcn' (tcgen05 with the column taps in N where W divides 32) for the
-    first conv."""
-    _check(lib().bnn_set_first_conv_kernel({"tc": 0, "mma": 1, "tcn": 2}[kind]))
+    'tcn' (tcgen05 with the column taps in N where W divides 32) or 'tx'
+    (tcgen05 with the weights in M and the positions in N) for the first
+    conv."""
+    _check(lib().bnn_set_first_conv_kernel({"tc": 0, "mma": 1, "tcn": 2, "tx": 3}[kind]))
 
 
 def device_wait_timeouts(device=0):

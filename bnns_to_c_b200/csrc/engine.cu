@@ -28,6 +28,7 @@
 
 #include "common.h"
 #include "kernels.cuh"
+#include "realin_tx.cuh"
 
 namespace bnn {
 
@@ -442,6 +443,8 @@ static int set_kernel_attrs(int device) {
         (e = cudaFuncSetAttribute(realin_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
             cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_dxn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
+            cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_tx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TX_MAX_SMEM)) !=
             cudaSuccess ||
         (e = attr_stem<8>()) != cudaSuccess || (e = attr_stem<16>()) != cudaSuccess ||
         (e = attr_stem<32>()) != cudaSuccess)
@@ -1208,6 +1211,21 @@ static bool rx_geometry(int W, RwGeo* g) {
 
 // first conv -> bit plane: int8 tensor cores decided by the error bound, then
 // the exact fix-up of undecided outputs (a memset and 2 kernels)
+// realin_tx_kernel: R rows of R*Wp <= TX_TO outputs, one N = TX_N tile per item
+static bool tx_geometry(int H, int W, RwGeo* g) {
+    if ((W % 4) != 0) return false;
+    g->Wp = W + 1;
+    g->NB = RW_NB;
+    g->R = std::min(H, TX_TO / g->Wp);
+    g->SP = (2 * g->Wp + TX_N + 7) & ~7;
+    if (g->R < 1 || g->SP > TX_MAX_SP) return false;
+    const size_t fixed = tx_fixed_bytes(W, g->R, g->SP);
+    if (fixed + 2 * tx_stage_bytes(g->SP) > TX_MAX_SMEM) return false;
+    g->NS = (int)std::min<size_t>(4, (TX_MAX_SMEM - fixed) / tx_stage_bytes(g->SP));
+    g->smem = std::max<size_t>(fixed + (size_t)g->NS * tx_stage_bytes(g->SP), (size_t)116 * 1024);
+    return true;
+}
+
 static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
                            cudaStream_t st) {
     if (N <= 0) return BNN_OK;
@@ -1216,12 +1234,13 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     RwGeo geo;
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
     const bool dxn = g_first_kind == 2 && d->rx_wu && rx_geometry(W, &geo);
+    const bool tx = !dxn && g_first_kind == 3 && d->rx_wu && tx_geometry(H, W, &geo);
     if (g_first_kind != 1 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP &&
-        (dxn || rw_geometry(H, W, &geo)) &&
+        (dxn || tx || rw_geometry(H, W, &geo)) &&
         (dxn ? first_conv_tmap3(x, N, Cin, H, W, rx_npos(W), &tm) : first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32))) {
         CK(cudaMemsetAsync(a.rm_ctl, 0, 3 * sizeof(unsigned int), st));
         RealinWsParams p{};
-        p.wu = dxn ? d->rx_wu : d->rw_wu; p.out = out;
+        p.wu = (dxn || tx) ? d->rx_wu : d->rw_wu; p.out = out;
         for (int c = 0; c < 32; ++c) {
             p.thrC[c] = d->rw_thr[c].C;
             p.thr_neg |= (uint32_t)(d->rw_thr[c].sgn < 0) << c;
@@ -1236,6 +1255,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         first_conv_cab(Cin, &p.ca, &p.cb);
         const int grid = std::min(p.n_items, sm_count());
         if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
+        else if (tx) realin_tx_kernel<<<grid, TX_NT, geo.smem, st>>>(tm, p);
         else realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
@@ -1843,9 +1863,10 @@ BNN_API int bnn_set_bconv_kernel(int kind) {
 }
 
 BNN_API int bnn_set_first_conv_kernel(int kind) {
-    if (kind < 0 || kind > 2)
+    if (kind < 0 || kind > 3)
         return set_error(BNN_ERR_ARG,
-                         "first conv kernel kind %d (0 = tcgen05, 1 = mma.sync, 2 = tcgen05 column taps in N)", kind);
+                         "first conv kernel kind %d (0 = tcgen05, 1 = mma.sync, 2 = tcgen05 column taps in N, "
+                         "3 = tcgen05 weights in M, positions in N)", kind);
     g_first_kind = kind;
     return BNN_OK;
 }

@@ -93,9 +93,10 @@ int bnn_set_bconv_kernel(int kind);
  * 0 = tcgen05, nine shifted taps (default; shapes it cannot stage fall back
  * to 1), 1 = mma.sync, 2 = tcgen05 with the three column taps of a kernel
  * row stacked in the MMA's N where the width divides 32 (kind 0 for other
- * widths).
- * Both decide every output by the same error bound and fix up the rest in
- * the reference's fp32 order, so both give the reference's bits. For a v2
+ * widths), 3 = tcgen05 with the weights in the MMA's M (kernel-row taps x
+ * channels) and the staged positions in N (kind 0 where it cannot stage).
+ * All decide every output by the same error bound and fix up the rest in
+ * the reference's fp32 order, so all give the reference's bits. For a v2
  * model's stem: 0 = the measured-faster of its two exact-order kernels for
  * the stem's width (register-streamed up to 16 channels, input streamed by
  * bulk copies through a shared-memory ring above), 1 = the other one. */

@@ -263,10 +263,11 @@ def test_multi_device_shards_match_single():
 
 
 # ------------------------------------------------------------------ first conv: tensor-core path
-@pytest.fixture(params=["tc", "mma", "tcn"])
+@pytest.fixture(params=["tc", "mma", "tcn", "tx"])
 def first_kind(request):
     """Every first-conv tensor-core kernel (tcgen05 nine-tap, mma.sync,
-    tcgen05 with the column taps in N where W divides 32); no bounded
+    tcgen05 with the column taps in N where W divides 32, tcgen05 with the
+    weights in M and the positions in N); no bounded
     device wait may have given up while it ran."""
     bn.set_first_conv_kernel(request.param)
     before = bn.device_wait_timeouts(0)
