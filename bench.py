@@ -422,7 +422,8 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": err}))
         return 0
     v = n * len(secs) / sum(secs)
-    sample = f"{n} patches per step ({args.ref_per_core} per core), {cores} single-threaded processes, {model}"
+    sample = (f"{n} patches per step ({args.ref_per_core} per core), {cores} single-threaded processes, "
+              f"-O3 -march={REF_BUILD['march']}, {model}")
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": round(v, 3), "unit": "patches/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -615,7 +616,8 @@ def run_ours(args):
             if secs:
                 cpu = {"value": round(n / secs[0], 3), "unit": "patches/s", "cores": cores, "kind": "reference",
                        "sample": f"{n} patches of the same workload, {cores} single-threaded processes of the "
-                                 f"reference engine built from its sources, {model}"}
+                                 f"reference engine built from its sources (-O3 -march={REF_BUILD['march']}), "
+                                 f"{model}"}
             else:
                 cpu = {"value": None, "unit": "patches/s", "cores": cores, "kind": "reference", "sample": err}
         frac_split = {k: round(v["ms"] / total_ms, 4) for k, v in by_op.items()} if total_ms else {}
