@@ -86,6 +86,7 @@ struct BinLayer {
     int ubn = 0;              // tcgen05 channel block (N of one MMA)
     int8_t* wx = nullptr;     // ubn == 32: the same weights for bconv_wsx_kernel [Kw][3 dy][2][3 dx][32][16]
     int8_t* w4 = nullptr;     // the same weights as e2m1 nibbles for the kind::mxf4 kernel (layout of wu, two words a step)
+    int8_t* wus = nullptr;    // the layout of wu in 32-channel blocks (small batches: more CTAs per layer)
     FoldIv* fold = nullptr;
     FoldIv* fold2 = nullptr;  // pooled branch (encoder conv2) or nullptr
 };
@@ -248,7 +249,7 @@ static FoldIv to_iv(int type, int t, int lo, int hi) {
 
 struct HostBin {
     std::vector<uint32_t> wt;
-    std::vector<int8_t> w8, wu, wx, w4;
+    std::vector<int8_t> w8, wu, wx, w4, wus;
     std::vector<int> wpop;
     std::vector<FoldIv> fold, fold2;
 };
@@ -317,14 +318,19 @@ static void relayout_bin(const uint64_t* packed, int nwords, int Cin, int Cout, 
     // pooled layers keep four phase accumulators in TMEM: channel blocks of at most 128
     const int bn = pooled ? std::min(ws_bn(Cout), 128) : ws_bn(Cout), ncb = cdiv(Cout, bn);
     L.ubn = bn;
-    h.wu.assign((size_t)ncb * L.Kw * 9 * 2 * bn * 16, (int8_t)0);
-    for (int cb = 0; cb < ncb; ++cb)
-        for (int kw = 0; kw < L.Kw; ++kw)
-            for (int t = 0; t < 9; ++t)
-                for (int hh = 0; hh < 2; ++hh)
-                    for (int c = 0; c < bn && cb * bn + c < Cout; ++c)
-                        memcpy(&h.wu[((((size_t)cb * L.Kw + kw) * 9 + t) * 2 + hh) * bn * 16 + (size_t)c * 16],
-                               &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * bn + c) * 32 + hh * 16], 16);
+    auto block_layout = [&](int b, std::vector<int8_t>& w) {
+        const int nb = cdiv(Cout, b);
+        w.assign((size_t)nb * L.Kw * 9 * 2 * b * 16, (int8_t)0);
+        for (int cb = 0; cb < nb; ++cb)
+            for (int kw = 0; kw < L.Kw; ++kw)
+                for (int t = 0; t < 9; ++t)
+                    for (int hh = 0; hh < 2; ++hh)
+                        for (int c = 0; c < b && cb * b + c < Cout; ++c)
+                            memcpy(&w[((((size_t)cb * L.Kw + kw) * 9 + t) * 2 + hh) * b * 16 + (size_t)c * 16],
+                                   &h.w8[(((size_t)kw * 9 + t) * L.CoutP + cb * b + c) * 32 + hh * 16], 16);
+    };
+    block_layout(bn, h.wu);
+    block_layout(32, h.wus);  // small batches (launch_bconv)
     // the kind::mxf4 kernel: per (channel block, K step of two words) the 9
     // taps' B operands [tap][word of the step][channel][16 bytes], each
     // 16 bytes = 32 e2m1 nibbles (channel j of the word in byte j/2, low
@@ -435,7 +441,8 @@ static int set_kernel_attrs(int device) {
         (e = attr_ws<64, BNN_F4_MT64, true, 4>()) != cudaSuccess ||
         (e = attr_ws_pool<32, 2>()) != cudaSuccess || (e = attr_ws_pool<64, 1>()) != cudaSuccess ||
         (e = attr_ws_pool<128, 1>()) != cudaSuccess || (e = attr_wsx<2>()) != cudaSuccess ||
-        (e = attr_ws_pool<64, 1, 4>()) != cudaSuccess ||
+        (e = attr_ws_pool<64, 1, 4>()) != cudaSuccess || (e = attr_ws<32, 1>()) != cudaSuccess ||
+        (e = attr_ws_pool<32, 1>()) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin3x3_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
@@ -648,7 +655,7 @@ static int dev_init(const Model* m, DevState* d) {
         folds_of(it.a, it.L->CoutP, it.h.fold);
         if (it.a2) folds_of(it.a2, it.L->CoutP, it.h.fold2);
         total += align256(it.h.wt.size() * 4) + align256(it.h.w8.size()) + align256(it.h.wu.size()) +
-                 align256(it.h.wx.size()) + align256(it.h.w4.size()) +
+                 align256(it.h.wx.size()) + align256(it.h.w4.size()) + align256(it.h.wus.size()) +
                  align256(it.h.wpop.size() * 4) +
                  align256(it.h.fold.size() * sizeof(FoldIv)) + align256(it.h.fold2.size() * sizeof(FoldIv));
     }
@@ -682,6 +689,7 @@ static int dev_init(const Model* m, DevState* d) {
         it.L->wu = (int8_t*)put(it.h.wu.data(), it.h.wu.size());
         it.L->wx = it.h.wx.empty() ? nullptr : (int8_t*)put(it.h.wx.data(), it.h.wx.size());
         it.L->w4 = it.h.w4.empty() ? nullptr : (int8_t*)put(it.h.w4.data(), it.h.w4.size());
+        it.L->wus = (int8_t*)put(it.h.wus.data(), it.h.wus.size());
         it.L->wpop = (int*)put(it.h.wpop.data(), it.h.wpop.size() * 4);
         it.L->fold = (FoldIv*)put(it.h.fold.data(), it.h.fold.size() * sizeof(FoldIv));
         it.L->fold2 = it.a2 ? (FoldIv*)put(it.h.fold2.data(), it.h.fold2.size() * sizeof(FoldIv)) : nullptr;
@@ -978,8 +986,20 @@ static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
     return BNN_OK;
 }
 
+// below this many padded-grid positions (N*(H+1)*(W+1)) a layer runs in
+// 32-channel blocks of 128-position items: a small batch then spreads over
+// many CTAs instead of streaming the whole layer through one or two
+constexpr long kSmallPositions = 16384;
+
 static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
     const bool tc = g_bconv_kind == 0 || g_bconv_kind >= 3;
+    if (g_bconv_kind == 0 && p.wus && (long)N * (p.H + 1) * (p.W + 1) < kSmallPositions) {
+        BconvParams q = p;
+        q.wu = p.wus;
+        q.ubn = 32;
+        const int rc = p.out2 ? launch_ws_pool<32, 1>(q, N, st) : launch_ws<32, 1>(q, N, st);
+        if (rc != BNN_ERR_UNSUPPORTED) return rc;
+    }
     if (tc && p.out2 && p.wu) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
@@ -1052,7 +1072,7 @@ static int run_bin(const BinLayer& L, const uint32_t* in0, const uint32_t* in1, 
     p.cW = std::min(upW, W);
     p.Cin = L.Cin; p.Cout = L.Cout; p.cwo = cw_of(L.Cout);
     p.wt = L.wt; p.wpop = L.wpop; p.w8 = L.w8; p.CoutP = L.CoutP; p.fold = L.fold; p.fold2 = out2 ? L.fold2 : nullptr;
-    p.wu = L.wu; p.ubn = L.ubn; p.wx = L.wx; p.w4 = L.w4;
+    p.wu = L.wu; p.ubn = L.ubn; p.wx = L.wx; p.w4 = L.w4; p.wus = L.wus;
     if ((g_bconv_kind != 1 && !L.w8) || (g_bconv_kind == 1 && (!L.wt || !L.wpop)) || !L.fold)
         return set_error(BNN_ERR_ARG, "binary conv layer has no weights for the selected kernel");
     p.out = out; p.out2 = out2; p.P = P; p.P2 = P2;
@@ -1173,11 +1193,13 @@ struct RwGeo {
     int R, Wp, SP, NS, NB;
     size_t smem;
 };
-static bool rw_geometry(int H, int W, RwGeo* g) {
+// rmax: at most this many rows per item (a small batch takes short items, so
+// that more CTAs share it)
+static bool rw_geometry(int H, int W, RwGeo* g, int rmax = 1 << 30) {
     if ((W % 4) != 0 || W > RW_MT * 128 - 1) return false;
     g->Wp = W + 1;
     g->NB = RW_NB;
-    g->R = std::min(H, (RW_MT * 128 - W) / g->Wp + 1);  // every output row of the item inside the tiles
+    g->R = std::min(std::min(H, rmax), (RW_MT * 128 - W) / g->Wp + 1);  // every output row inside the tiles
     g->SP = (RW_MT * 128 + 2 * g->Wp + 2 + 7) & ~7;
     if (g->R < 1 || g->SP > RW_MAX_SP || g->R + 2 > 256) return false;
     const size_t fixed = rw_fixed_bytes(W, g->R, g->SP);
@@ -1226,6 +1248,13 @@ static bool tx_geometry(int H, int W, RwGeo* g) {
     return true;
 }
 
+// fix-up grid: one warp per 16 pixels of the batch, at most 8 blocks per SM
+// (the kernel strides over its list; a small batch needs few blocks)
+static unsigned fixup_blocks(int N, int H, int W) {
+    const long px = (long)N * H * W;
+    return (unsigned)std::max<long>(1, std::min<long>(148 * 8, (px + 16 * FIX_WARPS - 1) / (16 * FIX_WARPS)));
+}
+
 static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, int H, int W, uint32_t* out,
                            cudaStream_t st) {
     if (N <= 0) return BNN_OK;
@@ -1235,8 +1264,10 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
     const bool dxn = g_first_kind == 2 && d->rx_wu && rx_geometry(W, &geo);
     const bool tx = !dxn && g_first_kind == 3 && d->rx_wu && tx_geometry(H, W, &geo);
+    // rows per item: as many as the tiles hold, fewer when that leaves most SMs idle
+    const int rmax = std::max(1, cdiv((long)N * H, std::max(1, sm_count() / 2)));
     if (g_first_kind != 1 && d->rw_wu && d->rw_thr.size() == 32 && Cout <= 32 && Cin <= RM_CINP &&
-        (dxn || tx || rw_geometry(H, W, &geo)) &&
+        (dxn || tx || rw_geometry(H, W, &geo, rmax)) &&
         (dxn ? first_conv_tmap3(x, N, Cin, H, W, rx_npos(W), &tm) : first_conv_tmap(x, N, Cin, H, W, &tm, W, geo.R + 2, 32))) {
         CK(cudaMemsetAsync(a.rm_ctl, 0, 3 * sizeof(unsigned int), st));
         RealinWsParams p{};
@@ -1261,7 +1292,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
                           Cout, p.cwo};
-        realin_fixup_kernel<<<148 * 8, FIX_WARPS * 32, 0, st>>>(f);
+        realin_fixup_kernel<<<fixup_blocks(N, H, W), FIX_WARPS * 32, 0, st>>>(f);
         e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
         return BNN_OK;
@@ -1281,7 +1312,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin mma launch: %s", cudaGetErrorString(e));
     RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, p.Cin, d->ri_CinP, H, W,
                       p.Cout, p.cwo};
-    realin_fixup_kernel<<<148 * 8, FIX_WARPS * 32, 0, st>>>(f);
+    realin_fixup_kernel<<<fixup_blocks(N, H, W), FIX_WARPS * 32, 0, st>>>(f);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
     return BNN_OK;
@@ -1350,7 +1381,7 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
     HeadParams p{in, d->head_W, d->head_b, out, N, H, W, m->head_Cin, cw_of(m->head_Cin), m->head_Cout};
     const size_t total = (size_t)N * H * W;
     if (total >= ((size_t)1 << 31)) return set_error(BNN_ERR_ARG, "N*H*W = %zu: at most 2^31 - 1 pixels", total);
-    unsigned blocks = (unsigned)std::min<size_t>((total + 511) / 512, 148 * 8);
+    unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 511) / 512, 148 * 8));
     head1x1_kernel<<<blocks, 256, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
@@ -2242,7 +2273,8 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
         folds_of(&a2, Lh->L.CoutP, h.fold2);
     }
     size_t total = align256(h.wt.size() * 4) + align256(h.w8.size()) + align256(h.wu.size()) +
-                   align256(h.wx.size()) + align256(h.w4.size()) + align256(h.wpop.size() * 4) +
+                   align256(h.wx.size()) + align256(h.w4.size()) + align256(h.wus.size()) +
+                   align256(h.wpop.size() * 4) +
                    2 * align256(h.fold.size() * sizeof(FoldIv));
     if (dev_malloc(&Lh->base, total) != cudaSuccess) {
         cudaGetLastError();
@@ -2262,6 +2294,7 @@ BNN_API int bnn_bconv_layer_create(int device, int Cin, int Cout, const uint64_t
     Lh->L.wu = (int8_t*)put(h.wu.data(), h.wu.size());
     Lh->L.wx = h.wx.empty() ? nullptr : (int8_t*)put(h.wx.data(), h.wx.size());
     Lh->L.w4 = h.w4.empty() ? nullptr : (int8_t*)put(h.w4.data(), h.w4.size());
+    Lh->L.wus = (int8_t*)put(h.wus.data(), h.wus.size());
     Lh->L.wpop = (int*)put(h.wpop.data(), h.wpop.size() * 4);
     Lh->L.fold = (FoldIv*)put(h.fold.data(), h.fold.size() * sizeof(FoldIv));
     Lh->L.fold2 = pool ? (FoldIv*)put(h.fold2.data(), h.fold2.size() * sizeof(FoldIv)) : nullptr;

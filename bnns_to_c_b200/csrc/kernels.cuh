@@ -57,6 +57,7 @@ struct BconvParams {
     int ubn;              // BN of wu
     const int8_t* wx;     // 32-channel blocks, column taps in N: [Cout/32][Kw][3 dy][2][3 dx][32][16], or nullptr
     const int8_t* w4;     // e2m1 weights for the kind::mxf4 kernel: [Cout/BN][ceil(Kw/2)][9][2 words][BN][16], or nullptr
+    const int8_t* wus;    // the layout of wu in 32-channel blocks (small batches), or nullptr
 };
 
 // set by a kernel whose bounded wait on an mbarrier gave up (never expected;
@@ -2339,7 +2340,7 @@ __global__ void __launch_bounds__(512, 1) bconv_wsx_kernel(const BconvParams p) 
 template <int BN, int MT, int EW_ = 8>
 struct WsPoolCfg {
     static constexpr int NPH = 4;
-    static constexpr int NBUF = 512 / (NPH * BN * MT);
+    static constexpr int NBUF = 512 / (NPH * BN * MT) >= 2 ? 2 : 1;
     static constexpr int PI = 128 * MT;   // half-res positions per item
     static constexpr int EW = EW_;  // epilogue warps 0..EW-1 (4 or 8), producers EW..13
     static constexpr int NEPI = 32 * EW, NPROD = 32 * (14 - EW), NT = 512;
