@@ -1260,7 +1260,7 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
     if (N <= 0) return BNN_OK;
     Arena& a = d->ar;
     CUtensorMap tm;
-    RwGeo geo;
+    RwGeo geo{};
     const int Cin = m->enc_conv1[0].Cin, Cout = m->enc_conv1[0].Cout;
     const bool dxn = g_first_kind == 2 && d->rx_wu && rx_geometry(W, &geo);
     const bool tx = !dxn && g_first_kind == 3 && d->rx_wu && tx_geometry(H, W, &geo);

@@ -3284,7 +3284,7 @@ __global__ void __launch_bounds__(RX_NT, 1) realin_dxn_kernel(const __grid_const
         // ------------------------------------------------------------ MMA issuers
         const int u = warp - RX_ISS0;
         const int nseq = my_items * KC;
-        RxCursor cur;  // input stream (issuer 1): the next box to load
+        RxCursor cur{};  // input stream (issuer 1): the next box to load
         auto load_box = [&](int seq) {  // chunk seq (the cursor's) into buffer seq % NB
             const uint32_t bar = smem_u32(&boxf_b[seq % NB]);
             mbar_expect_tx(bar, (uint32_t)box_bytes);
