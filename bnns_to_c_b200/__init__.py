@@ -121,6 +121,8 @@ def lib():
         "bnn_wait_probe": (ip, [ip, ip, ctypes.POINTER(ip), ctypes.POINTER(ctypes.c_uint)]),
         "bnn_debug_inject_fault": (ip, [ip, ip]),
         "bnn_bconv_last_kernel": (cp, []),
+        "bnn_set_arena_poison": (ip, [ip]),
+        "bnn_arena_poison": (ip, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -502,6 +504,18 @@ def device_wait_timeouts(device=0):
     n = ctypes.c_uint()
     _check(lib().bnn_device_error(device, ctypes.byref(n)))
     return n.value
+
+
+def set_arena_poison(byte):
+    """Fill the activation arenas with `byte` (0..255) before every forward,
+    or stop (None / -1): the debug mode BNN_ARENA_POISON turns on."""
+    _check(lib().bnn_set_arena_poison(-1 if byte is None else int(byte)))
+
+
+def arena_poison():
+    """The poison byte in force, None when off."""
+    b = lib().bnn_arena_poison()
+    return None if b < 0 else b
 
 
 def wait_probe(device=0, rounds=4096):

@@ -35,4 +35,10 @@ struct Topology {
 // stem_c > 0: the body of a v2 model whose stem has stem_c channels
 int validate_topology(const Model* m, Topology* t, int stem_c = 0);
 
+// Debug fill of the activation arenas before every forward (engine.cu):
+// the byte to write, or -1 for none. Read from BNN_ARENA_POISON (its value
+// & 255, as csrc/bnn_react_arena.c:30-32 reads it) on first use unless
+// bnn_set_arena_poison set it.
+int arena_poison_byte();
+
 }  // namespace bnn

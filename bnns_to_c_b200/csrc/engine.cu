@@ -49,6 +49,29 @@ static std::atomic<int> g_fail_alloc{0};   // the k-th next device allocation fa
 static std::atomic<int> g_fail_wait{0};    // the next synchronous call meets a wait that gives up
 static std::atomic<int> g_fail_shard{-1};  // this shard of the next multi-device batch fails
 
+// arena poison byte: -2 = not yet read from the environment, -1 = off
+static std::atomic<int> g_poison{-2};
+
+int arena_poison_byte() {
+    int v = g_poison.load();
+    if (v == -2) {
+        const char* e = getenv("BNN_ARENA_POISON");
+        const int want = e ? (atoi(e) & 255) : -1;
+        g_poison.compare_exchange_strong(v, want);
+        v = g_poison.load();
+    }
+    return v;
+}
+
+// fill a whole activation arena with the poison byte on stream s (no-op when off)
+static int poison_arena(void* base, size_t bytes, cudaStream_t s) {
+    const int b = arena_poison_byte();
+    if (b < 0 || !base) return BNN_OK;
+    if (cudaMemsetAsync(base, b, bytes, s) != cudaSuccess)
+        return set_error(BNN_ERR_CUDA, "arena poison: %s", cudaGetErrorString(cudaGetLastError()));
+    return BNN_OK;
+}
+
 // every device allocation of the engine goes through here
 template <class T>
 static cudaError_t dev_malloc(T** p, size_t bytes) {
@@ -1539,6 +1562,7 @@ static int forward_device(const Model* m, DevState* d, const float* x, int N, in
     // the activation arena is shared by every forward on this device: work
     // enqueued on different streams is ordered through ev_last
     CK(cudaStreamWaitEvent(user, d->ev_last, 0));
+    if ((rc = poison_arena(d->ar.base, d->ar.bytes, user))) return rc;
     if (E->prof.on || dbg) {
         ProfCtx pc;
         ProfCtx* ppc = nullptr;
@@ -1902,6 +1926,14 @@ BNN_API int bnn_set_first_conv_kernel(int kind) {
     return BNN_OK;
 }
 
+BNN_API int bnn_set_arena_poison(int byte) {
+    if (byte < -1 || byte > 255) return set_error(BNN_ERR_ARG, "poison byte %d (-1 = off, 0..255)", byte);
+    g_poison = byte;
+    return BNN_OK;
+}
+
+BNN_API int bnn_arena_poison(void) { return arena_poison_byte(); }
+
 BNN_API int bnn_device_error(int device, unsigned int* wait_timeouts) {
     if (!wait_timeouts) return set_error(BNN_ERR_ARG, "NULL argument");
     int prev = 0;
@@ -2018,6 +2050,9 @@ BNN_API int bnn_first_conv_device(const Model* m, int device, const float* d_inp
         rc = arena_reserve(m, d, N, H, W);
         if (!rc) {
             cudaStreamWaitEvent(st, d->ev_last, 0);
+            rc = poison_arena(d->ar.base, d->ar.bytes, st);
+        }
+        if (!rc) {
             const bool stem = eng(m)->stem_c > 0;
             const bool fast = !stem && !exact && first_conv_fast_ok(m, N, H, W);
             rc = stem   ? run_stem(d, m, d_input, N, H, W, d_bits, nullptr, st)
@@ -2155,6 +2190,7 @@ BNN_API int bnn_forward_stages(const Model* m, const float* input, int H, int W,
     rc = BNN_OK;
     auto fail = [&](int code) { cudaFree(buf); return code; };
     if (cudaMemcpy(din, input, ip * 4, cudaMemcpyHostToDevice) != cudaSuccess) return fail(set_error(BNN_ERR_CUDA, "H2D"));
+    if ((rc = poison_arena(d->ar.base, d->ar.bytes, d->cs))) return fail(rc);
     rc = forward_launches(m, d, din, 1, H, W, dout, d->cs, &dbg, nullptr);
     if (rc) return fail(rc);
     if (cudaStreamSynchronize(d->cs) != cudaSuccess) return fail(set_error(BNN_ERR_CUDA, "forward: %s", cudaGetErrorString(cudaGetLastError())));

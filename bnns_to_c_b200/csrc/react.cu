@@ -80,6 +80,7 @@ struct RDev {
     float *headW = nullptr, *headb = nullptr;
     // arena
     void* abase = nullptr;
+    size_t abytes = 0;
     int aN = 0, aH = 0, aW = 0;
     RBuf buf[9];
     uint32_t* scratch = nullptr;           // the binary convs' (unused) bit outputs
@@ -331,9 +332,20 @@ int arena(const ModelR* m, RDev* d, int N, int H, int W) {
         return set_error(BNN_ERR_OOM, "cudaMalloc ReAct arena (%zu bytes)", off);
     }
     for (auto& pr : plan) *pr.first = (char*)d->abase + pr.second;
+    d->abytes = off;
     d->aN = Nn;
     d->aH = H;
     d->aW = W;
+    return BNN_OK;
+}
+
+// the arena filled with BNN_ARENA_POISON's byte before a forward (debug;
+// every launch must write what it later reads)
+static int poison(RDev* d, cudaStream_t s) {
+    const int b = arena_poison_byte();
+    if (b < 0 || !d->abase) return BNN_OK;
+    if (cudaMemsetAsync(d->abase, b, d->abytes, s) != cudaSuccess)
+        return set_error(BNN_ERR_CUDA, "arena poison: %s", cudaGetErrorString(cudaGetLastError()));
     return BNN_OK;
 }
 
@@ -591,6 +603,7 @@ int forward_device(const ModelR* m, RDev* d, const float* x, int N, int H, int W
     if (rc || N == 0) return rc;
     REngine* E = (REngine*)m->engine;
     RCK(cudaStreamWaitEvent(user, d->ev_last, 0));
+    if ((rc = poison(d, user))) return rc;
     if (E->prof.on) {
         RProf pc;
         pc.prof = &E->prof;
@@ -824,6 +837,7 @@ BNN_API int bnn_forward_react_stages(const ModelR* m, const float* input, int H,
     auto fail = [&](int code) { cudaFree(din); cudaFree(dout); cudaFree(d8); return code; };
     if (cudaMemcpy(din, input, ip * 4, cudaMemcpyHostToDevice) != cudaSuccess)
         return fail(set_error(BNN_ERR_CUDA, "H2D"));
+    if ((rc = poison(d, d->cs))) return fail(rc);
     if ((rc = forward_launches(m, d, din, 1, H, W, dout, d->cs, nullptr))) return fail(rc);
     if (cudaStreamSynchronize(d->cs) != cudaSuccess)
         return fail(set_error(BNN_ERR_CUDA, "ReAct forward: %s", cudaGetErrorString(cudaGetLastError())));

@@ -102,6 +102,18 @@ int bnn_set_bconv_kernel(int kind);
  * bulk copies through a shared-memory ring above), 1 = the other one. */
 int bnn_set_first_conv_kernel(int kind);
 
+/* Debug fill of the activation arenas (the v1 / v2 engine's and the ReAct
+ * engine's), the device-side form of csrc/bnn_react_arena.c:30-32: with a
+ * byte set, every forward first writes that byte over its whole arena (bit
+ * planes, int32 planes, the undecided-output list), so a kernel that reads
+ * what no earlier launch of the same forward wrote changes the logits. The
+ * byte comes from BNN_ARENA_POISON (its integer value & 255) the first
+ * time it is needed, unless bnn_set_arena_poison set it: -1 = off (the
+ * default), 0..255 = the byte. bnn_arena_poison returns the byte in force
+ * (-1 = off). One cudaMemsetAsync per forward when on, nothing when off. */
+int bnn_set_arena_poison(int byte);
+int bnn_arena_poison(void);
+
 /* Number of bounded device-side waits (mbarriers of the TMA / tcgen05
  * pipelines) that gave up on `device` since the library was loaded; a
  * non-zero count means some output of those launches is not to be trusted.

@@ -120,6 +120,31 @@ def test_dropin_bnn_load_exits_like_reference(tmp_path):
     assert r.returncode == 1 and "cannot open" in r.stderr
 
 
+def test_arena_poison_setting():
+    """BNN_ARENA_POISON is read as the reference's arena reads it (integer
+    value & 255, csrc/bnn_react_arena.c:30); the setter overrides it and
+    checks its range. No GPU needed: the setting is host state."""
+    code = "import bnns_to_c_b200 as b; print(b.arena_poison())"
+    for val, want in ((None, "None"), ("165", "165"), ("421", str(421 & 255)), ("0", "0")):
+        env = {k: v for k, v in os.environ.items() if k != "BNN_ARENA_POISON"}
+        if val is not None:
+            env["BNN_ARENA_POISON"] = val
+        r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+        assert r.returncode == 0, r.stderr
+        assert r.stdout.strip() == want, (val, r.stdout)
+    try:
+        bn.set_arena_poison(7)
+        assert bn.arena_poison() == 7
+        bn.set_arena_poison(None)
+        assert bn.arena_poison() is None
+        for bad in (256, -2):
+            with pytest.raises(bn.BnnError) as e:
+                bn.set_arena_poison(bad)
+            assert e.value.code == bn.BNN_ERR_ARG
+    finally:
+        bn.set_arena_poison(None)
+
+
 def test_forward_without_gpu_raises_not_falls_back():
     import torch
     if torch.cuda.is_available():
