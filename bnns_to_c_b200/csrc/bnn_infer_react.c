@@ -11,29 +11,18 @@
  *
  * Report lines go to stdout in the reference's format ("# load", "# mode",
  * "# forward"); BNN_PROFILE=1 adds the per-op device-time table on stderr.
- * The reference streams a file input strip by strip to bound host memory;
- * here the cube is read once (same values). The GPU is the process's
- * current CUDA device.
+ * `rand` and mem:FILE run the in-memory forwards; a plain FILE goes to the
+ * FILE forms (bnn_forward_react_file / _patched_file), as in the reference,
+ * which streams it strip by strip to bound host memory and here reads the
+ * cube once (same values). The messages and exit statuses are the
+ * reference's, in its order (the input spec is checked after the blob has
+ * loaded). The GPU is the process's current CUDA device.
  */
 #include "bnn_model_react.h"
+#include "cli_core.h"
 
 #include <math.h>
 #include <stdint.h>
-#include <stdio.h>
-#include <stdlib.h>
-#include <string.h>
-#include <time.h>
-
-static double now_ms(void) {
-    struct timespec t;
-    clock_gettime(CLOCK_MONOTONIC, &t);
-    return (double)t.tv_sec * 1e3 + (double)t.tv_nsec * 1e-6;
-}
-
-static int cmp_d(const void *a, const void *b) {
-    double x = *(const double *)a, y = *(const double *)b;
-    return (x > y) - (x < y);
-}
 
 /* The reference's `rand` cube (csrc/main_react.c:28-40): Marsaglia
  * xorshift64 (shifts 13, 7, 17) from a fixed seed gives two uniforms in
@@ -72,79 +61,136 @@ static void profile_table(const ModelR *m) {
     }
 }
 
-int main(int argc, char **argv) {
+typedef struct {
+    const char *blob, *input, *output;
+    int H, W, reps;
+} Args;
+
+/* the input spec [patch<P>:][mem:]FILE | [patch<P>:]rand, checked after
+ * the blob has loaded (the reference's order of complaints) */
+typedef struct {
+    const char *path;  /* FILE with the prefixes removed */
+    int patch;         /* 0 = whole image */
+    int in_memory;     /* rand or mem:FILE; otherwise the FILE forms */
+    int is_rand;
+} Source;
+
+/* returns 0, or the exit status after printing the reason */
+static int parse(int argc, char **argv, Args *a) {
     if (argc < 6) {
         fprintf(stderr, "usage: %s blob input|rand output H W [reps]\n", argv[0]);
         return 2;
     }
-    const char *blob = argv[1], *inp = argv[2], *outp = argv[3];
-    int H = atoi(argv[4]), W = atoi(argv[5]);
-    int reps = argc > 6 ? atoi(argv[6]) : 1;
-    if (H <= 0 || W <= 0 || reps <= 0) {
+    a->blob = argv[1];
+    a->input = argv[2];
+    a->output = argv[3];
+    a->H = atoi(argv[4]);
+    a->W = atoi(argv[5]);
+    a->reps = argc > 6 ? atoi(argv[6]) : 1;
+    if (a->H <= 0 || a->W <= 0 || a->reps <= 0) {
         fprintf(stderr, "bad H/W/reps\n");
         return 2;
     }
-    double t0 = now_ms();
-    ModelR *m = bnn_load_react(blob);
-    double t_load = now_ms() - t0;
-    const char *prof = getenv("BNN_PROFILE");
-    if (prof && prof[0] && strcmp(prof, "0") != 0) bnn_react_profile_enable(m, 1);
+    return 0;
+}
 
-    size_t nin = (size_t)m->n_bands * H * W, nout = (size_t)m->n_classes * H * W;
-    int patchP = 0;
-    if (!strncmp(inp, "patch", 5)) {
-        patchP = atoi(inp + 5);
-        const char *q = strchr(inp, ':');
-        if (patchP <= 0 || !q) {
-            fprintf(stderr, "bad patch spec '%s' (use patch32:FILE)\n", inp);
+static int parse_source(const char *in, Source *s) {
+    s->patch = 0;
+    if (!strncmp(in, "patch", 5)) {
+        const char *colon = strchr(in, ':');
+        s->patch = atoi(in + 5);
+        if (s->patch <= 0 || !colon) {
+            fprintf(stderr, "bad patch spec '%s' (use patch32:FILE)\n", in);
             return 2;
         }
-        if (patchP % 16) {
+        if (s->patch % 16) {
             fprintf(stderr, "patch size must be a multiple of 16\n");
             return 2;
         }
-        inp = q + 1;
+        in = colon + 1;
     }
-    int is_rand = strcmp(inp, "rand") == 0;
-    const char *path = strncmp(inp, "mem:", 4) == 0 ? inp + 4 : inp;
-    float *in = malloc(nin * sizeof(float)), *out = malloc(nout * sizeof(float));
-    double *ts = malloc((size_t)reps * sizeof(double));
-    if (!in || !out || !ts) {
+    s->is_rand = !strcmp(in, "rand");
+    const int mem = !strncmp(in, "mem:", 4);
+    s->in_memory = s->is_rand || mem;
+    s->path = mem ? in + 4 : in;
+    return 0;
+}
+
+/* reps forwards from an in-memory cube (rand / mem:) or from the open file */
+static void forwards(const ModelR *m, const Source *s, const float *x, FILE *f, const Args *a, float *y,
+                     double *ms) {
+    for (int r = 0; r < a->reps; ++r) {
+        const double f0 = cli_ms();
+        if (x && s->patch)
+            bnn_forward_react_patched(m, x, a->H, a->W, y, s->patch);
+        else if (x)
+            bnn_forward_react(m, x, a->H, a->W, y);
+        else if (s->patch)
+            bnn_forward_react_patched_file(m, f, a->H, a->W, y, s->patch);
+        else
+            bnn_forward_react_file(m, f, a->H, a->W, y);
+        ms[r] = cli_ms() - f0;
+    }
+}
+
+int main(int argc, char **argv) {
+    Args a;
+    int rc = parse(argc, argv, &a);
+    if (rc) return rc;
+    const double load0 = cli_ms();
+    ModelR *m = bnn_load_react(a.blob);
+    const double load_ms = cli_ms() - load0;
+    const int prof = cli_env_on("BNN_PROFILE");
+    if (prof) bnn_react_profile_enable(m, 1);
+
+    const size_t n_in = (size_t)m->n_bands * a.H * a.W, n_out = (size_t)m->n_classes * a.H * a.W;
+    float *y = malloc(n_out * sizeof *y);
+    if (!y) {
+        fprintf(stderr, "OOM out\n");
+        return 1;
+    }
+    Source src;
+    if ((rc = parse_source(a.input, &src))) return rc;
+    double *ms = malloc((size_t)a.reps * sizeof *ms);
+    if (!ms) {
         fprintf(stderr, "OOM\n");
         return 1;
     }
-    if (is_rand) {
-        synthetic_cube(in, nin);
-    } else {
-        FILE *f = fopen(path, "rb");
-        if (!f || fread(in, sizeof(float), nin, f) != nin) {
-            fprintf(stderr, "bad input %s\n", path);
+    if (src.in_memory) {
+        float *x = malloc(n_in * sizeof *x);
+        if (!x) {
+            fprintf(stderr, "OOM in\n");
             return 1;
         }
+        if (src.is_rand)
+            synthetic_cube(x, n_in);
+        else if (cli_read_f32(src.path, x, n_in)) {
+            fprintf(stderr, "bad input %s\n", src.path);
+            return 1;
+        }
+        forwards(m, &src, x, NULL, &a, y, ms);
+        free(x);
+    } else {
+        FILE *f = fopen(src.path, "rb");
+        if (!f) {
+            fprintf(stderr, "cannot open %s\n", src.path);
+            return 1;
+        }
+        forwards(m, &src, NULL, f, &a, y, ms);
         fclose(f);
     }
-    for (int r = 0; r < reps; ++r) {
-        double a = now_ms();
-        if (patchP) bnn_forward_react_patched(m, in, H, W, out, patchP);
-        else bnn_forward_react(m, in, H, W, out);
-        ts[r] = now_ms() - a;
-    }
-    qsort(ts, (size_t)reps, sizeof(double), cmp_d);
-    FILE *g = fopen(outp, "wb");
-    if (!g) {
-        fprintf(stderr, "cannot open %s\n", outp);
+    const CliTimes t = cli_times(ms, a.reps);
+    if (cli_write_f32(a.output, y, n_out)) {
+        fprintf(stderr, "cannot open %s\n", a.output);
         return 1;
     }
-    fwrite(out, sizeof(float), nout, g);
-    fclose(g);
-    printf("# load %.1f ms\n", t_load);
-    if (patchP) printf("# mode: patch-wise P=%d\n", patchP);
-    printf("# forward %dx%d reps=%d  median %.1f ms  min %.1f  max %.1f\n", H, W, reps, ts[reps / 2], ts[0],
-           ts[reps - 1]);
-    if (prof && prof[0] && strcmp(prof, "0") != 0) profile_table(m);
-    free(ts);
-    free(in);
-    free(out);
+    printf("# load %.1f ms\n", load_ms);
+    if (src.patch) printf("# mode: patch-wise P=%d\n", src.patch);
+    printf("# forward %dx%d reps=%d  median %.1f ms  min %.1f  max %.1f\n", a.H, a.W, a.reps, t.median, t.min,
+           t.max);
+    if (prof) profile_table(m);
+    free(ms);
+    free(y);
     bnn_free_react(m);
     return 0;
 }

@@ -280,6 +280,38 @@ def test_stem_cli_usage_matches_reference():
     assert r.returncode == 1 and "usage:" in r.stderr and "weights_stem.blob" in r.stderr
 
 
+def test_cli_error_paths_match_reference(tmp_path):
+    """The CLIs' host-side failures, reached before any forward (so no GPU):
+    the reference's messages and exit statuses (csrc/main.c:36-46,
+    csrc/main_stem.c, csrc/main_react.c)."""
+    short = tmp_path / "short.bin"
+    short.write_bytes(b"\0" * 64)
+    out = str(tmp_path / "o.bin")
+    for cli, blob in ((bn.CLI_PATH, C8), (bn.CLI_STEM_PATH, S8)):
+        for inp in (str(short), str(tmp_path / "missing.bin")):
+            r = subprocess.run([cli, blob, inp, out], capture_output=True, text=True, timeout=60)
+            assert (r.returncode, r.stderr.strip()) == (1, "bad input file"), (cli, inp, r.stderr)
+        r = subprocess.run([cli, str(tmp_path / "nope.blob"), "rand", out], capture_output=True, text=True)
+        assert r.returncode == 1 and "cannot open" in r.stderr
+    cases = [
+        ([R8, "rand", out, "0", "32"], 2, "bad H/W/reps"),
+        ([R8, "rand", out, "32", "32", "0"], 2, "bad H/W/reps"),
+        ([R8, "patch:rand", out, "32", "32"], 2, "bad patch spec 'patch:rand' (use patch32:FILE)"),
+        ([R8, "patch24:rand", out, "48", "48"], 2, "patch size must be a multiple of 16"),
+        ([R8, "mem:" + str(short), out, "32", "32"], 1, f"bad input {short}"),
+        ([R8, "mem:" + str(tmp_path / "missing.bin"), out, "32", "32"], 1, f"bad input {tmp_path / 'missing.bin'}"),
+        ([R8, str(tmp_path / "missing.bin"), out, "32", "32"], 1, f"cannot open {tmp_path / 'missing.bin'}"),
+        ([R8, str(short), out, "32", "32"], 1, "file_reader: short read of the [120,32,32] cube"),
+        ([R8, "patch32:" + str(short), out, "32", "32"], 1, "file_reader: short read of the [120,32,32] cube"),
+        ([str(tmp_path / "nope.blob"), "patch24:rand", out, "32", "32"], 1, f"cannot open {tmp_path / 'nope.blob'}"),
+    ]
+    for args, code, msg in cases:
+        r = subprocess.run([bn.CLI_REACT_PATH] + args, capture_output=True, text=True, timeout=60)
+        assert (r.returncode, r.stderr.strip()) == (code, msg), (args, r.stderr)
+    r = subprocess.run([bn.CLI_REACT_PATH], capture_output=True, text=True)
+    assert r.returncode == 2 and "usage:" in r.stderr
+
+
 # ------------------------------------------------------------------ v3 ReActNet
 R8 = os.path.join(GOLD, "react_c8_s3.blob")
 

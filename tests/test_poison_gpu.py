@@ -70,7 +70,7 @@ def test_poisoned_arena_first_conv_alone():
     try:
         N, H, W = 4, 32, 32
         x = torch.from_numpy(synth(72, 0, N, m.n_bands, H, W)).cuda()
-        cw = (m.enc_c1_cout + 31) // 32
+        cw = (m.base_channels + 31) // 32  # enc1.conv1 has base_channels outputs
         outs = []
         for b in (None,) + BYTES:
             bn.set_arena_poison(b)
