@@ -2706,21 +2706,33 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 // |x| per position for the bound, and two issuers run 27 MMAs per tile
 // (9 taps x 3 planes, N = 32 channels; the weights of all chunks stay in
 // shared memory). TMEM: two accumulators of RW_MT tiles x 3 planes x 32.
-// Warps: 0-3 epilogue (both tiles), 4-13 producers (the first also drives
-// the TMA ring), 14.. MMA issue (the six accumulators round-robin; the last
-// issuer warp allocates TMEM; measured: 3 or 6 issuers are slower than 2).
+// Warps: 0-7 epilogue (warp w: TMEM lane quarter w%4 of tile w/4), 8-17
+// producers (the first also drives the TMA ring; each thread has a staged
+// position's 32 band loads in flight at once), 18.. MMA issue (the six
+// accumulators round-robin; the last issuer warp allocates TMEM). Measured:
+// 3 or 6 issuers are slower than 2; 8 epilogue warps with 32 loads in
+// flight 2% faster than 4 warps (both tiles each) with 16.
 // Every wait is bounded; a CTA that gives up raises ctl[1] (the fix-up then
 // recomputes the whole batch).
 // ---------------------------------------------------------------------
-constexpr int RW_MT = 2;              // tiles per item
-constexpr int RW_NB = 2;              // fp32 box buffers
-constexpr int RW_NEPI = 128;          // warps 0-3: epilogue (both tiles)
-constexpr int RW_NPROD = 320;         // warps 4-13: producers
+#ifndef BNN_RW_NEPI
+#define BNN_RW_NEPI 256
+#endif
+#ifndef BNN_RW_LD32
+#define BNN_RW_LD32 1
+#endif
 #ifndef BNN_RW_NISS
 #define BNN_RW_NISS 2
 #endif
-constexpr int RW_NISS = BNN_RW_NISS;  // warps 14..: MMA issue (the six accumulators round-robin)
-constexpr int RW_NT = 32 * (14 + RW_NISS);
+constexpr int RW_MT = 2;              // tiles per item
+constexpr int RW_NB = 2;              // fp32 box buffers
+constexpr int RW_NEPI = BNN_RW_NEPI;  // warps 0..: epilogue (128: both tiles per warp; 256: one tile per warp)
+constexpr int RW_NPROD = 320;         // the next 10 warps: producers
+constexpr int RW_PW0 = RW_NEPI / 32;  // first producer warp
+constexpr int RW_IW0 = RW_PW0 + 10;   // first MMA-issue warp
+constexpr int RW_NISS = BNN_RW_NISS;  // MMA issue (the six accumulators round-robin)
+constexpr int RW_NT = 32 * (RW_IW0 + RW_NISS);
+static_assert(RW_NEPI == 128 || RW_NEPI == 256, "epilogue: 4 or 8 warps");
 constexpr int RW_NQ = 3;              // staged positions per producer thread, at most
 constexpr int RW_MAX_SP = RW_NPROD * RW_NQ;
 constexpr size_t RW_WBYTES = (size_t)4 * 9 * 2 * 32 * 16;  // +-1 weights, 4 chunks x 9 taps
@@ -2817,7 +2829,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
     const uint32_t tmem = tmem_s;
     const uint32_t sm0 = smem_u32(rw_smem);
 
-    if (warp >= 4 && warp < 14) {
+    if (warp >= RW_PW0 && warp < RW_IW0) {
         // ------------------------------------------------------------ producers
         const int pt = tid - RW_NEPI;
         const int nseq = my_items * KC;
@@ -2866,11 +2878,20 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                         for (int k = 0; k < 8; ++k) w[0][k] = w[1][k] = w[2][k] = 0u;
                         if (col >= 1 && row < R + 2) {
                             const float* src = bx + (size_t)row * p.W + (col - 1);
+#if BNN_RW_LD32
+                            float xa[32];  // all 32 bands' loads in flight at once
 #pragma unroll
-                            for (int g2 = 0; g2 < 4; g2 += 2) {  // 16 bands loaded at once
+                            for (int i = 0; i < 32; ++i) xa[i] = src[(size_t)i * bstride];
+#endif
+#pragma unroll
+                            for (int g2 = 0; g2 < 4; g2 += 2) {  // 16 bands at a time
+#if BNN_RW_LD32
+                                const float* xv = xa + g2 * 8;
+#else
                                 float xv[16];
 #pragma unroll
                                 for (int i = 0; i < 16; ++i) xv[i] = src[(size_t)(g2 * 8 + i) * bstride];
+#endif
                                 // sum |x| in two rounded-up chains (any order bounds the sum
                                 // from above); the band-weighted sum takes the 16 bands at the
                                 // weight of the first, Cin - (kc*32 + g2*8), the largest
@@ -2943,11 +2964,11 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             }
             mbar_arrive(smem_u32(&bpxf_b[buf]));
         }
-    } else if (warp >= 14) {
+    } else if (warp >= RW_IW0) {
         // ------------------------------------------------------------ MMA issuers
         // one thread issues an MMA per ~70 clk, so the six accumulators of an
         // item (2 tiles x 3 planes, a = tile*3 + plane) go round-robin to the issuers
-        const int u = warp - 14;
+        const int u = warp - RW_IW0;
         if (lane == 0 && mbar_wait_ab(smem_u32(&wrdy_b), 0u, abort_v)) {
             // A: plane 0 signed, planes 1-2 unsigned; B signed; D s32; N = 32, M = 128
             const uint32_t id_s = (2u << 4) | (1u << 7) | (1u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
@@ -2986,8 +3007,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue
-        // warp w: TMEM lanes 32w.., both tiles
-        const int quad = warp, r = quad * 32 + lane;
+        // warp w: TMEM lanes 32(w%4).. (the lane quarter its sub-partition may
+        // read), tiles w/4, w/4 + RW_NEPI/128, ...
+        const int quad = warp & 3, r = quad * 32 + lane;
         for (int it = 0; it < my_items && !*abort_v; ++it) {
             const int buf = it & 1;
             const int item = (int)blockIdx.x + it * (int)gridDim.x;
@@ -2997,7 +3019,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             tc_fence_after();
             const float* bt = bpx + buf * SP;
 #pragma unroll 1
-            for (int mt = 0; mt < RW_MT; ++mt) {
+            for (int mt = warp >> 2; mt < RW_MT; mt += RW_NEPI / 128) {
                 const int qo = mt * 128 + r + Wp + 1;  // staged position of this lane's output
                 const int orow = qo / Wp, ocol = qo - orow * Wp;
                 const int y = y0 + orow - 1, x = ocol - 1;
