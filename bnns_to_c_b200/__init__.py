@@ -25,6 +25,8 @@ LIB_PATH = os.path.join(HERE, "lib", "libbnn_b200.so")
 CLI_PATH = os.path.join(HERE, "lib", "bnn_infer")
 CLI_STEM_PATH = os.path.join(HERE, "lib", "bnn_infer_stem")
 CLI_REACT_PATH = os.path.join(HERE, "lib", "bnn_infer_react")
+# the reference's kernel-level ABI under its own names (include/bnn_kernels.h)
+KERNELS_PATH = os.path.join(HERE, "lib", "libbnn_kernels.so")
 
 BNN_OK, BNN_ERR_IO, BNN_ERR_FORMAT, BNN_ERR_UNSUPPORTED, BNN_ERR_ARG, BNN_ERR_CUDA, BNN_ERR_OOM = range(7)
 

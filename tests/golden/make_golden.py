@@ -51,6 +51,9 @@ sys.path.insert(0, ROOT)
 from bnns_to_c_b200 import blob as B  # noqa: E402
 from bnns_to_c_b200 import blob_react as BR  # noqa: E402
 
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+from oracle_util import bind_kernel_abi  # noqa: E402
+
 STAGE_CB = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int,
                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p)
 DT = {0: np.int8, 1: np.int32, 2: np.float32}
@@ -328,13 +331,109 @@ def kernel_cases(lib):
     return res
 
 
+# (Cin, H, W, Cout, kh, kw, pad, stride) of the kernel-ABI binary convs: the
+# forward's 3x3 stride-1 shapes and the general ones (strides, 1x1 / 5x5 /
+# non-square kernels, pad > 1, pad > k where the reference's two packed
+# kernels count the valid taps differently)
+ABI_BCONV = [(3, 9, 7, 5, 3, 3, 1, 1), (64, 8, 8, 16, 3, 3, 0, 1), (7, 9, 7, 5, 3, 3, 1, 2),
+             (100, 11, 13, 24, 3, 3, 1, 2), (5, 6, 9, 4, 1, 1, 0, 1), (20, 10, 10, 8, 5, 5, 2, 1),
+             (36, 7, 6, 8, 3, 3, 2, 1), (65, 5, 5, 3, 2, 2, 0, 2), (4, 3, 3, 2, 1, 1, 2, 1),
+             (12, 6, 5, 3, 3, 5, 1, 1), (40, 4, 4, 4, 1, 1, 3, 2), (8, 2, 2, 3, 3, 3, 2, 3)]
+ABI_REALIN = [(120, 9, 7, 8, 3, 3, 1, 1), (7, 9, 7, 5, 3, 3, 1, 1), (5, 6, 9, 4, 1, 1, 0, 1),
+              (6, 8, 8, 3, 3, 3, 0, 1), (9, 10, 11, 4, 5, 5, 2, 2), (300, 5, 5, 2, 3, 3, 1, 1),
+              (4, 4, 4, 3, 1, 1, 1, 1)]
+ABI_POOL = [(3, 9, 8, 2, 2), (2, 7, 7, 3, 1), (4, 6, 6, 2, 1), (2, 9, 9, 3, 2), (1, 5, 4, 1, 1)]
+
+
+def out_dim(n, k, pad, stride):
+    return (n + 2 * pad - k) // stride + 1
+
+
+def kernel_abi_cases(lib):
+    """Inputs and the reference's own outputs for every function of the
+    kernel-level ABI (include/bnn_kernels.h), from the reference's sources
+    compiled unmodified (oracle/_ref/libref.so)."""
+    rng = np.random.default_rng(4321)
+    res = {}
+    for i, (cin, h, w, cout, kh, kw, pad, st) in enumerate(ABI_BCONV):
+        a = rng.choice(np.array([-1, 0, 1], np.int8), size=(cin, h, w), p=[0.45, 0.1, 0.45])
+        ws = rng.choice(np.array([-1, 1], np.int8), size=(cout, cin, kh, kw))
+        nw = (cin * kh * kw + 63) // 64
+        packed = np.zeros((cout, nw), np.uint64)
+        lib.pack_weights(ws.ctypes.data, packed.ctypes.data, cout, cin, kh, kw)
+        assert np.array_equal(packed, B.pack_kidx(ws))
+        shape = (cout, out_dim(h, kh, pad, st), out_dim(w, kw, pad, st))
+        outs = {}
+        for fn in ("bconv_naive_int", "bconv_xnor", "bconv_xnor_packed", "bconv_dispatch"):
+            P = np.zeros(shape, np.int32)
+            wp = ws if fn == "bconv_naive_int" else packed
+            getattr(lib, fn)(a.ctypes.data, wp.ctypes.data, P.ctypes.data, cin, h, w, cout, kh, kw, pad, st)
+            outs[fn] = P
+        res.update({f"bc{i}_a": a, f"bc{i}_ws": ws, f"bc{i}_packed": packed,
+                    f"bc{i}_shape": np.array([cin, h, w, cout, kh, kw, pad, st], np.int32)})
+        res.update({f"bc{i}_{fn}": P for fn, P in outs.items()})
+    for i, (cin, h, w, cout, kh, kw, pad, st) in enumerate(ABI_REALIN):
+        x = (rng.standard_normal((cin, h, w)) * 2).astype(np.float32)
+        ws = rng.choice(np.array([-1, 1], np.int8), size=(cout, cin, kh, kw))
+        alpha = rng.uniform(0.1, 2.0, cout).astype(np.float32)
+        out = np.zeros((cout, out_dim(h, kh, pad, st), out_dim(w, kw, pad, st)), np.float32)
+        lib.conv_realin_naive(x.ctypes.data, ws.ctypes.data, alpha.ctypes.data, out.ctypes.data, cin, h, w, cout,
+                              kh, kw, pad, st)
+        res.update({f"ri{i}_x": x, f"ri{i}_ws": ws, f"ri{i}_alpha": alpha, f"ri{i}_out": out,
+                    f"ri{i}_shape": np.array([cin, h, w, cout, kh, kw, pad, st], np.int32)})
+    for i, (c, h, w, k, st) in enumerate(ABI_POOL):
+        P = rng.integers(-2**31, 2**31 - 1, size=(c, h, w), dtype=np.int64).astype(np.int32)
+        out = np.zeros((c, (h - k) // st + 1, (w - k) // st + 1), np.int32)
+        lib.maxpool_P(P.ctypes.data, out.ctypes.data, c, h, w, k, st)
+        res.update({f"mp{i}_in": P, f"mp{i}_out": out, f"mp{i}_shape": np.array([c, h, w, k, st], np.int32)})
+    # integer fold: every rule type, an unknown code, thresholds inside the P range
+    C, h, w = 7, 6, 5
+    P = rng.integers(-20, 20, size=(C, h, w)).astype(np.int32)
+    ty = np.array([0, 0, 1, 2, 3, 4, 7], np.int32)
+    t = np.array([1, -1, 3, -2, 0, 0, 0], np.int32)
+    lo = np.array([0, 0, 0, 0, -5, -4, 0], np.int32)
+    hi = np.array([0, 0, 0, 0, 6, 3, 0], np.int32)
+    out = np.zeros((C, h, w), np.int8)
+    lib.apply_fold_int(P.ctypes.data, out.ctypes.data, C, h, w, ty.ctypes.data, t.ctypes.data, lo.ctypes.data,
+                       hi.ctypes.data)
+    res.update({"fi_P": P, "fi_type": ty, "fi_t": t, "fi_lo": lo, "fi_hi": hi, "fi_out": out})
+    # real fold on values spread around each channel's switching point
+    C, h, w = 5, 9, 11
+    A = rng.standard_normal(C).astype(np.float32)
+    Bv = rng.standard_normal(C).astype(np.float32)
+    slope = rng.uniform(0.0, 0.5, C).astype(np.float32)
+    rs = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    x = (rng.standard_normal((C, h, w)) * 3).astype(np.float32)
+    out = np.zeros((C, h, w), np.int8)
+    lib.apply_fold_real(x.ctypes.data, out.ctypes.data, C, h, w, A.ctypes.data, Bv.ctypes.data, slope.ctypes.data,
+                        rs.ctypes.data)
+    res.update({"fr_x": x, "fr_A": A, "fr_B": Bv, "fr_slope": slope, "fr_rsign": rs, "fr_out": out})
+    # head: the network's +-1 input, and arbitrary floats
+    cin, h, w, cout = 37, 5, 7, 3
+    Wt = rng.standard_normal((cout, cin)).astype(np.float32)
+    bias = rng.standard_normal(cout).astype(np.float32)
+    for tag, a in (("pm1", rng.choice(np.array([-1.0, 1.0], np.float32), size=(cin, h, w))),
+                   ("f32", rng.standard_normal((cin, h, w)).astype(np.float32))):
+        out = np.zeros((cout, h, w), np.float32)
+        lib.head_1x1(a.ctypes.data, Wt.ctypes.data, bias.ctypes.data, out.ctypes.data, cin, h, w, cout)
+        res.update({f"hd_{tag}_a": a, f"hd_{tag}_out": out})
+    res.update({"hd_W": Wt, "hd_bias": bias})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("BNN_REFERENCE"),
                     help="the reference project's root (default: $BNN_REFERENCE)")
+    ap.add_argument("--only", choices=["kernel_abi"],
+                    help="write just this fixture set (kernel_abi.npz) and leave the others as they are")
     args = ap.parse_args()
     if not args.ref or not os.path.isdir(os.path.join(args.ref, "csrc")):
         ap.error("the reference tree is needed: pass --ref or set BNN_REFERENCE")
+    abi = kernel_abi_cases(bind_kernel_abi(os.path.join(ROOT, "oracle", "_ref", "libref.so")))
+    np.savez_compressed(os.path.join(HERE, "kernel_abi.npz"), **abi)
+    if args.only:
+        return
     lib, slib = ref_lib(), ref_stem_lib()
     manifest = []
     models = [(n, b, r, s, 0, runs) for n, b, r, s, runs in MODELS + [C32]] + STEMS

@@ -217,3 +217,30 @@ def maxpool(P):
     out = np.zeros((C, (H - 2) // 2 + 1, (W - 2) // 2 + 1), np.int32)
     olib().oracle_maxpool(P.ctypes.data, out.ctypes.data, C, H, W, 2, 2)
     return out
+
+
+# The reference's kernel-level C ABI (csrc/bnn_model.h:7-23, csrc/bnn_conv.c):
+# argument types per function, for binding the reference build
+# (oracle/_ref/libref.so, fixtures) and lib/libbnn_kernels.so (tests) alike.
+_V, _I = ctypes.c_void_p, ctypes.c_int
+KERNEL_ABI = {
+    "bconv_naive_int": [_V] * 3 + [_I] * 8,
+    "pack_weights": [_V] * 2 + [_I] * 4,
+    "bconv_xnor": [_V] * 3 + [_I] * 8,
+    "bconv_xnor_packed": [_V] * 3 + [_I] * 8,
+    "bconv_dispatch": [_V] * 3 + [_I] * 8,
+    "conv_realin_naive": [_V] * 4 + [_I] * 8,
+    "maxpool_P": [_V] * 2 + [_I] * 5,
+    "apply_fold_int": [_V] * 2 + [_I] * 3 + [_V] * 4,
+    "apply_fold_real": [_V] * 2 + [_I] * 3 + [_V] * 4,
+    "head_1x1": [_V] * 4 + [_I] * 4,
+}
+
+
+def bind_kernel_abi(path):
+    """ctypes handle on a library that exports KERNEL_ABI, argtypes set."""
+    L = ctypes.CDLL(path)
+    for name, args in KERNEL_ABI.items():
+        f = getattr(L, name)
+        f.argtypes, f.restype = args, None
+    return L
