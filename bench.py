@@ -397,10 +397,10 @@ def react_blob():
 
 def variant(args):
     """(stem channels, metric, workload name) of the network benched."""
+    shape = f"{args.patches}x{args.H}x{args.W}x120"
     if args.workload == "stem":
-        return (STEM_C, "v2 spectral-stem UNet patches/s (32x32x120)",
-                f"stem{STEM_C}_unet_c32_4096x32x32x120")
-    return 0, METRIC, "unet_c32_4096x32x32x120"
+        return STEM_C, "v2 spectral-stem UNet patches/s (32x32x120)", f"stem{STEM_C}_unet_c32_{shape}"
+    return 0, METRIC, f"unet_c32_{shape}"
 
 
 def run_reference(args):

@@ -1218,11 +1218,15 @@ struct RwGeo {
 };
 // rmax: at most this many rows per item (a small batch takes short items, so
 // that more CTAs share it)
+#ifndef BNN_RW_RCAP
+#define BNN_RW_RCAP (1 << 30)  // rows per first-conv item, at most (A/B builds)
+#endif
 static bool rw_geometry(int H, int W, RwGeo* g, int rmax = 1 << 30) {
     if ((W % 4) != 0 || W > RW_MT * 128 - 1) return false;
     g->Wp = W + 1;
     g->NB = RW_NB;
-    g->R = std::min(std::min(H, rmax), (RW_MT * 128 - W) / g->Wp + 1);  // every output row inside the tiles
+    // every output row inside the tiles
+    g->R = std::min(std::min(H, rmax), std::min(BNN_RW_RCAP, (RW_MT * 128 - W) / g->Wp + 1));
     g->SP = (RW_MT * 128 + 2 * g->Wp + 2 + 7) & ~7;
     if (g->R < 1 || g->SP > RW_MAX_SP || g->R + 2 > 256) return false;
     const size_t fixed = rw_fixed_bytes(W, g->R, g->SP);

@@ -2725,7 +2725,10 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 #define BNN_RW_NISS 2
 #endif
 constexpr int RW_MT = 2;              // tiles per item
-constexpr int RW_NB = 2;              // fp32 box buffers
+#ifndef BNN_RW_NB
+#define BNN_RW_NB 2
+#endif
+constexpr int RW_NB = BNN_RW_NB;      // fp32 box buffers
 constexpr int RW_NEPI = BNN_RW_NEPI;  // warps 0..: epilogue (128: both tiles per warp; 256: one tile per warp)
 constexpr int RW_NPROD = 320;         // the next 10 warps: producers
 constexpr int RW_PW0 = RW_NEPI / 32;  // first producer warp
@@ -2856,11 +2859,12 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             for (int j = 0; j < RW_NQ; ++j) { tsum[j] = 0.0f; wsum[j] = 0.0f; amax[j] = 0.0f; }
             for (int kc = 0; kc < KC; ++kc, ++seq) {
                 const int bb = seq % RW_NB;
-                if (pt == 0 && seq >= 1 && seq + 1 < nseq) {
-                    // refill the buffer of chunk seq-1 once every producer is done with it
-                    if (!mbar_wait_ab(smem_u32(&boxe_b[(seq + 1) % RW_NB]), (uint32_t)((seq - 1) / RW_NB) & 1u,
+                if (pt == 0 && seq >= 1 && seq + RW_NB - 1 < nseq) {
+                    // refill the buffer of chunk seq-1 with chunk seq+RW_NB-1 once
+                    // every producer is done with it
+                    if (!mbar_wait_ab(smem_u32(&boxe_b[(seq - 1) % RW_NB]), (uint32_t)((seq - 1) / RW_NB) & 1u,
                                       abort_v)) { ok = false; break; }
-                    issue_box(seq + 1);
+                    issue_box(seq + RW_NB - 1);
                 }
                 if (!mbar_wait_ab(smem_u32(&boxf_b[bb]), (uint32_t)(seq / RW_NB) & 1u, abort_v)) { ok = false; break; }
                 if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }

@@ -157,11 +157,12 @@ __global__ void __launch_bounds__(TX_NT, 1) realin_tx_kernel(const __grid_consta
             for (int j = 0; j < TX_NQ; ++j) { tsum[j] = 0.0f; wsum[j] = 0.0f; amax[j] = 0.0f; }
             for (int kc = 0; kc < KC; ++kc, ++seq) {
                 const int bb = seq % RW_NB;
-                if (pt == 0 && seq >= 1 && seq + 1 < nseq) {
-                    // refill the buffer of chunk seq-1 once every producer is done with it
-                    if (!mbar_wait_ab(smem_u32(&boxe_b[(seq + 1) % RW_NB]), (uint32_t)((seq - 1) / RW_NB) & 1u,
+                if (pt == 0 && seq >= 1 && seq + RW_NB - 1 < nseq) {
+                    // refill the buffer of chunk seq-1 with chunk seq+RW_NB-1 once
+                    // every producer is done with it
+                    if (!mbar_wait_ab(smem_u32(&boxe_b[(seq - 1) % RW_NB]), (uint32_t)((seq - 1) / RW_NB) & 1u,
                                       abort_v)) { ok = false; break; }
-                    issue_box(seq + 1);
+                    issue_box(seq + RW_NB - 1);
                 }
                 if (!mbar_wait_ab(smem_u32(&boxf_b[bb]), (uint32_t)(seq / RW_NB) & 1u, abort_v)) { ok = false; break; }
                 if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
