@@ -163,6 +163,7 @@ struct DevState {
     int8_t* rw_wu = nullptr;    // first conv +-1 int8 weights for realin_ws_kernel (Cin <= 128, Cout <= 32)
     int8_t* rx_wu = nullptr;    // the same for realin_dxn_kernel (column taps stacked in N)
     std::vector<RwThr> rw_thr;  // first conv fold thresholds for realin_ws_kernel (host copy, 32 entries)
+    long long rw_wsum[32] = {};  // per channel: the sum of its first-conv weights over taps and bands
     float* st_w = nullptr;      // v2 stem weights [slice][band][st_CB] (+-1, 0)
     float* st_fold = nullptr;   // v2 stem [channel][5]: alpha, A, B, slope, rsign
     int st_CB = 0, st_slices = 0;
@@ -639,7 +640,14 @@ static int dev_init(const Model* m, DevState* d) {
                                 rxu[((((size_t)kc * 3 + t / 3) * 2 + h) * 96 + (t % 3) * 32 + co) * 16 + i] =
                                     rwu[((((size_t)kc * 9 + t) * 2 + h) * 32 + co) * 16 + i];
         }
-        if (!rwu.empty()) rthr.assign(32, RwThr{1ll << 62, 1, 0});
+        if (!rwu.empty()) {
+            rthr.assign(32, RwThr{1ll << 62, 1, 0});
+            for (int co = 0; co < CoutR; ++co) {
+                long long s = 0;
+                for (size_t k = 0; k < (size_t)Cin * 9; ++k) s += c1->wsign[(size_t)co * Cin * 9 + k];
+                d->rw_wsum[co] = s;
+            }
+        }
         for (int co = 0; co < CoutR; ++co) {
             const float v[5] = {c1->alpha[co], a1->A[co], a1->B[co], a1->slope[co], a1->rsign[co]};
             bool ok = v[3] >= 0.0f;
@@ -1303,6 +1311,11 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
             p.thrC[c] = d->rw_thr[c].C;
             p.thr_neg |= (uint32_t)(d->rw_thr[c].sgn < 0) << c;
             p.thr_exact |= (uint32_t)(d->rw_thr[c].exact != 0) << c;
+            // realin_ws_kernel's plane 0 carries +64 per element (every staged
+            // position, padding included): its sums exceed the exact ones by
+            // 64 * 2^16 * (the channel's weight sum), for the fold's test on Q or -Q
+            if (BNN_RW_UP0 && !dxn && !tx)
+                p.thrC[c] += (d->rw_thr[c].sgn < 0 ? -1 : 1) * (d->rw_wsum[c] << 22);
         }
         p.list = a.rm_list; p.ctl = a.rm_ctl; p.cap = a.rm_cap;
         p.N = N; p.Cin = Cin; p.H = H; p.W = W; p.Cout = Cout; p.cwo = cw_of(Cout);

@@ -2692,9 +2692,14 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 // ---------------------------------------------------------------------
 // First conv on tcgen05 (kind::i8), persistent and warp-specialised, with the
 // numerics of realin_mma_kernel: fixed-point planes q = rint(x*2^18) split
-// into three int8 planes, exact plane sums from the MMAs, the per-pixel error
+// into three byte planes, exact plane sums from the MMAs, the per-pixel error
 // bound, the monotone fold decided at both ends of the interval, undecided
-// outputs listed for realin_fixup_kernel.
+// outputs listed for realin_fixup_kernel. The planes are the bytes of the
+// magic-added float bits fma(x, 2^18, 1.5*2^23) as they come: bytes 0-1 are
+// q's, byte 2 is (q >> 16) + 64 in 0..127 (|q| < 2^22), read unsigned. Every
+// staged position carries that +64 (padding is written as the encoding of
+// 0.0), so a channel's plane-0 sum exceeds the exact one by 64 * (its weight
+// sum over taps and bands), a constant the host folds into its threshold.
 // Item = R consecutive rows of one image. Staged rows y0-1 .. y0+R, each W
 // pixels plus one zero column (width Wp = W + 1), flattened: position
 // q = row*Wp + col, col 0 = zero, col c = pixel x = c-1. The output of TMEM
@@ -2720,6 +2725,11 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 #endif
 #ifndef BNN_RW_LD32
 #define BNN_RW_LD32 1
+#endif
+// plane 0 as the unsigned byte 2 of the magic-added float bits (q>>16) + 64,
+// its bias folded into the thresholds; 0: signed plane 0 (q - magic first)
+#ifndef BNN_RW_UP0
+#define BNN_RW_UP0 1
 #endif
 #ifndef BNN_RW_NISS
 #define BNN_RW_NISS 2
@@ -2876,10 +2886,14 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                     const int q = pt + RW_NPROD * j;
                     if (q < SP) {
                         const int row = q / Wp, col = q - row * Wp;
-                        // plane 0 = byte 2 (signed), plane 1 = byte 1, plane 2 = byte 0; word k = bands 4k..4k+3
+                        // plane 0 = byte 2 (unsigned: (q >> 16) + 64), plane 1 = byte 1, plane 2 = byte 0;
+                        // word k = bands 4k..4k+3
                         uint32_t w[3][8];
 #pragma unroll
-                        for (int k = 0; k < 8; ++k) w[0][k] = w[1][k] = w[2][k] = 0u;
+                        for (int k = 0; k < 8; ++k) {
+                            w[0][k] = BNN_RW_UP0 ? 0x40404040u : 0u;  // the encoding of 0.0 in every plane
+                            w[1][k] = w[2][k] = 0u;
+                        }
                         if (col >= 1 && row < R + 2) {
                             const float* src = bx + (size_t)row * p.W + (col - 1);
 #if BNN_RW_LD32
@@ -2916,9 +2930,11 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                                 for (int i = 0; i < 8; ++i) {
                                     // rm_fix in one rounding: x * 2^18 is exact, so
                                     // fma(x, 2^18, 1.5*2^23) == fadd(fmul(x, 2^18), 1.5*2^23)
+                                    // byte 2 of the raw bits is (q >> 16) + 64 (|q| < 2^22),
+                                    // bytes 0-1 are q's own
                                     qv[i] = (uint32_t)(__float_as_int(__fmaf_rn(xv[(g - g2) * 8 + i], (float)(1 << RM_FIX),
                                                                                12582912.0f)) -
-                                                       0x4B400000);
+                                                       (BNN_RW_UP0 ? 0 : 0x4B400000));
                                 }
 #pragma unroll
                                 for (int h = 0; h < 2; ++h) {
@@ -2995,7 +3011,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                         const int tile = acc / 3, pl = acc - tile * 3;
                         const uint32_t d = tmem + (uint32_t)(buf * 256 + tile * 96 + pl * 32);
                         const uint64_t ap = a0 + (uint64_t)(pl * 2 * SP + tile * 128);
-                        const uint32_t id = pl == 0 ? id_s : id_u;
+                        const uint32_t id = (pl == 0 && !BNN_RW_UP0) ? id_s : id_u;
 #pragma unroll
                         for (int t = 0; t < 9; ++t)
                             tc_mma_i8(d, ap + (uint64_t)((t / 3) * Wp + t % 3), w0 + (uint64_t)((kc * 9 + t) * 2 * 32), id,
