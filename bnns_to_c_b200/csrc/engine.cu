@@ -655,6 +655,12 @@ static int dev_init(const Model* m, DevState* d) {
             rexact[co] = ok ? 0 : 1;
             if (!rthr.empty()) rthr[co] = fold_threshold(v, !ok);
         }
+        // realin_ws_kernel computes -Q for decreasing folds (the dxn / tx copies above keep the signs)
+        if (BNN_RW_NEGW && !rwu.empty())
+            for (int co = 0; co < CoutR; ++co)
+                if (rthr[co].sgn < 0)
+                    for (size_t blk = 0; blk < (size_t)4 * 9 * 2; ++blk)
+                        for (int i = 0; i < 16; ++i) rwu[(blk * 32 + co) * 16 + i] = (int8_t)-rwu[(blk * 32 + co) * 16 + i];
     }
     // binary convs
     struct Item {

@@ -2731,6 +2731,11 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 #ifndef BNN_RW_UP0
 #define BNN_RW_UP0 1
 #endif
+// realin_ws_kernel's weights of decreasing folds negated on the host, so its
+// epilogue tests Q against the threshold without a per-channel sign
+#ifndef BNN_RW_NEGW
+#define BNN_RW_NEGW 1
+#endif
 #ifndef BNN_RW_NISS
 #define BNN_RW_NISS 2
 #endif
@@ -3063,6 +3068,18 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                     tc_ld16(ta + 64 + c0, s0);
                     tc_wait_ld();
                     if (valid) {
+#if BNN_RW_NEGW
+                        // the host negated the weights of decreasing folds, so every
+                        // channel tests Q itself: D = Q - C, 1 when D >= E, 0 when
+                        // D < -E, undecided between (|s2*256 + s1| < 2^26)
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int qh = (int)s2[k] * 256 + (int)s1[k];
+                            const long long D = (long long)qh * 256 + (long long)(int)s0[k] - p.thrC[c0 + k];
+                            if (D >= E) bits |= 1u << (c0 + k);
+                            else if (D >= -E) und |= 1u << (c0 + k);
+                        }
+#else
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
                             const int co = c0 + k;
@@ -3075,8 +3092,19 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                             if (ok && Qs - E >= C) bits |= 1u << co;
                             else if (!(ok && Qs + E < C)) und |= 1u << co;
                         }
+#endif
                     }
                 }
+#if BNN_RW_NEGW
+                {
+                    // channels whose fold is not monotone, or a non-finite bound: all
+                    // to the fix-up; channels past Cout: neither decided nor listed
+                    const uint32_t okm = finite ? ~p.thr_exact : 0u;
+                    const uint32_t cm = p.Cout >= 32 ? 0xffffffffu : (1u << p.Cout) - 1u;
+                    bits &= okm & cm;
+                    und = (und | ~okm) & cm;
+                }
+#endif
                 if (valid) {
                     p.out[pix * p.cwo] = bits;
                     if (und) realin_list(p.list, p.ctl, p.cap, pix, 0, und);
