@@ -2864,6 +2864,15 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             bulk_g2s(sm0, p.wu, (uint32_t)RW_WBYTES, smem_u32(&wrdy_b));
             for (int s = 0; s < RW_NB && s < nseq; ++s) issue_box(s);
         }
+        // row and column of this thread's staged positions (the same for every
+        // item and chunk); a position holds data when col >= 1 and row < R + 2
+        int prow[RW_NQ], pcol[RW_NQ];
+#pragma unroll
+        for (int j = 0; j < RW_NQ; ++j) {
+            const int q = pt + RW_NPROD * j;
+            prow[j] = q / Wp;
+            pcol[j] = q - prow[j] * Wp;
+        }
         int stage = 0, seq = 0;
         uint32_t phase = 0;
         bool ok = true;
@@ -2890,7 +2899,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                 for (int j = 0; j < RW_NQ; ++j) {
                     const int q = pt + RW_NPROD * j;
                     if (q < SP) {
-                        const int row = q / Wp, col = q - row * Wp;
+                        const int row = prow[j], col = pcol[j];
                         // plane 0 = byte 2 (unsigned: (q >> 16) + 64), plane 1 = byte 1, plane 2 = byte 0;
                         // word k = bands 4k..4k+3
                         uint32_t w[3][8];
@@ -2979,7 +2988,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             for (int j = 0; j < RW_NQ; ++j) {
                 const int q = pt + RW_NPROD * j;
                 if (q < SP) {
-                    const int row = q / Wp, col = q - row * Wp;
+                    const int row = prow[j], col = pcol[j];
                     float e = 0.0f;  // zero columns and positions past the box are exact zeros
                     if (col >= 1 && row < R + 2)
                         e = amax[j] < 16.0f ? __fmaf_ru(p.ca, wsum[j], __fmaf_ru(p.cb, tsum[j], rnd))
@@ -3035,6 +3044,15 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         // warp w: TMEM lanes 32(w%4).. (the lane quarter its sub-partition may
         // read), tiles w/4, w/4 + RW_NEPI/128, ...
         const int quad = warp & 3, r = quad * 32 + lane;
+        // this lane's staged output position in each of its tiles, and its row
+        // and column there (the same for every item)
+        int qo_t[RW_MT], orow_t[RW_MT], ocol_t[RW_MT];
+#pragma unroll
+        for (int mt = 0; mt < RW_MT; ++mt) {
+            qo_t[mt] = mt * 128 + r + Wp + 1;
+            orow_t[mt] = qo_t[mt] / Wp;
+            ocol_t[mt] = qo_t[mt] - orow_t[mt] * Wp;
+        }
         for (int it = 0; it < my_items && !*abort_v; ++it) {
             const int buf = it & 1;
             const int item = (int)blockIdx.x + it * (int)gridDim.x;
@@ -3045,8 +3063,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             const float* bt = bpx + buf * SP;
 #pragma unroll 1
             for (int mt = warp >> 2; mt < RW_MT; mt += RW_NEPI / 128) {
-                const int qo = mt * 128 + r + Wp + 1;  // staged position of this lane's output
-                const int orow = qo / Wp, ocol = qo - orow * Wp;
+                static_assert(RW_MT == 2, "the per-tile values below are picked from two");
+                const int qo = mt ? qo_t[1] : qo_t[0], orow = mt ? orow_t[1] : orow_t[0];
+                const int ocol = mt ? ocol_t[1] : ocol_t[0];
                 const int y = y0 + orow - 1, x = ocol - 1;
                 const bool valid = orow >= 1 && orow <= R && ocol >= 1 && y < p.H;
                 float ef = 0.0f;
