@@ -471,8 +471,10 @@ static int set_kernel_attrs(int device) {
                                   RI_HP * 260 * 4)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RM_SMEM)) !=
             cudaSuccess ||
-        (e = cudaFuncSetAttribute(realin_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
-            cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_ws_kernel<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)RW_MAX_SMEM)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(realin_ws_kernel<32, 7>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)RW_MAX_SMEM)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_dxn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RW_MAX_SMEM)) !=
             cudaSuccess ||
         (e = cudaFuncSetAttribute(realin_tx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TX_MAX_SMEM)) !=
@@ -1241,7 +1243,7 @@ static bool rw_geometry(int H, int W, RwGeo* g, int rmax = 1 << 30) {
     g->NB = RW_NB;
     // every output row inside the tiles
     g->R = std::min(std::min(H, rmax), std::min(BNN_RW_RCAP, (RW_MT * 128 - W) / g->Wp + 1));
-    g->SP = (RW_MT * 128 + 2 * g->Wp + 2 + 7) & ~7;
+    g->SP = rw_sp(W);
     if (g->R < 1 || g->SP > RW_MAX_SP || g->R + 2 > 256) return false;
     const size_t fixed = rw_fixed_bytes(W, g->R, g->SP);
     if (fixed + 2 * rw_stage_bytes(g->SP) > RW_MAX_SMEM) return false;
@@ -1333,7 +1335,9 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         const int grid = std::min(p.n_items, sm_count());
         if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
         else if (tx) realin_tx_kernel<<<grid, TX_NT, geo.smem, st>>>(tm, p);
-        else realin_ws_kernel<<<grid, RW_NT, geo.smem, st>>>(tm, p);
+        // the benchmark's 32-wide patches in 7-row items get the compile-time geometry
+        else if (W == 32 && geo.R == 7) realin_ws_kernel<32, 7><<<grid, RW_NT, geo.smem, st>>>(tm, p);
+        else realin_ws_kernel<0, 0><<<grid, RW_NT, geo.smem, st>>>(tm, p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,

@@ -2788,6 +2788,9 @@ struct RealinWsParams {
     float ca, cb;
 };
 
+// staged positions of an item of realin_ws_kernel at width W: both tiles, the
+// nine taps' reach past them (2 staged rows + 2), rounded up to a multiple of 8
+__host__ __device__ constexpr int rw_sp(int W) { return (RW_MT * 128 + 2 * (W + 1) + 2 + 7) & ~7; }
 __host__ __device__ inline size_t rw_box_bytes(int W, int R) { return (size_t)W * (R + 2) * 32 * 4; }
 __host__ __device__ inline size_t rw_stage_bytes(int SP) { return (size_t)3 * 2 * SP * 16; }
 __host__ __device__ inline size_t rw_fixed_bytes(int W, int R, int SP) {
@@ -2802,6 +2805,9 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
         : "r"(taddr));
 }
 
+// TW, TR > 0: the image width and rows per item fixed at compile time (the
+// box and stage strides become immediate offsets); 0: both from p
+template <int TW, int TR>
 __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const RealinWsParams p) {
     extern __shared__ __align__(1024) unsigned char rw_smem[];
@@ -2811,8 +2817,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
     __shared__ int abort_s;
     volatile int* abort_v = &abort_s;
 
-    const int SP = p.SP, Wp = p.Wp, R = p.R, NS = p.NS, KC = p.KC;
-    const size_t box_bytes = rw_box_bytes(p.W, R), stage_bytes = rw_stage_bytes(SP);
+    const int W = TW > 0 ? TW : p.W, R = TR > 0 ? TR : p.R, Wp = W + 1;
+    const int SP = TW > 0 ? rw_sp(TW) : p.SP, NS = p.NS, KC = p.KC;
+    const size_t box_bytes = rw_box_bytes(W, R), stage_bytes = rw_stage_bytes(SP);
     unsigned char* boxes = rw_smem + RW_WBYTES;                        // [RW_NB][32][R+2][W] f32
     unsigned char* stages = boxes + RW_NB * box_bytes;                 // [NS][3 planes][2 halves][SP][16]
     float* bpx = reinterpret_cast<float*>(stages + NS * stage_bytes);  // [2][SP] error bound per position
@@ -2894,7 +2901,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                 if (!mbar_wait_ab(smem_u32(&empty_b[stage]), phase ^ 1u, abort_v)) { ok = false; break; }
                 const float* bx = reinterpret_cast<const float*>(boxes + bb * box_bytes);
                 unsigned char* st = stages + stage * stage_bytes;
-                const size_t bstride = (size_t)(R + 2) * p.W;  // floats between bands in the box
+                const size_t bstride = (size_t)(R + 2) * W;  // floats between bands in the box
 #pragma unroll
                 for (int j = 0; j < RW_NQ; ++j) {
                     const int q = pt + RW_NPROD * j;
@@ -2909,7 +2916,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                             w[1][k] = w[2][k] = 0u;
                         }
                         if (col >= 1 && row < R + 2) {
-                            const float* src = bx + (size_t)row * p.W + (col - 1);
+                            const float* src = bx + (size_t)row * W + (col - 1);
 #if BNN_RW_LD32
                             float xa[32];  // all 32 bands' loads in flight at once
 #pragma unroll
@@ -3076,7 +3083,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                 // E = ceil(e * 2^18) (exact scaling); e past 2^40, inf or NaN: nothing is decided
                 const bool finite = ef <= 1.0995116e12f;
                 const long long E = finite ? __float2ll_ru(ef * 262144.0f) : 0ll;
-                const size_t pix = ((size_t)n * p.H + y) * p.W + x;
+                const size_t pix = ((size_t)n * p.H + y) * W + x;
                 uint32_t bits = 0u, und = 0u;
                 const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * 256 + mt * 96);
 #pragma unroll 1
