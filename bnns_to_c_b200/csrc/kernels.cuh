@@ -2820,6 +2820,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
     const int W = TW > 0 ? TW : p.W, R = TR > 0 ? TR : p.R, Wp = W + 1;
     const int SP = TW > 0 ? rw_sp(TW) : p.SP, NS = p.NS, KC = p.KC;
     const size_t box_bytes = rw_box_bytes(W, R), stage_bytes = rw_stage_bytes(SP);
+    // staged positions per producer thread, at most (2 at a compile-time width up to 100)
+    constexpr int NQ = TW > 0 ? (rw_sp(TW) + RW_NPROD - 1) / RW_NPROD : RW_NQ;
+    static_assert(NQ <= RW_NQ, "staged positions per producer thread");
     unsigned char* boxes = rw_smem + RW_WBYTES;                        // [RW_NB][32][R+2][W] f32
     unsigned char* stages = boxes + RW_NB * box_bytes;                 // [NS][3 planes][2 halves][SP][16]
     float* bpx = reinterpret_cast<float*>(stages + NS * stage_bytes);  // [2][SP] error bound per position
@@ -2873,9 +2876,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         }
         // row and column of this thread's staged positions (the same for every
         // item and chunk); a position holds data when col >= 1 and row < R + 2
-        int prow[RW_NQ], pcol[RW_NQ];
+        int prow[NQ], pcol[NQ];
 #pragma unroll
-        for (int j = 0; j < RW_NQ; ++j) {
+        for (int j = 0; j < NQ; ++j) {
             const int q = pt + RW_NPROD * j;
             prow[j] = q / Wp;
             pcol[j] = q - prow[j] * Wp;
@@ -2885,9 +2888,9 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
         bool ok = true;
         for (int it = 0; it < my_items && ok && !*abort_v; ++it) {
             // per staged position: sum |x| and sum (Cin - band) |x| (both rounded up)
-            float tsum[RW_NQ], wsum[RW_NQ], amax[RW_NQ];
+            float tsum[NQ], wsum[NQ], amax[NQ];
 #pragma unroll
-            for (int j = 0; j < RW_NQ; ++j) { tsum[j] = 0.0f; wsum[j] = 0.0f; amax[j] = 0.0f; }
+            for (int j = 0; j < NQ; ++j) { tsum[j] = 0.0f; wsum[j] = 0.0f; amax[j] = 0.0f; }
             for (int kc = 0; kc < KC; ++kc, ++seq) {
                 const int bb = seq % RW_NB;
                 if (pt == 0 && seq >= 1 && seq + RW_NB - 1 < nseq) {
@@ -2903,7 +2906,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
                 unsigned char* st = stages + stage * stage_bytes;
                 const size_t bstride = (size_t)(R + 2) * W;  // floats between bands in the box
 #pragma unroll
-                for (int j = 0; j < RW_NQ; ++j) {
+                for (int j = 0; j < NQ; ++j) {
                     const int q = pt + RW_NPROD * j;
                     if (q < SP) {
                         const int row = prow[j], col = pcol[j];
@@ -2992,7 +2995,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
             float* bt = bpx + buf * SP;
             const float rnd = __fmul_ru((float)p.Cin, 1.0f / (float)(1 << (RM_FIX + 1)));
 #pragma unroll
-            for (int j = 0; j < RW_NQ; ++j) {
+            for (int j = 0; j < NQ; ++j) {
                 const int q = pt + RW_NPROD * j;
                 if (q < SP) {
                     const int row = prow[j], col = pcol[j];
