@@ -1050,13 +1050,15 @@ static int launch_bconv(BconvParams p, int N, cudaStream_t st) {
         if (rc != BNN_ERR_UNSUPPORTED) return rc;
     }
     // e2m1 MMAs where they measured faster than int8 (4096 32x32 patches):
-    // 64- and 128-channel layers with at least 4 input words (dec3.conv1
-    // 0.090 vs 0.117 ms, dec2.conv1 0.162 vs 0.175, dec3.conv2 0.058 vs
-    // 0.060), 256-channel layers with at least 16, in 128-channel blocks
-    // (dec4.conv1 0.105 vs 0.120, bott.conv2 0.060 vs 0.062; shallower ones
-    // are slower that way); kind 5 takes them for every non-pooled layer
-    const bool f4 = (g_bconv_kind == 0 && (p.ubn == 64 || p.ubn == 128) && p.Kw >= 4) ||
-                    (g_bconv_kind == 0 && p.ubn == 256 && p.Kw >= 16) || g_bconv_kind == 5;
+    // 64- and 128-channel layers with at least 2 input words (dec3.conv1
+    // 0.084 vs 0.118 ms, dec2.conv1 0.131 vs 0.169, enc3.conv1 0.046 vs
+    // 0.048, dec2.conv2 0.076 vs 0.077), 256-channel layers with at least 8,
+    // in 128-channel blocks (dec4.conv1 0.103 vs 0.119, dec4.conv2 0.051 vs
+    // 0.054, bott.conv2 0.056 vs 0.061); one input word (enc2.conv1 0.074 vs
+    // 0.060) and the 32-channel layers (dec1.conv1 0.278 vs 0.209) stay int8;
+    // kind 5 takes e2m1 for every non-pooled layer
+    const bool f4 = (g_bconv_kind == 0 && (p.ubn == 64 || p.ubn == 128) && p.Kw >= 2) ||
+                    (g_bconv_kind == 0 && p.ubn == 256 && p.Kw >= 8) || g_bconv_kind == 5;
     if (f4 && !p.out2 && p.w4) {
         int rc = BNN_ERR_UNSUPPORTED;
         switch (p.ubn) {
