@@ -249,6 +249,7 @@ struct Scratch {
     }
     template <class T>
     T* alloc(size_t count) {
+        if (n == (int)(sizeof p / sizeof p[0])) die(fn, "internal: more device buffers than one call holds");
         void* q = nullptr;
         if (cudaMalloc(&q, count ? count * sizeof(T) : 1) != cudaSuccess) {
             cudaGetLastError();
