@@ -1434,7 +1434,10 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
     const size_t total = (size_t)N * H * W;
     if (total >= ((size_t)1 << 31)) return set_error(BNN_ERR_ARG, "N*H*W = %zu: at most 2^31 - 1 pixels", total);
     unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 511) / 512, 148 * 8));
-    head1x1_kernel<<<blocks, 256, 0, st>>>(p);
+    if (p.Cin == 32 && p.ncls == 3)
+        head1x1_c32_kernel<3><<<blocks, 256, 0, st>>>(p);  // the common head: weights in registers
+    else
+        head1x1_kernel<<<blocks, 256, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
     return BNN_OK;

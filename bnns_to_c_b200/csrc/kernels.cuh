@@ -3618,6 +3618,51 @@ struct HeadParams {
 // pixel and channel, shared by the classes), the two pixels' chains of a
 // class advanced by one fp32x2 add. 32-bit indexing (the forward keeps
 // N*H*W < 2^31).
+// The head for one 32-channel word per pixel and NC classes, the common
+// case: the NC x 32 weights in registers, the signs of four channels at a
+// time from a 16-entry table of +-1.0 quadruples, and per class the
+// reference's chain bias, then channels 0..31 in order, as fma(+-1, w, acc):
+// the product is exact, so each step is acc + (+-w) rounded once, the same
+// bits as the generic kernel below and as csrc/bnn_head.c:21-34.
+template <int NC>
+__global__ void __launch_bounds__(256) head1x1_c32_kernel(const HeadParams p) {
+    __shared__ float4 pm[16];  // nibble b: bit k of b -> +1.0, else -1.0, in component k
+    if (threadIdx.x < 16) {
+        const unsigned b = threadIdx.x;
+        pm[b] = make_float4(b & 1u ? 1.0f : -1.0f, b & 2u ? 1.0f : -1.0f, b & 4u ? 1.0f : -1.0f,
+                            b & 8u ? 1.0f : -1.0f);
+    }
+    float w[NC][32], bias[NC];
+#pragma unroll
+    for (int o = 0; o < NC; ++o) {
+        bias[o] = __ldg(p.bias + o);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) w[o][c] = __ldg(p.Wt + o * 32 + c);
+    }
+    __syncthreads();
+    const unsigned HW = (unsigned)p.H * (unsigned)p.W, total = (unsigned)p.N * HW;
+    for (unsigned g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+        const uint32_t bits = __ldg(p.in + g);
+        float acc[NC];
+#pragma unroll
+        for (int o = 0; o < NC; ++o) acc[o] = bias[o];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 sg = pm[(bits >> (4 * q)) & 15u];
+#pragma unroll
+            for (int o = 0; o < NC; ++o) {
+                acc[o] = __fmaf_rn(sg.x, w[o][4 * q + 0], acc[o]);
+                acc[o] = __fmaf_rn(sg.y, w[o][4 * q + 1], acc[o]);
+                acc[o] = __fmaf_rn(sg.z, w[o][4 * q + 2], acc[o]);
+                acc[o] = __fmaf_rn(sg.w, w[o][4 * q + 3], acc[o]);
+            }
+        }
+        const unsigned n = g / HW, px = g - n * HW;
+#pragma unroll
+        for (int o = 0; o < NC; ++o) p.out[(size_t)(n * NC + o) * HW + px] = acc[o];
+    }
+}
+
 constexpr int HEAD_MAXC = 8;        // classes handled per pass
 constexpr int HEAD_MAXW = 64 * 32;  // weights held in shared memory (ncls*Cin)
 __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
