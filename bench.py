@@ -606,7 +606,8 @@ def run_ours(args):
         e2e = P * world * args.steps / e2e_s if e2e_s else None
         model, cores = cpu_info()
         cpu = None
-        if not args.no_cpu_baseline:
+        # the reference on the host cores: rank 0 of a single-GPU run only
+        if world == 1 and not args.no_cpu_baseline:
             with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
                 f.write(model_blob(stem))
                 path = f.name
@@ -972,7 +973,8 @@ def run_react(args):
         value = P * world * args.steps / (dev_ms / 1e3)
         model, cores = cpu_info()
         cpu = None
-        if not args.no_cpu_baseline:
+        # the reference on the host cores: rank 0 of a single-GPU run only
+        if world == 1 and not args.no_cpu_baseline:
             with tempfile.NamedTemporaryFile(suffix=".blob", delete=False) as f:
                 f.write(react_blob())
                 path = f.name
