@@ -644,8 +644,12 @@ def run_ours(args):
                     if (e2e and h2d_agg_gbs) else None,
                     "h2d_aggregate_how": "all ranks copy their pinned 2 GB input at once after a barrier; "
                                          "world x bytes / the slowest rank's copy time",
-                    "affinity": affinity},
-            "gpu_launches": launches_per_fwd * args.steps * (1 + (0 if args.no_e2e else chunks)),
+                    "affinity": affinity,
+                    # this repo's kernels in the end-to-end timed region (the batch runs in
+                    # 256-patch chunks, one graph replay each)
+                    "gpu_launches": None if args.no_e2e else launches_per_fwd * args.steps * chunks},
+            # this repo's kernels launched in the device-resident timed region (per rank)
+            "gpu_launches": launches_per_fwd * args.steps,
             "device_wait_timeouts": bn.device_wait_timeouts(local),
             "roofline": (
                 {"bound": "tensor",
@@ -831,7 +835,9 @@ def run_scene(args):
                     "h2d_bytes_per_step": 120 * H * W * 4 * ns * world, "d2h_bytes_per_step": 3 * H * W * 4 * ns * world,
                     "api": "bnn_forward_patched (pinned host cubes)", "matches_device_path": same,
                     "sample": f"{ns} cubes per rank"},
-            "gpu_launches": None,
+            # per cube and step: the tile gather, the batched forward, the stitch
+            # (a cube's tiles fit one forward chunk), rank 0's share
+            "gpu_launches": len(mine) * args.steps * (2 + m.launches(tiles, Pt, Pt)),
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
