@@ -62,12 +62,12 @@ FFMA_PER_CLK_SM = 128       # fp32 fused multiply-adds / clock / SM (nominal; pr
 SEED_MODEL, SEED_INPUT = 0, 1
 POPC_PER_CLK_SM = 16        # 32-bit population count results / clock / SM (CUDA guide; probe: 15.6)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 17 binary-conv
-# launches of one forward of the default workload at 512 patches, summed over one
-# ncu capture per kernel instance (commit ab0ffc7 kernels); scaled by patches in
-# the bench line
-BCONV_DRAM_BYTES_PER_512 = 21.5e6
+# launches of one forward of the default workload at 512 patches, from one ncu
+# capture of that forward's 20 launches (the kernels with the register-weight head
+# and the e2m1 rule of 2 / 8 words); scaled by patches in the bench line
+BCONV_DRAM_BYTES_PER_512 = 23.7e6
 # the same for the first conv's main kernel (its 251.66 MB input read once)
-REALIN_DRAM_BYTES_PER_512 = 253.0e6
+REALIN_DRAM_BYTES_PER_512 = 256.1e6
 # bit planes the 17 binary convs read and write per 32x32 patch at base 32
 # (inputs, concat halves, outputs and pooled outputs)
 BCONV_ALGO_BYTES_PER_PATCH = 58112
