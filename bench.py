@@ -669,6 +669,9 @@ def run_ours(args):
                  "frac_of_popc_peak": round(bconv_ach / popc_peak, 4),
                  # the e2m1 layers (default: the deeper 64/128/256-channel ones) have twice the int8 rate
                  "frac_of_e2m1_peak": round(bconv_ach / (2 * tensor_i8_peak), 4),
+                 # what bounds them, from ncu (not this run): the tensor-core operand interface
+                 "tc_interface_busy_ncu": {"dec1.conv1 bconv_ws_kernel<32,8,0,4>, 4096 patches": 0.785,
+                                           "source": "ncu --set full, one launch of the 4096-patch forward"},
                  "time_share": frac_split.get("bconv")}
                 if args.bconv in ("tc", "tc8", "tc4", "tcx", "mma") else
                 {"bound": "popc", "kernel": "bconv3x3_kernel (17 fused binary convs, XOR + POPC)",
@@ -700,6 +703,10 @@ def run_ours(args):
                                                    / peaks["hbm_gbs"], 4) if peaks.get("hbm_gbs") else None,
                               "traffic": round(REALIN_DRAM_BYTES_PER_512 * P / 512)
                               if (H, W) == (32, 32) and not stem else None,
+                              # what bounds it, from ncu (not this run): the tensor-core operand interface
+                              "tc_interface_busy_ncu": {"realin_ws_kernel<32,7>, 512 patches": 0.719,
+                                                        "source": "ncu --set full, one launch at 512 patches"}
+                              if args.first == "tc" else None,
                               "time_share": frac_split.get("conv_real")},
                 "hbm_input": {"bytes_per_step": P * 120 * H * W * 4, "peak_gbs": peaks.get("hbm_gbs"),
                               "min_ms": round(P * 120 * H * W * 4 / (peaks.get("hbm_gbs", 6538.9) * 1e6), 4)},
