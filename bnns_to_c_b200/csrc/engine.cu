@@ -72,6 +72,42 @@ static int poison_arena(void* base, size_t bytes, cudaStream_t s) {
     return BNN_OK;
 }
 
+// Programmatic dependent launch for the forward's kernels when the batch is
+// small (most SMs idle, so the next kernel's prologue - TMEM, barriers,
+// weights - overlaps this one's tail): set per forward by forward_launches,
+// read by the launch sites below. BNN_PDL=0 in the environment turns it off.
+static thread_local bool t_pdl = false;
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("BNN_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+constexpr double kPdlPixels = 16.0 * 1024;  // batches of at most 16 32x32 patches
+
+// launch kern<<<grid, block, smem, st>>>(args...), with the programmatic
+// stream serialisation attribute when t_pdl is set
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+    if (!t_pdl) {
+        kern<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // every device allocation of the engine goes through here
 template <class T>
 static cudaError_t dev_malloc(T** p, size_t bytes) {
@@ -958,8 +994,7 @@ static int launch_ws(BconvParams p, int N, cudaStream_t st) {
     const size_t smem = std::max<size_t>(
         (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
     const int grid = (int)std::min<long>(groups * ncb, sm_count());
-    bconv_ws_kernel<BN, MT, F4, EW><<<grid, Cfg::NT, smem, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(bconv_ws_kernel<BN, MT, F4, EW>, (unsigned)grid, Cfg::NT, smem, st, p);
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 launch: %s", cudaGetErrorString(e));
     note_kernel("bconv_ws_kernel<%d,%d,%s,%d> (tcgen05 %s)", BN, MT, F4 ? "e2m1" : "i8", EW,
                 F4 ? "kind::mxf4" : "kind::i8");
@@ -1018,8 +1053,7 @@ static int launch_ws_pool(BconvParams p, int N, cudaStream_t st) {
     const size_t smem = std::max<size_t>(
         (size_t)ns * Cfg::stage_bytes((int)sp) + Cfg::fixed_bytes((int)sp, (int)Gw, p.Cout), (size_t)116 * 1024);
     const int grid = (int)std::min<long>(groups * ncb, sm_count());
-    bconv_ws_pool_kernel<BN, MT, EW><<<grid, Cfg::NT, smem, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(bconv_ws_pool_kernel<BN, MT, EW>, (unsigned)grid, Cfg::NT, smem, st, p);
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "bconv tcgen05 pooled launch: %s", cudaGetErrorString(e));
     note_kernel("bconv_ws_pool_kernel<%d,%d,%d> (tcgen05 kind::i8, polyphase 2x2 pool)", BN, MT, EW);
     return BNN_OK;
@@ -1338,14 +1372,13 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
         else if (tx) realin_tx_kernel<<<grid, TX_NT, geo.smem, st>>>(tm, p);
         // the benchmark's 32-wide patches in 7-row items get the compile-time geometry
-        else if (W == 32 && geo.R == 7) realin_ws_kernel<32, 7><<<grid, RW_NT, geo.smem, st>>>(tm, p);
-        else realin_ws_kernel<0, 0><<<grid, RW_NT, geo.smem, st>>>(tm, p);
+        else if (W == 32 && geo.R == 7) launch_k(realin_ws_kernel<32, 7>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
+        else launch_k(realin_ws_kernel<0, 0>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
                           Cout, p.cwo};
-        realin_fixup_kernel<<<fixup_blocks(N, H, W), FIX_WARPS * 32, 0, st>>>(f);
-        e = cudaGetLastError();
+        e = launch_k(realin_fixup_kernel, (unsigned)fixup_blocks(N, H, W), FIX_WARPS * 32, 0, st, f);
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin fixup launch: %s", cudaGetErrorString(e));
         return BNN_OK;
     }
@@ -1435,9 +1468,9 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
     if (total >= ((size_t)1 << 31)) return set_error(BNN_ERR_ARG, "N*H*W = %zu: at most 2^31 - 1 pixels", total);
     unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 511) / 512, 148 * 8));
     if (p.Cin == 32 && p.ncls == 3)
-        head1x1_c32_kernel<3><<<blocks, 256, 0, st>>>(p);  // the common head: weights in registers
+        launch_k(head1x1_c32_kernel<3>, blocks, 256, 0, st, p);  // the common head: weights in registers
     else
-        head1x1_kernel<<<blocks, 256, 0, st>>>(p);
+        launch_k(head1x1_kernel, blocks, 256, 0, st, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
     return BNN_OK;
@@ -1488,6 +1521,11 @@ struct ProfCtx {
 
 static int forward_launches(const Model* m, DevState* d, const float* x, int N, int H, int W, float* logits,
                             cudaStream_t st, const Dbg* dbg, ProfCtx* pc) {
+    // small batches: dependent launches (the flag is reset on every return)
+    struct PdlScope {
+        explicit PdlScope(bool on) { t_pdl = on; }
+        ~PdlScope() { t_pdl = false; }
+    } pdl_scope(pdl_enabled() && (double)N * H * W <= kPdlPixels);
     static const char* EN[4] = {"enc1", "enc2", "enc3", "enc4"};
     static const char* DN[4] = {"dec4", "dec3", "dec2", "dec1"};
     Arena& a = d->ar;

@@ -64,6 +64,14 @@ struct BconvParams {
 // read by bnn_device_error)
 __device__ unsigned int g_bnn_wait_timeouts = 0;
 
+// Programmatic dependent launch (small batches): a kernel lets the next one
+// in the stream start its prologue as soon as every CTA of this one is
+// resident (pdl_trigger), and waits for the previous kernel to finish and
+// its writes to be visible before it reads that kernel's output
+// (pdl_wait). Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 template <int KC>
 struct KcTraits {
     static constexpr int VW = KC >= 4 ? 4 : KC;                 // words per smem load
@@ -953,6 +961,8 @@ constexpr int FIX_PER_LANE = (9 * FIX_MAXC + 31) / 32;  // window elements a lan
 
 __global__ void __launch_bounds__(FIX_WARPS * 32) realin_fixup_kernel(const RealinFixParams p) {
     __shared__ float win[FIX_WARPS][9][FIX_MAXC];
+    pdl_trigger();
+    pdl_wait();  // the list, the counters and the bits are the first conv's
     const unsigned int cnt = min(p.ctl[0], (unsigned)p.cap);
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const size_t plane = (size_t)p.H * p.W;
@@ -1566,6 +1576,7 @@ struct GridWalk {
 // p.TNI = pipeline stages
 template <int BN, int MT, bool F4, int EW>
 __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
+    pdl_trigger();
     using C = WsCfg<BN, MT, F4, EW>;
     constexpr int NBUF = C::NBUF, PI = C::PI, NQ = C::NQ, NPROD = C::NPROD, NEPI = C::NEPI;
     constexpr int NCH = BN / 32, NPAIR = MT * NCH;  // epilogue units: (tile, 32-column chunk)
@@ -1678,6 +1689,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_kernel(const BconvParams p) {
 
     if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
+        pdl_wait();  // the input planes are the previous layers'
         const int pt = tid - NEPI;
         // map the staged positions q = pt + NPROD*j of `item` into table `tb`
         // (staged position 0 = first output - Gw - 1)
@@ -2369,6 +2381,7 @@ struct WsPoolCfg {
 // blocks; p.TNI = pipeline stages; p.gk / p.Gw: the half-res grid
 template <int BN, int MT, int EW>
 __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams p) {
+    pdl_trigger();
     using C = WsPoolCfg<BN, MT, EW>;
     constexpr int NPH = C::NPH, NBUF = C::NBUF, PI = C::PI, NQP = C::NQP, NPROD = C::NPROD, NEPI = C::NEPI;
     constexpr int NCH = BN / 32, NPAIR = MT * NCH;
@@ -2464,6 +2477,7 @@ __global__ void __launch_bounds__(512, 1) bconv_ws_pool_kernel(const BconvParams
 
     if (warp >= C::EW && warp < 14) {
         // ------------------------------------------------------------ producers
+        pdl_wait();  // the input plane is the previous layer's
         const int pt = tid - NEPI;
         // one half-res grid position per staged q; its four full-res pixels
         // are the phases (row parity, column parity)
@@ -2810,6 +2824,7 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
 template <int TW, int TR>
 __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const RealinWsParams p) {
+    pdl_trigger();
     extern __shared__ __align__(1024) unsigned char rw_smem[];
     __shared__ __align__(8) unsigned long long boxf_b[RW_NB], boxe_b[RW_NB], full_b[4], empty_b[4], accf_b[2],
         acce_b[2], bpxf_b[2], wrdy_b;
@@ -2859,6 +2874,7 @@ __global__ void __launch_bounds__(RW_NT, 1) realin_ws_kernel(const __grid_consta
 
     if (warp >= RW_PW0 && warp < RW_IW0) {
         // ------------------------------------------------------------ producers
+        pdl_wait();
         const int pt = tid - RW_NEPI;
         const int nseq = my_items * KC;
         auto issue_box = [&](int seq) {  // TMA of chunk kc of item seq/KC into buffer seq % RW_NB
@@ -3627,6 +3643,7 @@ struct HeadParams {
 template <int NC>
 __global__ void __launch_bounds__(256) head1x1_c32_kernel(const HeadParams p) {
     __shared__ float4 pm[16];  // nibble b: bit k of b -> +1.0, else -1.0, in component k
+    pdl_trigger();
     if (threadIdx.x < 16) {
         const unsigned b = threadIdx.x;
         pm[b] = make_float4(b & 1u ? 1.0f : -1.0f, b & 2u ? 1.0f : -1.0f, b & 4u ? 1.0f : -1.0f,
@@ -3640,6 +3657,7 @@ __global__ void __launch_bounds__(256) head1x1_c32_kernel(const HeadParams p) {
         for (int c = 0; c < 32; ++c) w[o][c] = __ldg(p.Wt + o * 32 + c);
     }
     __syncthreads();
+    pdl_wait();  // the bits are the last layer's
     const unsigned HW = (unsigned)p.H * (unsigned)p.W, total = (unsigned)p.N * HW;
     for (unsigned g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
         const uint32_t bits = __ldg(p.in + g);
@@ -3668,6 +3686,8 @@ constexpr int HEAD_MAXW = 64 * 32;  // weights held in shared memory (ncls*Cin)
 __global__ void __launch_bounds__(256) head1x1_kernel(const HeadParams p) {
     __shared__ float ws[HEAD_MAXW];
     __shared__ float bs[HEAD_MAXC];
+    pdl_trigger();
+    pdl_wait();
     const int nw = p.ncls * p.Cin;
     for (int i = threadIdx.x; i < nw && i < HEAD_MAXW; i += blockDim.x) ws[i] = p.Wt[i];
     if (threadIdx.x < p.ncls && threadIdx.x < HEAD_MAXC) bs[threadIdx.x] = p.bias[threadIdx.x];
