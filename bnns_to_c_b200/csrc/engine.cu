@@ -1369,12 +1369,18 @@ static int run_realin_fast(DevState* d, const Model* m, const float* x, int N, i
         p.c9 = first_conv_c9(Cin);
         first_conv_cab(Cin, &p.ca, &p.cb);
         const int grid = std::min(p.n_items, sm_count());
-        if (dxn) realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
-        else if (tx) realin_tx_kernel<<<grid, TX_NT, geo.smem, st>>>(tm, p);
-        // the benchmark's 32-wide patches in 7-row items get the compile-time geometry
-        else if (W == 32 && geo.R == 7) launch_k(realin_ws_kernel<32, 7>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
-        else launch_k(realin_ws_kernel<0, 0>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e;
+        if (dxn) {
+            realin_dxn_kernel<<<grid, RX_NT, geo.smem, st>>>(tm, p);
+            e = cudaGetLastError();
+        } else if (tx) {
+            realin_tx_kernel<<<grid, TX_NT, geo.smem, st>>>(tm, p);
+            e = cudaGetLastError();
+        } else if (W == 32 && geo.R == 7) {  // the benchmark's 32-wide patches in 7-row items: geometry compiled in
+            e = launch_k(realin_ws_kernel<32, 7>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
+        } else {
+            e = launch_k(realin_ws_kernel<0, 0>, (unsigned)grid, RW_NT, geo.smem, st, tm, p);
+        }
         if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "realin tcgen05 launch: %s", cudaGetErrorString(e));
         RealinFixParams f{x, d->ri_wf, d->ri_fold, out, a.rm_list, a.rm_ctl, a.rm_cap, N, Cin, d->ri_CinP, H, W,
                           Cout, p.cwo};
@@ -1467,11 +1473,9 @@ static int run_head(DevState* d, const Model* m, const uint32_t* in, int N, int 
     const size_t total = (size_t)N * H * W;
     if (total >= ((size_t)1 << 31)) return set_error(BNN_ERR_ARG, "N*H*W = %zu: at most 2^31 - 1 pixels", total);
     unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 511) / 512, 148 * 8));
-    if (p.Cin == 32 && p.ncls == 3)
-        launch_k(head1x1_c32_kernel<3>, blocks, 256, 0, st, p);  // the common head: weights in registers
-    else
-        launch_k(head1x1_kernel, blocks, 256, 0, st, p);
-    cudaError_t e = cudaGetLastError();
+    const cudaError_t e = p.Cin == 32 && p.ncls == 3
+                              ? launch_k(head1x1_c32_kernel<3>, blocks, 256, 0, st, p)  // weights in registers
+                              : launch_k(head1x1_kernel, blocks, 256, 0, st, p);
     if (e != cudaSuccess) return set_error(BNN_ERR_CUDA, "head launch: %s", cudaGetErrorString(e));
     return BNN_OK;
 }
